@@ -1,0 +1,619 @@
+// Flash Attention 2 forward on sm_100a (tcgen05 + TMA + TMEM).
+//
+// Reference kernels:
+//   tests/test_flash_attention.py:79-247  flash_attention_fwd(Q,K,V,O,N,stride_qo,
+//       stride_kv,scale): single head, fp16 Q/K/V, fp32 O; online softmax per
+//       BN-key block; P rounded to the input dtype before P.V (:139-142);
+//       O = O / l at the end.
+//   tests/test_rel_pos_fa2.py:155-252  rel_pos_fa2_fwd: head on grid y, dense
+//       fp16 bias added before the scale, scores = (QK + bias) * scale (:202-206),
+//       fp16 O.
+//   Extensions with no reference kernel: [B,H,S,D] multi-head, causal masking,
+//       and an fp32 relative-position table [H, 2S-1] indexed i - j + S - 1.
+//
+// Work unit: one CTA = one (batch*head, 256 query rows) = two 128-row Q tiles
+// that ping-pong so the tensor core runs one tile's MMAs while the other
+// tile's softmax runs on the CUDA cores. Keys are consumed in 128-key blocks.
+//   warp 0       TMA producer: Q tiles once, then K_j / V_j into KV rings.
+//   warp 1       single-thread tcgen05.mma issuer:
+//                  S_t  = Q_t . K_j^T    (SS, M=128 N=128 K=16 steps, fp32 in TMEM)
+//                  O_t += P_t . V_j      (TS: P from TMEM, V MN-major from smem)
+//   warp 2       TMEM allocator (512 columns).
+//   warps 4-7    softmax + epilogue for tile 0; warps 8-11 for tile 1. Thread
+//                r owns query row r: it reads its S row from TMEM, computes the
+//                row max / exp2 / row sum in registers, writes fp16 P back to
+//                TMEM and, only when the running max grew by more than 2^8,
+//                rescales its O row in TMEM (lazy rescaling: exact in real
+//                arithmetic because O and l always share one reference max).
+// TMEM columns: S0 [0,128) S1 [128,256) O0 [256,256+D) O1 [256+D,256+2D);
+//   D = 64: P0/P1 in [384,448)/[448,512); D = 128: P_t aliases the first 64
+//   columns of S_t and the issuer waits for PV_t(j) before QK_t(j+1).
+#include <cmath>
+
+#include "runtime.h"
+
+namespace neso {
+namespace {
+
+constexpr int kThreads = 384;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale only when max grows by > 2^8
+
+enum BiasMode : int { kBiasNone = 0, kBiasTable = 1, kBiasDense = 2 };
+
+template <int D>
+struct FaCfg {
+  static constexpr int kChunks = D / 64;           // 128-byte TMA boxes per row
+  static constexpr int kTileBytes = 128 * D * 2;   // one Q, K or V tile
+  static constexpr int kStages = (D == 64) ? 3 : 2;
+  static constexpr bool kAliasP = (D > 64);
+  __host__ __device__ static constexpr uint32_t s_col(int t) { return t ? 128u : 0u; }
+  __host__ __device__ static constexpr uint32_t o_col(int t) { return t ? 256u + D : 256u; }
+  __host__ __device__ static constexpr uint32_t p_col(int t) {
+    return kAliasP ? s_col(t) : (t ? 256u + 2 * D + 64 : 256u + 2 * D);
+  }
+  static constexpr int kTmemCols = 512;
+  static constexpr int kSmemBytes = (2 + 2 * kStages) * kTileBytes + 1024 + 512;
+};
+
+struct FaArgs {
+  void* O;
+  int64_t o_row;   // elements
+  int64_t o_head;  // elements
+  int S;
+  int H;
+  float qk_log2;  // scale * log2(e)
+  const float* table;       // kBiasTable: [H, 2S-1] fp32
+  const __half* bias;       // kBiasDense: [BH][S][S] fp16 (row stride bias_row)
+  int64_t bias_head, bias_row;
+  int num_qblocks;
+  int out_f16;
+  DevStatus st;
+};
+
+template <int D, bool kCausal, int kBias>
+__global__ void __launch_bounds__(kThreads, 1)
+    fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                   const __grid_constant__ CUtensorMap tmV, FaArgs a) {
+  using Cfg = FaCfg<D>;
+  constexpr int KS = Cfg::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;                                // 2 tiles
+  uint8_t* sK = smem + 2 * Cfg::kTileBytes;          // KS tiles
+  uint8_t* sV = sK + KS * Cfg::kTileBytes;           // KS tiles
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + KS * Cfg::kTileBytes);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = bars + 1;
+  uint64_t* k_empty = k_full + KS;
+  uint64_t* v_full = k_empty + KS;
+  uint64_t* v_empty = v_full + KS;
+  uint64_t* s_full = v_empty + KS;   // [2]
+  uint64_t* p_full = s_full + 2;     // [2]
+  uint64_t* o_done = p_full + 2;     // [2]
+  uint64_t* mma_done = o_done + 2;   // [1]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const uint32_t warp = warp_id();
+  const uint32_t lane = lane_id();
+  const int S = a.S;
+  const int qb = kCausal ? (a.num_qblocks - 1 - static_cast<int>(blockIdx.x)) : static_cast<int>(blockIdx.x);
+  const int bh = blockIdx.y;
+  const int q0 = qb * 256;
+  const int nkv = (S + 127) / 128;
+  int ntile[2];
+#pragma unroll
+  for (int t = 0; t < 2; ++t) {
+    const int start = q0 + 128 * t;
+    ntile[t] = (start >= S) ? 0 : (kCausal ? min(nkv, start / 128 + 1) : nkv);
+  }
+  const int nmax = max(ntile[0], ntile[1]);
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < KS; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&s_full[t], 1);
+      mbar_init(&p_full[t], 4);
+      mbar_init(&o_done[t], 1);
+    }
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  if (warp == 2) {
+    tmem_alloc(tmem_slot, Cfg::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // ------------------------------------------------------------ producer --
+    const uint32_t qbytes = (ntile[1] > 0 ? 2 : 1) * Cfg::kTileBytes;
+    mbar_arrive_expect_tx(q_full, qbytes);
+    for (int t = 0; t < 2; ++t) {
+      if (ntile[t] == 0) continue;
+#pragma unroll
+      for (int c = 0; c < Cfg::kChunks; ++c) {
+        tma_load_3d(sQ + t * Cfg::kTileBytes + c * 16384, &tmQ, q_full, c * 64, q0 + 128 * t, bh);
+      }
+    }
+    int issued = 0;
+    bool aborted = false;
+    for (int j = 0; j < nmax; ++j) {
+      const int s = j % KS;
+      const uint32_t ph = (j / KS) & 1;
+      if (!mbar_wait(&k_empty[s], ph ^ 1, abort_flag, a.st, 0x1100)) { aborted = true; break; }
+      mbar_arrive_expect_tx(&k_full[s], Cfg::kTileBytes);
+#pragma unroll
+      for (int c = 0; c < Cfg::kChunks; ++c) {
+        tma_load_3d(sK + s * Cfg::kTileBytes + c * 16384, &tmK, &k_full[s], c * 64, j * 128, bh);
+      }
+      if (!mbar_wait(&v_empty[s], ph ^ 1, abort_flag, a.st, 0x1101)) {
+        issued = j;  // K_j is in flight; V_j is not
+        DevStatus quiet = a.st;
+        quiet.word = nullptr;
+        volatile int never = 0;
+        mbar_wait(&k_full[s], ph, &never, quiet, 0);
+        aborted = true;
+        break;
+      }
+      mbar_arrive_expect_tx(&v_full[s], Cfg::kTileBytes);
+#pragma unroll
+      for (int c = 0; c < Cfg::kChunks; ++c) {
+        tma_load_3d(sV + s * Cfg::kTileBytes + c * 16384, &tmV, &v_full[s], c * 64, j * 128, bh);
+      }
+      issued = j + 1;
+    }
+    if (aborted) {
+      DevStatus quiet = a.st;
+      quiet.word = nullptr;
+      volatile int never = 0;
+      mbar_wait(q_full, 0, &never, quiet, 0);
+      for (int i = (issued > KS ? issued - KS : 0); i < issued; ++i) {
+        mbar_wait(&k_full[i % KS], (i / KS) & 1, &never, quiet, 0);
+        mbar_wait(&v_full[i % KS], (i / KS) & 1, &never, quiet, 0);
+      }
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ---------------------------------------------------------- MMA issuer --
+    constexpr uint32_t idesc_qk = idesc_f16_f32(128, 128, 0, 0);
+    constexpr uint32_t idesc_pv = idesc_f16_f32(128, D, 0, 1);
+    auto issue_qk = [&](int t, int j) {
+      const uint32_t qa = smem_u32(sQ + t * Cfg::kTileBytes);
+      const uint32_t kb = smem_u32(sK + (j % KS) * Cfg::kTileBytes);
+#pragma unroll
+      for (int k = 0; k < D / 16; ++k) {
+        const uint32_t off = (k >> 2) * 16384 + (k & 3) * 32;
+        umma_f16_ss(tmem + Cfg::s_col(t), sdesc_sw128(qa + off, 16, 1024), sdesc_sw128(kb + off, 16, 1024), idesc_qk,
+                    k > 0 ? 1u : 0u);
+      }
+      umma_commit(&s_full[t]);
+    };
+    auto issue_pv = [&](int t, int j) {
+      const uint32_t vb = smem_u32(sV + (j % KS) * Cfg::kTileBytes);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        umma_f16_ts(tmem + Cfg::o_col(t), tmem + Cfg::p_col(t) + k * 8, sdesc_sw128(vb + k * 2048, 16384, 1024), idesc_pv,
+                    (j > 0 || k > 0) ? 1u : 0u);
+      }
+      umma_commit(&o_done[t]);
+    };
+
+    bool ok_run = mbar_wait(q_full, 0, abort_flag, a.st, 0x1200) &&
+                  (nmax == 0 || mbar_wait(&k_full[0], 0, abort_flag, a.st, 0x1201));
+    if (ok_run && nmax > 0) {
+      tc_fence_after();
+      for (int t = 0; t < 2; ++t)
+        if (ntile[t] > 0) issue_qk(t, 0);
+      umma_commit(&k_empty[0]);
+    }
+    for (int j = 0; ok_run && j < nmax; ++j) {
+      const int s = j % KS;
+      const uint32_t ph = (j / KS) & 1;
+      const int sn = (j + 1) % KS;
+      const uint32_t phn = ((j + 1) / KS) & 1;
+      bool v_ready = false, k_next_ready = false;
+      for (int t = 0; t < 2 && ok_run; ++t) {
+        if (j < ntile[t]) {
+          if (!mbar_wait(&p_full[t], j & 1, abort_flag, a.st, 0x1210 + t)) { ok_run = false; break; }
+          if (!v_ready) {
+            if (!mbar_wait(&v_full[s], ph, abort_flag, a.st, 0x1212)) { ok_run = false; break; }
+            v_ready = true;
+          }
+          tc_fence_after();
+          issue_pv(t, j);
+        }
+        if (!Cfg::kAliasP && j + 1 < ntile[t]) {
+          if (!k_next_ready) {
+            if (!mbar_wait(&k_full[sn], phn, abort_flag, a.st, 0x1213)) { ok_run = false; break; }
+            k_next_ready = true;
+            tc_fence_after();
+          }
+          issue_qk(t, j + 1);
+        }
+      }
+      if (Cfg::kAliasP) {
+        for (int t = 0; t < 2 && ok_run; ++t) {
+          if (j + 1 < ntile[t]) {
+            // P_t lives in S_t's columns: PV_t(j) must have read it.
+            if (!mbar_wait(&o_done[t], j & 1, abort_flag, a.st, 0x1214 + t)) { ok_run = false; break; }
+            if (!k_next_ready) {
+              if (!mbar_wait(&k_full[sn], phn, abort_flag, a.st, 0x1216)) { ok_run = false; break; }
+              k_next_ready = true;
+            }
+            tc_fence_after();
+            issue_qk(t, j + 1);
+          }
+        }
+      }
+      if (!ok_run) break;
+      umma_commit(&v_empty[s]);
+      if (j + 1 < nmax) umma_commit(&k_empty[sn]);
+    }
+    umma_commit(mma_done);
+    DevStatus quiet = a.st;
+    quiet.word = nullptr;
+    volatile int never = 0;
+    mbar_wait(mma_done, 0, &never, quiet, 0);
+  } else if (warp >= 4) {
+    // ------------------------------------------------- softmax / epilogue --
+    const int t = (warp - 4) >> 2;
+    const uint32_t q = warp & 3;
+    const int row = q * 32 + lane;
+    const int qrow = q0 + 128 * t + row;
+    const uint32_t lane_base = tmem + ((q * 32) << 16);
+    const int n_t = ntile[t];
+    const int h = bh % a.H;
+    const float* trow = nullptr;
+    if (kBias == kBiasTable) trow = a.table + static_cast<int64_t>(h) * (2 * S - 1) + (min(qrow, S - 1) + S - 1);
+    const __half* brow = nullptr;
+    if (kBias == kBiasDense) brow = a.bias + bh * a.bias_head + static_cast<int64_t>(min(qrow, S - 1)) * a.bias_row;
+
+    float m_used = -INFINITY;
+    float l = 0.f;
+    bool ok_run = true;
+    for (int j = 0; j < n_t; ++j) {
+      // Warp-uniform: every lane must agree before the .sync.aligned TMEM ops.
+      if (!__all_sync(0xffffffffu, mbar_wait(&s_full[t], j & 1, abort_flag, a.st, 0x1300 + t))) {
+        ok_run = false;
+        break;
+      }
+      tc_fence_after();
+      float z[128];
+      {
+        uint32_t r[32];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          tmem_ld32(lane_base + Cfg::s_col(t) + c * 32, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) z[c * 32 + i] = __uint_as_float(r[i]);
+        }
+      }
+      const int k0 = j * 128;
+      const bool edge = (k0 + 128 > S) || (kCausal && k0 + 127 > qrow);
+      float rmax = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        if (kBias == kBiasDense) {
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            const int key = k0 + c * 32 + v * 8;
+            uint4 raw = make_uint4(0, 0, 0, 0);
+            if (key + 8 <= S) raw = __ldg(reinterpret_cast<const uint4*>(brow + key));
+            const __half2* hp = reinterpret_cast<const __half2*>(&raw);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              float2 f = __half22float2(hp[e]);
+              z[c * 32 + v * 8 + 2 * e] += f.x;
+              z[c * 32 + v * 8 + 2 * e + 1] += f.y;
+            }
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int col = c * 32 + i;
+          float v;
+          if (kBias == kBiasTable) {
+            const int key = k0 + col;
+            const float tb = (key < S) ? __ldg(trow - key) : 0.f;
+            v = fmaf(z[col], a.qk_log2, tb * kLog2e);
+          } else {
+            v = z[col] * a.qk_log2;
+          }
+          if (edge) {
+            const int key = k0 + col;
+            if (key >= S || (kCausal && key > qrow)) v = -INFINITY;
+          }
+          z[col] = v;
+          rmax = fmaxf(rmax, v);
+        }
+      }
+      const float m_new = fmaxf(m_used, rmax);
+      const bool need = m_new > m_used + kRescaleThreshold;
+      float alpha = 1.f;
+      if (need) {
+        alpha = ex2_approx(m_used - m_new);
+        m_used = m_new;
+      }
+      const float m_sub = (m_used == -INFINITY) ? 0.f : m_used;
+      float sum = 0.f;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float p0 = ex2_approx(z[c * 32 + 2 * i] - m_sub);
+          const float p1 = ex2_approx(z[c * 32 + 2 * i + 1] - m_sub);
+          sum += p0 + p1;
+          pk[i] = pack_half2(p0, p1);
+        }
+        tmem_st16(lane_base + Cfg::p_col(t) + c * 16, pk);
+      }
+      l = l * alpha + sum;
+      if (j > 0 && __any_sync(0xffffffffu, need)) {
+        // PV_t(j-1) is complete: s_full for block j is committed after it.
+        uint32_t r[32];
+#pragma unroll 1
+        for (int c = 0; c < D / 32; ++c) {
+          tmem_ld32(lane_base + Cfg::o_col(t) + c * 32, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+          tmem_st32(lane_base + Cfg::o_col(t) + c * 32, r);
+        }
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[t]);
+    }
+    if (ok_run && n_t > 0 &&
+        __all_sync(0xffffffffu, mbar_wait(&o_done[t], (n_t - 1) & 1, abort_flag, a.st, 0x1310 + t))) {
+      tc_fence_after();
+      const float inv_l = 1.f / l;
+      const bool store = qrow < S;
+      uint32_t r[32];
+#pragma unroll 1
+      for (int c = 0; c < D / 32; ++c) {
+        tmem_ld32(lane_base + Cfg::o_col(t) + c * 32, r);
+        tmem_wait_ld();
+        if (store) {
+          if (a.out_f16) {
+            __half* orow = static_cast<__half*>(a.O) + bh * a.o_head + static_cast<int64_t>(qrow) * a.o_row + c * 32;
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              uint4 w;
+              w.x = pack_half2(__uint_as_float(r[8 * v + 0]) * inv_l, __uint_as_float(r[8 * v + 1]) * inv_l);
+              w.y = pack_half2(__uint_as_float(r[8 * v + 2]) * inv_l, __uint_as_float(r[8 * v + 3]) * inv_l);
+              w.z = pack_half2(__uint_as_float(r[8 * v + 4]) * inv_l, __uint_as_float(r[8 * v + 5]) * inv_l);
+              w.w = pack_half2(__uint_as_float(r[8 * v + 6]) * inv_l, __uint_as_float(r[8 * v + 7]) * inv_l);
+              *reinterpret_cast<uint4*>(orow + 8 * v) = w;
+            }
+          } else {
+            float* orow = static_cast<float*>(a.O) + bh * a.o_head + static_cast<int64_t>(qrow) * a.o_row + c * 32;
+#pragma unroll
+            for (int v = 0; v < 8; ++v) {
+              *reinterpret_cast<float4*>(orow + 4 * v) =
+                  make_float4(__uint_as_float(r[4 * v]) * inv_l, __uint_as_float(r[4 * v + 1]) * inv_l,
+                              __uint_as_float(r[4 * v + 2]) * inv_l, __uint_as_float(r[4 * v + 3]) * inv_l);
+            }
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem, Cfg::kTmemCols);
+  }
+}
+
+struct FaProblem {
+  const void *Q, *K, *V;
+  int64_t q_row, q_head, k_row, k_head, v_row, v_head;  // elements
+  void* O;
+  int64_t o_row, o_head;
+  bool out_f16;
+  int BH, H, S, D;
+  float scale;
+  bool causal;
+  int bias_mode;
+  const float* table;
+  const void* bias;
+  int64_t bias_head, bias_row;
+};
+
+template <int D, bool kCausal, int kBias>
+int launch_fa2_t(const FaProblem& p, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+                 FaArgs& args, cudaStream_t stream) {
+  using Cfg = FaCfg<D>;
+  auto kern = fa2_fwd_kernel<D, kCausal, kBias>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(fa2)");
+  dim3 grid(args.num_qblocks, p.BH, 1);
+  kern<<<grid, kThreads, Cfg::kSmemBytes, stream>>>(tq, tk, tv, args);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "fa2 launch");
+  return ok();
+}
+
+template <int D>
+int launch_fa2_d(const FaProblem& p, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+                 FaArgs& args, cudaStream_t stream) {
+  if (p.causal) {
+    if (p.bias_mode == kBiasTable) return launch_fa2_t<D, true, kBiasTable>(p, tq, tk, tv, args, stream);
+    if (p.bias_mode == kBiasDense) return launch_fa2_t<D, true, kBiasDense>(p, tq, tk, tv, args, stream);
+    return launch_fa2_t<D, true, kBiasNone>(p, tq, tk, tv, args, stream);
+  }
+  if (p.bias_mode == kBiasTable) return launch_fa2_t<D, false, kBiasTable>(p, tq, tk, tv, args, stream);
+  if (p.bias_mode == kBiasDense) return launch_fa2_t<D, false, kBiasDense>(p, tq, tk, tv, args, stream);
+  return launch_fa2_t<D, false, kBiasNone>(p, tq, tk, tv, args, stream);
+}
+
+int make_qkv_map(CUtensorMap* m, const void* base, int D, int S, int BH, int64_t row, int64_t head) {
+  uint64_t dims[3] = {static_cast<uint64_t>(D), static_cast<uint64_t>(S), static_cast<uint64_t>(BH)};
+  uint64_t strides[2] = {static_cast<uint64_t>(row) * 2, static_cast<uint64_t>(head) * 2};
+  uint32_t box[3] = {64, 128, 1};
+  return encode_tmap(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, base, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+int launch_fa2(const FaProblem& p, cudaStream_t stream) {
+  if (p.D != 64 && p.D != 128) return fail(NESO_ERR_UNSUPPORTED, "head dim %d not supported (64 or 128)", p.D);
+  if (p.S <= 0 || p.BH <= 0) return ok();
+  if (p.Q == nullptr || p.K == nullptr || p.V == nullptr || p.O == nullptr) {
+    return fail(NESO_ERR_INVALID_ARG, "null Q/K/V/O pointer");
+  }
+  if (p.q_row < p.D || p.k_row < p.D || p.v_row < p.D || p.o_row < p.D) {
+    return fail(NESO_ERR_INVALID_ARG, "row stride smaller than the head dim");
+  }
+  if ((reinterpret_cast<uintptr_t>(p.O) & 15u) != 0 || (p.o_row % 8) != 0 || (p.o_head % 8) != 0) {
+    return fail(NESO_ERR_MISALIGNED, "O must be 16-byte aligned with row/head strides multiple of 8 elements");
+  }
+  if (p.bias_mode == kBiasDense &&
+      ((reinterpret_cast<uintptr_t>(p.bias) & 15u) != 0 || p.bias_row % 8 != 0 || p.bias_head % 8 != 0)) {
+    return fail(NESO_ERR_MISALIGNED, "bias must be 16-byte aligned with strides multiple of 8 elements");
+  }
+  if (p.bias_mode == kBiasTable && p.table == nullptr) return fail(NESO_ERR_INVALID_ARG, "null table");
+  if (p.bias_mode == kBiasDense && p.bias == nullptr) return fail(NESO_ERR_INVALID_ARG, "null bias");
+  CUtensorMap tq, tk, tv;
+  int rc = make_qkv_map(&tq, p.Q, p.D, p.S, p.BH, p.q_row, p.q_head);
+  if (rc == NESO_OK) rc = make_qkv_map(&tk, p.K, p.D, p.S, p.BH, p.k_row, p.k_head);
+  if (rc == NESO_OK) rc = make_qkv_map(&tv, p.V, p.D, p.S, p.BH, p.v_row, p.v_head);
+  if (rc != NESO_OK) return rc;
+  FaArgs args{};
+  args.O = p.O;
+  args.o_row = p.o_row;
+  args.o_head = p.o_head;
+  args.S = p.S;
+  args.H = p.H;
+  args.qk_log2 = p.scale * kLog2e;
+  args.table = p.table;
+  args.bias = static_cast<const __half*>(p.bias);
+  args.bias_head = p.bias_head;
+  args.bias_row = p.bias_row;
+  args.num_qblocks = (p.S + 255) / 256;
+  args.out_f16 = p.out_f16 ? 1 : 0;
+  rc = device_status(&args.st);
+  if (rc != NESO_OK) return rc;
+  if (p.D == 64) return launch_fa2_d<64>(p, tq, tk, tv, args, stream);
+  return launch_fa2_d<128>(p, tq, tk, tv, args, stream);
+}
+
+// The reference's BM is a compile-time tile height (8..128, power of two);
+// its grid is (N / BM, ...). Accept exactly those grids.
+int check_ref_grid_x(uint32_t gx, int N) {
+  if (gx == 0 || N % static_cast<int>(gx) != 0) {
+    return fail(NESO_ERR_GRID, "grid_x=%u does not divide N=%d (reference grid is (N/BM, ...))", gx, N);
+  }
+  const int bm = N / static_cast<int>(gx);
+  if (bm < 8 || bm > 128 || (bm & (bm - 1)) != 0) {
+    return fail(NESO_ERR_GRID, "grid_x=%u implies BM=%d; the reference BM is a power of two in [8,128]", gx, bm);
+  }
+  return NESO_OK;
+}
+
+}  // namespace
+}  // namespace neso
+
+using namespace neso;
+
+extern "C" {
+
+int neso_flash_attention_fwd(const void* Q, const void* K, const void* V, float* O, int32_t N, int32_t stride_qo,
+                             int32_t stride_kv, float scale, int32_t HEAD_DIM, uint32_t grid_x, uint32_t grid_y,
+                             uint32_t grid_z, neso_stream_t stream) {
+  if (N <= 0) return fail(NESO_ERR_INVALID_ARG, "N must be positive");
+  int rc = check_ref_grid_x(grid_x, N);
+  if (rc != NESO_OK) return rc;
+  if (grid_y != 1 || grid_z != 1) return fail(NESO_ERR_GRID, "single-head FA2 grid must be (N/BM, 1, 1)");
+  FaProblem p{};
+  p.Q = Q; p.K = K; p.V = V; p.O = O;
+  p.q_row = stride_qo; p.k_row = stride_kv; p.v_row = stride_kv; p.o_row = stride_qo;
+  p.q_head = static_cast<int64_t>(stride_qo) * N;
+  p.k_head = static_cast<int64_t>(stride_kv) * N;
+  p.v_head = p.k_head;
+  p.o_head = p.q_head;
+  p.out_f16 = false;
+  p.BH = 1; p.H = 1; p.S = N; p.D = HEAD_DIM;
+  p.scale = scale;
+  p.causal = false;
+  p.bias_mode = kBiasNone;
+  return launch_fa2(p, as_stream(stream));
+}
+
+int neso_rel_pos_fa2_fwd(const void* Q, const void* K, const void* V, const void* bias, void* O, int32_t T,
+                         int32_t stride, float scale, int32_t stride_h, int32_t bias_stride_h, int32_t HEAD_DIM,
+                         uint32_t grid_x, uint32_t grid_y, uint32_t grid_z, neso_stream_t stream) {
+  if (T <= 0) return fail(NESO_ERR_INVALID_ARG, "T must be positive");
+  int rc = check_ref_grid_x(grid_x, T);
+  if (rc != NESO_OK) return rc;
+  if (grid_y == 0 || grid_z != 1) return fail(NESO_ERR_GRID, "rel-pos FA2 grid must be (T/BM, nh, 1)");
+  if (static_cast<int64_t>(bias_stride_h) < static_cast<int64_t>(T) * T) {
+    return fail(NESO_ERR_INVALID_ARG, "bias_stride_h %d < T*T", bias_stride_h);
+  }
+  FaProblem p{};
+  p.Q = Q; p.K = K; p.V = V; p.O = O;
+  p.q_row = p.k_row = p.v_row = p.o_row = stride;
+  p.q_head = p.k_head = p.v_head = p.o_head = stride_h;
+  p.out_f16 = true;
+  p.BH = static_cast<int>(grid_y); p.H = p.BH; p.S = T; p.D = HEAD_DIM;
+  p.scale = scale;
+  p.causal = false;
+  p.bias_mode = kBiasDense;
+  p.bias = bias;
+  p.bias_head = bias_stride_h;
+  p.bias_row = T;
+  return launch_fa2(p, as_stream(stream));
+}
+
+int neso_fa2_fwd(const void* Q, const void* K, const void* V, float* O, int32_t B, int32_t H, int32_t S, int32_t D,
+                 float scale, int32_t causal, neso_stream_t stream) {
+  if (B < 0 || H < 0 || S < 0) return fail(NESO_ERR_INVALID_ARG, "negative size");
+  if (static_cast<int64_t>(B) * H > 65535) return fail(NESO_ERR_UNSUPPORTED, "B*H must be <= 65535");
+  FaProblem p{};
+  p.Q = Q; p.K = K; p.V = V; p.O = O;
+  p.q_row = p.k_row = p.v_row = p.o_row = D;
+  p.q_head = p.k_head = p.v_head = p.o_head = static_cast<int64_t>(S) * D;
+  p.out_f16 = false;
+  p.BH = B * H; p.H = H; p.S = S; p.D = D;
+  p.scale = scale;
+  p.causal = causal != 0;
+  p.bias_mode = kBiasNone;
+  return launch_fa2(p, as_stream(stream));
+}
+
+int neso_fa2_fwd_relpos_table(const void* Q, const void* K, const void* V, const float* table, float* O, int32_t B,
+                              int32_t H, int32_t S, int32_t D, float scale, int32_t causal, neso_stream_t stream) {
+  if (B < 0 || H < 0 || S < 0) return fail(NESO_ERR_INVALID_ARG, "negative size");
+  if (static_cast<int64_t>(B) * H > 65535) return fail(NESO_ERR_UNSUPPORTED, "B*H must be <= 65535");
+  FaProblem p{};
+  p.Q = Q; p.K = K; p.V = V; p.O = O;
+  p.q_row = p.k_row = p.v_row = p.o_row = D;
+  p.q_head = p.k_head = p.v_head = p.o_head = static_cast<int64_t>(S) * D;
+  p.out_f16 = false;
+  p.BH = B * H; p.H = H; p.S = S; p.D = D;
+  p.scale = scale;
+  p.causal = causal != 0;
+  p.bias_mode = kBiasTable;
+  p.table = table;
+  return launch_fa2(p, as_stream(stream));
+}
+
+}  // extern "C"

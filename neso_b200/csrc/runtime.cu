@@ -1,0 +1,208 @@
+// Host runtime: error strings, device selection, per-device status word,
+// tensor-map encoding, the bounded-wait self test and launch metadata.
+#include <cudaTypedefs.h>
+
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "runtime.h"
+
+namespace neso {
+
+namespace {
+thread_local std::string g_last_error;
+
+constexpr int kMaxDevices = 64;
+std::once_flag g_status_once[kMaxDevices];
+int* g_status_ptr[kMaxDevices] = {};
+int g_status_err[kMaxDevices] = {};
+std::once_flag g_sm_once[kMaxDevices];
+int g_sm_count[kMaxDevices] = {};
+
+std::once_flag g_encode_once;
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+}  // namespace
+
+int fail(int code, const char* fmt, ...) {
+  char buf[1024];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int ok() {
+  g_last_error.clear();
+  return NESO_OK;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(NESO_ERR_LAUNCH, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+static int current_device(int* dev) {
+  cudaError_t e = cudaGetDevice(dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (*dev < 0 || *dev >= kMaxDevices) return fail(NESO_ERR_NO_DEVICE, "device ordinal %d out of range", *dev);
+  return NESO_OK;
+}
+
+int device_status(DevStatus* out) {
+  int dev = 0;
+  int rc = current_device(&dev);
+  if (rc != NESO_OK) return rc;
+  std::call_once(g_status_once[dev], [dev]() {
+    int* p = nullptr;
+    cudaError_t e = cudaMalloc(&p, 16 * sizeof(int));
+    if (e == cudaSuccess) e = cudaMemset(p, 0, 16 * sizeof(int));
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    g_status_err[dev] = static_cast<int>(e);
+    g_status_ptr[dev] = (e == cudaSuccess) ? p : nullptr;
+  });
+  if (g_status_ptr[dev] == nullptr) {
+    return cuda_fail(static_cast<cudaError_t>(g_status_err[dev]), "allocating the device status word");
+  }
+  out->word = g_status_ptr[dev];
+  out->budget_ns = kWaitBudgetNs;
+  return NESO_OK;
+}
+
+int sm_count() {
+  int dev = 0;
+  if (current_device(&dev) != NESO_OK) return 148;
+  std::call_once(g_sm_once[dev], [dev]() {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    g_sm_count[dev] = n;
+  });
+  return g_sm_count[dev];
+}
+
+int encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const void* gaddr, const uint64_t* dims,
+                const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle swizzle) {
+  std::call_once(g_encode_once, []() {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess) {
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }
+  });
+  if (g_encode == nullptr) return fail(NESO_ERR_NO_DEVICE, "cuTensorMapEncodeTiled is unavailable (no driver?)");
+  if (!aligned16(gaddr)) return fail(NESO_ERR_MISALIGNED, "TMA base address %p is not 16-byte aligned", gaddr);
+  for (int i = 0; i + 1 < rank; ++i) {
+    if (strides_bytes[i] % 16 != 0) {
+      return fail(NESO_ERR_MISALIGNED, "TMA stride %llu bytes (dim %d) is not a multiple of 16",
+                  static_cast<unsigned long long>(strides_bytes[i]), i + 1);
+    }
+  }
+  cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  CUresult r = g_encode(map, dtype, static_cast<cuuint32_t>(rank), const_cast<void*>(gaddr),
+                        reinterpret_cast<const cuuint64_t*>(dims), reinterpret_cast<const cuuint64_t*>(strides_bytes),
+                        reinterpret_cast<const cuuint32_t*>(box), estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(NESO_ERR_UNSUPPORTED, "cuTensorMapEncodeTiled failed (CUresult %d)", (int)r);
+  return NESO_OK;
+}
+
+// One CTA, one thread waits on an mbarrier that nothing arrives at.
+__global__ void selftest_wait_kernel(DevStatus st) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    (void)mbar_wait(&bar, 0, &abort_flag, st, 0x5e1f);
+  }
+  __syncthreads();
+}
+
+}  // namespace neso
+
+using namespace neso;
+
+extern "C" {
+
+const char* neso_last_error_string(void) { return g_last_error.c_str(); }
+
+int neso_version(void) { return 100; }
+
+int neso_set_device(int device) {
+  cudaError_t e = cudaSetDevice(device);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+  return ok();
+}
+
+int neso_device_status(int device, int* code, int* where, int* block, int* thread) {
+  if (device < 0 || device >= kMaxDevices) return fail(NESO_ERR_INVALID_ARG, "bad device %d", device);
+  int prev = 0;
+  cudaGetDevice(&prev);
+  cudaError_t e = cudaSetDevice(device);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+  DevStatus st{};
+  int rc = device_status(&st);
+  int h[4] = {0, 0, 0, 0};
+  if (rc == NESO_OK) {
+    e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) e = cudaMemcpy(h, st.word, sizeof(h), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) rc = cuda_fail(e, "reading the device status word");
+  }
+  cudaSetDevice(prev);
+  if (rc != NESO_OK) return rc;
+  if (code) *code = h[0];
+  if (where) *where = h[1];
+  if (block) *block = h[2];
+  if (thread) *thread = h[3];
+  if (h[0] != 0) {
+    return fail(NESO_ERR_DEVICE_TIMEOUT, "device wait timed out (site 0x%x, block %d, thread %d)", h[1], h[2], h[3]);
+  }
+  return ok();
+}
+
+int neso_clear_device_status(int device) {
+  if (device < 0 || device >= kMaxDevices) return fail(NESO_ERR_INVALID_ARG, "bad device %d", device);
+  int prev = 0;
+  cudaGetDevice(&prev);
+  cudaError_t e = cudaSetDevice(device);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+  DevStatus st{};
+  int rc = device_status(&st);
+  if (rc == NESO_OK) {
+    e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) e = cudaMemset(st.word, 0, 16 * sizeof(int));
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) rc = cuda_fail(e, "clearing the device status word");
+  }
+  cudaSetDevice(prev);
+  return rc == NESO_OK ? ok() : rc;
+}
+
+int neso_selftest_wait_timeout(int budget_us, neso_stream_t stream) {
+  if (budget_us < 0 || budget_us > 2000000) return fail(NESO_ERR_INVALID_ARG, "budget_us must be in [0, 2e6]");
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  int rc = neso_clear_device_status(dev);
+  if (rc != NESO_OK) return rc;
+  DevStatus st{};
+  rc = device_status(&st);
+  if (rc != NESO_OK) return rc;
+  st.budget_ns = static_cast<unsigned long long>(budget_us) * 1000ull;
+  selftest_wait_kernel<<<1, 32, 0, as_stream(stream)>>>(st);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "selftest_wait_kernel launch");
+  e = cudaStreamSynchronize(as_stream(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "selftest_wait_kernel");
+  int code = 0;
+  rc = neso_device_status(dev, &code, nullptr, nullptr, nullptr);
+  return rc;
+}
+
+}  // extern "C"

@@ -1,0 +1,45 @@
+// Host-side runtime shared by every C-ABI entry point: status codes, the
+// thread-local error string, the per-device status word that bounded device
+// waits report into, and TMA tensor-map encoding through the driver entry
+// point (so the library links only the static CUDA runtime and still loads on
+// a machine without a GPU driver).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdint>
+#include <string>
+
+#include "../../include/neso_b200.h"
+#include "common.cuh"
+
+namespace neso {
+
+// Record an error message for neso_last_error_string() and return `code`.
+int fail(int code, const char* fmt, ...);
+// Clear the thread's error string and return NESO_OK.
+int ok();
+
+// Map a CUDA runtime error to NESO_ERR_LAUNCH with a message.
+int cuda_fail(cudaError_t e, const char* what);
+
+// Device status block for the device that owns `stream` (lazily allocated
+// once per device, 4 ints: code, where, block, thread).
+int device_status(DevStatus* out);
+
+// Number of SMs on the current device (cached per device).
+int sm_count();
+
+// Encode a tiled tensor map (fp16/int8/...) with 128-byte swizzle and zero OOB
+// fill. dims/strides follow the driver convention (dims[0] innermost; strides
+// are byte strides of dims 1..rank-1).
+int encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const void* gaddr, const uint64_t* dims,
+                const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle swizzle);
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+inline cudaStream_t as_stream(neso_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
+
+}  // namespace neso

@@ -1,0 +1,113 @@
+"""C-ABI checks that need no GPU: the library loads, exports exactly what the
+header declares, reports reference-schema metadata, and rejects invalid
+launches (wrong reference grid, unsupported strides, bad constexprs) before
+touching the device."""
+import ctypes
+import json
+
+import pytest
+
+from neso_b200 import _lib
+
+
+def test_library_loads_and_exports_every_header_symbol():
+    lib = _lib.lib()
+    declared = _lib.header_functions()
+    assert len(declared) >= 20
+    for name in declared:
+        assert hasattr(lib, name), f"{name} declared in include/neso_b200.h but not exported"
+        assert name in _lib.SIGNATURES, f"{name} has no ctypes signature"
+    assert set(_lib.SIGNATURES) == set(declared)
+    assert lib.neso_version() >= 100
+
+
+def test_metadata_matches_reference_schema():
+    lib = _lib.lib()
+    # keys of AOTResult.to_metadata() (src/neso/aot_compile.py:108-117)
+    keys = {"kernel_name", "params", "constants", "threadgroup_size", "num_warps", "grid"}
+    for name in ["vector_add", "add_kernel", "scale", "flash_attention_fwd", "rel_pos_fa2_fwd", "matmul_kernel",
+                 "matmul_tiled", "w8a16_matmul", "w8a16_scaled_matmul", "fa2_fwd", "fa2_fwd_relpos_table",
+                 "w8a16_matmul_mnk", "w4a16_g128_matmul"]:
+        meta = json.loads(lib.neso_kernel_metadata(name.encode()).decode())
+        assert set(meta) == keys, name
+        assert meta["kernel_name"] == name
+        assert meta["threadgroup_size"] == 32 * meta["num_warps"]
+        assert len(meta["grid"]) == 3
+        for i, p in enumerate(meta["params"]):
+            # KernelParameter fields (src/neso/backend/abi.py:19-27) and no rust_type (tests/test_aot.py:136)
+            assert {"index", "name", "type", "metal_type", "is_pointer"} <= set(p)
+            assert "rust_type" not in p
+            assert p["index"] == i
+            assert p["is_pointer"] == p["type"].startswith("*")
+    assert lib.neso_kernel_metadata(b"no_such_kernel") is None
+    add = json.loads(lib.neso_kernel_metadata(b"add_kernel").decode())
+    assert add["constants"] == {"BLOCK_SIZE": 1024}
+    assert [p["name"] for p in add["params"]] == ["x_ptr", "y_ptr", "z_ptr", "n_elements"]
+
+
+def test_scale_metadata_argument_indices_match_harness():
+    # macos/harness.rs:229-236 binds factor at index 2 and n at index 3.
+    meta = json.loads(_lib.lib().neso_kernel_metadata(b"scale").decode())
+    idx = {p["name"]: p["index"] for p in meta["params"]}
+    assert idx["factor"] == 2 and idx["n_elements"] == 3
+
+
+@pytest.mark.parametrize("n,block,grid,expect", [
+    (10, 1024, (2, 1, 1), _lib.NESO_ERR_GRID),
+    (65537, 256, (256, 1, 1), _lib.NESO_ERR_GRID),
+    (65537, 256, (257, 2, 1), _lib.NESO_ERR_GRID),
+    (10, 1000, (1, 1, 1), _lib.NESO_ERR_INVALID_ARG),   # BLOCK_SIZE not a power of two
+    (-1, 1024, (0, 1, 1), _lib.NESO_ERR_INVALID_ARG),
+])
+def test_elementwise_rejects_bad_launch(n, block, grid, expect):
+    lib = _lib.lib()
+    assert lib.neso_vector_add(None, None, None, n, block, *grid, None) == expect
+    assert _lib.last_error()
+    assert lib.neso_scale(None, None, 1.0, n, block, *grid, None) == expect
+
+
+def test_zero_elements_is_a_no_op():
+    assert _lib.lib().neso_vector_add(None, None, None, 0, 1024, 0, 1, 1, None) == _lib.NESO_OK
+
+
+@pytest.mark.parametrize("N,grid", [(128, (3, 1, 1)), (128, (256, 1, 1)), (128, (128, 1, 1)), (128, (8, 2, 1))])
+def test_fa2_reference_grid_checked(N, grid):
+    # grid (N/BM, 1, 1) with BM a power of two in [8, 128] (tests/test_flash_attention.py:290)
+    rc = _lib.lib().neso_flash_attention_fwd(None, None, None, None, N, 64, 64, 0.125, 64, *grid, None)
+    assert rc == _lib.NESO_ERR_GRID
+
+
+def test_matmul_grid_and_strides_checked():
+    lib = _lib.lib()
+    rc = lib.neso_matmul_kernel(None, None, None, 256, 256, 64, 64, 1, 256, 1, 256, 1, 128, 128, 32, 3, 2, 1, None)
+    assert rc == _lib.NESO_ERR_GRID
+    rc = lib.neso_matmul_kernel(None, None, None, 256, 256, 64, 64, 2, 256, 1, 256, 1, 128, 128, 32, 2, 2, 1, None)
+    assert rc == _lib.NESO_ERR_UNSUPPORTED
+    rc = lib.neso_matmul_kernel(None, None, None, 256, 256, 64, 64, 1, 256, 1, 256, 1, 0, 128, 32, 2, 2, 1, None)
+    assert rc == _lib.NESO_ERR_INVALID_ARG
+
+
+def test_error_string_is_thread_local():
+    import threading
+
+    lib = _lib.lib()
+    lib.neso_vector_add(None, None, None, 10, 1024, 7, 1, 1, None)
+    main_msg = _lib.last_error()
+    seen = {}
+
+    def worker():
+        seen["msg"] = _lib.last_error()
+
+    t = threading.Thread(target=worker)
+    t.start()
+    t.join()
+    assert "grid" in main_msg
+    assert seen["msg"] == ""
+
+
+def test_status_codes_match_header():
+    text = _lib.HEADER_PATH.read_text()
+    for name in ["NESO_OK", "NESO_ERR_INVALID_ARG", "NESO_ERR_MISALIGNED", "NESO_ERR_UNSUPPORTED", "NESO_ERR_GRID",
+                 "NESO_ERR_LAUNCH", "NESO_ERR_DEVICE_TIMEOUT", "NESO_ERR_NO_DEVICE"]:
+        val = getattr(_lib, name)
+        assert f"#define {name} ({val})" in text or f"#define {name} {val}" in text

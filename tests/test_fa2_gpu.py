@@ -1,0 +1,127 @@
+"""Flash Attention 2 forward on the GPU against the oracle (atol = rtol = 2e-3,
+fp32 output) and against the reference's golden vectors at the reference's own
+tolerances (tests/test_flash_attention.py:318-341, tests/test_rel_pos_fa2.py:371-373)."""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from neso_b200 import _lib, kernels, ops
+
+pytestmark = pytest.mark.gpu
+TOL = dict(atol=2e-3, rtol=2e-3)
+
+
+def _qkv(B, H, S, D, seed=0):
+    # BASELINE: Q/K/V ~ N(0, 1) fp16 from a seed
+    g = torch.Generator().manual_seed(seed)
+    return tuple(torch.randn(B, H, S, D, generator=g).half() for _ in range(3))
+
+
+def _check(dev, B, H, S, D, causal=False, table=None, seed=0):
+    q, k, v = _qkv(B, H, S, D, seed)
+    sc = 1.0 / math.sqrt(D)
+    o = ops.flash_attention(q.to(dev), k.to(dev), v.to(dev), sc, causal=causal,
+                            table=None if table is None else table.to(dev))
+    ref = oracle.attention(q, k, v, sc, causal=causal, table=table)
+    torch.testing.assert_close(o.cpu(), ref, **TOL)
+
+
+def test_harness_kat_uniform_softmax(dev):
+    # macos/harness.rs:241-271: Q = K = 0 -> O rows = column mean of f16(V); N = 64, d = 64, tol 2e-3
+    n, d = 64, 64
+    _, _, v = oracle.harness_fa2_values(n, d)
+    v16 = v.half()
+    z = torch.zeros(n, d, dtype=torch.float16, device=dev)
+    o = torch.empty(n, d, device=dev)
+    kernels.flash_attention_fwd[(n // 16, 1, 1)](z, z, v16.to(dev), o, n, d, d, 1 / math.sqrt(d))
+    exp = v16.float().mean(0, keepdim=True).expand(n, d)
+    assert (o.cpu() - exp).abs().max().item() <= 2e-3
+
+
+@pytest.mark.parametrize("name", ["fa2_N128_d64", "fa2_N256_d128"])
+def test_reference_golden_single_head(dev, golden_dir, name):
+    g = dict(np.load(golden_dir / f"{name}.npz"))
+    N, d = int(g["N"]), int(g["d"])
+    q, k, v = (torch.from_numpy(g[t]).half() for t in ("q", "k", "v"))
+    o = torch.empty(N, d, device=dev)
+    # reference launch: grid (N / BM, 1, 1) with BM = 16 (tests/test_flash_attention.py:290)
+    kernels.flash_attention_fwd[(N // 16, 1, 1)](q.to(dev), k.to(dev), v.to(dev), o, N, d, d, float(g["scale"]))
+    out = o.cpu().numpy()
+    # the reference's f16 criterion on rows 0 and N/2 (tests/test_flash_attention.py:318-341)
+    assert np.abs(out[[0, N // 2]] - g["ref_out"][[0, N // 2]]).max() < 0.05
+    # BASELINE criterion against the oracle on the same fp16 inputs
+    ref = oracle.attention(q, k, v, float(g["scale"]))
+    torch.testing.assert_close(o.cpu(), ref, **TOL)
+
+
+@pytest.mark.parametrize("name", ["relpos_T32_d64_nh2", "relpos_T64_d128_nh4"])
+def test_reference_golden_relpos_dense(dev, golden_dir, name):
+    g = dict(np.load(golden_dir / f"{name}.npz"))
+    T, d, nh = int(g["T"]), int(g["d"]), int(g["nh"])
+    qu = torch.from_numpy(g["Q_u"]).half()
+    k = torch.from_numpy(g["K"]).half()
+    v = torch.from_numpy(g["V"]).half()
+    bias = torch.from_numpy(g["rel_bias"]).half()
+    o = torch.empty(nh, T, d, dtype=torch.float16, device=dev)
+    kernels.rel_pos_fa2_fwd[(T // 16, nh, 1)](qu.to(dev), k.to(dev), v.to(dev), bias.to(dev), o, T, d,
+                                              float(g["scale"]), T * d, T * T)
+    out = o.float().cpu()
+    # the reference's criterion: max abs error < 0.1 vs reference_rel_pos_attention (tests/test_rel_pos_fa2.py:371-373)
+    assert np.abs(out.numpy() - g["ref_out"]).max() < 0.1
+    ref = oracle.attention(qu, k, v, float(g["scale"]), dense_bias=bias)
+    torch.testing.assert_close(out, ref, **TOL)
+
+
+def test_config1_b1_h8_s512_d64(dev):
+    _check(dev, 1, 8, 512, 64)
+
+
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("S", [128, 256, 384, 1000])
+@pytest.mark.parametrize("causal", [False, True])
+def test_sweep_small(dev, D, S, causal):
+    _check(dev, 2, 3, S, D, causal=causal, seed=S + D)
+
+
+@pytest.mark.parametrize("S", [1, 17, 129])
+def test_tiny_and_ragged(dev, S):
+    _check(dev, 1, 2, S, 64, seed=S)
+    _check(dev, 1, 2, S, 128, causal=True, seed=S)
+
+
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("causal", [False, True])
+def test_relpos_table(dev, D, causal):
+    B, H, S = 2, 3, 384
+    g = torch.Generator().manual_seed(11)
+    table = torch.randn(H, 2 * S - 1, generator=g) * 0.02  # BASELINE: N(0, 0.02)
+    _check(dev, B, H, S, D, causal=causal, table=table, seed=12)
+
+
+@pytest.mark.parametrize("D", [64, 128])
+def test_baseline_sweep_s2048_sampled(dev, D):
+    # Full BASELINE shape B = H = 16, S = 2048; a sample of heads against the oracle.
+    B, H, S = 16, 16, 2048
+    gd = torch.Generator(device=dev).manual_seed(D)
+    q, k, v = (torch.randn(B, H, S, D, device=dev, generator=gd).half() for _ in range(3))
+    for causal in (False, True):
+        o = ops.flash_attention(q, k, v, 1 / math.sqrt(D), causal=causal)
+        for (b, h) in [(0, 0), (7, 9), (15, 15)]:
+            ref = oracle.attention(q[b, h].cpu(), k[b, h].cpu(), v[b, h].cpu(), 1 / math.sqrt(D), causal=causal)
+            torch.testing.assert_close(o[b, h].cpu(), ref, **TOL)
+
+
+def test_unsupported_head_dim(dev):
+    q = torch.zeros(1, 1, 128, 96, dtype=torch.float16, device=dev)
+    with pytest.raises(_lib.NesoError) as ei:
+        ops.flash_attention(q, q, q)
+    assert ei.value.code == _lib.NESO_ERR_UNSUPPORTED
+
+
+def test_device_status_clean_after_runs(dev):
+    code = torch.zeros(1, dtype=torch.int32)
+    rc = _lib.lib().neso_device_status(0, None, None, None, None)
+    assert rc == _lib.NESO_OK, _lib.last_error()
