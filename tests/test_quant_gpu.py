@@ -1,0 +1,110 @@
+"""Dequant-fused quantized matmul on the GPU against the oracle (atol = rtol =
+2e-3, fp32 output) and the reference's golden vectors at its own criterion
+(max_err / max|ref| < 1 %, tests/test_quantized_matmul.py:356-359)."""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from neso_b200 import _lib, kernels, ops
+
+pytestmark = pytest.mark.gpu
+TOL = dict(atol=2e-3, rtol=2e-3)
+
+
+def _w8(M, N, K, seed=0):
+    # BASELINE: X ~ N(0,1) fp16, W int8 uniform [-127, 127], scale U[0.001, 0.02] fp16
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(M, K, generator=g).half()
+    w = torch.randint(-127, 128, (K, N), generator=g, dtype=torch.int8)
+    s = (torch.rand(N, generator=g) * 0.019 + 0.001).half()
+    return x, w, s
+
+
+def _w4(M, N, K, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(M, K, generator=g).half()
+    q = torch.randint(-8, 8, (K, N), generator=g, dtype=torch.int8)
+    s = (torch.rand(K // 128, N, generator=g) * 0.019 + 0.001).half()
+    return x, q, s
+
+
+@pytest.mark.parametrize("name,seed_kind", [("w8a16_64", "plain"), ("w4a16_64", "plain"),
+                                            ("w8a16_scaled_64", "scaled")])
+def test_reference_golden(dev, golden_dir, name, seed_kind):
+    g = dict(np.load(golden_dir / f"{name}.npz"))
+    M, N, K = int(g["M"]), int(g["N"]), int(g["K"])
+    a = torch.from_numpy(g["a"]).half()
+    b = torch.from_numpy(g["b"])
+    c = torch.empty(M, N, device=dev)
+    if "scale" in g:
+        s = torch.from_numpy(g["scale"]).half()
+        # reference launch: grid (cdiv(M, BM), cdiv(N, BN), 1) (tests/test_quantized_matmul.py:433-438)
+        kernels.w8a16_scaled_matmul[(M // 32, N // 32, 1)](a.to(dev), b.to(dev), c, s.to(dev), K, K, N, N,
+                                                           BM=32, BN=32, BK=32)
+    else:
+        s = None
+        kernels.w8a16_matmul[(M // 32, N // 64, 1)](a.to(dev), b.to(dev), c, K, K, N, N, BM=32, BN=64, BK=32)
+    out = c.cpu().numpy()
+    rel = np.abs(out - g["ref"]).max() / np.abs(g["ref"]).max()
+    assert rel < 0.01  # the reference's own criterion
+    torch.testing.assert_close(c.cpu(), oracle.w8a16_matmul(a, b, s), **TOL)
+
+
+@pytest.mark.parametrize("M", [1, 5, 16, 17, 32, 64, 65, 128, 300])
+def test_w8a16_scaled_sizes(dev, M):
+    N, K = 384, 512
+    x, w, s = _w8(M, N, K, seed=M)
+    y = ops.w8a16_matmul(x.to(dev), w.to(dev), s.to(dev))
+    torch.testing.assert_close(y.cpu(), oracle.w8a16_matmul(x, w, s), **TOL)
+    y2 = ops.w8a16_matmul(x.to(dev), w.to(dev))
+    torch.testing.assert_close(y2.cpu(), oracle.w8a16_matmul(x, w), **TOL)
+
+
+@pytest.mark.parametrize("M", [1, 16, 128, 2048])
+def test_w8a16_baseline_shapes(dev, M):
+    # BASELINE: K = 4096, N = 11008 (ragged last n-tile: 11008 = 86 x 128)
+    N, K = 11008, 4096
+    x, w, s = _w8(M, N, K, seed=100 + M)
+    y = ops.w8a16_matmul(x.to(dev), w.to(dev), s.to(dev))
+    if M > 128:
+        rows = torch.tensor([0, 1, 255, 1024, M - 1])
+        torch.testing.assert_close(y[rows.to(dev)].cpu(), oracle.w8a16_matmul(x[rows], w, s), **TOL)
+    else:
+        torch.testing.assert_close(y.cpu(), oracle.w8a16_matmul(x, w, s), **TOL)
+
+
+@pytest.mark.parametrize("M", [1, 3, 16, 40, 64, 100, 128])
+def test_w4a16_sizes(dev, M):
+    N, K = 256, 384
+    x, q, s = _w4(M, N, K, seed=M)
+    wq = oracle.pack_int4(q)
+    y = ops.w4a16_g128_matmul(x.to(dev), wq.to(dev), s.to(dev))
+    torch.testing.assert_close(y.cpu(), oracle.w4a16_g128_matmul(x, wq, s), **TOL)
+
+
+@pytest.mark.parametrize("M", [1, 16, 128, 2048])
+def test_w4a16_baseline_shapes(dev, M):
+    N, K = 11008, 4096
+    x, q, s = _w4(M, N, K, seed=200 + M)
+    wq = oracle.pack_int4(q)
+    y = ops.w4a16_g128_matmul(x.to(dev), wq.to(dev), s.to(dev))
+    if M > 128:
+        rows = torch.tensor([0, 7, 500, M - 1])
+        torch.testing.assert_close(y[rows.to(dev)].cpu(), oracle.w4a16_g128_matmul(x[rows], wq, s), **TOL)
+    else:
+        torch.testing.assert_close(y.cpu(), oracle.w4a16_g128_matmul(x, wq, s), **TOL)
+
+
+def test_product_pack_matches_oracle_layout(dev):
+    q = torch.randint(-8, 8, (256, 64), dtype=torch.int8)
+    assert torch.equal(ops.pack_int4(q), oracle.pack_int4(q))
+
+
+def test_int4_k_not_multiple_of_128_rejected(dev):
+    x = torch.zeros(4, 192, dtype=torch.float16, device=dev)
+    wq = torch.zeros(96, 64, dtype=torch.uint8, device=dev)
+    s = torch.zeros(2, 64, dtype=torch.float16, device=dev)
+    with pytest.raises(_lib.NesoError) as ei:
+        ops.w4a16_g128_matmul(x, wq, s)
+    assert ei.value.code == _lib.NESO_ERR_UNSUPPORTED
