@@ -244,6 +244,19 @@ __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
+// Warpgroup register reallocation. Every warp of the warpgroup must execute
+// it. The block's pool is (threads x registers at launch): the host checks
+// with cudaFuncGetAttributes that a split fits before launching, because an
+// inc that cannot be funded waits forever.
+template <uint32_t N>
+__device__ __forceinline__ void setmaxnreg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+__device__ __forceinline__ void setmaxnreg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 // ----------------------------------------------------------- descriptors --
 // UMMA shared-memory matrix descriptor, 128-byte swizzle (layout type 2),
 // descriptor version 1 (sm_100). Byte offsets are encoded >> 4.

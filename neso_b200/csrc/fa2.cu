@@ -36,6 +36,11 @@ namespace neso {
 namespace {
 
 constexpr int kThreads = 384;
+// Register split: warpgroup 0 (TMA, MMA, TMEM warps) shrinks, the two softmax
+// warpgroups grow. 128 * kRegsLow + 256 * kRegsHigh must not exceed the
+// block's launch pool (384 x registers per thread), checked on the host.
+constexpr uint32_t kRegsLow = 56;
+constexpr uint32_t kRegsHigh = 216;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale only when max grows by > 2^8
 
@@ -91,7 +96,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* s_full = v_empty + KS;   // [2]
   uint64_t* p_full = s_full + 2;     // [2]
   uint64_t* o_done = p_full + 2;     // [2]
-  uint64_t* mma_done = o_done + 2;   // [1]
+  uint64_t* s_free = o_done + 2;     // [2] softmax has read S_t (4 warps)
+  uint64_t* mma_done = s_free + 2;   // [1]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -122,6 +128,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&s_full[t], 1);
       mbar_init(&p_full[t], 4);
       mbar_init(&o_done[t], 1);
+      mbar_init(&s_free[t], 4);
     }
     mbar_init(mma_done, 1);
     *abort_flag = 0;
@@ -138,138 +145,160 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-
-  if (warp == 0 && lane == 0) {
-    // ------------------------------------------------------------ producer --
-    const uint32_t qbytes = (ntile[1] > 0 ? 2 : 1) * Cfg::kTileBytes;
-    mbar_arrive_expect_tx(q_full, qbytes);
-    for (int t = 0; t < 2; ++t) {
-      if (ntile[t] == 0) continue;
+  if (warp < 4) {
+    // Warpgroup 0: TMA producer, MMA issuer, TMEM allocator.
+    setmaxnreg_dec<kRegsLow>();
+    if (warp == 0 && lane == 0) {
+      // ------------------------------------------------------------ producer --
+      const uint32_t qbytes = (ntile[1] > 0 ? 2 : 1) * Cfg::kTileBytes;
+      mbar_arrive_expect_tx(q_full, qbytes);
+      for (int t = 0; t < 2; ++t) {
+        if (ntile[t] == 0) continue;
 #pragma unroll
-      for (int c = 0; c < Cfg::kChunks; ++c) {
-        tma_load_3d(sQ + t * Cfg::kTileBytes + c * 16384, &tmQ, q_full, c * 64, q0 + 128 * t, bh);
+        for (int c = 0; c < Cfg::kChunks; ++c) {
+          tma_load_3d(sQ + t * Cfg::kTileBytes + c * 16384, &tmQ, q_full, c * 64, q0 + 128 * t, bh);
+        }
       }
-    }
-    int issued = 0;
-    bool aborted = false;
-    for (int j = 0; j < nmax; ++j) {
-      const int s = j % KS;
-      const uint32_t ph = (j / KS) & 1;
-      if (!mbar_wait(&k_empty[s], ph ^ 1, abort_flag, a.st, 0x1100)) { aborted = true; break; }
-      mbar_arrive_expect_tx(&k_full[s], Cfg::kTileBytes);
+      int issued = 0;
+      bool aborted = false;
+      for (int j = 0; j < nmax; ++j) {
+        const int s = j % KS;
+        const uint32_t ph = (j / KS) & 1;
+        if (!mbar_wait(&k_empty[s], ph ^ 1, abort_flag, a.st, 0x1100)) { aborted = true; break; }
+        mbar_arrive_expect_tx(&k_full[s], Cfg::kTileBytes);
 #pragma unroll
-      for (int c = 0; c < Cfg::kChunks; ++c) {
-        tma_load_3d(sK + s * Cfg::kTileBytes + c * 16384, &tmK, &k_full[s], c * 64, j * 128, bh);
+        for (int c = 0; c < Cfg::kChunks; ++c) {
+          tma_load_3d(sK + s * Cfg::kTileBytes + c * 16384, &tmK, &k_full[s], c * 64, j * 128, bh);
+        }
+        if (!mbar_wait(&v_empty[s], ph ^ 1, abort_flag, a.st, 0x1101)) {
+          issued = j;  // K_j is in flight; V_j is not
+          DevStatus quiet = a.st;
+          quiet.word = nullptr;
+          volatile int never = 0;
+          mbar_wait(&k_full[s], ph, &never, quiet, 0);
+          aborted = true;
+          break;
+        }
+        mbar_arrive_expect_tx(&v_full[s], Cfg::kTileBytes);
+#pragma unroll
+        for (int c = 0; c < Cfg::kChunks; ++c) {
+          tma_load_3d(sV + s * Cfg::kTileBytes + c * 16384, &tmV, &v_full[s], c * 64, j * 128, bh);
+        }
+        issued = j + 1;
       }
-      if (!mbar_wait(&v_empty[s], ph ^ 1, abort_flag, a.st, 0x1101)) {
-        issued = j;  // K_j is in flight; V_j is not
+      if (aborted) {
         DevStatus quiet = a.st;
         quiet.word = nullptr;
         volatile int never = 0;
-        mbar_wait(&k_full[s], ph, &never, quiet, 0);
-        aborted = true;
-        break;
+        mbar_wait(q_full, 0, &never, quiet, 0);
+        for (int i = (issued > KS ? issued - KS : 0); i < issued; ++i) {
+          mbar_wait(&k_full[i % KS], (i / KS) & 1, &never, quiet, 0);
+          mbar_wait(&v_full[i % KS], (i / KS) & 1, &never, quiet, 0);
+        }
       }
-      mbar_arrive_expect_tx(&v_full[s], Cfg::kTileBytes);
+    } else if (warp == 1 && lane == 0) {
+      // ---------------------------------------------------------- MMA issuer --
+      constexpr uint32_t idesc_qk = idesc_f16_f32(128, 128, 0, 0);
+      constexpr uint32_t idesc_pv = idesc_f16_f32(128, D, 0, 1);
+      auto issue_qk = [&](int t, int j) {
+        const uint32_t qa = smem_u32(sQ + t * Cfg::kTileBytes);
+        const uint32_t kb = smem_u32(sK + (j % KS) * Cfg::kTileBytes);
 #pragma unroll
-      for (int c = 0; c < Cfg::kChunks; ++c) {
-        tma_load_3d(sV + s * Cfg::kTileBytes + c * 16384, &tmV, &v_full[s], c * 64, j * 128, bh);
+        for (int k = 0; k < D / 16; ++k) {
+          const uint32_t off = (k >> 2) * 16384 + (k & 3) * 32;
+          umma_f16_ss(tmem + Cfg::s_col(t), sdesc_sw128(qa + off, 16, 1024), sdesc_sw128(kb + off, 16, 1024), idesc_qk,
+                      k > 0 ? 1u : 0u);
+        }
+        umma_commit(&s_full[t]);
+      };
+      auto issue_pv = [&](int t, int j) {
+        const uint32_t vb = smem_u32(sV + (j % KS) * Cfg::kTileBytes);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          umma_f16_ts(tmem + Cfg::o_col(t), tmem + Cfg::p_col(t) + k * 8, sdesc_sw128(vb + k * 2048, 16384, 1024), idesc_pv,
+                      (j > 0 || k > 0) ? 1u : 0u);
+        }
+        umma_commit(&o_done[t]);
+      };
+
+      bool ok_run = mbar_wait(q_full, 0, abort_flag, a.st, 0x1200) &&
+                    (nmax == 0 || mbar_wait(&k_full[0], 0, abort_flag, a.st, 0x1201));
+      if (ok_run && nmax > 0) {
+        tc_fence_after();
+        for (int t = 0; t < 2; ++t)
+          if (ntile[t] > 0) issue_qk(t, 0);
+        umma_commit(&k_empty[0]);
       }
-      issued = j + 1;
-    }
-    if (aborted) {
+      for (int j = 0; ok_run && j < nmax; ++j) {
+        const int s = j % KS;
+        const uint32_t ph = (j / KS) & 1;
+        const int sn = (j + 1) % KS;
+        const uint32_t phn = ((j + 1) / KS) & 1;
+        if (!Cfg::kAliasP) {
+          // P has its own columns: S_t(j+1) = Q_t K_{j+1}^T may overwrite S_t as
+          // soon as the softmax warps have pulled S_t(j) into registers, so the
+          // next QK runs under softmax_t(j)'s exp work.
+          if (j + 1 < nmax) {
+            if (!mbar_wait(&k_full[sn], phn, abort_flag, a.st, 0x1213)) { ok_run = false; break; }
+            for (int t = 0; t < 2 && ok_run; ++t) {
+              if (j + 1 < ntile[t]) {
+                if (!mbar_wait(&s_free[t], j & 1, abort_flag, a.st, 0x1218 + t)) { ok_run = false; break; }
+                tc_fence_after();
+                issue_qk(t, j + 1);
+              }
+            }
+            if (!ok_run) break;
+            umma_commit(&k_empty[sn]);
+          }
+          if (!mbar_wait(&v_full[s], ph, abort_flag, a.st, 0x1212)) { ok_run = false; break; }
+          for (int t = 0; t < 2 && ok_run; ++t) {
+            if (j < ntile[t]) {
+              if (!mbar_wait(&p_full[t], j & 1, abort_flag, a.st, 0x1210 + t)) { ok_run = false; break; }
+              tc_fence_after();
+              issue_pv(t, j);
+            }
+          }
+          if (!ok_run) break;
+          umma_commit(&v_empty[s]);
+        } else {
+          bool v_ready = false, k_next_ready = false;
+          for (int t = 0; t < 2 && ok_run; ++t) {
+            if (j < ntile[t]) {
+              if (!mbar_wait(&p_full[t], j & 1, abort_flag, a.st, 0x1210 + t)) { ok_run = false; break; }
+              if (!v_ready) {
+                if (!mbar_wait(&v_full[s], ph, abort_flag, a.st, 0x1212)) { ok_run = false; break; }
+                v_ready = true;
+              }
+              tc_fence_after();
+              issue_pv(t, j);
+            }
+          }
+          for (int t = 0; t < 2 && ok_run; ++t) {
+            if (j + 1 < ntile[t]) {
+              // P_t lives in S_t's columns: PV_t(j) must have read it.
+              if (!mbar_wait(&o_done[t], j & 1, abort_flag, a.st, 0x1214 + t)) { ok_run = false; break; }
+              if (!k_next_ready) {
+                if (!mbar_wait(&k_full[sn], phn, abort_flag, a.st, 0x1216)) { ok_run = false; break; }
+                k_next_ready = true;
+              }
+              tc_fence_after();
+              issue_qk(t, j + 1);
+            }
+          }
+          if (!ok_run) break;
+          umma_commit(&v_empty[s]);
+          if (j + 1 < nmax) umma_commit(&k_empty[sn]);
+        }
+      }
+      umma_commit(mma_done);
       DevStatus quiet = a.st;
       quiet.word = nullptr;
       volatile int never = 0;
-      mbar_wait(q_full, 0, &never, quiet, 0);
-      for (int i = (issued > KS ? issued - KS : 0); i < issued; ++i) {
-        mbar_wait(&k_full[i % KS], (i / KS) & 1, &never, quiet, 0);
-        mbar_wait(&v_full[i % KS], (i / KS) & 1, &never, quiet, 0);
-      }
+      mbar_wait(mma_done, 0, &never, quiet, 0);
     }
-  } else if (warp == 1 && lane == 0) {
-    // ---------------------------------------------------------- MMA issuer --
-    constexpr uint32_t idesc_qk = idesc_f16_f32(128, 128, 0, 0);
-    constexpr uint32_t idesc_pv = idesc_f16_f32(128, D, 0, 1);
-    auto issue_qk = [&](int t, int j) {
-      const uint32_t qa = smem_u32(sQ + t * Cfg::kTileBytes);
-      const uint32_t kb = smem_u32(sK + (j % KS) * Cfg::kTileBytes);
-#pragma unroll
-      for (int k = 0; k < D / 16; ++k) {
-        const uint32_t off = (k >> 2) * 16384 + (k & 3) * 32;
-        umma_f16_ss(tmem + Cfg::s_col(t), sdesc_sw128(qa + off, 16, 1024), sdesc_sw128(kb + off, 16, 1024), idesc_qk,
-                    k > 0 ? 1u : 0u);
-      }
-      umma_commit(&s_full[t]);
-    };
-    auto issue_pv = [&](int t, int j) {
-      const uint32_t vb = smem_u32(sV + (j % KS) * Cfg::kTileBytes);
-#pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        umma_f16_ts(tmem + Cfg::o_col(t), tmem + Cfg::p_col(t) + k * 8, sdesc_sw128(vb + k * 2048, 16384, 1024), idesc_pv,
-                    (j > 0 || k > 0) ? 1u : 0u);
-      }
-      umma_commit(&o_done[t]);
-    };
-
-    bool ok_run = mbar_wait(q_full, 0, abort_flag, a.st, 0x1200) &&
-                  (nmax == 0 || mbar_wait(&k_full[0], 0, abort_flag, a.st, 0x1201));
-    if (ok_run && nmax > 0) {
-      tc_fence_after();
-      for (int t = 0; t < 2; ++t)
-        if (ntile[t] > 0) issue_qk(t, 0);
-      umma_commit(&k_empty[0]);
-    }
-    for (int j = 0; ok_run && j < nmax; ++j) {
-      const int s = j % KS;
-      const uint32_t ph = (j / KS) & 1;
-      const int sn = (j + 1) % KS;
-      const uint32_t phn = ((j + 1) / KS) & 1;
-      bool v_ready = false, k_next_ready = false;
-      for (int t = 0; t < 2 && ok_run; ++t) {
-        if (j < ntile[t]) {
-          if (!mbar_wait(&p_full[t], j & 1, abort_flag, a.st, 0x1210 + t)) { ok_run = false; break; }
-          if (!v_ready) {
-            if (!mbar_wait(&v_full[s], ph, abort_flag, a.st, 0x1212)) { ok_run = false; break; }
-            v_ready = true;
-          }
-          tc_fence_after();
-          issue_pv(t, j);
-        }
-        if (!Cfg::kAliasP && j + 1 < ntile[t]) {
-          if (!k_next_ready) {
-            if (!mbar_wait(&k_full[sn], phn, abort_flag, a.st, 0x1213)) { ok_run = false; break; }
-            k_next_ready = true;
-            tc_fence_after();
-          }
-          issue_qk(t, j + 1);
-        }
-      }
-      if (Cfg::kAliasP) {
-        for (int t = 0; t < 2 && ok_run; ++t) {
-          if (j + 1 < ntile[t]) {
-            // P_t lives in S_t's columns: PV_t(j) must have read it.
-            if (!mbar_wait(&o_done[t], j & 1, abort_flag, a.st, 0x1214 + t)) { ok_run = false; break; }
-            if (!k_next_ready) {
-              if (!mbar_wait(&k_full[sn], phn, abort_flag, a.st, 0x1216)) { ok_run = false; break; }
-              k_next_ready = true;
-            }
-            tc_fence_after();
-            issue_qk(t, j + 1);
-          }
-        }
-      }
-      if (!ok_run) break;
-      umma_commit(&v_empty[s]);
-      if (j + 1 < nmax) umma_commit(&k_empty[sn]);
-    }
-    umma_commit(mma_done);
-    DevStatus quiet = a.st;
-    quiet.word = nullptr;
-    volatile int never = 0;
-    mbar_wait(mma_done, 0, &never, quiet, 0);
-  } else if (warp >= 4) {
+  } else {
     // ------------------------------------------------- softmax / epilogue --
+    setmaxnreg_inc<kRegsHigh>();
     const int t = (warp - 4) >> 2;
     const uint32_t q = warp & 3;
     const int row = q * 32 + lane;
@@ -282,6 +311,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const __half* brow = nullptr;
     if (kBias == kBiasDense) brow = a.bias + bh * a.bias_head + static_cast<int64_t>(min(qrow, S - 1)) * a.bias_row;
 
+    const bool fast_path = a.qk_log2 > 0.f;
     float m_used = -INFINITY;
     float l = 0.f;
     bool ok_run = true;
@@ -294,54 +324,73 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       float z[128];
       {
-        uint32_t r[32];
+        // Four TMEM loads in flight, one wait.
+        uint32_t r0[32], r1[32], r2[32], r3[32];
+        tmem_ld32(lane_base + Cfg::s_col(t) + 0, r0);
+        tmem_ld32(lane_base + Cfg::s_col(t) + 32, r1);
+        tmem_ld32(lane_base + Cfg::s_col(t) + 64, r2);
+        tmem_ld32(lane_base + Cfg::s_col(t) + 96, r3);
+        tmem_wait_ld();
+        if (!Cfg::kAliasP) {
+          // S_t(j) is in registers: the issuer may compute S_t(j+1) now.
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&s_free[t]);
+        }
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          tmem_ld32(lane_base + Cfg::s_col(t) + c * 32, r);
-          tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) z[c * 32 + i] = __uint_as_float(r[i]);
+        for (int i = 0; i < 32; ++i) {
+          z[i] = __uint_as_float(r0[i]);
+          z[32 + i] = __uint_as_float(r1[i]);
+          z[64 + i] = __uint_as_float(r2[i]);
+          z[96 + i] = __uint_as_float(r3[i]);
         }
       }
       const int k0 = j * 128;
       const bool edge = (k0 + 128 > S) || (kCausal && k0 + 127 > qrow);
-      float rmax = -INFINITY;
+      // Without a bias and with a positive scale, max(s) * c = max(s * c): the
+      // row max is taken on the raw scores and each probability costs one FFMA
+      // + one ex2. Otherwise z holds the log2-domain logits.
+      const bool raw_scores = (kBias == kBiasNone) && fast_path;
+      if (kBias == kBiasDense) {
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        if (kBias == kBiasDense) {
+        for (int v = 0; v < 16; ++v) {
+          const int key = k0 + v * 8;
+          uint4 raw = make_uint4(0, 0, 0, 0);
+          if (key + 8 <= S) raw = __ldg(reinterpret_cast<const uint4*>(brow + key));
+          const __half2* hp = reinterpret_cast<const __half2*>(&raw);
 #pragma unroll
-          for (int v = 0; v < 4; ++v) {
-            const int key = k0 + c * 32 + v * 8;
-            uint4 raw = make_uint4(0, 0, 0, 0);
-            if (key + 8 <= S) raw = __ldg(reinterpret_cast<const uint4*>(brow + key));
-            const __half2* hp = reinterpret_cast<const __half2*>(&raw);
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              float2 f = __half22float2(hp[e]);
-              z[c * 32 + v * 8 + 2 * e] += f.x;
-              z[c * 32 + v * 8 + 2 * e + 1] += f.y;
-            }
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = __half22float2(hp[e]);
+            z[v * 8 + 2 * e] = (z[v * 8 + 2 * e] + f.x) * a.qk_log2;
+            z[v * 8 + 2 * e + 1] = (z[v * 8 + 2 * e + 1] + f.y) * a.qk_log2;
           }
         }
+      } else if (kBias == kBiasTable) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int col = c * 32 + i;
-          float v;
-          if (kBias == kBiasTable) {
-            const int key = k0 + col;
-            const float tb = (key < S) ? __ldg(trow - key) : 0.f;
-            v = fmaf(z[col], a.qk_log2, tb * kLog2e);
-          } else {
-            v = z[col] * a.qk_log2;
-          }
-          if (edge) {
-            const int key = k0 + col;
-            if (key >= S || (kCausal && key > qrow)) v = -INFINITY;
-          }
-          z[col] = v;
-          rmax = fmaxf(rmax, v);
+        for (int col = 0; col < 128; ++col) {
+          const int key = k0 + col;
+          const float tb = (key < S) ? __ldg(trow - key) : 0.f;
+          z[col] = fmaf(z[col], a.qk_log2, tb * kLog2e);
+        }
+      } else if (!raw_scores) {
+#pragma unroll
+        for (int col = 0; col < 128; ++col) z[col] *= a.qk_log2;
+      }
+      if (edge) {
+#pragma unroll
+        for (int col = 0; col < 128; ++col) {
+          const int key = k0 + col;
+          if (key >= S || (kCausal && key > qrow)) z[col] = -INFINITY;
         }
       }
+      float pm[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) pm[i] = z[i];
+#pragma unroll
+      for (int col = 8; col < 128; ++col) pm[col & 7] = fmaxf(pm[col & 7], z[col]);
+      float rmax = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])),
+                         fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7])));
+      if (raw_scores) rmax *= a.qk_log2;
       const float m_new = fmaxf(m_used, rmax);
       const bool need = m_new > m_used + kRescaleThreshold;
       float alpha = 1.f;
@@ -349,23 +398,40 @@ __global__ void __launch_bounds__(kThreads, 1)
         alpha = ex2_approx(m_used - m_new);
         m_used = m_new;
       }
-      const float m_sub = (m_used == -INFINITY) ? 0.f : m_used;
-      float sum = 0.f;
+      const float neg_m = (m_used == -INFINITY) ? 0.f : -m_used;
+      const float zc = raw_scores ? a.qk_log2 : 1.f;
+      float ps[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ps[i] = 0.f;
+      uint32_t pk[64];
+#pragma unroll
+      for (int i = 0; i < 64; ++i) {
+        const float p0 = ex2_approx(fmaf(z[2 * i], zc, neg_m));
+        const float p1 = ex2_approx(fmaf(z[2 * i + 1], zc, neg_m));
+        ps[(2 * i) & 7] += p0;
+        ps[(2 * i + 1) & 7] += p1;
+        pk[i] = pack_half2(p0, p1);
+      }
+      const float sum = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
+      if (!Cfg::kAliasP && j > 0) {
+        // P_t and O_t are still in use by PV_t(j-1) until it completes.
+        if (!__all_sync(0xffffffffu, mbar_wait(&o_done[t], (j - 1) & 1, abort_flag, a.st, 0x1320 + t))) {
+          ok_run = false;
+          break;
+        }
+        tc_fence_after();
+      }
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
-        uint32_t pk[16];
+        uint32_t q16[16];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float p0 = ex2_approx(z[c * 32 + 2 * i] - m_sub);
-          const float p1 = ex2_approx(z[c * 32 + 2 * i + 1] - m_sub);
-          sum += p0 + p1;
-          pk[i] = pack_half2(p0, p1);
-        }
-        tmem_st16(lane_base + Cfg::p_col(t) + c * 16, pk);
+        for (int i = 0; i < 16; ++i) q16[i] = pk[c * 16 + i];
+        tmem_st16(lane_base + Cfg::p_col(t) + c * 16, q16);
       }
       l = l * alpha + sum;
       if (j > 0 && __any_sync(0xffffffffu, need)) {
-        // PV_t(j-1) is complete: s_full for block j is committed after it.
+        // PV_t(j-1) is complete (waited on above, or implied by s_full when P
+        // aliases S).
         uint32_t r[32];
 #pragma unroll 1
         for (int c = 0; c < D / 32; ++c) {
@@ -447,6 +513,13 @@ int launch_fa2_t(const FaProblem& p, const CUtensorMap& tq, const CUtensorMap& t
   auto kern = fa2_fwd_kernel<D, kCausal, kBias>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(fa2)");
+  cudaFuncAttributes fa{};
+  e = cudaFuncGetAttributes(&fa, kern);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncGetAttributes(fa2)");
+  if (static_cast<int64_t>(fa.numRegs) * kThreads < 128 * kRegsLow + 256 * kRegsHigh) {
+    return fail(NESO_ERR_LAUNCH, "fa2: %d registers/thread cannot fund the %u/%u warpgroup split", fa.numRegs,
+                kRegsLow, kRegsHigh);
+  }
   dim3 grid(args.num_qblocks, p.BH, 1);
   kern<<<grid, kThreads, Cfg::kSmemBytes, stream>>>(tq, tk, tv, args);
   e = cudaGetLastError();
