@@ -15,9 +15,10 @@
 // that ping-pong so the tensor core runs one tile's MMAs while the other
 // tile's softmax runs on the CUDA cores. Keys are consumed in 128-key blocks.
 //   warp 0       TMA producer: Q tiles once, then K_j / V_j into KV rings.
-//   warp 1       single-thread tcgen05.mma issuer:
-//                  S_t  = Q_t . K_j^T    (SS, M=128 N=128 K=16 steps, fp32 in TMEM)
-//                  O_t += P_t . V_j      (TS: P from TMEM, V MN-major from smem)
+//   warp 1       single-thread tcgen05.mma issuer of S_t = Q_t . K_j^T (SS,
+//                M=128 N=128 K=16 steps, fp32 in TMEM)
+//   warp 3       single-thread tcgen05.mma issuer of O_t += P_t . V_j (TS: P
+//                from TMEM, V MN-major from smem)
 //   warp 2       TMEM allocator (512 columns).
 //   warps 4-7    softmax + epilogue for tile 0; warps 8-11 for tile 1. Thread
 //                r owns query row r: it reads its S row from TMEM, computes the
@@ -57,6 +58,7 @@ struct FaCfg {
   __host__ __device__ static constexpr uint32_t p_col(int t) {
     return kAliasP ? s_col(t) : (t ? 256u + 2 * D + 64 : 256u + 2 * D);
   }
+  static constexpr uint32_t kPHalfStride = 32u;  // P columns are contiguous (64 per tile)
   static constexpr int kTmemCols = 512;
   static constexpr int kSmemBytes = (2 + 2 * kStages) * kTileBytes + 1024 + 512;
 };
@@ -97,9 +99,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* p_full = s_full + 2;     // [2]
   uint64_t* o_done = p_full + 2;     // [2]
   uint64_t* s_free = o_done + 2;     // [2] softmax has read S_t (4 warps)
-  uint64_t* mma_done = s_free + 2;   // [1]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  uint64_t* mma_done = s_free + 2;   // [2] one per MMA issuer
+  uint64_t* turn = mma_done + 2;     // [2][4] exp-loop turn of tile t, lane quarter q
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(turn + 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* never_flag = abort_flag + 1;  // stays 0: drain waits ignore the abort
 
   const uint32_t warp = warp_id();
   const uint32_t lane = lane_id();
@@ -108,13 +112,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int bh = blockIdx.y;
   const int q0 = qb * 256;
   const int nkv = (S + 127) / 128;
-  int ntile[2];
-#pragma unroll
-  for (int t = 0; t < 2; ++t) {
-    const int start = q0 + 128 * t;
-    ntile[t] = (start >= S) ? 0 : (kCausal ? min(nkv, start / 128 + 1) : nkv);
-  }
-  const int nmax = max(ntile[0], ntile[1]);
+  // KV blocks each Q tile visits (0 for a tile that starts past S)
+  const int ntile0 = kCausal ? min(nkv, q0 / 128 + 1) : nkv;
+  const int ntile1 = (q0 + 128 >= S) ? 0 : (kCausal ? min(nkv, q0 / 128 + 2) : nkv);
+  const int nmax = max(ntile0, ntile1);
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -130,8 +131,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&o_done[t], 1);
       mbar_init(&s_free[t], 4);
     }
-    mbar_init(mma_done, 1);
+    mbar_init(&mma_done[0], 1);
+    mbar_init(&mma_done[1], 1);
+    for (int i = 0; i < 8; ++i) mbar_init(&turn[i], 1);
     *abort_flag = 0;
+    *never_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tmQ);
     tma_prefetch_desc(&tmK);
@@ -150,10 +154,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     setmaxnreg_dec<kRegsLow>();
     if (warp == 0 && lane == 0) {
       // ------------------------------------------------------------ producer --
-      const uint32_t qbytes = (ntile[1] > 0 ? 2 : 1) * Cfg::kTileBytes;
+      const uint32_t qbytes = (ntile1 > 0 ? 2 : 1) * Cfg::kTileBytes;
       mbar_arrive_expect_tx(q_full, qbytes);
       for (int t = 0; t < 2; ++t) {
-        if (ntile[t] == 0) continue;
+        if ((t ? ntile1 : ntile0) == 0) continue;
 #pragma unroll
         for (int c = 0; c < Cfg::kChunks; ++c) {
           tma_load_3d(sQ + t * Cfg::kTileBytes + c * 16384, &tmQ, q_full, c * 64, q0 + 128 * t, bh);
@@ -174,8 +178,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           issued = j;  // K_j is in flight; V_j is not
           DevStatus quiet = a.st;
           quiet.word = nullptr;
-          volatile int never = 0;
-          mbar_wait(&k_full[s], ph, &never, quiet, 0);
+          mbar_wait(&k_full[s], ph, never_flag, quiet, 0);
           aborted = true;
           break;
         }
@@ -189,112 +192,102 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (aborted) {
         DevStatus quiet = a.st;
         quiet.word = nullptr;
-        volatile int never = 0;
-        mbar_wait(q_full, 0, &never, quiet, 0);
+        mbar_wait(q_full, 0, never_flag, quiet, 0);
         for (int i = (issued > KS ? issued - KS : 0); i < issued; ++i) {
-          mbar_wait(&k_full[i % KS], (i / KS) & 1, &never, quiet, 0);
-          mbar_wait(&v_full[i % KS], (i / KS) & 1, &never, quiet, 0);
+          mbar_wait(&k_full[i % KS], (i / KS) & 1, never_flag, quiet, 0);
+          mbar_wait(&v_full[i % KS], (i / KS) & 1, never_flag, quiet, 0);
         }
       }
-    } else if (warp == 1 && lane == 0) {
-      // ---------------------------------------------------------- MMA issuer --
+    } else if ((warp == 1 || warp == 3) && lane == 0) {
+      // ------------------------------------------------------- MMA issuers --
+      // Two single-thread issuers on different SM sub-partitions: warp 1
+      // issues S = Q K^T, warp 3 issues O += P V. A tcgen05.mma issue blocks
+      // until the tensor pipe accepts it, so one thread serving both streams
+      // (and sharing its scheduler with busy softmax warps) leaves the pipe
+      // idle between MMAs. The streams only meet through mbarriers.
       constexpr uint32_t idesc_qk = idesc_f16_f32(128, 128, 0, 0);
       constexpr uint32_t idesc_pv = idesc_f16_f32(128, D, 0, 1);
-      auto issue_qk = [&](int t, int j) {
-        const uint32_t qa = smem_u32(sQ + t * Cfg::kTileBytes);
-        const uint32_t kb = smem_u32(sK + (j % KS) * Cfg::kTileBytes);
+      // Descriptor bases, computed once; a K step only moves the start
+      // address field (low bits), so the per-MMA work is one 64-bit add.
+      const uint64_t q_desc0 = sdesc_sw128(smem_u32(sQ), 16, 1024);
+      const uint64_t k_desc0 = sdesc_sw128(smem_u32(sK), 16, 1024);
+      const uint64_t v_desc0 = sdesc_sw128(smem_u32(sV), 16384, 1024);
+      auto n_of = [=](int t) { return t ? ntile1 : ntile0; };
+      bool ok_run = true;
+      if (warp == 1) {
+        auto issue_qk = [=](int t, int j) {
+          const uint64_t qd = q_desc0 + static_cast<uint64_t>((t * Cfg::kTileBytes) >> 4);
+          const uint64_t kd = k_desc0 + static_cast<uint64_t>(((j % KS) * Cfg::kTileBytes) >> 4);
+          const uint32_t d_tmem = tmem + Cfg::s_col(t);
 #pragma unroll
-        for (int k = 0; k < D / 16; ++k) {
-          const uint32_t off = (k >> 2) * 16384 + (k & 3) * 32;
-          umma_f16_ss(tmem + Cfg::s_col(t), sdesc_sw128(qa + off, 16, 1024), sdesc_sw128(kb + off, 16, 1024), idesc_qk,
-                      k > 0 ? 1u : 0u);
+          for (int k = 0; k < D / 16; ++k) {
+            const uint64_t off = static_cast<uint64_t>(((k >> 2) * 16384 + (k & 3) * 32) >> 4);
+            umma_f16_ss(d_tmem, qd + off, kd + off, idesc_qk, k > 0 ? 1u : 0u);
+          }
+          umma_commit(&s_full[t]);
+        };
+        ok_run = mbar_wait(q_full, 0, abort_flag, a.st, 0x1200) &&
+                 (nmax == 0 || mbar_wait(&k_full[0], 0, abort_flag, a.st, 0x1201));
+        if (ok_run && nmax > 0) {
+          tc_fence_after();
+          for (int t = 0; t < 2; ++t)
+            if (n_of(t) > 0) issue_qk(t, 0);
+          umma_commit(&k_empty[0]);
         }
-        umma_commit(&s_full[t]);
-      };
-      auto issue_pv = [&](int t, int j) {
-        const uint32_t vb = smem_u32(sV + (j % KS) * Cfg::kTileBytes);
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          umma_f16_ts(tmem + Cfg::o_col(t), tmem + Cfg::p_col(t) + k * 8, sdesc_sw128(vb + k * 2048, 16384, 1024), idesc_pv,
-                      (j > 0 || k > 0) ? 1u : 0u);
-        }
-        umma_commit(&o_done[t]);
-      };
-
-      bool ok_run = mbar_wait(q_full, 0, abort_flag, a.st, 0x1200) &&
-                    (nmax == 0 || mbar_wait(&k_full[0], 0, abort_flag, a.st, 0x1201));
-      if (ok_run && nmax > 0) {
-        tc_fence_after();
-        for (int t = 0; t < 2; ++t)
-          if (ntile[t] > 0) issue_qk(t, 0);
-        umma_commit(&k_empty[0]);
-      }
-      for (int j = 0; ok_run && j < nmax; ++j) {
-        const int s = j % KS;
-        const uint32_t ph = (j / KS) & 1;
-        const int sn = (j + 1) % KS;
-        const uint32_t phn = ((j + 1) / KS) & 1;
-        if (!Cfg::kAliasP) {
-          // P has its own columns: S_t(j+1) = Q_t K_{j+1}^T may overwrite S_t as
-          // soon as the softmax warps have pulled S_t(j) into registers, so the
-          // next QK runs under softmax_t(j)'s exp work.
-          if (j + 1 < nmax) {
-            if (!mbar_wait(&k_full[sn], phn, abort_flag, a.st, 0x1213)) { ok_run = false; break; }
-            for (int t = 0; t < 2 && ok_run; ++t) {
-              if (j + 1 < ntile[t]) {
+        for (int j = 0; ok_run && j + 1 < nmax; ++j) {
+          const int sn = (j + 1) % KS;
+          const uint32_t phn = ((j + 1) / KS) & 1;
+          if (!mbar_wait(&k_full[sn], phn, abort_flag, a.st, 0x1213)) { ok_run = false; break; }
+          for (int t = 0; t < 2 && ok_run; ++t) {
+            if (j + 1 < n_of(t)) {
+              if (Cfg::kAliasP) {
+                // P_t lives in S_t's columns: PV_t(j) must have read it.
+                if (!mbar_wait(&o_done[t], j & 1, abort_flag, a.st, 0x1214 + t)) { ok_run = false; break; }
+              } else {
+                // P has its own columns: S_t may be overwritten once the softmax
+                // warps hold S_t(j) in registers, so QK(j+1) runs under softmax(j).
                 if (!mbar_wait(&s_free[t], j & 1, abort_flag, a.st, 0x1218 + t)) { ok_run = false; break; }
-                tc_fence_after();
-                issue_qk(t, j + 1);
-              }
-            }
-            if (!ok_run) break;
-            umma_commit(&k_empty[sn]);
-          }
-          if (!mbar_wait(&v_full[s], ph, abort_flag, a.st, 0x1212)) { ok_run = false; break; }
-          for (int t = 0; t < 2 && ok_run; ++t) {
-            if (j < ntile[t]) {
-              if (!mbar_wait(&p_full[t], j & 1, abort_flag, a.st, 0x1210 + t)) { ok_run = false; break; }
-              tc_fence_after();
-              issue_pv(t, j);
-            }
-          }
-          if (!ok_run) break;
-          umma_commit(&v_empty[s]);
-        } else {
-          bool v_ready = false, k_next_ready = false;
-          for (int t = 0; t < 2 && ok_run; ++t) {
-            if (j < ntile[t]) {
-              if (!mbar_wait(&p_full[t], j & 1, abort_flag, a.st, 0x1210 + t)) { ok_run = false; break; }
-              if (!v_ready) {
-                if (!mbar_wait(&v_full[s], ph, abort_flag, a.st, 0x1212)) { ok_run = false; break; }
-                v_ready = true;
-              }
-              tc_fence_after();
-              issue_pv(t, j);
-            }
-          }
-          for (int t = 0; t < 2 && ok_run; ++t) {
-            if (j + 1 < ntile[t]) {
-              // P_t lives in S_t's columns: PV_t(j) must have read it.
-              if (!mbar_wait(&o_done[t], j & 1, abort_flag, a.st, 0x1214 + t)) { ok_run = false; break; }
-              if (!k_next_ready) {
-                if (!mbar_wait(&k_full[sn], phn, abort_flag, a.st, 0x1216)) { ok_run = false; break; }
-                k_next_ready = true;
               }
               tc_fence_after();
               issue_qk(t, j + 1);
             }
           }
           if (!ok_run) break;
+          umma_commit(&k_empty[sn]);
+        }
+      } else {
+        auto issue_pv = [=](int t, int j) {
+          const uint64_t vd = v_desc0 + static_cast<uint64_t>(((j % KS) * Cfg::kTileBytes) >> 4);
+          const uint32_t d_tmem = tmem + Cfg::o_col(t);
+          const uint32_t p_tmem = tmem + Cfg::p_col(t);
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            umma_f16_ts(d_tmem, p_tmem + (k >> 2) * Cfg::kPHalfStride + (k & 3) * 8,
+                        vd + static_cast<uint64_t>((k * 2048) >> 4), idesc_pv, (j > 0 || k > 0) ? 1u : 0u);
+          }
+          umma_commit(&o_done[t]);
+        };
+        for (int j = 0; ok_run && j < nmax; ++j) {
+          const int s = j % KS;
+          const uint32_t ph = (j / KS) & 1;
+          if (!mbar_wait(&v_full[s], ph, abort_flag, a.st, 0x1212)) { ok_run = false; break; }
+          for (int t = 0; t < 2 && ok_run; ++t) {
+            if (j < n_of(t)) {
+              if (!mbar_wait(&p_full[t], j & 1, abort_flag, a.st, 0x1210 + t)) { ok_run = false; break; }
+              tc_fence_after();
+              issue_pv(t, j);
+            }
+          }
+          if (!ok_run) break;
           umma_commit(&v_empty[s]);
-          if (j + 1 < nmax) umma_commit(&k_empty[sn]);
         }
       }
-      umma_commit(mma_done);
+      // Every MMA this thread issued must be complete before TMEM is freed.
+      uint64_t* done = warp == 1 ? mma_done : mma_done + 1;
+      umma_commit(done);
       DevStatus quiet = a.st;
       quiet.word = nullptr;
-      volatile int never = 0;
-      mbar_wait(mma_done, 0, &never, quiet, 0);
+      mbar_wait(done, 0, never_flag, quiet, 0);
     }
   } else {
     // ------------------------------------------------- softmax / epilogue --
@@ -304,7 +297,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row = q * 32 + lane;
     const int qrow = q0 + 128 * t + row;
     const uint32_t lane_base = tmem + ((q * 32) << 16);
-    const int n_t = ntile[t];
+    const int n_t = t ? ntile1 : ntile0;
     const int h = bh % a.H;
     const float* trow = nullptr;
     if (kBias == kBiasTable) trow = a.table + static_cast<int64_t>(h) * (2 * S - 1) + (min(qrow, S - 1) + S - 1);
@@ -383,11 +376,23 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (key >= S || (kCausal && key > qrow)) z[col] = -INFINITY;
         }
       }
+      // Row max, 8 independent chains (D = 128: 3-input max). The variant
+      // per head dim is the faster one measured on B200.
       float pm[8];
+      if constexpr (D == 128) {
 #pragma unroll
-      for (int i = 0; i < 8; ++i) pm[i] = z[i];
+        for (int i = 0; i < 8; ++i) pm[i] = fmaxf(z[i], z[8 + i]);
 #pragma unroll
-      for (int col = 8; col < 128; ++col) pm[col & 7] = fmaxf(pm[col & 7], z[col]);
+        for (int c = 16; c < 128; c += 16) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) pm[i] = fmax3(pm[i], z[c + i], z[c + 8 + i]);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) pm[i] = z[i];
+#pragma unroll
+        for (int col = 8; col < 128; ++col) pm[col & 7] = fmaxf(pm[col & 7], z[col]);
+      }
       float rmax = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])),
                          fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7])));
       if (raw_scores) rmax *= a.qk_log2;
@@ -400,19 +405,60 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const float neg_m = (m_used == -INFINITY) ? 0.f : -m_used;
       const float zc = raw_scores ? a.qk_log2 : 1.f;
+      // Ping-pong on the exp unit: the two warps that share this SM
+      // sub-partition (same lane quarter q, tiles 0 and 1) take strict turns
+      // for their exp loops, tile 0 first. Everything else a tile does (TMEM
+      // traffic, row max, P store, its MMAs) then hides under the other
+      // tile's exps instead of both tiles stalling at the same time.
+      // Tile 0 block j waits for tile 1's block j-1 (when tile 1 exists);
+      // tile 1 block j waits for tile 0's block j (an existing tile 1 never
+      // has fewer blocks than tile 0).
+      const bool wait_turn = (t == 0) ? (j > 0 && ntile1 > 0) : (j < ntile0);
+      if (wait_turn) {
+        const uint32_t par = (t == 0) ? ((j - 1) & 1) : (j & 1);
+        if (!__all_sync(0xffffffffu, mbar_wait(&turn[t * 4 + q], par, abort_flag, a.st, 0x1340 + t))) {
+          ok_run = false;
+          break;
+        }
+      }
+      // p = 2^(z * zc - m), one ex2 per element, fp32 row sums in 8
+      // partials. D = 128 forms the exponent arguments and the sums two
+      // lanes per instruction (packed fp32 FMA / add).
       float ps[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) ps[i] = 0.f;
       uint32_t pk[64];
+      if constexpr (D == 128) {
+        const uint64_t zc2 = f2_pack(zc, zc);
+        const uint64_t nm2 = f2_pack(neg_m, neg_m);
+        uint64_t acc2[4] = {0ull, 0ull, 0ull, 0ull};
 #pragma unroll
-      for (int i = 0; i < 64; ++i) {
-        const float p0 = ex2_approx(fmaf(z[2 * i], zc, neg_m));
-        const float p1 = ex2_approx(fmaf(z[2 * i + 1], zc, neg_m));
-        ps[(2 * i) & 7] += p0;
-        ps[(2 * i + 1) & 7] += p1;
-        pk[i] = pack_half2(p0, p1);
+        for (int i = 0; i < 64; ++i) {
+          const uint64_t x2 = ffma2(f2_pack(z[2 * i], z[2 * i + 1]), zc2, nm2);
+          const float p0 = ex2_approx(f2_lo(x2));
+          const float p1 = ex2_approx(f2_hi(x2));
+          acc2[i & 3] = fadd2(acc2[i & 3], f2_pack(p0, p1));
+          pk[i] = pack_half2(p0, p1);
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          ps[2 * i] = f2_lo(acc2[i]);
+          ps[2 * i + 1] = f2_hi(acc2[i]);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) ps[i] = 0.f;
+#pragma unroll
+        for (int i = 0; i < 64; ++i) {
+          const float p0 = ex2_approx(fmaf(z[2 * i], zc, neg_m));
+          const float p1 = ex2_approx(fmaf(z[2 * i + 1], zc, neg_m));
+          ps[(2 * i) & 7] += p0;
+          ps[(2 * i + 1) & 7] += p1;
+          pk[i] = pack_half2(p0, p1);
+        }
       }
       const float sum = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
+      // Hand the exp unit to the partner warp of the other tile.
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&turn[(1 - t) * 4 + q]);
       if (!Cfg::kAliasP && j > 0) {
         // P_t and O_t are still in use by PV_t(j-1) until it completes.
         if (!__all_sync(0xffffffffu, mbar_wait(&o_done[t], (j - 1) & 1, abort_flag, a.st, 0x1320 + t))) {

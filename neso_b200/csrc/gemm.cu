@@ -71,6 +71,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* mma_done = bars + 2 * S + 4;    // [1]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 5);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* never_flag = abort_flag + 1;  // stays 0: drain waits ignore the abort
 
   const uint32_t warp = warp_id();
   const uint32_t lane = lane_id();
@@ -87,6 +88,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     mbar_init(mma_done, 1);
     *abort_flag = 0;
+    *never_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
@@ -126,9 +128,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Drain this CTA's own copies still in flight before the CTA exits.
       DevStatus quiet = args.st;
       quiet.word = nullptr;
-      volatile int never = 0;
       for (int i = (it > S ? it - S : 0); i < it; ++i) {
-        mbar_wait(&full[i % S], (i / S) & 1, &never, quiet, 0);
+        mbar_wait(&full[i % S], (i / S) & 1, never_flag, quiet, 0);
       }
     }
   } else if (warp == 1 && lane == 0) {
@@ -166,8 +167,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     umma_commit(mma_done);
     DevStatus quiet = args.st;
     quiet.word = nullptr;
-    volatile int never = 0;
-    mbar_wait(mma_done, 0, &never, quiet, 0);
+    mbar_wait(mma_done, 0, never_flag, quiet, 0);
   } else if (warp >= 4) {
     // --------------------------------------------------------- epilogue --
     const uint32_t q = warp & 3;  // TMEM lane quarter this warp may access

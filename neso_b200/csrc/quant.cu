@@ -107,6 +107,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* mma_done = acc_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* never_flag = abort_flag + 1;  // stays 0: drain waits ignore the abort
 
   const uint32_t warp = warp_id();
   const uint32_t lane = lane_id();
@@ -124,6 +125,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     mbar_init(mma_done, 1);
     *abort_flag = 0;
+    *never_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tmX);
     tma_prefetch_desc(&tmW);
@@ -163,8 +165,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (aborted) {
       DevStatus quiet = args.st;
       quiet.word = nullptr;
-      volatile int never = 0;
-      for (int i = (it > S ? it - S : 0); i < it; ++i) mbar_wait(&load_full[i % S], (i / S) & 1, &never, quiet, 0);
+      for (int i = (it > S ? it - S : 0); i < it; ++i) mbar_wait(&load_full[i % S], (i / S) & 1, never_flag, quiet, 0);
     }
   } else if (warp == 1 && lane == 0) {
     // ---------------------------------------------------------- MMA issuer --
@@ -211,8 +212,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     umma_commit(mma_done);
     DevStatus quiet = args.st;
     quiet.word = nullptr;
-    volatile int never = 0;
-    mbar_wait(mma_done, 0, &never, quiet, 0);
+    mbar_wait(mma_done, 0, never_flag, quiet, 0);
   } else if (warp >= 4 && warp < 8) {
     // ------------------------------------------------------------- convert --
     const int ct = threadIdx.x - 128;  // 0..127
