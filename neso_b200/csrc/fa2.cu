@@ -557,18 +557,16 @@ int launch_fa2_t(const FaProblem& p, const CUtensorMap& tq, const CUtensorMap& t
                  FaArgs& args, cudaStream_t stream) {
   using Cfg = FaCfg<D>;
   auto kern = fa2_fwd_kernel<D, kCausal, kBias>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(fa2)");
   cudaFuncAttributes fa{};
-  e = cudaFuncGetAttributes(&fa, kern);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncGetAttributes(fa2)");
+  int rc = kernel_setup(reinterpret_cast<const void*>(kern), Cfg::kSmemBytes, &fa);
+  if (rc != NESO_OK) return rc;
   if (static_cast<int64_t>(fa.numRegs) * kThreads < 128 * kRegsLow + 256 * kRegsHigh) {
     return fail(NESO_ERR_LAUNCH, "fa2: %d registers/thread cannot fund the %u/%u warpgroup split", fa.numRegs,
                 kRegsLow, kRegsHigh);
   }
   dim3 grid(args.num_qblocks, p.BH, 1);
   kern<<<grid, kThreads, Cfg::kSmemBytes, stream>>>(tq, tk, tv, args);
-  e = cudaGetLastError();
+  cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "fa2 launch");
   return ok();
 }

@@ -264,10 +264,12 @@ int launch_gemm_bn(const void* A, int64_t lda, const void* B, int64_t ldb, float
   const int tiles = args.num_m * args.num_n;
   const int grid = tiles < sm_count() ? tiles : sm_count();
   auto kern = gemm_f16_tcgen05_kernel<BN>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemm)");
+  {
+    int src = kernel_setup(reinterpret_cast<const void*>(kern), Cfg::kSmemBytes, nullptr);
+    if (src != NESO_OK) return src;
+  }
   kern<<<grid, kThreads, Cfg::kSmemBytes, stream>>>(tmA, tmB, args);
-  e = cudaGetLastError();
+  cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "gemm launch");
   return ok();
 }

@@ -25,6 +25,8 @@
 // operand; M <= 64 swaps operands (A = dequantised W^T with M' = 128 output
 // channels, B = X with N' = M rounded up to 16/32/64) so decode-sized batches
 // still run on the tensor cores and the weight stream stays at HBM speed.
+#include <algorithm>
+
 #include "runtime.h"
 
 namespace neso {
@@ -38,35 +40,61 @@ enum QuantKind : int { kInt8 = 0, kInt4G128 = 1 };
 
 template <int kQ, bool kSwap, int kNX>
 struct QCfg {
-  static constexpr int kXBytes = kNX * kBK * 2;                  // X tile [kNX rows][64 k] fp16
-  static constexpr int kRawBytes = (kQ == kInt8) ? 64 * 128 : 32 * 128;
-  static constexpr int kW16Bytes = kBK * kTileN * 2;             // 16 KB per fp16 copy
-  static constexpr int kNumW16 = (kQ == kInt8) ? 1 : 2;          // int4: hi + lo
-  static constexpr int kScaleBytes = (kQ == kInt8) ? 0 : 1024;   // 256 B used, padded for alignment
-  static constexpr int kStageBytes = kXBytes + kRawBytes + kNumW16 * kW16Bytes + kScaleBytes;
-  static constexpr int kStagesRaw = (220 * 1024) / kStageBytes;
-  static constexpr int kStages = kStagesRaw > 8 ? 8 : kStagesRaw;
-  static constexpr int kAccCols = kSwap ? kNX : kTileN;          // accumulator columns per buffer
+  // Three decoupled rings so weight bytes stay in flight independently of
+  // the dequant and MMA rate:
+  //   R  raw weight tiles (int8 [64 k][128 n] or packed int4 [32][128] plus
+  //      the group's 128 fp16 scales), deep: TMA -> convert warps;
+  //   X  activation tiles [kNX rows][64 k] fp16: TMA -> MMA;
+  //   F  dequantised fp16 weight tiles (int4: hi and lo copies): convert -> MMA.
+  static constexpr int kRawBytes = (kQ == kInt8) ? 64 * 128 : 32 * 128 + 1024;
+  static constexpr int kXBytes = kNX * kBK * 2;
+  static constexpr int kW16Bytes = kBK * kTileN * 2;            // 16 KB per fp16 copy
+  static constexpr int kNumW16 = (kQ == kInt8) ? 1 : 2;
+  static constexpr int kFBytes = kNumW16 * kW16Bytes;
+  static constexpr int kFStages = 3;
+  static constexpr int kXStages = kSwap ? 8 : 4;
+  static constexpr int kBudget = 220 * 1024;
+  static constexpr int kRStagesFit = (kBudget - kFStages * kFBytes - kXStages * kXBytes) / kRawBytes;
+  static constexpr int kRStages = kRStagesFit > 16 ? 16 : kRStagesFit;
+  static constexpr int kOffR = 0;
+  static constexpr int kOffX = kRStages * kRawBytes;
+  static constexpr int kOffF = kOffX + kXStages * kXBytes;
+  static constexpr int kOffBars = kOffF + kFStages * kFBytes;
+  static constexpr int kRawTx = (kQ == kInt8) ? 64 * 128 : 32 * 128 + 256;
+  static constexpr int kAccCols = kSwap ? kNX : kTileN;         // accumulator columns per buffer
   static constexpr int kTmemCols = (2 * kAccCols <= 32) ? 32 : (2 * kAccCols <= 64) ? 64
                                    : (2 * kAccCols <= 128) ? 128 : 256;
-  static constexpr int kTxBytes = kXBytes + kRawBytes + ((kQ == kInt8) ? 0 : 256);
-  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + 512;
-  // offsets within a stage (all 1024-aligned)
-  static constexpr int kOffX = 0;
-  static constexpr int kOffRaw = kXBytes;
-  static constexpr int kOffW16 = kXBytes + kRawBytes;
-  static constexpr int kOffScale = kOffW16 + kNumW16 * kW16Bytes;
-  static_assert(kXBytes % 1024 == 0 && kRawBytes % 1024 == 0, "stage parts must stay 1024-aligned");
+  static constexpr int kSmemBytes = kOffBars + 1024 + 1024;
+  static_assert(kRStages >= 4, "raw ring too shallow");
+  static_assert(kXBytes % 1024 == 0 && kRawBytes % 1024 == 0 && kFBytes % 1024 == 0, "1024-aligned stages");
 };
 
 struct QArgs {
   float* Y;
   int64_t ldy;
   const __half* chan_scale;  // int8: per-channel scale [N] (nullable)
+  float* partial;            // split-K: [splits][M][N] fp32 partial sums, else null
   int M, N, K;
   int num_m, num_n, num_k;
+  int splits, kb_per_split;  // K blocks are split into `splits` ranges
   DevStatus st;
 };
+
+// One work unit = (M tile, N tile, K range). K-split index fastest so the
+// units of one output tile run side by side and share X in L2.
+struct QUnit {
+  int mb, nb, ks, kb0, kb1;
+};
+__device__ __forceinline__ QUnit unit_of(int t, const QArgs& a) {
+  QUnit u;
+  u.ks = t % a.splits;
+  const int r = t / a.splits;
+  u.mb = r % a.num_m;
+  u.nb = r / a.num_m;
+  u.kb0 = u.ks * a.kb_per_split;
+  u.kb1 = min(a.num_k, u.kb0 + a.kb_per_split);
+  return u;
+}
 
 // fp16 pair (lo = byte b0, hi = byte b1 of x) -> 0x6400 | byte, i.e. 1024 + byte.
 __device__ __forceinline__ uint32_t bytes_to_h2(uint32_t x, uint32_t sel) {
@@ -95,15 +123,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     wq_gemm_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
                    const __grid_constant__ CUtensorMap tmS, QArgs args) {
   using Cfg = QCfg<kQ, kSwap, kNX>;
-  constexpr int S = Cfg::kStages;
+  constexpr int RS = Cfg::kRStages, XS = Cfg::kXStages, FS = Cfg::kFStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStageBytes);
-  uint64_t* load_full = bars;            // [S] TMA bytes landed
-  uint64_t* conv_full = bars + S;        // [S] fp16 weights written (4 warps)
-  uint64_t* stage_empty = bars + 2 * S;  // [S] MMAs done with the stage
-  uint64_t* acc_full = bars + 3 * S;     // [2]
-  uint64_t* acc_empty = acc_full + 2;    // [2] (4 epilogue warps)
+  uint8_t* sR = smem + Cfg::kOffR;
+  uint8_t* sX = smem + Cfg::kOffX;
+  uint8_t* sF = smem + Cfg::kOffF;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kOffBars);
+  uint64_t* r_full = bars;              // [RS] raw tile landed (TMA)
+  uint64_t* r_empty = r_full + RS;      // [RS] raw tile read by the 4 convert warps
+  uint64_t* x_full = r_empty + RS;      // [XS] activation tile landed (TMA)
+  uint64_t* x_empty = x_full + XS;      // [XS] MMAs done with it
+  uint64_t* f_full = x_empty + XS;      // [FS] fp16 weights written (4 convert warps)
+  uint64_t* f_empty = f_full + FS;      // [FS] MMAs done with them
+  uint64_t* acc_full = f_empty + FS;    // [2]
+  uint64_t* acc_empty = acc_full + 2;   // [2] (4 epilogue warps)
   uint64_t* mma_done = acc_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -111,13 +145,20 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const uint32_t warp = warp_id();
   const uint32_t lane = lane_id();
-  const int num_tiles = args.num_m * args.num_n;
+  const int num_units = args.num_m * args.num_n * args.splits;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < S; ++s) {
-      mbar_init(&load_full[s], 1);
-      mbar_init(&conv_full[s], 4);
-      mbar_init(&stage_empty[s], 1);
+    for (int i = 0; i < RS; ++i) {
+      mbar_init(&r_full[i], 1);
+      mbar_init(&r_empty[i], 4);
+    }
+    for (int i = 0; i < XS; ++i) {
+      mbar_init(&x_full[i], 1);
+      mbar_init(&x_empty[i], 1);
+    }
+    for (int i = 0; i < FS; ++i) {
+      mbar_init(&f_full[i], 4);
+      mbar_init(&f_empty[i], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
@@ -139,33 +180,42 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  DevStatus quiet = args.st;
+  quiet.word = nullptr;
 
-  if (warp == 0 && lane == 0) {
-    // ------------------------------------------------------------ producer --
+  if ((warp == 0 || warp == 3) && lane == 0) {
+    // ----------------------------------------------- TMA producers (R / X) --
+    const bool raw = warp == 0;
+    const int depth = raw ? RS : XS;
+    uint64_t* full = raw ? r_full : x_full;
+    uint64_t* empty = raw ? r_empty : x_empty;
     int it = 0;
     bool aborted = false;
-    for (int t = blockIdx.x; t < num_tiles && !aborted; t += gridDim.x) {
-      const int mb = t % args.num_m;
-      const int nb = t / args.num_m;
-      for (int kb = 0; kb < args.num_k; ++kb, ++it) {
-        const int s = it % S;
-        const uint32_t ph = (it / S) & 1;
-        if (!mbar_wait(&stage_empty[s], ph ^ 1, abort_flag, args.st, 0x2100)) { aborted = true; break; }
-        uint8_t* st = smem + s * Cfg::kStageBytes;
-        mbar_arrive_expect_tx(&load_full[s], Cfg::kTxBytes);
-        tma_load_2d(st + Cfg::kOffX, &tmX, &load_full[s], kb * kBK, kSwap ? 0 : mb * 128);
-        if (kQ == kInt8) {
-          tma_load_2d(st + Cfg::kOffRaw, &tmW, &load_full[s], nb * kTileN, kb * kBK);
+    for (int t = blockIdx.x; t < num_units && !aborted; t += gridDim.x) {
+      const QUnit u = unit_of(t, args);
+      for (int kb = u.kb0; kb < u.kb1; ++kb, ++it) {
+        const int s = it % depth;
+        const uint32_t ph = (it / depth) & 1;
+        if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, args.st, raw ? 0x2100 : 0x2101)) { aborted = true; break; }
+        if (raw) {
+          uint8_t* st = sR + s * Cfg::kRawBytes;
+          mbar_arrive_expect_tx(&full[s], Cfg::kRawTx);
+          if (kQ == kInt8) {
+            tma_load_2d(st, &tmW, &full[s], u.nb * kTileN, kb * kBK);
+          } else {
+            tma_load_2d(st, &tmW, &full[s], u.nb * kTileN, kb * (kBK / 2));
+            tma_load_2d(st + 4096, &tmS, &full[s], u.nb * kTileN, (kb * kBK) / 128);
+          }
         } else {
-          tma_load_2d(st + Cfg::kOffRaw, &tmW, &load_full[s], nb * kTileN, kb * (kBK / 2));
-          tma_load_2d(st + Cfg::kOffScale, &tmS, &load_full[s], nb * kTileN, (kb * kBK) / 128);
+          mbar_arrive_expect_tx(&full[s], Cfg::kXBytes);
+          tma_load_2d(sX + s * Cfg::kXBytes, &tmX, &full[s], kb * kBK, kSwap ? 0 : u.mb * 128);
         }
       }
     }
     if (aborted) {
-      DevStatus quiet = args.st;
-      quiet.word = nullptr;
-      for (int i = (it > S ? it - S : 0); i < it; ++i) mbar_wait(&load_full[i % S], (i / S) & 1, never_flag, quiet, 0);
+      for (int i = (it > depth ? it - depth : 0); i < it; ++i) {
+        mbar_wait(&full[i % depth], (i / depth) & 1, never_flag, quiet, 0);
+      }
     }
   } else if (warp == 1 && lane == 0) {
     // ---------------------------------------------------------- MMA issuer --
@@ -174,30 +224,30 @@ __global__ void __launch_bounds__(kThreads, 1)
     constexpr uint32_t idesc = kSwap ? idesc_f16_f32(128, kNX, 1, 0) : idesc_f16_f32(128, kTileN, 0, 1);
     int it = 0, tc = 0;
     bool aborted = false;
-    for (int t = blockIdx.x; t < num_tiles && !aborted; t += gridDim.x, ++tc) {
+    for (int t = blockIdx.x; t < num_units && !aborted; t += gridDim.x, ++tc) {
+      const QUnit u = unit_of(t, args);
       const int buf = tc & 1;
       const uint32_t use = tc >> 1;
       if (!mbar_wait(&acc_empty[buf], (use & 1) ^ 1, abort_flag, args.st, 0x2200)) break;
       tc_fence_after();
       const uint32_t d_tmem = tmem + buf * Cfg::kAccCols;
-      for (int kb = 0; kb < args.num_k; ++kb, ++it) {
-        const int s = it % S;
-        const uint32_t ph = (it / S) & 1;
-        if (!mbar_wait(&conv_full[s], ph, abort_flag, args.st, 0x2201) ||
-            !mbar_wait(&load_full[s], ph, abort_flag, args.st, 0x2202)) {
+      for (int kb = u.kb0; kb < u.kb1; ++kb, ++it) {
+        const int fs = it % FS, xs = it % XS;
+        if (!mbar_wait(&f_full[fs], (it / FS) & 1, abort_flag, args.st, 0x2201) ||
+            !mbar_wait(&x_full[xs], (it / XS) & 1, abort_flag, args.st, 0x2202)) {
           aborted = true;
           break;
         }
         tc_fence_after();
-        const uint32_t xs = smem_u32(smem + s * Cfg::kStageBytes + Cfg::kOffX);
-        const uint32_t ws = smem_u32(smem + s * Cfg::kStageBytes + Cfg::kOffW16);
+        const uint64_t xd0 = sdesc_sw128(smem_u32(sX + xs * Cfg::kXBytes), 16, 1024);
+        const uint64_t wd0 = sdesc_sw128(smem_u32(sF + fs * Cfg::kFBytes), 8192, 1024);
 #pragma unroll
         for (int k = 0; k < kBK / 16; ++k) {
-          const uint64_t xd = sdesc_sw128(xs + k * 32, 16, 1024);
+          const uint64_t xd = xd0 + static_cast<uint64_t>((k * 32) >> 4);
 #pragma unroll
           for (int p = 0; p < Cfg::kNumW16; ++p) {
-            const uint64_t wd = sdesc_sw128(ws + p * Cfg::kW16Bytes + k * 2048, 8192, 1024);
-            const uint32_t acc = (kb | k | p) != 0 ? 1u : 0u;
+            const uint64_t wd = wd0 + static_cast<uint64_t>((p * Cfg::kW16Bytes + k * 2048) >> 4);
+            const uint32_t acc = (kb != u.kb0 || k != 0 || p != 0) ? 1u : 0u;
             if (kSwap) {
               umma_f16_ss(d_tmem, wd, xd, idesc, acc);
             } else {
@@ -205,98 +255,105 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
         }
-        umma_commit(&stage_empty[s]);
+        umma_commit(&f_empty[fs]);
+        umma_commit(&x_empty[xs]);
       }
       if (!aborted) umma_commit(&acc_full[buf]);
     }
     umma_commit(mma_done);
-    DevStatus quiet = args.st;
-    quiet.word = nullptr;
     mbar_wait(mma_done, 0, never_flag, quiet, 0);
   } else if (warp >= 4 && warp < 8) {
     // ------------------------------------------------------------- convert --
     const int ct = threadIdx.x - 128;  // 0..127
     int it = 0;
     bool ok_run = true;
-    for (int t = blockIdx.x; t < num_tiles && ok_run; t += gridDim.x) {
-      for (int kb = 0; kb < args.num_k; ++kb, ++it) {
-        const int s = it % S;
-        const uint32_t ph = (it / S) & 1;
-        if (!mbar_wait(&load_full[s], ph, abort_flag, args.st, 0x2300)) { ok_run = false; break; }
-        uint8_t* st = smem + s * Cfg::kStageBytes;
-        const uint8_t* raw = st + Cfg::kOffRaw;
-        uint8_t* w16 = st + Cfg::kOffW16;
+    for (int t = blockIdx.x; t < num_units && ok_run; t += gridDim.x) {
+      const QUnit u = unit_of(t, args);
+      for (int kb = u.kb0; kb < u.kb1; ++kb, ++it) {
+        const int rs = it % RS, fs = it % FS;
+        if (!mbar_wait(&r_full[rs], (it / RS) & 1, abort_flag, args.st, 0x2300)) { ok_run = false; break; }
+        const uint8_t* raw = sR + rs * Cfg::kRawBytes;
+        uint8_t* w16 = sF + fs * Cfg::kFBytes;
         if (kQ == kInt8) {
           // thread -> (k row r, n half h); raw unit u of row r sits at unit u ^ (r & 7)
           const int r = ct >> 1;
           const int h = ct & 1;
           const int sw = r & 7;
+          uint4 o[8];
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
-            const int u = 4 * h + i;
-            const uint4 rv = *reinterpret_cast<const uint4*>(raw + r * 128 + ((u ^ sw) << 4));
-            uint4 o0, o1;
-            dequant_i8x16(rv, o0, o1);
-            uint8_t* dst = w16 + h * 8192 + r * 128;
-            *reinterpret_cast<uint4*>(dst + (((2 * i) ^ sw) << 4)) = o0;
-            *reinterpret_cast<uint4*>(dst + (((2 * i + 1) ^ sw) << 4)) = o1;
+            const uint4 rv = *reinterpret_cast<const uint4*>(raw + r * 128 + (((4 * h + i) ^ sw) << 4));
+            dequant_i8x16(rv, o[2 * i], o[2 * i + 1]);
           }
+          // The raw slot is released only once its bytes have been consumed
+          // into registers (the dequantised values depend on them): a release
+          // right after issuing the loads lets the next TMA write overtake
+          // loads that have not been performed yet.
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&r_empty[rs]);
+          if (!mbar_wait(&f_empty[fs], ((it / FS) & 1) ^ 1, abort_flag, args.st, 0x2301)) { ok_run = false; break; }
+          uint8_t* dst = w16 + h * 8192 + r * 128;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) *reinterpret_cast<uint4*>(dst + ((i ^ sw) << 4)) = o[i];
         } else {
           // thread -> (byte row kk: k rows 2kk and 2kk+1, n quarter qn: 32 channels)
           const int kk = ct >> 2;
           const int qn = ct & 3;
-          const int swr = kk & 7;                 // swizzle of the raw row
-          const int r0 = 2 * kk, r1 = 2 * kk + 1;  // fp16 rows
-          const __half* sc = reinterpret_cast<const __half*>(st + Cfg::kOffScale) + qn * 32;
+          const int swr = kk & 7;
+          const __half* sc = reinterpret_cast<const __half*>(raw + 4096) + qn * 32;
           const __half2 b8 = __float2half2_rn(1032.f);  // 1024 + 8
+          uint32_t hv[2][2][8], lv[2][2][8];  // [raw unit i][row r0/r1][16 channels as 8 half2]
+#pragma unroll
+          for (int i = 0; i < 2; ++i) {
+            const uint4 rv = *reinterpret_cast<const uint4*>(raw + kk * 128 + (((2 * qn + i) ^ swr) << 4));
+            const uint32_t words[4] = {rv.x, rv.y, rv.z, rv.w};
+#pragma unroll
+            for (int wdx = 0; wdx < 4; ++wdx) {
+              const uint32_t lo_n = (words[wdx] & 0x0F0F0F0Fu) ^ 0x08080808u;         // k even
+              const uint32_t hi_n = ((words[wdx] >> 4) & 0x0F0F0F0Fu) ^ 0x08080808u;  // k odd
+#pragma unroll
+              for (int half_sel = 0; half_sel < 2; ++half_sel) {
+                const uint32_t sel = half_sel ? 0x7362u : 0x5140u;
+                const __half2 s2 = *reinterpret_cast<const __half2*>(sc + 16 * i + 4 * wdx + 2 * half_sel);
+                const __half2 q0 = __hsub2(u32_as_h2(bytes_to_h2(lo_n, sel)), b8);
+                const __half2 q1 = __hsub2(u32_as_h2(bytes_to_h2(hi_n, sel)), b8);
+                const __half2 w0h = __hmul2(q0, s2);
+                const __half2 w1h = __hmul2(q1, s2);
+                hv[i][0][wdx * 2 + half_sel] = h2_as_u32(w0h);
+                lv[i][0][wdx * 2 + half_sel] = h2_as_u32(__hfma2(q0, s2, __hneg2(w0h)));
+                hv[i][1][wdx * 2 + half_sel] = h2_as_u32(w1h);
+                lv[i][1][wdx * 2 + half_sel] = h2_as_u32(__hfma2(q1, s2, __hneg2(w1h)));
+              }
+            }
+          }
+          // Release the raw slot only after its bytes are consumed (see int8).
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&r_empty[rs]);
+          if (!mbar_wait(&f_empty[fs], ((it / FS) & 1) ^ 1, abort_flag, args.st, 0x2301)) { ok_run = false; break; }
           uint8_t* hi = w16;
           uint8_t* lo = w16 + Cfg::kW16Bytes;
           const int chunk = qn >> 1;
 #pragma unroll
           for (int i = 0; i < 2; ++i) {
-            const int u = 2 * qn + i;
-            const uint4 rv = *reinterpret_cast<const uint4*>(raw + kk * 128 + ((u ^ swr) << 4));
-            const uint32_t words[4] = {rv.x, rv.y, rv.z, rv.w};
-            uint32_t hv0[8], lv0[8], hv1[8], lv1[8];  // rows r0 / r1, 16 channels each
-#pragma unroll
-            for (int wdx = 0; wdx < 4; ++wdx) {
-              const uint32_t lo_n = (words[wdx] & 0x0F0F0F0Fu) ^ 0x08080808u;        // k even
-              const uint32_t hi_n = ((words[wdx] >> 4) & 0x0F0F0F0Fu) ^ 0x08080808u; // k odd
-              const __half2 s01 = *reinterpret_cast<const __half2*>(sc + i * 16 + wdx * 4);
-              const __half2 s23 = *reinterpret_cast<const __half2*>(sc + i * 16 + wdx * 4 + 2);
-#pragma unroll
-              for (int half_sel = 0; half_sel < 2; ++half_sel) {
-                const uint32_t sel = half_sel ? 0x7362u : 0x5140u;
-                const __half2 s2 = half_sel ? s23 : s01;
-                const __half2 q0 = __hsub2(u32_as_h2(bytes_to_h2(lo_n, sel)), b8);
-                const __half2 q1 = __hsub2(u32_as_h2(bytes_to_h2(hi_n, sel)), b8);
-                const __half2 w0h = __hmul2(q0, s2);
-                const __half2 w1h = __hmul2(q1, s2);
-                const __half2 w0l = __hfma2(q0, s2, __hneg2(w0h));
-                const __half2 w1l = __hfma2(q1, s2, __hneg2(w1h));
-                hv0[wdx * 2 + half_sel] = h2_as_u32(w0h);
-                lv0[wdx * 2 + half_sel] = h2_as_u32(w0l);
-                hv1[wdx * 2 + half_sel] = h2_as_u32(w1h);
-                lv1[wdx * 2 + half_sel] = h2_as_u32(w1l);
-              }
-            }
             // 16 channels = two fp16 units; column within the chunk = 32 (qn & 1) + 16 i
             const int v0 = 4 * (qn & 1) + 2 * i;
 #pragma unroll
-            for (int e = 0; e < 2; ++e) {
-              const int v = v0 + e;
-              const int o0 = chunk * 8192 + r0 * 128 + ((v ^ (r0 & 7)) << 4);
-              const int o1 = chunk * 8192 + r1 * 128 + ((v ^ (r1 & 7)) << 4);
-              *reinterpret_cast<uint4*>(hi + o0) = make_uint4(hv0[4 * e], hv0[4 * e + 1], hv0[4 * e + 2], hv0[4 * e + 3]);
-              *reinterpret_cast<uint4*>(lo + o0) = make_uint4(lv0[4 * e], lv0[4 * e + 1], lv0[4 * e + 2], lv0[4 * e + 3]);
-              *reinterpret_cast<uint4*>(hi + o1) = make_uint4(hv1[4 * e], hv1[4 * e + 1], hv1[4 * e + 2], hv1[4 * e + 3]);
-              *reinterpret_cast<uint4*>(lo + o1) = make_uint4(lv1[4 * e], lv1[4 * e + 1], lv1[4 * e + 2], lv1[4 * e + 3]);
+            for (int rr = 0; rr < 2; ++rr) {
+              const int row = 2 * kk + rr;
+#pragma unroll
+              for (int e = 0; e < 2; ++e) {
+                const int off = chunk * 8192 + row * 128 + (((v0 + e) ^ (row & 7)) << 4);
+                *reinterpret_cast<uint4*>(hi + off) = make_uint4(hv[i][rr][4 * e], hv[i][rr][4 * e + 1],
+                                                                 hv[i][rr][4 * e + 2], hv[i][rr][4 * e + 3]);
+                *reinterpret_cast<uint4*>(lo + off) = make_uint4(lv[i][rr][4 * e], lv[i][rr][4 * e + 1],
+                                                                 lv[i][rr][4 * e + 2], lv[i][rr][4 * e + 3]);
+              }
             }
           }
         }
         fence_async_smem();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&conv_full[s]);
+        if (lane == 0) mbar_arrive(&f_full[fs]);
       }
     }
   } else if (warp >= 8) {
@@ -305,9 +362,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int lrow = q * 32 + lane;  // TMEM lane: m (normal) or n (swap)
     const uint32_t lane_base = tmem + ((q * 32) << 16);
     int tc = 0;
-    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++tc) {
-      const int mb = t % args.num_m;
-      const int nb = t / args.num_m;
+    for (int t = blockIdx.x; t < num_units; t += gridDim.x, ++tc) {
+      const QUnit u = unit_of(t, args);
+      const int mb = u.mb;
+      const int nb = u.nb;
+      // split-K: raw partial sums (no scale) go to partial[ks]; the reduce
+      // kernel applies the scale. Otherwise straight to Y.
+      float* ydst = args.partial != nullptr ? args.partial + static_cast<int64_t>(u.ks) * args.M * args.N : args.Y;
+      const int64_t ld = args.partial != nullptr ? args.N : args.ldy;
+      const __half* csc = args.partial != nullptr ? nullptr : args.chan_scale;
       const int buf = tc & 1;
       const uint32_t use = tc >> 1;
       if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[buf], use & 1, abort_flag, args.st, 0x2400))) break;
@@ -315,7 +378,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t acc = lane_base + buf * Cfg::kAccCols;
       if (kSwap) {
         const int n = nb * kTileN + lrow;
-        const float sc = (args.chan_scale != nullptr && n < args.N) ? __half2float(args.chan_scale[n]) : 1.f;
+        const float sc = (csc != nullptr && n < args.N) ? __half2float(csc[n]) : 1.f;
 #pragma unroll
         for (int c = 0; c < (kNX + 31) / 32; ++c) {
           uint32_t r[32];
@@ -332,13 +395,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int i = 0; i < (kNX >= 32 ? 32 : kNX); ++i) {
               const int m = c * 32 + i;
-              if (m < args.M) args.Y[static_cast<int64_t>(m) * args.ldy + n] = __uint_as_float(r[i]) * sc;
+              if (m < args.M) ydst[static_cast<int64_t>(m) * ld + n] = __uint_as_float(r[i]) * sc;
             }
           }
         }
       } else {
         const int m = mb * 128 + lrow;
-        float* yrow = args.Y + static_cast<int64_t>(m) * args.ldy;
+        float* yrow = ydst + static_cast<int64_t>(m) * ld;
 #pragma unroll 1
         for (int c = 0; c < kTileN / 32; ++c) {
           uint32_t r[32];
@@ -350,7 +413,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int i = 0; i < 32; ++i) {
               const int n = n0 + i;
               if (n < args.N) {
-                const float sc = args.chan_scale != nullptr ? __half2float(__ldg(args.chan_scale + n)) : 1.f;
+                const float sc = csc != nullptr ? __half2float(__ldg(csc + n)) : 1.f;
                 yrow[n] = __uint_as_float(r[i]) * sc;
               }
             }
@@ -382,7 +445,58 @@ struct QProblem {
   int64_t ldy;
   int M, N, K;
   int kind;
+  // split-K plan (filled by plan_splits) and the fp32 partial-sum buffer
+  int splits = 1;
+  int kb_per_split = 0;
+  float* partial = nullptr;
+  DevStatus st{};
 };
+
+// Split K when the output tiles alone cannot fill the SMs (small M): pick the
+// split count whose units fill the persistent grid best, preferring fewer
+// splits (each split adds an M x N fp32 partial write and read).
+void plan_splits(QProblem& p, int sms) {
+  const bool swap = p.M <= 64;
+  const int num_m = swap ? 1 : (p.M + 127) / 128;
+  const int num_n = (p.N + kTileN - 1) / kTileN;
+  const int num_k = (p.K + kBK - 1) / kBK;
+  const int base = num_m * num_n;
+  p.splits = 1;
+  p.kb_per_split = num_k;
+  if (base >= sms || num_k < 2) return;
+  // Each split writes and re-reads an M x N fp32 partial: keep that traffic
+  // under a tenth of the weight stream.
+  const double wbytes = (p.kind == kInt8 ? 1.0 : 0.5) * static_cast<double>(p.K) * p.N;
+  const int max_splits = static_cast<int>(0.1 * wbytes / (8.0 * p.M * p.N));
+  if (max_splits < 2) return;
+  double best = static_cast<double>(base) / sms;
+  for (int sp = 2; sp <= 16 && sp <= num_k && sp <= max_splits; ++sp) {
+    const int kbps = (num_k + sp - 1) / sp;
+    const int real = (num_k + kbps - 1) / kbps;  // no empty split
+    const int64_t units = static_cast<int64_t>(base) * real;
+    const int64_t waves = (units + sms - 1) / sms;
+    const double eff = static_cast<double>(units) / static_cast<double>(waves * sms) * (1.0 - 0.01 * real);
+    if (eff > best + 0.02) {
+      best = eff;
+      p.splits = real;
+      p.kb_per_split = kbps;
+    }
+  }
+}
+
+// Y[m, n] = scale[n] * sum_s partial[s][m][n], fixed summation order.
+__global__ void splitk_reduce_kernel(const float* __restrict__ partial, int splits, int M, int N,
+                                     const __half* __restrict__ scale, float* __restrict__ Y, int64_t ldy) {
+  const int64_t total = static_cast<int64_t>(M) * N;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    float acc = 0.f;
+    for (int sp = 0; sp < splits; ++sp) acc += partial[sp * total + i];
+    const int n = static_cast<int>(i % N);
+    if (scale != nullptr) acc *= __half2float(scale[n]);
+    Y[(i / N) * ldy + n] = acc;
+  }
+}
 
 template <int kQ, bool kSwap, int kNX>
 int launch_wq(const QProblem& p, cudaStream_t stream) {
@@ -417,22 +531,33 @@ int launch_wq(const QProblem& p, cudaStream_t stream) {
   args.Y = p.Y;
   args.ldy = p.ldy;
   args.chan_scale = kQ == kInt8 ? static_cast<const __half*>(p.scale) : nullptr;
+  args.partial = p.splits > 1 ? p.partial : nullptr;
   args.M = p.M;
   args.N = p.N;
   args.K = p.K;
   args.num_m = kSwap ? 1 : (p.M + 127) / 128;
   args.num_n = (p.N + kTileN - 1) / kTileN;
   args.num_k = (p.K + kBK - 1) / kBK;
-  int rc = device_status(&args.st);
-  if (rc != NESO_OK) return rc;
-  const int tiles = args.num_m * args.num_n;
-  const int grid = tiles < sm_count() ? tiles : sm_count();
+  args.splits = p.splits;
+  args.kb_per_split = p.kb_per_split;
+  args.st = p.st;
+  const int units = args.num_m * args.num_n * args.splits;
+  const int grid = units < sm_count() ? units : sm_count();
   auto kern = wq_gemm_kernel<kQ, kSwap, kNX>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(wq_gemm)");
+  {
+    int src = kernel_setup(reinterpret_cast<const void*>(kern), Cfg::kSmemBytes, nullptr);
+    if (src != NESO_OK) return src;
+  }
   kern<<<grid, kThreads, Cfg::kSmemBytes, stream>>>(tmX, tmW, tmS, args);
-  e = cudaGetLastError();
+  cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "wq_gemm launch");
+  if (args.partial != nullptr) {
+    const int64_t total = static_cast<int64_t>(p.M) * p.N;
+    const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, 4 * sm_count()));
+    splitk_reduce_kernel<<<blocks, 256, 0, stream>>>(args.partial, args.splits, p.M, p.N, args.chan_scale, p.Y, p.ldy);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "split-K reduce launch");
+  }
   return ok();
 }
 
@@ -468,12 +593,24 @@ int run_wq(const QProblem& p, cudaStream_t stream) {
   if (p.ldw % 16 != 0) return fail(NESO_ERR_MISALIGNED, "weight row stride must be a multiple of 16 bytes");
   if (p.kind == kInt8) {
     if (p.ldw < p.N) return fail(NESO_ERR_INVALID_ARG, "weight row stride < N");
-    return dispatch_wq<kInt8>(p, stream);
+  } else {
+    if (p.K % 128 != 0) return fail(NESO_ERR_UNSUPPORTED, "int4 group-128 needs K %% 128 == 0 (K=%d)", p.K);
+    if (p.scale == nullptr) return fail(NESO_ERR_INVALID_ARG, "null scales");
+    if (p.lds < p.N || (p.lds * 2) % 16 != 0) {
+      return fail(NESO_ERR_MISALIGNED, "scale row stride must be >= N, multiple of 8");
+    }
   }
-  if (p.K % 128 != 0) return fail(NESO_ERR_UNSUPPORTED, "int4 group-128 needs K %% 128 == 0 (K=%d)", p.K);
-  if (p.scale == nullptr) return fail(NESO_ERR_INVALID_ARG, "null scales");
-  if (p.lds < p.N || (p.lds * 2) % 16 != 0) return fail(NESO_ERR_MISALIGNED, "scale row stride must be >= N, multiple of 8");
-  return dispatch_wq<kInt4G128>(p, stream);
+  QProblem q = p;
+  int rc = device_status(&q.st);
+  if (rc != NESO_OK) return rc;
+  plan_splits(q, sm_count());
+  if (q.splits > 1) {
+    void* ws = nullptr;
+    rc = stream_workspace(stream, static_cast<size_t>(q.splits) * q.M * q.N * sizeof(float), &ws);
+    if (rc != NESO_OK) return rc;
+    q.partial = static_cast<float*>(ws);
+  }
+  return q.kind == kInt8 ? dispatch_wq<kInt8>(q, stream) : dispatch_wq<kInt4G128>(q, stream);
 }
 
 }  // namespace

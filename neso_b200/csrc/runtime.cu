@@ -4,7 +4,9 @@
 
 #include <cstdio>
 #include <cstring>
+#include <map>
 #include <mutex>
+#include <utility>
 
 #include "runtime.h"
 
@@ -67,6 +69,52 @@ int device_status(DevStatus* out) {
   }
   out->word = g_status_ptr[dev];
   out->budget_ns = kWaitBudgetNs;
+  return NESO_OK;
+}
+
+int stream_workspace(cudaStream_t stream, size_t bytes, void** out) {
+  static std::mutex mu;
+  static std::map<std::pair<int, cudaStream_t>, std::pair<void*, size_t>> bufs;
+  int dev = 0;
+  int rc = current_device(&dev);
+  if (rc != NESO_OK) return rc;
+  std::lock_guard<std::mutex> lock(mu);
+  auto& slot = bufs[{dev, stream}];
+  if (slot.second < bytes) {
+    cudaError_t e = cudaSuccess;
+    if (slot.first != nullptr) {
+      e = cudaStreamSynchronize(stream);  // earlier work on this stream may still read the old buffer
+      if (e == cudaSuccess) e = cudaFree(slot.first);
+      slot = {nullptr, 0};
+      if (e != cudaSuccess) return cuda_fail(e, "releasing the split-K workspace");
+    }
+    const size_t want = bytes + bytes / 4;
+    void* p = nullptr;
+    e = cudaMalloc(&p, want);
+    if (e != cudaSuccess) return cuda_fail(e, "allocating the split-K workspace");
+    slot = {p, want};
+  }
+  *out = slot.first;
+  return NESO_OK;
+}
+
+int kernel_setup(const void* kern, int smem_bytes, cudaFuncAttributes* attrs) {
+  static std::mutex mu;
+  static std::map<std::pair<int, const void*>, cudaFuncAttributes> cache;
+  int dev = 0;
+  int rc = current_device(&dev);
+  if (rc != NESO_OK) return rc;
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = cache.find({dev, kern});
+  if (it == cache.end()) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
+    cudaFuncAttributes fa{};
+    e = cudaFuncGetAttributes(&fa, kern);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncGetAttributes");
+    it = cache.emplace(std::make_pair(dev, kern), fa).first;
+  }
+  if (attrs != nullptr) *attrs = it->second;
   return NESO_OK;
 }
 

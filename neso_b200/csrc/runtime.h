@@ -29,6 +29,16 @@ int cuda_fail(cudaError_t e, const char* what);
 // once per device, 4 ints: code, where, block, thread).
 int device_status(DevStatus* out);
 
+// Scratch buffer of at least `bytes` for work queued on `stream` (one buffer
+// per device and stream, grown on demand; growing synchronises the stream
+// first). Stays allocated until the process exits.
+int stream_workspace(cudaStream_t stream, size_t bytes, void** out);
+
+// Opt a kernel into `smem_bytes` of dynamic shared memory and return its
+// attributes; done once per (device, kernel) and cached, so per-call launches
+// do not pay for the attribute calls.
+int kernel_setup(const void* kern, int smem_bytes, cudaFuncAttributes* attrs);
+
 // Number of SMs on the current device (cached per device).
 int sm_count();
 
