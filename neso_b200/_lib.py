@@ -80,6 +80,7 @@ SIGNATURES: dict[str, tuple[object, list]] = {
     "neso_w8a16_scaled_matmul": (_int, [_p, _p, _p, _p] + [_i32] * 7 + [*_GRID, _p]),
     "neso_w8a16_matmul_mnk": (_int, [_p, _p, _p, _p, _i32, _i32, _i32, _p]),
     "neso_w4a16_g128_matmul": (_int, [_p, _p, _p, _p, _i32, _i32, _i32, _p]),
+    "neso_w8a16_matmul_mnk_noalloc": (_int, [_p, _p, _p, _p, _i32, _i32, _i32, _p]),
 }
 
 _lib: ctypes.CDLL | None = None

@@ -26,6 +26,7 @@
 // channels, B = X with N' = M rounded up to 16/32/64) so decode-sized batches
 // still run on the tensor cores and the weight stream stays at HBM speed.
 #include <algorithm>
+#include <mutex>
 
 #include "runtime.h"
 
@@ -613,7 +614,61 @@ int run_wq(const QProblem& p, cudaStream_t stream) {
   return q.kind == kInt8 ? dispatch_wq<kInt8>(q, stream) : dispatch_wq<kInt4G128>(q, stream);
 }
 
+// ---------------------------------------------------- allocation-free entry --
+// Scratch for neso_w8a16_matmul_mnk_noalloc: the split-K partial sums and a
+// status block, in fixed device arrays that exist in every GPU's copy of this
+// library from load until process exit. Host code never dereferences these
+// names (on the host they are only stand-ins for the device symbols); their
+// device addresses come from cudaGetSymbolAddress, once per device.
+constexpr size_t kNoAllocScratchFloats = size_t(1) << 20;  // 4 MiB of fp32 partial sums
+static __device__ __align__(256) float g_noalloc_partial[kNoAllocScratchFloats];
+static __device__ __align__(256) int g_noalloc_status[16];
+
+struct NoAllocDevice {
+  std::once_flag once;
+  float* partial = nullptr;
+  int* status = nullptr;
+  cudaError_t err = cudaSuccess;
+};
+NoAllocDevice g_noalloc_dev[64];
+
+// Device addresses of the fixed scratch for the current device (first call
+// per device resolves them; it must run before any stream capture).
+int noalloc_scratch(float** partial, int** status) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= 64) return fail(NESO_ERR_NO_DEVICE, "device ordinal %d out of range", dev);
+  NoAllocDevice& d = g_noalloc_dev[dev];
+  std::call_once(d.once, [&d]() {
+    void* p = nullptr;
+    void* q = nullptr;
+    d.err = cudaGetSymbolAddress(&p, g_noalloc_partial);
+    if (d.err == cudaSuccess) d.err = cudaGetSymbolAddress(&q, g_noalloc_status);
+    if (d.err == cudaSuccess) {
+      d.partial = static_cast<float*>(p);
+      d.status = static_cast<int*>(q);
+    }
+  });
+  if (d.err != cudaSuccess) return cuda_fail(d.err, "cudaGetSymbolAddress(no-allocation scratch)");
+  *partial = d.partial;
+  *status = d.status;
+  return NESO_OK;
+}
+
 }  // namespace
+
+// Status block of the allocation-free entry point on the current device
+// (4 ints: code, where, block, thread); read without allocating.
+int noalloc_status_read(int* host4) {
+  float* partial = nullptr;
+  int* status = nullptr;
+  int rc = noalloc_scratch(&partial, &status);
+  if (rc != NESO_OK) return rc;
+  cudaError_t e = cudaMemcpy(host4, status, 4 * sizeof(int), cudaMemcpyDeviceToHost);
+  return e == cudaSuccess ? NESO_OK : cuda_fail(e, "reading the no-allocation status block");
+}
+
 }  // namespace neso
 
 using namespace neso;
@@ -670,6 +725,48 @@ int neso_w4a16_g128_matmul(const void* X, const uint8_t* Wq, const void* scales,
   p.M = M; p.N = N; p.K = K;
   p.kind = kInt4G128;
   return run_wq(p, as_stream(stream));
+}
+
+
+int neso_w8a16_matmul_mnk_noalloc(const void* X, const int8_t* W, const void* scale, float* Y, int32_t M, int32_t N,
+                                  int32_t K, neso_stream_t stream) {
+  // Same problem and result as neso_w8a16_matmul_mnk, for callers that must
+  // not allocate device memory: the split-K scratch is the fixed array above
+  // and no CUDA allocation is made (the first call on a device resolves the
+  // array's address, see noalloc_scratch).
+  if (M < 0 || N < 0 || K < 0) return fail(NESO_ERR_INVALID_ARG, "negative size");
+  if (M == 0 || N == 0) return ok();
+  if (X == nullptr || W == nullptr || Y == nullptr) return fail(NESO_ERR_INVALID_ARG, "null pointer");
+  if (K % 8 != 0 || N % 16 != 0) {
+    return fail(NESO_ERR_MISALIGNED, "noalloc W8A16 needs K %% 8 == 0 and N %% 16 == 0 (K=%d N=%d)", K, N);
+  }
+  if (K == 0) return fail(NESO_ERR_UNSUPPORTED, "noalloc W8A16 needs K > 0");
+  QProblem q{};
+  q.X = X; q.ldx = K;
+  q.W = W; q.ldw = N;
+  q.scale = scale; q.lds = 0;
+  q.Y = Y; q.ldy = N;
+  q.M = M; q.N = N; q.K = K;
+  q.kind = kInt8;
+  plan_splits(q, sm_count());
+  const size_t need = q.splits > 1 ? static_cast<size_t>(q.splits) * M * N : 0;
+  if (need > kNoAllocScratchFloats) {
+    return fail(NESO_ERR_UNSUPPORTED,
+                "noalloc W8A16: M=%d N=%d needs %zu split-K partial floats (%d splits), above the fixed scratch "
+                "of %zu floats; use neso_w8a16_matmul_mnk", M, N, need, q.splits, kNoAllocScratchFloats);
+  }
+  float* partial = nullptr;
+  int* status = nullptr;
+  int rc = noalloc_scratch(&partial, &status);
+  if (rc != NESO_OK) return rc;
+  // The status block must start at zero for each call; the partial sums need
+  // no clearing (every split writes all of its M x N entries).
+  cudaError_t e = cudaMemsetAsync(status, 0, 16 * sizeof(int), as_stream(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "clearing the no-allocation status block");
+  q.st.word = status;
+  q.st.budget_ns = kWaitBudgetNs;
+  q.partial = need > 0 ? partial : nullptr;
+  return dispatch_wq<kInt8>(q, as_stream(stream));
 }
 
 }  // extern "C"

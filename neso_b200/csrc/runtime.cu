@@ -118,6 +118,8 @@ int kernel_setup(const void* kern, int smem_bytes, cudaFuncAttributes* attrs) {
   return NESO_OK;
 }
 
+int noalloc_status_read(int* host4);  // quant.cu
+
 int sm_count() {
   int dev = 0;
   if (current_device(&dev) != NESO_OK) return 148;
@@ -201,6 +203,13 @@ int neso_device_status(int device, int* code, int* where, int* block, int* threa
     e = cudaDeviceSynchronize();
     if (e == cudaSuccess) e = cudaMemcpy(h, st.word, sizeof(h), cudaMemcpyDeviceToHost);
     if (e != cudaSuccess) rc = cuda_fail(e, "reading the device status word");
+  }
+  if (rc == NESO_OK && h[0] == 0) {
+    // Waits inside the allocation-free entry point report to its own block.
+    int g[4] = {0, 0, 0, 0};
+    if (noalloc_status_read(g) == NESO_OK && g[0] != 0) {
+      for (int i = 0; i < 4; ++i) h[i] = g[i];
+    }
   }
   cudaSetDevice(prev);
   if (rc != NESO_OK) return rc;
