@@ -24,6 +24,8 @@ ROOT = PKG.parent
 CSRC = PKG / "csrc"
 BUILD = ROOT / "_build"
 LIB = PKG / "libneso_b200.so"
+HARNESS_SRC = PKG / "harness" / "neso_harness.cpp"
+HARNESS = PKG / "neso_harness"
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 CFLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
@@ -81,7 +83,21 @@ def build(force: bool = False, verbose: bool = False, ptxas_info: bool = False) 
         if res.returncode != 0:
             raise RuntimeError(f"link failed:\n{' '.join(cmd)}\n{res.stdout}\n{res.stderr}")
         os.replace(tmp, LIB)
+    build_harness(force)
     return LIB
+
+
+def build_harness(force: bool = False) -> Path:
+    """Link the native test/bench harness against libneso_b200.so (rpath $ORIGIN)."""
+    if (not force and HARNESS.exists() and HARNESS.stat().st_mtime > LIB.stat().st_mtime
+            and HARNESS.stat().st_mtime > HARNESS_SRC.stat().st_mtime):
+        return HARNESS
+    cmd = [nvcc(), *ARCH, "-O2", "-std=c++17", f"-I{ROOT / 'include'}", str(HARNESS_SRC), "-o", str(HARNESS),
+           f"-L{PKG}", "-lneso_b200", "-Xlinker", "-rpath,$ORIGIN"]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError(f"harness build failed:\n{' '.join(cmd)}\n{res.stdout}\n{res.stderr}")
+    return HARNESS
 
 
 def main() -> None:

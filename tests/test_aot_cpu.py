@@ -1,0 +1,70 @@
+"""AOT metadata shim and CLI (reference: src/neso/aot_compile.py, src/neso/backend/abi.py,
+tests/test_aot.py), CPU only."""
+import json
+
+import pytest
+
+from neso_b200 import aot
+
+
+def test_compile_add_kernel_metadata():
+    # tests/test_aot.py:104-138
+    r = aot.compile_kernel("add_kernel", "*fp32, *fp32, *fp32, i32, 1024", num_warps=4,
+                           grid=["cdiv(n_elements, 1024)", "1", "1"])
+    assert r.kernel_name == "add_kernel"
+    assert r.constants == {"BLOCK_SIZE": 1024}
+    assert r.grid == ["cdiv(n_elements, 1024)", "1", "1"]
+    names = [p["name"] for p in r.params]
+    assert names == ["x_ptr", "y_ptr", "z_ptr", "n_elements"] and "BLOCK_SIZE" not in names
+    meta = json.loads(json.dumps(r.to_metadata()))
+    assert set(meta) == {"kernel_name", "params", "constants", "threadgroup_size", "num_warps", "grid"}
+    assert meta["constants"]["BLOCK_SIZE"] == 1024
+    assert all("rust_type" not in p for p in meta["params"])
+    assert meta["threadgroup_size"] == 32 * meta["num_warps"]
+
+
+def test_compile_matmul_with_hints():
+    # tests/test_aot.py:197-202 signature form
+    r = aot.compile_kernel("matmul_kernel",
+                           "*fp16:16, *fp16:16, *fp32:16, i32, i32, i32, i32, i32, i32, i32, i32, i32, 128, 128, 32",
+                           num_warps=8, grid=["cdiv(M,128)", "cdiv(N,128)", "1"])
+    assert r.constants == {"BLOCK_M": 128, "BLOCK_N": 128, "BLOCK_K": 32}
+    assert [p["index"] for p in r.params] == list(range(12))
+    assert r.params[0]["is_pointer"] and not r.params[3]["is_pointer"]
+
+
+def test_signature_errors_match_reference():
+    with pytest.raises(ValueError, match="signature has 3 entries but kernel has 5 arguments"):
+        aot.compile_kernel("vector_add", "*fp32, *fp32, *fp32")
+    with pytest.raises(ValueError, match="only specialization hints 1 and 16 are supported"):
+        aot.compile_kernel("vector_add", "*fp32:8, *fp32, *fp32, i32, 1024")
+    with pytest.raises(ValueError, match="must have the form"):
+        aot.compile_kernel("vector_add", "*fp32, *fp32, *fp32, i32, 1024", target="neso:2")
+    with pytest.raises(ValueError, match="expected a Neso target"):
+        aot.compile_kernel("vector_add", "*fp32, *fp32, *fp32, i32, 1024", target="cuda:100:32")
+    with pytest.raises(KeyError):
+        aot.compile_kernel("softmax_kernel", "*fp32, *fp32, i32, 1024")
+    with pytest.raises(ValueError, match="constexpr"):
+        aot.compile_kernel("vector_add", "*fp32, *fp32, *fp32, i32, i32")
+
+
+def test_parse_signature_reference_semantics():
+    ps = aot.parse_signature(["a", "b", "c", "d"], "*fp16:16, i32:1, 64, N", {"N": 7})
+    assert ps.constants == {"b": 1, "c": 64, "d": 7}
+    assert ps.attributes == {(0,): [["tt.divisibility", 16]]}
+    assert ps.triton_signature == {"a": "*fp16", "b": "constexpr", "c": "constexpr", "d": "constexpr"}
+
+
+def test_cli_writes_metadata(tmp_path):
+    out = tmp_path / "vadd"
+    rc = aot.main(["--kernel", "vector_add", "--signature", "*fp32, *fp32, *fp32, i32, 256",
+                   "--grid", "cdiv(n_elements, 256), 1, 1", "--output", str(out)])
+    assert rc == 0
+    meta = json.loads((tmp_path / "vadd.json").read_text())
+    assert meta["kernel_name"] == "vector_add"
+    assert meta["constants"] == {"BLOCK_SIZE": 256}
+    assert meta["grid"] == ["cdiv(n_elements, 256)", "1", "1"]
+    # argument indices the native harness binds (macos/harness.rs:215-222)
+    assert [(p["index"], p["name"]) for p in meta["params"]] == [(0, "x"), (1, "y"), (2, "output"),
+                                                                 (3, "n_elements")]
+    assert aot.main(["--kernel", "nope", "--signature", "i32"]) == 1
