@@ -232,6 +232,9 @@ def main() -> None:
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
+    # One JSON line on stdout: keep NCCL's informational banner off it unless
+    # the caller asked for NCCL logging.
+    os.environ.setdefault("NCCL_DEBUG", "WARN")
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
