@@ -11,9 +11,12 @@
 //   Extensions with no reference kernel: [B,H,S,D] multi-head, causal masking,
 //       and an fp32 relative-position table [H, 2S-1] indexed i - j + S - 1.
 //
-// Work unit: one CTA = one (batch*head, 256 query rows) = two 128-row Q tiles
-// that ping-pong so the tensor core runs one tile's MMAs while the other
-// tile's softmax runs on the CUDA cores. Keys are consumed in 128-key blocks.
+// Work unit: one (batch*head, 256 query rows) = two 128-row Q tiles that
+// ping-pong so the tensor core runs one tile's MMAs while the other tile's
+// softmax runs on the CUDA cores. Keys are consumed in 128-key blocks. Two
+// kernels share this design: fa2_tile_kernel runs one unit per CTA (D = 64),
+// fa2_persistent_kernel keeps one CTA per SM and hands units out from a
+// per-launch counter (D = 128); the host picks the faster one per head dim.
 //   warp 0       TMA producer: Q tiles once, then K_j / V_j into KV rings.
 //   warp 1       single-thread tcgen05.mma issuer of S_t = Q_t . K_j^T (SS,
 //                M=128 N=128 K=16 steps, fp32 in TMEM)
@@ -42,8 +45,13 @@ constexpr int kThreads = 384;
 // block's launch pool (384 x registers per thread), checked on the host.
 constexpr uint32_t kRegsLow = 56;
 constexpr uint32_t kRegsHigh = 216;
+// The persistent kernel's producer and issuers keep per-unit state across
+// units and get more registers; 128 * 72 + 256 * 216 fills the launch pool.
+constexpr uint32_t kRegsLowPersistent = 72;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale only when max grows by > 2^8
+constexpr int kUnitRing = 4;      // unit indices the persistent producer may publish ahead
+constexpr int kUnitReaders = 10;  // QK issuer, PV issuer and the 8 softmax warps
 
 enum BiasMode : int { kBiasNone = 0, kBiasTable = 1, kBiasDense = 2 };
 
@@ -52,6 +60,7 @@ struct FaCfg {
   static constexpr int kChunks = D / 64;           // 128-byte TMA boxes per row
   static constexpr int kTileBytes = 128 * D * 2;   // one Q, K or V tile
   static constexpr int kStages = (D == 64) ? 3 : 2;
+  static constexpr int kQBuffers = 1;  // persistent kernel: Q tiles per unit in flight
   static constexpr bool kAliasP = (D > 64);
   __host__ __device__ static constexpr uint32_t s_col(int t) { return t ? 128u : 0u; }
   __host__ __device__ static constexpr uint32_t o_col(int t) { return t ? 256u + D : 256u; }
@@ -60,7 +69,7 @@ struct FaCfg {
   }
   static constexpr uint32_t kPHalfStride = 32u;  // P columns are contiguous (64 per tile)
   static constexpr int kTmemCols = 512;
-  static constexpr int kSmemBytes = (2 + 2 * kStages) * kTileBytes + 1024 + 512;
+  static constexpr int kSmemBytes = (2 * kQBuffers + 2 * kStages) * kTileBytes + 1024 + 512;
 };
 
 struct FaArgs {
@@ -74,13 +83,18 @@ struct FaArgs {
   const __half* bias;       // kBiasDense: [BH][S][S] fp16 (row stride bias_row)
   int64_t bias_head, bias_row;
   int num_qblocks;
+  int BH;
   int out_f16;
+  // Persistent kernel: [0] next unit ticket, [1] CTAs finished. Zero at
+  // launch; the last CTA to finish puts both back to zero for the next launch
+  // on the stream.
+  int* unit_counter;
   DevStatus st;
 };
 
 template <int D, bool kCausal, int kBias>
 __global__ void __launch_bounds__(kThreads, 1)
-    fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+    fa2_tile_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, FaArgs a) {
   using Cfg = FaCfg<D>;
   constexpr int KS = Cfg::kStages;
@@ -537,6 +551,600 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// One work unit = (query block of 256 rows, batch*head). Units are walked
+// heaviest first when causal, and grouped by head otherwise so the CTAs that
+// run at the same time share K/V in L2.
+__device__ __forceinline__ void unit_coords(int w, int nqb, int BH, bool causal, int& qb, int& bh) {
+  if (causal) {
+    qb = nqb - 1 - w / BH;
+    bh = w % BH;
+  } else {
+    bh = w / nqb;
+    qb = w % nqb;
+  }
+}
+
+// Unit k of this CTA as published by the producer (-1: no more units; -2:
+// the wait was abandoned); counts the caller as one of the slot's readers.
+__device__ __noinline__ int fetch_unit(uint64_t* full, uint64_t* empty, volatile int* ring, int k,
+                                       volatile int* abort_flag, DevStatus st) {
+  if (!mbar_wait(&full[k % kUnitRing], (k / kUnitRing) & 1, abort_flag, st, 0x1401)) return -2;
+  const int w = ring[k % kUnitRing];
+  mbar_arrive(&empty[k % kUnitRing]);
+  return w;
+}
+
+// Persistent variant of the kernel above: one CTA per SM walks work units
+// until a per-launch ticket counter runs past the last one. The producer
+// takes the tickets and publishes each unit index in a small smem ring
+// (unit_full / unit_empty) that every other role reads in the same order, so
+// a CTA's prologue (barrier init, TMEM allocation) is paid once per SM and an
+// SM that runs faster takes more units. Every mbarrier phase is tracked with
+// running counters across units; o_free[t] lets the first PV of the next unit
+// overwrite O_t only after the epilogue has read it, and the exp-unit turn
+// handshake continues across unit boundaries.
+template <int D, bool kCausal, int kBias>
+__global__ void __launch_bounds__(kThreads, 1)
+    fa2_persistent_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                          const __grid_constant__ CUtensorMap tmV, FaArgs a) {
+  using Cfg = FaCfg<D>;
+  constexpr int KS = Cfg::kStages;
+  constexpr int QB = Cfg::kQBuffers;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;                                   // QB x (2 tiles)
+  uint8_t* sK = smem + QB * 2 * Cfg::kTileBytes;        // KS tiles
+  uint8_t* sV = sK + KS * Cfg::kTileBytes;              // KS tiles
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + KS * Cfg::kTileBytes);
+  uint64_t* q_full = bars;              // [QB]
+  uint64_t* q_empty = q_full + QB;      // [QB] last QK of the unit done
+  uint64_t* k_full = q_empty + QB;      // [KS]
+  uint64_t* k_empty = k_full + KS;
+  uint64_t* v_full = k_empty + KS;
+  uint64_t* v_empty = v_full + KS;
+  uint64_t* s_full = v_empty + KS;      // [2]
+  uint64_t* p_full = s_full + 2;        // [2]
+  uint64_t* o_done = p_full + 2;        // [2]
+  uint64_t* s_free = o_done + 2;        // [2] softmax has read S_t (4 warps)
+  uint64_t* o_free = s_free + 2;        // [2] epilogue has read O_t (4 warps)
+  uint64_t* mma_done = o_free + 2;      // [2] one per MMA issuer
+  uint64_t* turn = mma_done + 2;        // [2][4] exp-loop turn of tile t, lane quarter q
+  uint64_t* unit_full = turn + 8;       // [kUnitRing] unit index published
+  uint64_t* unit_empty = unit_full + kUnitRing;  // [kUnitRing] read by all consumers
+  volatile int* unit_ring = reinterpret_cast<volatile int*>(unit_empty + kUnitRing);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(unit_empty + kUnitRing) + kUnitRing;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* never_flag = abort_flag + 1;  // stays 0: drain waits ignore the abort
+
+  const uint32_t warp = warp_id();
+  const uint32_t lane = lane_id();
+  const int S = a.S;
+  const int nkv = (S + 127) / 128;
+  const int num_units = a.num_qblocks * a.BH;
+  // KV blocks each Q tile of unit (q0) visits (0 for a tile that starts past S)
+  auto ntile = [&](int q0, int t) {
+    const int start = q0 + 128 * t;
+    return start >= S ? 0 : (kCausal ? min(nkv, start / 128 + 1) : nkv);
+  };
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < QB; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
+    }
+    for (int s = 0; s < KS; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&s_full[t], 1);
+      mbar_init(&p_full[t], 4);
+      mbar_init(&o_done[t], 1);
+      mbar_init(&s_free[t], 4);
+      mbar_init(&o_free[t], 4);
+      mbar_init(&mma_done[t], 1);
+    }
+    for (int i = 0; i < 8; ++i) mbar_init(&turn[i], 1);
+    for (int i = 0; i < kUnitRing; ++i) {
+      mbar_init(&unit_full[i], 1);
+      mbar_init(&unit_empty[i], kUnitReaders);
+    }
+    *abort_flag = 0;
+    *never_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  if (warp == 2) {
+    tmem_alloc(tmem_slot, Cfg::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  DevStatus quiet = a.st;
+  quiet.word = nullptr;
+  // Unit k of this CTA for a single-thread consumer (see fetch_unit).
+  auto take_unit = [&](int k) -> int {
+    if (!mbar_wait(&unit_full[k % kUnitRing], (k / kUnitRing) & 1, abort_flag, a.st, 0x1400)) return -2;
+    const int w = unit_ring[k % kUnitRing];
+    mbar_arrive(&unit_empty[k % kUnitRing]);
+    return w;
+  };
+
+  if (warp < 4) {
+    // Warpgroup 0: TMA producer, MMA issuers, TMEM allocator.
+    setmaxnreg_dec<kRegsLowPersistent>();
+    if (warp == 0 && lane == 0) {
+      // ------------------------------------------------------------ producer --
+      int g = 0;
+      int q_issued = 0;
+      bool aborted = false;
+      // Units are handed out dynamically: the first one by block index, the
+      // rest from a per-launch counter, so SMs that run faster take more.
+      int w = blockIdx.x;
+      for (int k = 0; !aborted; ++k) {
+        if (!mbar_wait(&unit_empty[k % kUnitRing], ((k / kUnitRing) & 1) ^ 1, abort_flag, a.st, 0x1103)) {
+          aborted = true;
+          break;
+        }
+        unit_ring[k % kUnitRing] = w < num_units ? w : -1;
+        mbar_arrive(&unit_full[k % kUnitRing]);
+        if (w >= num_units) break;
+        const int w_next = static_cast<int>(gridDim.x) + atomicAdd(a.unit_counter, 1);
+        int qb, bh;
+        unit_coords(w, a.num_qblocks, a.BH, kCausal, qb, bh);
+        const int q0 = qb * 256;
+        const int n0 = ntile(q0, 0), n1 = ntile(q0, 1), nmax = max(n0, n1);
+        const int qi = k % QB;
+        if (!mbar_wait(&q_empty[qi], ((k / QB) & 1) ^ 1, abort_flag, a.st, 0x1102)) { aborted = true; break; }
+        mbar_arrive_expect_tx(&q_full[qi], (n1 > 0 ? 2 : 1) * Cfg::kTileBytes);
+        for (int t = 0; t < 2; ++t) {
+          if ((t ? n1 : n0) == 0) continue;
+#pragma unroll
+          for (int c = 0; c < Cfg::kChunks; ++c) {
+            tma_load_3d(sQ + (qi * 2 + t) * Cfg::kTileBytes + c * 16384, &tmQ, &q_full[qi], c * 64, q0 + 128 * t, bh);
+          }
+        }
+        q_issued = k + 1;
+        for (int j = 0; j < nmax; ++j, ++g) {
+          const int s = g % KS;
+          const uint32_t ph = (g / KS) & 1;
+          if (!mbar_wait(&k_empty[s], ph ^ 1, abort_flag, a.st, 0x1100)) { aborted = true; break; }
+          mbar_arrive_expect_tx(&k_full[s], Cfg::kTileBytes);
+#pragma unroll
+          for (int c = 0; c < Cfg::kChunks; ++c) {
+            tma_load_3d(sK + s * Cfg::kTileBytes + c * 16384, &tmK, &k_full[s], c * 64, j * 128, bh);
+          }
+          if (!mbar_wait(&v_empty[s], ph ^ 1, abort_flag, a.st, 0x1101)) {
+            mbar_wait(&k_full[s], ph, never_flag, quiet, 0);  // K_j is in flight; V_j is not
+            aborted = true;
+            break;
+          }
+          mbar_arrive_expect_tx(&v_full[s], Cfg::kTileBytes);
+#pragma unroll
+          for (int c = 0; c < Cfg::kChunks; ++c) {
+            tma_load_3d(sV + s * Cfg::kTileBytes + c * 16384, &tmV, &v_full[s], c * 64, j * 128, bh);
+          }
+        }
+        w = w_next;
+      }
+      if (aborted) {
+        // Drain this CTA's own copies still in flight before it exits.
+        for (int i = (q_issued > QB ? q_issued - QB : 0); i < q_issued; ++i) {
+          mbar_wait(&q_full[i % QB], (i / QB) & 1, never_flag, quiet, 0);
+        }
+        for (int i = (g > KS ? g - KS : 0); i < g; ++i) {
+          mbar_wait(&k_full[i % KS], (i / KS) & 1, never_flag, quiet, 0);
+          mbar_wait(&v_full[i % KS], (i / KS) & 1, never_flag, quiet, 0);
+        }
+      }
+    } else if (warp == 1 && lane == 0) {
+      // -------------------------------------------------------- QK issuer --
+      // Two single-thread MMA issuers on different SM sub-partitions: warp 1
+      // issues S = Q K^T, warp 3 issues O += P V. A tcgen05.mma issue blocks
+      // until the tensor pipe accepts it, so one thread serving both streams
+      // (and sharing its scheduler with busy softmax warps) leaves the pipe
+      // idle between MMAs. The streams only meet through mbarriers.
+      constexpr uint32_t idesc_qk = idesc_f16_f32(128, 128, 0, 0);
+      // Descriptor bases, computed once; a K step only moves the start
+      // address field (low bits), so the per-MMA work is one 64-bit add.
+      const uint64_t q_desc0 = sdesc_sw128(smem_u32(sQ), 16, 1024);
+      const uint64_t k_desc0 = sdesc_sw128(smem_u32(sK), 16, 1024);
+      // bits 0-1: parity of the blocks tile 0/1 has had; bits 2-3: tile 0/1
+      // has had a block (its S buffer has a reader to wait for).
+      uint32_t ph = 0;
+      int s = 0;           // K stage
+      uint32_t kph = 0;    // K stage phase
+      bool ok_run = true;
+      for (int k = 0; ok_run; ++k) {
+        const int w = take_unit(k);
+        if (w < 0) break;
+        int qb, bh;
+        unit_coords(w, a.num_qblocks, a.BH, kCausal, qb, bh);
+        const int q0 = qb * 256;
+        const int n0 = ntile(q0, 0), n1 = ntile(q0, 1), nmax = max(n0, n1);
+        const int qi = QB == 1 ? 0 : (k & 1);
+        if (!mbar_wait(&q_full[qi], (k / QB) & 1, abort_flag, a.st, 0x1200)) break;
+        for (int j = 0; ok_run && j < nmax; ++j) {
+          if (!mbar_wait(&k_full[s], kph, abort_flag, a.st, 0x1213)) { ok_run = false; break; }
+#pragma unroll
+          for (int t = 0; t < 2; ++t) {
+            if (j >= (t ? n1 : n0)) continue;
+            if (ph & (4u << t)) {
+              // S_t is overwritten: the previous block's S must be in the softmax
+              // registers (P own columns) or, when P aliases S, read by its PV.
+              uint64_t* gate = Cfg::kAliasP ? &o_done[t] : &s_free[t];
+              if (!mbar_wait(gate, ((ph >> t) & 1u) ^ 1u, abort_flag, a.st, 0x1218 + t)) { ok_run = false; break; }
+            }
+            tc_fence_after();
+            const uint64_t qd = q_desc0 + static_cast<uint64_t>(((qi * 2 + t) * Cfg::kTileBytes) >> 4);
+            const uint64_t kd = k_desc0 + static_cast<uint64_t>((s * Cfg::kTileBytes) >> 4);
+#pragma unroll
+            for (int kk = 0; kk < D / 16; ++kk) {
+              const uint64_t off = static_cast<uint64_t>(((kk >> 2) * 16384 + (kk & 3) * 32) >> 4);
+              umma_f16_ss(tmem + Cfg::s_col(t), qd + off, kd + off, idesc_qk, kk > 0 ? 1u : 0u);
+            }
+            umma_commit(&s_full[t]);
+            ph = (ph ^ (1u << t)) | (4u << t);
+          }
+          if (!ok_run) break;
+          umma_commit(&k_empty[s]);
+          if (++s == KS) { s = 0; kph ^= 1u; }
+        }
+        if (ok_run) umma_commit(&q_empty[qi]);  // Q buffer free once this unit's QKs finish
+      }
+      // Every MMA this thread issued must be complete before TMEM is freed.
+      umma_commit(&mma_done[0]);
+      mbar_wait(&mma_done[0], 0, never_flag, quiet, 0);
+    } else if (warp == 3 && lane == 0) {
+      // -------------------------------------------------------- PV issuer --
+      constexpr uint32_t idesc_pv = idesc_f16_f32(128, D, 0, 1);
+      const uint64_t v_desc0 = sdesc_sw128(smem_u32(sV), 16384, 1024);
+      // bits 0-1: parity of the blocks tile 0/1 has had; bits 2-3: parity of
+      // the units tile 0/1 has finished; bits 4-5: tile 0/1 has finished a
+      // unit (its O buffer has an epilogue to wait for).
+      uint32_t ph = 0;
+      int s = 0;
+      uint32_t vph = 0;
+      bool ok_run = true;
+      for (int k = 0; ok_run; ++k) {
+        const int w = take_unit(k);
+        if (w < 0) break;
+        int qb, bh;
+        unit_coords(w, a.num_qblocks, a.BH, kCausal, qb, bh);
+        const int q0 = qb * 256;
+        const int n0 = ntile(q0, 0), n1 = ntile(q0, 1), nmax = max(n0, n1);
+        for (int j = 0; ok_run && j < nmax; ++j) {
+          if (!mbar_wait(&v_full[s], vph, abort_flag, a.st, 0x1212)) { ok_run = false; break; }
+#pragma unroll
+          for (int t = 0; t < 2; ++t) {
+            if (j >= (t ? n1 : n0)) continue;
+            if (j == 0 && (ph & (16u << t))) {
+              // The first PV of a unit overwrites O_t: the previous unit's
+              // epilogue must have read it.
+              if (!mbar_wait(&o_free[t], ((ph >> (2 + t)) & 1u) ^ 1u, abort_flag, a.st, 0x1222 + t)) {
+                ok_run = false;
+                break;
+              }
+            }
+            if (!mbar_wait(&p_full[t], (ph >> t) & 1u, abort_flag, a.st, 0x1210 + t)) { ok_run = false; break; }
+            tc_fence_after();
+            const uint64_t vd = v_desc0 + static_cast<uint64_t>((s * Cfg::kTileBytes) >> 4);
+            const uint32_t p_tmem = tmem + Cfg::p_col(t);
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk) {
+              umma_f16_ts(tmem + Cfg::o_col(t), p_tmem + (kk >> 2) * Cfg::kPHalfStride + (kk & 3) * 8,
+                          vd + static_cast<uint64_t>((kk * 2048) >> 4), idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
+            }
+            umma_commit(&o_done[t]);
+            ph ^= 1u << t;
+          }
+          if (!ok_run) break;
+          umma_commit(&v_empty[s]);
+          if (++s == KS) { s = 0; vph ^= 1u; }
+        }
+        if (n0 > 0) ph = (ph ^ 4u) | 16u;
+        if (n1 > 0) ph = (ph ^ 8u) | 32u;
+      }
+      umma_commit(&mma_done[1]);
+      mbar_wait(&mma_done[1], 0, never_flag, quiet, 0);
+    }
+  } else {
+    // ------------------------------------------------- softmax / epilogue --
+    setmaxnreg_inc<kRegsHigh>();
+    const int t = (warp - 4) >> 2;
+    const uint32_t q = warp & 3;
+    const int row = q * 32 + lane;
+    const uint32_t lane_base = tmem + ((q * 32) << 16);
+    const bool fast_path = a.qk_log2 > 0.f;
+    bool ok_run = true;
+    // Phase word, kept in one register across units: bit 0 = parity of the
+    // blocks this tile has handled (s_full; o_done of the previous block is
+    // its complement), bit 1 = parity of the turns this warp has waited for,
+    // bit 2 = the previous unit had a tile 1 (tile 0 only).
+    uint32_t ph = 0;
+    for (int k = 0; ok_run; ++k) {
+      // Lane 0 takes the unit for the warp. The wait sits in a call so the
+      // register allocation of the softmax loop below does not have to keep
+      // the wait loop's state.
+      int w = -2;
+      if (lane == 0) w = fetch_unit(unit_full, unit_empty, unit_ring, k, abort_flag, a.st);
+      w = __shfl_sync(0xffffffffu, w, 0);
+      if (w < 0) break;
+      int qb, bh;
+      unit_coords(w, a.num_qblocks, a.BH, kCausal, qb, bh);
+      const int q0 = qb * 256;
+      const int n_t = ntile(q0, t);
+      const int partner = ntile(q0, 1 - t);  // blocks of the other tile
+      const bool first_wait = (ph & 4u) != 0;
+      if (t == 0) ph = (ph & ~4u) | (partner > 0 ? 4u : 0u);
+      if (n_t == 0) continue;
+      const int qrow = q0 + 128 * t + row;
+      const int h = bh % a.H;
+      const float* trow = nullptr;
+      if (kBias == kBiasTable) trow = a.table + static_cast<int64_t>(h) * (2 * S - 1) + (min(qrow, S - 1) + S - 1);
+      const __half* brow = nullptr;
+      if (kBias == kBiasDense) brow = a.bias + bh * a.bias_head + static_cast<int64_t>(min(qrow, S - 1)) * a.bias_row;
+      float m_used = -INFINITY;
+      float l = 0.f;
+      for (int j = 0; j < n_t; ++j, ph ^= 1u) {
+        // Warp-uniform: every lane must agree before the .sync.aligned TMEM ops.
+        if (!__all_sync(0xffffffffu, mbar_wait(&s_full[t], ph & 1u, abort_flag, a.st, 0x1300 + t))) {
+          ok_run = false;
+          break;
+        }
+        tc_fence_after();
+        float z[128];
+        {
+          // Four TMEM loads in flight, one wait.
+          uint32_t r0[32], r1[32], r2[32], r3[32];
+          tmem_ld32(lane_base + Cfg::s_col(t) + 0, r0);
+          tmem_ld32(lane_base + Cfg::s_col(t) + 32, r1);
+          tmem_ld32(lane_base + Cfg::s_col(t) + 64, r2);
+          tmem_ld32(lane_base + Cfg::s_col(t) + 96, r3);
+          tmem_wait_ld();
+          if (!Cfg::kAliasP) {
+            // S_t is in registers: the issuer may compute the next S_t now.
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&s_free[t]);
+          }
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            z[i] = __uint_as_float(r0[i]);
+            z[32 + i] = __uint_as_float(r1[i]);
+            z[64 + i] = __uint_as_float(r2[i]);
+            z[96 + i] = __uint_as_float(r3[i]);
+          }
+        }
+        const int k0 = j * 128;
+        const bool edge = (k0 + 128 > S) || (kCausal && k0 + 127 > qrow);
+        // Without a bias and with a positive scale, max(s) * c = max(s * c): the
+        // row max is taken on the raw scores and each probability costs one FFMA
+        // + one ex2. Otherwise z holds the log2-domain logits.
+        const bool raw_scores = (kBias == kBiasNone) && fast_path;
+        if (kBias == kBiasDense) {
+#pragma unroll
+          for (int v = 0; v < 16; ++v) {
+            const int key = k0 + v * 8;
+            uint4 raw = make_uint4(0, 0, 0, 0);
+            if (key + 8 <= S) raw = __ldg(reinterpret_cast<const uint4*>(brow + key));
+            const __half2* hp = reinterpret_cast<const __half2*>(&raw);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 f = __half22float2(hp[e]);
+              z[v * 8 + 2 * e] = (z[v * 8 + 2 * e] + f.x) * a.qk_log2;
+              z[v * 8 + 2 * e + 1] = (z[v * 8 + 2 * e + 1] + f.y) * a.qk_log2;
+            }
+          }
+        } else if (kBias == kBiasTable) {
+#pragma unroll
+          for (int col = 0; col < 128; ++col) {
+            const int key = k0 + col;
+            const float tb = (key < S) ? __ldg(trow - key) : 0.f;
+            z[col] = fmaf(z[col], a.qk_log2, tb * kLog2e);
+          }
+        } else if (!raw_scores) {
+#pragma unroll
+          for (int col = 0; col < 128; ++col) z[col] *= a.qk_log2;
+        }
+        if (edge) {
+#pragma unroll
+          for (int col = 0; col < 128; ++col) {
+            const int key = k0 + col;
+            if (key >= S || (kCausal && key > qrow)) z[col] = -INFINITY;
+          }
+        }
+        // Row max, 8 independent chains (D = 128: 3-input max). The variant
+        // per head dim is the faster one measured on B200.
+        float pm[8];
+        if constexpr (D == 128) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) pm[i] = fmaxf(z[i], z[8 + i]);
+#pragma unroll
+          for (int c = 16; c < 128; c += 16) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) pm[i] = fmax3(pm[i], z[c + i], z[c + 8 + i]);
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) pm[i] = z[i];
+#pragma unroll
+          for (int col = 8; col < 128; ++col) pm[col & 7] = fmaxf(pm[col & 7], z[col]);
+        }
+        float rmax = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])),
+                           fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7])));
+        if (raw_scores) rmax *= a.qk_log2;
+        const float m_new = fmaxf(m_used, rmax);
+        const bool need = m_new > m_used + kRescaleThreshold;
+        float alpha = 1.f;
+        if (need) {
+          alpha = ex2_approx(m_used - m_new);
+          m_used = m_new;
+        }
+        const float neg_m = (m_used == -INFINITY) ? 0.f : -m_used;
+        const float zc = raw_scores ? a.qk_log2 : 1.f;
+        // Ping-pong on the exp unit: the two warps that share this SM
+        // sub-partition (same lane quarter q, tiles 0 and 1) take strict turns
+        // for their exp loops. Over the CTA's units the exp loops form one
+        // sequence 0_0 1_0 0_1 1_1 ... (tile 1 may have one block more, or
+        // none); a loop waits for the partner when the item before it in that
+        // sequence is the partner's, and arrives when the item after it is
+        // (tile 1's last block always arrives: if no unit follows, that phase
+        // is simply never waited for). Each turn barrier thus completes one
+        // phase per wait and never runs two phases ahead of its waiter.
+        const bool wait_turn = (t == 0) ? (j > 0 ? partner > 0 : first_wait) : (j < partner);
+        if (wait_turn) {
+          if (!__all_sync(0xffffffffu, mbar_wait(&turn[t * 4 + q], (ph >> 1) & 1u, abort_flag, a.st, 0x1340 + t))) {
+            ok_run = false;
+            break;
+          }
+          ph ^= 2u;
+        }
+        // p = 2^(z * zc - m), one ex2 per element, fp32 row sums in 8
+        // partials. D = 128 forms the exponent arguments and the sums two
+        // lanes per instruction (packed fp32 FMA / add).
+        float ps[8];
+        uint32_t pk[64];
+        if constexpr (D == 128) {
+          const uint64_t zc2 = f2_pack(zc, zc);
+          const uint64_t nm2 = f2_pack(neg_m, neg_m);
+          uint64_t acc2[4] = {0ull, 0ull, 0ull, 0ull};
+#pragma unroll
+          for (int i = 0; i < 64; ++i) {
+            const uint64_t x2 = ffma2(f2_pack(z[2 * i], z[2 * i + 1]), zc2, nm2);
+            const float p0 = ex2_approx(f2_lo(x2));
+            const float p1 = ex2_approx(f2_hi(x2));
+            acc2[i & 3] = fadd2(acc2[i & 3], f2_pack(p0, p1));
+            pk[i] = pack_half2(p0, p1);
+          }
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            ps[2 * i] = f2_lo(acc2[i]);
+            ps[2 * i + 1] = f2_hi(acc2[i]);
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) ps[i] = 0.f;
+#pragma unroll
+          for (int i = 0; i < 64; ++i) {
+            const float p0 = ex2_approx(fmaf(z[2 * i], zc, neg_m));
+            const float p1 = ex2_approx(fmaf(z[2 * i + 1], zc, neg_m));
+            ps[(2 * i) & 7] += p0;
+            ps[(2 * i + 1) & 7] += p1;
+            pk[i] = pack_half2(p0, p1);
+          }
+        }
+        const float sum = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
+        // Hand the exp unit to the partner warp when its loop comes next.
+        if (t == 0 ? (partner > 0)
+                   : (j + 1 < partner || j + 1 == n_t)) {
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&turn[(1 - t) * 4 + q]);
+        }
+        if (!Cfg::kAliasP && j > 0) {
+          // P_t and O_t are still in use by the previous PV until it completes
+          // (for j == 0 the previous unit's epilogue already waited for it).
+          if (!__all_sync(0xffffffffu, mbar_wait(&o_done[t], (ph & 1u) ^ 1u, abort_flag, a.st, 0x1320 + t))) {
+            ok_run = false;
+            break;
+          }
+          tc_fence_after();
+        }
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t q16[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) q16[i] = pk[c * 16 + i];
+          tmem_st16(lane_base + Cfg::p_col(t) + c * 16, q16);
+        }
+        l = l * alpha + sum;
+        if (j > 0 && __any_sync(0xffffffffu, need)) {
+          // The previous PV is complete (waited on above, or implied by s_full
+          // when P aliases S).
+          uint32_t r[32];
+#pragma unroll 1
+          for (int c = 0; c < D / 32; ++c) {
+            tmem_ld32(lane_base + Cfg::o_col(t) + c * 32, r);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+            tmem_st32(lane_base + Cfg::o_col(t) + c * 32, r);
+          }
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[t]);
+      }
+      if (!ok_run) break;
+      // ----------------------------------------------------------- epilogue --
+      if (!__all_sync(0xffffffffu, mbar_wait(&o_done[t], (ph & 1u) ^ 1u, abort_flag, a.st, 0x1310 + t))) {
+        ok_run = false;
+        break;
+      }
+      tc_fence_after();
+      const float inv_l = 1.f / l;
+      const bool store = qrow < S;
+      uint32_t r[32];
+#pragma unroll 1
+      for (int c = 0; c < D / 32; ++c) {
+        tmem_ld32(lane_base + Cfg::o_col(t) + c * 32, r);
+        tmem_wait_ld();
+        if (c == D / 32 - 1) {
+          // O_t is in registers: the next unit's first PV may overwrite it.
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&o_free[t]);
+        }
+        if (store) {
+          if (a.out_f16) {
+            __half* orow = static_cast<__half*>(a.O) + bh * a.o_head + static_cast<int64_t>(qrow) * a.o_row + c * 32;
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              uint4 wv;
+              wv.x = pack_half2(__uint_as_float(r[8 * v + 0]) * inv_l, __uint_as_float(r[8 * v + 1]) * inv_l);
+              wv.y = pack_half2(__uint_as_float(r[8 * v + 2]) * inv_l, __uint_as_float(r[8 * v + 3]) * inv_l);
+              wv.z = pack_half2(__uint_as_float(r[8 * v + 4]) * inv_l, __uint_as_float(r[8 * v + 5]) * inv_l);
+              wv.w = pack_half2(__uint_as_float(r[8 * v + 6]) * inv_l, __uint_as_float(r[8 * v + 7]) * inv_l);
+              *reinterpret_cast<uint4*>(orow + 8 * v) = wv;
+            }
+          } else {
+            float* orow = static_cast<float*>(a.O) + bh * a.o_head + static_cast<int64_t>(qrow) * a.o_row + c * 32;
+#pragma unroll
+            for (int v = 0; v < 8; ++v) {
+              *reinterpret_cast<float4*>(orow + 4 * v) =
+                  make_float4(__uint_as_float(r[4 * v]) * inv_l, __uint_as_float(r[4 * v + 1]) * inv_l,
+                              __uint_as_float(r[4 * v + 2]) * inv_l, __uint_as_float(r[4 * v + 3]) * inv_l);
+            }
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem, Cfg::kTmemCols);
+  }
+  if (threadIdx.x == 0) {
+    // Thread 0 took this CTA's last ticket above; once every CTA has counted
+    // itself out nobody reads the counter again in this launch.
+    __threadfence();
+    if (atomicAdd(a.unit_counter + 1, 1) == static_cast<int>(gridDim.x) - 1) {
+      atomicExch(a.unit_counter, 0);
+      atomicExch(a.unit_counter + 1, 0);
+    }
+  }
+}
+
 struct FaProblem {
   const void *Q, *K, *V;
   int64_t q_row, q_head, k_row, k_head, v_row, v_head;  // elements
@@ -552,23 +1160,39 @@ struct FaProblem {
   int64_t bias_head, bias_row;
 };
 
+template <class Kernel>
+int run_fa2_kernel(Kernel kern, uint32_t regs_low, dim3 grid, int smem_bytes, const CUtensorMap& tq,
+                   const CUtensorMap& tk, const CUtensorMap& tv, const FaArgs& args, cudaStream_t stream) {
+  cudaFuncAttributes fa{};
+  int rc = kernel_setup(reinterpret_cast<const void*>(kern), smem_bytes, &fa);
+  if (rc != NESO_OK) return rc;
+  if (static_cast<int64_t>(fa.numRegs) * kThreads < 128 * regs_low + 256 * kRegsHigh) {
+    return fail(NESO_ERR_LAUNCH, "fa2: %d registers/thread cannot fund the %u/%u warpgroup split", fa.numRegs,
+                regs_low, kRegsHigh);
+  }
+  kern<<<grid, kThreads, smem_bytes, stream>>>(tq, tk, tv, args);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "fa2 launch");
+  return ok();
+}
+
+// Kernel per head dim, the faster one measured on B200: D = 128 runs the
+// persistent kernel, D = 64 one CTA per work unit.
 template <int D, bool kCausal, int kBias>
 int launch_fa2_t(const FaProblem& p, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                  FaArgs& args, cudaStream_t stream) {
   using Cfg = FaCfg<D>;
-  auto kern = fa2_fwd_kernel<D, kCausal, kBias>;
-  cudaFuncAttributes fa{};
-  int rc = kernel_setup(reinterpret_cast<const void*>(kern), Cfg::kSmemBytes, &fa);
-  if (rc != NESO_OK) return rc;
-  if (static_cast<int64_t>(fa.numRegs) * kThreads < 128 * kRegsLow + 256 * kRegsHigh) {
-    return fail(NESO_ERR_LAUNCH, "fa2: %d registers/thread cannot fund the %u/%u warpgroup split", fa.numRegs,
-                kRegsLow, kRegsHigh);
+  if constexpr (D == 128) {
+    const int units = args.num_qblocks * p.BH;
+    int rc = stream_counters(stream, &args.unit_counter);
+    if (rc != NESO_OK) return rc;
+    return run_fa2_kernel(fa2_persistent_kernel<D, kCausal, kBias>, kRegsLowPersistent,
+                          dim3(units < sm_count() ? units : sm_count(), 1, 1), Cfg::kSmemBytes, tq, tk, tv, args,
+                          stream);
+  } else {
+    return run_fa2_kernel(fa2_tile_kernel<D, kCausal, kBias>, kRegsLow, dim3(args.num_qblocks, p.BH, 1),
+                          Cfg::kSmemBytes, tq, tk, tv, args, stream);
   }
-  dim3 grid(args.num_qblocks, p.BH, 1);
-  kern<<<grid, kThreads, Cfg::kSmemBytes, stream>>>(tq, tk, tv, args);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e, "fa2 launch");
-  return ok();
 }
 
 template <int D>
@@ -626,6 +1250,8 @@ int launch_fa2(const FaProblem& p, cudaStream_t stream) {
   args.bias_head = p.bias_head;
   args.bias_row = p.bias_row;
   args.num_qblocks = (p.S + 255) / 256;
+  args.BH = p.BH;
+  args.unit_counter = nullptr;
   args.out_f16 = p.out_f16 ? 1 : 0;
   rc = device_status(&args.st);
   if (rc != NESO_OK) return rc;

@@ -98,6 +98,29 @@ int stream_workspace(cudaStream_t stream, size_t bytes, void** out) {
   return NESO_OK;
 }
 
+int stream_counters(cudaStream_t stream, int** out) {
+  static std::mutex mu;
+  static std::map<std::pair<int, cudaStream_t>, int*> blocks;
+  int dev = 0;
+  int rc = current_device(&dev);
+  if (rc != NESO_OK) return rc;
+  std::lock_guard<std::mutex> lock(mu);
+  int*& slot = blocks[{dev, stream}];
+  if (slot == nullptr) {
+    int* p = nullptr;
+    cudaError_t e = cudaMalloc(&p, 64 * sizeof(int));
+    if (e != cudaSuccess) return cuda_fail(e, "allocating the work counters");
+    e = cudaMemset(p, 0, 64 * sizeof(int));
+    if (e != cudaSuccess) {
+      cudaFree(p);
+      return cuda_fail(e, "zeroing the work counters");
+    }
+    slot = p;
+  }
+  *out = slot;
+  return NESO_OK;
+}
+
 int kernel_setup(const void* kern, int smem_bytes, cudaFuncAttributes* attrs) {
   static std::mutex mu;
   static std::map<std::pair<int, const void*>, cudaFuncAttributes> cache;
