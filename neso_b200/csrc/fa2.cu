@@ -14,9 +14,16 @@
 // Work unit: one (batch*head, 256 query rows) = two 128-row Q tiles that
 // ping-pong so the tensor core runs one tile's MMAs while the other tile's
 // softmax runs on the CUDA cores. Keys are consumed in 128-key blocks. Two
-// kernels share this design: fa2_tile_kernel runs one unit per CTA (D = 64),
-// fa2_persistent_kernel keeps one CTA per SM and hands units out from a
-// per-launch counter (D = 128); the host picks the faster one per head dim.
+// kernels share this design and the host picks the faster one per head dim
+// (measured on B200):
+//   D = 64   fa2_tile_kernel with one 128-row tile per CTA and two CTAs per
+//            SM (256 TMEM columns, 82 KB of shared memory each): the tiles
+//            of the two CTAs overlap as the ping-pong pair does, and one
+//            CTA's prologue and epilogue run under the other's main loop.
+//   D = 128  fa2_persistent_kernel: one two-tile CTA per SM walks units
+//            handed out from a per-launch counter.
+// The description below is of the two-tile form; the one-tile form drops
+// warps 8-11 and the turn handshake.
 //   warp 0       TMA producer: Q tiles once, then K_j / V_j into KV rings.
 //   warp 1       single-thread tcgen05.mma issuer of S_t = Q_t . K_j^T (SS,
 //                M=128 N=128 K=16 steps, fp32 in TMEM)
@@ -32,6 +39,7 @@
 // TMEM columns: S0 [0,128) S1 [128,256) O0 [256,256+D) O1 [256+D,256+2D);
 //   D = 64: P0/P1 in [384,448)/[448,512); D = 128: P_t aliases the first 64
 //   columns of S_t and the issuer waits for PV_t(j) before QK_t(j+1).
+//   One-tile form (D = 64): S [0,128) O [128,192) P [192,256).
 #include <cmath>
 
 #include "runtime.h"
@@ -39,11 +47,9 @@
 namespace neso {
 namespace {
 
-constexpr int kThreads = 384;
-// Register split: warpgroup 0 (TMA, MMA, TMEM warps) shrinks, the two softmax
-// warpgroups grow. 128 * kRegsLow + 256 * kRegsHigh must not exceed the
-// block's launch pool (384 x registers per thread), checked on the host.
-constexpr uint32_t kRegsLow = 56;
+// Register split: warpgroup 0 (TMA, MMA, TMEM warps) shrinks to
+// FaCfg::kRegsLow, the softmax warpgroups grow to kRegsHigh; the host checks
+// that the split fits the block's launch pool.
 constexpr uint32_t kRegsHigh = 216;
 // The persistent kernel's producer and issuers keep per-unit state across
 // units and get more registers; 128 * 72 + 256 * 216 fills the launch pool.
@@ -55,21 +61,30 @@ constexpr int kUnitReaders = 10;  // QK issuer, PV issuer and the 8 softmax warp
 
 enum BiasMode : int { kBiasNone = 0, kBiasTable = 1, kBiasDense = 2 };
 
-template <int D>
+// kT = Q tiles per CTA: 2 (ping-pong pair, one CTA per SM) or 1 (two CTAs
+// per SM, each with half the TMEM and shared memory).
+template <int D, int kT = 2>
 struct FaCfg {
+  static constexpr int kThreads = 128 * (1 + kT);
+  static constexpr int kMinBlocks = kT == 1 ? 2 : 1;
   static constexpr int kChunks = D / 64;           // 128-byte TMA boxes per row
   static constexpr int kTileBytes = 128 * D * 2;   // one Q, K or V tile
-  static constexpr int kStages = (D == 64) ? 3 : 2;
+  static constexpr int kStages = (D == 64 && kT == 2) ? 3 : 2;
   static constexpr int kQBuffers = 1;  // persistent kernel: Q tiles per unit in flight
   static constexpr bool kAliasP = (D > 64);
+  // Warpgroup 0 register budget; 128 * kRegsLow + 128 * kT * kRegsHigh must
+  // fit the launch pool (kThreads x registers per thread).
+  static constexpr uint32_t kRegsLow = kT == 1 ? 40 : 56;
   __host__ __device__ static constexpr uint32_t s_col(int t) { return t ? 128u : 0u; }
-  __host__ __device__ static constexpr uint32_t o_col(int t) { return t ? 256u + D : 256u; }
+  __host__ __device__ static constexpr uint32_t o_col(int t) {
+    return kT == 1 ? 128u : (t ? 256u + D : 256u);
+  }
   __host__ __device__ static constexpr uint32_t p_col(int t) {
-    return kAliasP ? s_col(t) : (t ? 256u + 2 * D + 64 : 256u + 2 * D);
+    return kAliasP ? s_col(t) : (kT == 1 ? 128u + D : (t ? 256u + 2 * D + 64 : 256u + 2 * D));
   }
   static constexpr uint32_t kPHalfStride = 32u;  // P columns are contiguous (64 per tile)
-  static constexpr int kTmemCols = 512;
-  static constexpr int kSmemBytes = (2 * kQBuffers + 2 * kStages) * kTileBytes + 1024 + 512;
+  static constexpr int kTmemCols = kT == 1 ? 256 : 512;
+  static constexpr int kSmemBytes = (kT * kQBuffers + 2 * kStages) * kTileBytes + 1024 + 512;
 };
 
 struct FaArgs {
@@ -92,16 +107,16 @@ struct FaArgs {
   DevStatus st;
 };
 
-template <int D, bool kCausal, int kBias>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int D, int kT, bool kCausal, int kBias>
+__global__ void __launch_bounds__(FaCfg<D, kT>::kThreads, FaCfg<D, kT>::kMinBlocks)
     fa2_tile_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                   const __grid_constant__ CUtensorMap tmV, FaArgs a) {
-  using Cfg = FaCfg<D>;
+                    const __grid_constant__ CUtensorMap tmV, FaArgs a) {
+  using Cfg = FaCfg<D, kT>;
   constexpr int KS = Cfg::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;                                // 2 tiles
-  uint8_t* sK = smem + 2 * Cfg::kTileBytes;          // KS tiles
+  uint8_t* sQ = smem;                                // kT tiles
+  uint8_t* sK = smem + kT * Cfg::kTileBytes;         // KS tiles
   uint8_t* sV = sK + KS * Cfg::kTileBytes;           // KS tiles
   uint64_t* bars = reinterpret_cast<uint64_t*>(sV + KS * Cfg::kTileBytes);
   uint64_t* q_full = bars;
@@ -124,11 +139,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int S = a.S;
   const int qb = kCausal ? (a.num_qblocks - 1 - static_cast<int>(blockIdx.x)) : static_cast<int>(blockIdx.x);
   const int bh = blockIdx.y;
-  const int q0 = qb * 256;
+  const int q0 = qb * 128 * kT;
   const int nkv = (S + 127) / 128;
   // KV blocks each Q tile visits (0 for a tile that starts past S)
   const int ntile0 = kCausal ? min(nkv, q0 / 128 + 1) : nkv;
-  const int ntile1 = (q0 + 128 >= S) ? 0 : (kCausal ? min(nkv, q0 / 128 + 2) : nkv);
+  const int ntile1 = (kT == 1 || q0 + 128 >= S) ? 0 : (kCausal ? min(nkv, q0 / 128 + 2) : nkv);
   const int nmax = max(ntile0, ntile1);
 
   if (threadIdx.x == 0) {
@@ -165,7 +180,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = *tmem_slot;
   if (warp < 4) {
     // Warpgroup 0: TMA producer, MMA issuer, TMEM allocator.
-    setmaxnreg_dec<kRegsLow>();
+    setmaxnreg_dec<Cfg::kRegsLow>();
     if (warp == 0 && lane == 0) {
       // ------------------------------------------------------------ producer --
       const uint32_t qbytes = (ntile1 > 0 ? 2 : 1) * Cfg::kTileBytes;
@@ -427,7 +442,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Tile 0 block j waits for tile 1's block j-1 (when tile 1 exists);
       // tile 1 block j waits for tile 0's block j (an existing tile 1 never
       // has fewer blocks than tile 0).
-      const bool wait_turn = (t == 0) ? (j > 0 && ntile1 > 0) : (j < ntile0);
+      const bool wait_turn = kT == 2 && ((t == 0) ? (j > 0 && ntile1 > 0) : (j < ntile0));
       if (wait_turn) {
         const uint32_t par = (t == 0) ? ((j - 1) & 1) : (j & 1);
         if (!__all_sync(0xffffffffu, mbar_wait(&turn[t * 4 + q], par, abort_flag, a.st, 0x1340 + t))) {
@@ -471,8 +486,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const float sum = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
       // Hand the exp unit to the partner warp of the other tile.
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&turn[(1 - t) * 4 + q]);
+      if (kT == 2) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&turn[(1 - t) * 4 + q]);
+      }
       if (!Cfg::kAliasP && j > 0) {
         // P_t and O_t are still in use by PV_t(j-1) until it completes.
         if (!__all_sync(0xffffffffu, mbar_wait(&o_done[t], (j - 1) & 1, abort_flag, a.st, 0x1320 + t))) {
@@ -584,7 +601,7 @@ __device__ __noinline__ int fetch_unit(uint64_t* full, uint64_t* empty, volatile
 // overwrite O_t only after the epilogue has read it, and the exp-unit turn
 // handshake continues across unit boundaries.
 template <int D, bool kCausal, int kBias>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(FaCfg<D>::kThreads, 1)
     fa2_persistent_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                           const __grid_constant__ CUtensorMap tmV, FaArgs a) {
   using Cfg = FaCfg<D>;
@@ -1161,16 +1178,16 @@ struct FaProblem {
 };
 
 template <class Kernel>
-int run_fa2_kernel(Kernel kern, uint32_t regs_low, dim3 grid, int smem_bytes, const CUtensorMap& tq,
+int run_fa2_kernel(Kernel kern, int threads, uint32_t regs_low, dim3 grid, int smem_bytes, const CUtensorMap& tq,
                    const CUtensorMap& tk, const CUtensorMap& tv, const FaArgs& args, cudaStream_t stream) {
   cudaFuncAttributes fa{};
   int rc = kernel_setup(reinterpret_cast<const void*>(kern), smem_bytes, &fa);
   if (rc != NESO_OK) return rc;
-  if (static_cast<int64_t>(fa.numRegs) * kThreads < 128 * regs_low + 256 * kRegsHigh) {
+  if (static_cast<int64_t>(fa.numRegs) * threads < 128 * regs_low + (threads - 128) * kRegsHigh) {
     return fail(NESO_ERR_LAUNCH, "fa2: %d registers/thread cannot fund the %u/%u warpgroup split", fa.numRegs,
                 regs_low, kRegsHigh);
   }
-  kern<<<grid, kThreads, smem_bytes, stream>>>(tq, tk, tv, args);
+  kern<<<grid, threads, smem_bytes, stream>>>(tq, tk, tv, args);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "fa2 launch");
   return ok();
@@ -1186,12 +1203,15 @@ int launch_fa2_t(const FaProblem& p, const CUtensorMap& tq, const CUtensorMap& t
     const int units = args.num_qblocks * p.BH;
     int rc = stream_counters(stream, &args.unit_counter);
     if (rc != NESO_OK) return rc;
-    return run_fa2_kernel(fa2_persistent_kernel<D, kCausal, kBias>, kRegsLowPersistent,
+    return run_fa2_kernel(fa2_persistent_kernel<D, kCausal, kBias>, Cfg::kThreads, kRegsLowPersistent,
                           dim3(units < sm_count() ? units : sm_count(), 1, 1), Cfg::kSmemBytes, tq, tk, tv, args,
                           stream);
   } else {
-    return run_fa2_kernel(fa2_tile_kernel<D, kCausal, kBias>, kRegsLow, dim3(args.num_qblocks, p.BH, 1),
-                          Cfg::kSmemBytes, tq, tk, tv, args, stream);
+    // 128-row units, two CTAs per SM.
+    using Cfg1 = FaCfg<D, 1>;
+    args.num_qblocks = (p.S + 127) / 128;
+    return run_fa2_kernel(fa2_tile_kernel<D, 1, kCausal, kBias>, Cfg1::kThreads, Cfg1::kRegsLow,
+                          dim3(args.num_qblocks, p.BH, 1), Cfg1::kSmemBytes, tq, tk, tv, args, stream);
   }
 }
 
