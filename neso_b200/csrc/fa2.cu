@@ -405,22 +405,14 @@ __global__ void __launch_bounds__(FaCfg<D, kT>::kThreads, FaCfg<D, kT>::kMinBloc
           if (key >= S || (kCausal && key > qrow)) z[col] = -INFINITY;
         }
       }
-      // Row max, 8 independent chains (D = 128: 3-input max). The variant
-      // per head dim is the faster one measured on B200.
+      // Row max, 8 independent chains of 3-input max.
       float pm[8];
-      if constexpr (D == 128) {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) pm[i] = fmaxf(z[i], z[8 + i]);
+      for (int i = 0; i < 8; ++i) pm[i] = fmaxf(z[i], z[8 + i]);
 #pragma unroll
-        for (int c = 16; c < 128; c += 16) {
+      for (int c = 16; c < 128; c += 16) {
 #pragma unroll
-          for (int i = 0; i < 8; ++i) pm[i] = fmax3(pm[i], z[c + i], z[c + 8 + i]);
-        }
-      } else {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) pm[i] = z[i];
-#pragma unroll
-        for (int col = 8; col < 128; ++col) pm[col & 7] = fmaxf(pm[col & 7], z[col]);
+        for (int i = 0; i < 8; ++i) pm[i] = fmax3(pm[i], z[c + i], z[c + 8 + i]);
       }
       float rmax = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])),
                          fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7])));
@@ -451,38 +443,25 @@ __global__ void __launch_bounds__(FaCfg<D, kT>::kThreads, FaCfg<D, kT>::kMinBloc
         }
       }
       // p = 2^(z * zc - m), one ex2 per element, fp32 row sums in 8
-      // partials. D = 128 forms the exponent arguments and the sums two
+      // partials; the exponent arguments and the sums are formed two
       // lanes per instruction (packed fp32 FMA / add).
       float ps[8];
       uint32_t pk[64];
-      if constexpr (D == 128) {
-        const uint64_t zc2 = f2_pack(zc, zc);
-        const uint64_t nm2 = f2_pack(neg_m, neg_m);
-        uint64_t acc2[4] = {0ull, 0ull, 0ull, 0ull};
+      const uint64_t zc2 = f2_pack(zc, zc);
+      const uint64_t nm2 = f2_pack(neg_m, neg_m);
+      uint64_t acc2[4] = {0ull, 0ull, 0ull, 0ull};
 #pragma unroll
-        for (int i = 0; i < 64; ++i) {
-          const uint64_t x2 = ffma2(f2_pack(z[2 * i], z[2 * i + 1]), zc2, nm2);
-          const float p0 = ex2_approx(f2_lo(x2));
-          const float p1 = ex2_approx(f2_hi(x2));
-          acc2[i & 3] = fadd2(acc2[i & 3], f2_pack(p0, p1));
-          pk[i] = pack_half2(p0, p1);
-        }
+      for (int i = 0; i < 64; ++i) {
+        const uint64_t x2 = ffma2(f2_pack(z[2 * i], z[2 * i + 1]), zc2, nm2);
+        const float p0 = ex2_approx(f2_lo(x2));
+        const float p1 = ex2_approx(f2_hi(x2));
+        acc2[i & 3] = fadd2(acc2[i & 3], f2_pack(p0, p1));
+        pk[i] = pack_half2(p0, p1);
+      }
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          ps[2 * i] = f2_lo(acc2[i]);
-          ps[2 * i + 1] = f2_hi(acc2[i]);
-        }
-      } else {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) ps[i] = 0.f;
-#pragma unroll
-        for (int i = 0; i < 64; ++i) {
-          const float p0 = ex2_approx(fmaf(z[2 * i], zc, neg_m));
-          const float p1 = ex2_approx(fmaf(z[2 * i + 1], zc, neg_m));
-          ps[(2 * i) & 7] += p0;
-          ps[(2 * i + 1) & 7] += p1;
-          pk[i] = pack_half2(p0, p1);
-        }
+      for (int i = 0; i < 4; ++i) {
+        ps[2 * i] = f2_lo(acc2[i]);
+        ps[2 * i + 1] = f2_hi(acc2[i]);
       }
       const float sum = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
       // Hand the exp unit to the partner warp of the other tile.
@@ -977,22 +956,14 @@ __global__ void __launch_bounds__(FaCfg<D>::kThreads, 1)
             if (key >= S || (kCausal && key > qrow)) z[col] = -INFINITY;
           }
         }
-        // Row max, 8 independent chains (D = 128: 3-input max). The variant
-        // per head dim is the faster one measured on B200.
+        // Row max, 8 independent chains of 3-input max.
         float pm[8];
-        if constexpr (D == 128) {
 #pragma unroll
-          for (int i = 0; i < 8; ++i) pm[i] = fmaxf(z[i], z[8 + i]);
+        for (int i = 0; i < 8; ++i) pm[i] = fmaxf(z[i], z[8 + i]);
 #pragma unroll
-          for (int c = 16; c < 128; c += 16) {
+        for (int c = 16; c < 128; c += 16) {
 #pragma unroll
-            for (int i = 0; i < 8; ++i) pm[i] = fmax3(pm[i], z[c + i], z[c + 8 + i]);
-          }
-        } else {
-#pragma unroll
-          for (int i = 0; i < 8; ++i) pm[i] = z[i];
-#pragma unroll
-          for (int col = 8; col < 128; ++col) pm[col & 7] = fmaxf(pm[col & 7], z[col]);
+          for (int i = 0; i < 8; ++i) pm[i] = fmax3(pm[i], z[c + i], z[c + 8 + i]);
         }
         float rmax = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])),
                            fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7])));
@@ -1024,38 +995,25 @@ __global__ void __launch_bounds__(FaCfg<D>::kThreads, 1)
           ph ^= 2u;
         }
         // p = 2^(z * zc - m), one ex2 per element, fp32 row sums in 8
-        // partials. D = 128 forms the exponent arguments and the sums two
+        // partials; the exponent arguments and the sums are formed two
         // lanes per instruction (packed fp32 FMA / add).
         float ps[8];
         uint32_t pk[64];
-        if constexpr (D == 128) {
-          const uint64_t zc2 = f2_pack(zc, zc);
-          const uint64_t nm2 = f2_pack(neg_m, neg_m);
-          uint64_t acc2[4] = {0ull, 0ull, 0ull, 0ull};
+        const uint64_t zc2 = f2_pack(zc, zc);
+        const uint64_t nm2 = f2_pack(neg_m, neg_m);
+        uint64_t acc2[4] = {0ull, 0ull, 0ull, 0ull};
 #pragma unroll
-          for (int i = 0; i < 64; ++i) {
-            const uint64_t x2 = ffma2(f2_pack(z[2 * i], z[2 * i + 1]), zc2, nm2);
-            const float p0 = ex2_approx(f2_lo(x2));
-            const float p1 = ex2_approx(f2_hi(x2));
-            acc2[i & 3] = fadd2(acc2[i & 3], f2_pack(p0, p1));
-            pk[i] = pack_half2(p0, p1);
-          }
+        for (int i = 0; i < 64; ++i) {
+          const uint64_t x2 = ffma2(f2_pack(z[2 * i], z[2 * i + 1]), zc2, nm2);
+          const float p0 = ex2_approx(f2_lo(x2));
+          const float p1 = ex2_approx(f2_hi(x2));
+          acc2[i & 3] = fadd2(acc2[i & 3], f2_pack(p0, p1));
+          pk[i] = pack_half2(p0, p1);
+        }
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            ps[2 * i] = f2_lo(acc2[i]);
-            ps[2 * i + 1] = f2_hi(acc2[i]);
-          }
-        } else {
-#pragma unroll
-          for (int i = 0; i < 8; ++i) ps[i] = 0.f;
-#pragma unroll
-          for (int i = 0; i < 64; ++i) {
-            const float p0 = ex2_approx(fmaf(z[2 * i], zc, neg_m));
-            const float p1 = ex2_approx(fmaf(z[2 * i + 1], zc, neg_m));
-            ps[(2 * i) & 7] += p0;
-            ps[(2 * i + 1) & 7] += p1;
-            pk[i] = pack_half2(p0, p1);
-          }
+        for (int i = 0; i < 4; ++i) {
+          ps[2 * i] = f2_lo(acc2[i]);
+          ps[2 * i + 1] = f2_hi(acc2[i]);
         }
         const float sum = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
         // Hand the exp unit to the partner warp when its loop comes next.
