@@ -280,7 +280,7 @@ def main() -> None:
     roofline = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                 "frac": achieved / peak, "traffic": traffic,
                 "peak_source": f"{peak_src} bf16_tflops (burst, kernel timed alone)",
-                "kernel": "fa2_fwd_kernel<64,false,0>"}
+                "kernel": "fa2_tile_kernel<64,1,false,0>"}
 
     # Verification after timing: NCCL all-gather of each rank's first head to rank 0.
     verified = None
