@@ -562,6 +562,286 @@ int launch_wq(const QProblem& p, cudaStream_t stream) {
   return ok();
 }
 
+// ------------------------------------------------------- small-M GEMV path --
+// For M <= 4 (int8) or M <= 2 (int4) the tensor-core path spends its time in
+// the hand-offs between the weight ring, the dequant warps and the MMAs; the
+// work per weight byte is a handful of multiply-adds. This path reads W
+// straight from HBM with 16-byte streaming loads (lane = 16 channels of one
+// stored row: one k for int8, two k for packed int4), converts in registers
+// and accumulates M dot products per channel in fp32. A CTA covers 512
+// channels x one slice of K; its 8 warps split the slice and reduce through
+// shared memory; the last CTA of a channel block to finish adds the slices in
+// a fixed order (deterministic) and writes Y.
+//   int8: fp32(b) = float_bits(0x4B000000 | (b ^ 0x80)) - (2^23 + 128), exact;
+//         the per-channel scale multiplies the final sum (as the reference's
+//         scaled kernel applies it in the epilogue, tests/test_quantized_matmul.py:250-260).
+//   int4: the same on nibbles (q + 8, minus 2^23 + 8); a K slice is one
+//         128-wide group, so its sum is multiplied by that group's scale once
+//         before the slices are added.
+constexpr int kGvThreads = 256;
+constexpr int kGvWarps = kGvThreads / 32;
+constexpr int kGvChanPerLane = 16;
+constexpr int kGvChannels = 32 * kGvChanPerLane;  // 512 per CTA
+constexpr int kGvSmemBytes = kGvWarps * kGvChannels * 4;
+
+struct GvArgs {
+  const __half* X;
+  int64_t ldx;
+  const uint8_t* W;
+  int64_t ldw;          // bytes per stored row (int8: per k; int4: per pair of k)
+  const __half* scale;  // int8: [N] per channel (nullable); int4: [K/128][lds]
+  int64_t lds;
+  float* Y;
+  int64_t ldy;
+  float* partial;  // [slices][M][N] when there is more than one slice
+  int* counters;   // one per channel block, zero between launches
+  int M, N;
+  int rows;            // stored rows (int8: K, int4: K / 2)
+  int rows_per_slice;  // stored rows per CTA (int4: 64 = one group)
+};
+
+// 4 bytes (b ^ 0x80 for int8, q + 8 for int4 nibbles) -> 4 exact fp32 values
+// offset by `bias` (2^23 + 128 or 2^23 + 8).
+__device__ __forceinline__ void bytes_to_f32(uint32_t t, float bias, float* f) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) f[j] = __int_as_float(__byte_perm(t, 0x4B000000u, 0x7440u + j)) - bias;
+}
+
+template <int kQ, int kM>
+__global__ void __launch_bounds__(kGvThreads) wq_gemv_kernel(GvArgs a) {
+  constexpr int CPL = kGvChanPerLane;
+  constexpr int U = 4;  // stored rows per batch; two batches in flight per lane
+  constexpr int KPR = kQ == kInt8 ? 1 : 2;  // k per stored row
+  extern __shared__ float gsm[];  // [kGvWarps][kGvChannels], and first the slice of X as fp32
+  __shared__ int is_last;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int cb = blockIdx.x;
+  const int sl = blockIdx.y;
+  const int slices = gridDim.y;
+  const int n0 = cb * kGvChannels + lane * CPL;
+  const bool active = n0 < a.N;  // the host guarantees N % 16 == 0
+  const int r0 = sl * a.rows_per_slice;
+  const int r1 = min(r0 + a.rows_per_slice, a.rows);
+  const int per_warp = (r1 - r0 + kGvWarps - 1) / kGvWarps;
+  const int wr0 = r0 + warp * per_warp;
+  const int wr1 = min(wr0 + per_warp, r1);
+
+  // The slice of X (k in [KPR r0, KPR r1)) as fp32 in shared memory.
+  float* xs = gsm;  // [kM][KPR * rows_per_slice]
+  const int kspan = KPR * a.rows_per_slice;
+  for (int i = threadIdx.x; i < kM * kspan; i += kGvThreads) {
+    const int m = i / kspan, k = KPR * r0 + (i % kspan);
+    xs[i] = (m < a.M && k < KPR * r1) ? __half2float(a.X[static_cast<int64_t>(m) * a.ldx + k]) : 0.f;
+  }
+  __syncthreads();
+
+  float acc[kM][CPL];
+#pragma unroll
+  for (int m = 0; m < kM; ++m)
+#pragma unroll
+    for (int i = 0; i < CPL; ++i) acc[m][i] = 0.f;
+
+  if (active) {
+    const uint8_t* wp = a.W + n0;
+    auto load = [&](uint4* dst, int r) {
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        dst[u] = (r + u < wr1) ? __ldcs(reinterpret_cast<const uint4*>(wp + static_cast<int64_t>(r + u) * a.ldw))
+                               : make_uint4(0u, 0u, 0u, 0u);
+      }
+    };
+    uint4 cur[U], nxt[U];
+    load(cur, wr0);
+    for (int r = wr0; r < wr1; r += U) {
+      if (r + U < wr1) load(nxt, r + U);  // next batch in flight while this one is used
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int kl = KPR * (r + u - r0);  // k index within the slice
+        const uint32_t words[4] = {cur[u].x, cur[u].y, cur[u].z, cur[u].w};
+        if (kQ == kInt8) {
+          float xv[kM];
+#pragma unroll
+          for (int m = 0; m < kM; ++m) xv[m] = (r + u < wr1) ? xs[m * kspan + kl] : 0.f;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            float f[4];
+            bytes_to_f32(words[q] ^ 0x80808080u, 8388736.f, f);
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+#pragma unroll
+              for (int m = 0; m < kM; ++m) acc[m][4 * q + j] = fmaf(xv[m], f[j], acc[m][4 * q + j]);
+          }
+        } else {
+          // stored row r holds k = 2r (low nibbles) and k = 2r + 1 (high nibbles)
+          float x0[kM], x1[kM];
+#pragma unroll
+          for (int m = 0; m < kM; ++m) {
+            x0[m] = (r + u < wr1) ? xs[m * kspan + kl] : 0.f;
+            x1[m] = (r + u < wr1) ? xs[m * kspan + kl + 1] : 0.f;
+          }
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            float lo[4], hi[4];
+            bytes_to_f32((words[q] & 0x0F0F0F0Fu) ^ 0x08080808u, 8388616.f, lo);
+            bytes_to_f32(((words[q] >> 4) & 0x0F0F0F0Fu) ^ 0x08080808u, 8388616.f, hi);
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+#pragma unroll
+              for (int m = 0; m < kM; ++m)
+                acc[m][4 * q + j] = fmaf(x1[m], hi[j], fmaf(x0[m], lo[j], acc[m][4 * q + j]));
+          }
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) cur[u] = nxt[u];
+    }
+    if (kQ == kInt4G128 && wr0 < wr1) {
+      // A warp's rows lie in one 128-wide group (64 stored rows): scale its sums.
+      const __half* sg = a.scale + static_cast<int64_t>(wr0 / 64) * a.lds + n0;
+      const uint4 s0 = *reinterpret_cast<const uint4*>(sg);
+      const uint4 s1 = *reinterpret_cast<const uint4*>(sg + 8);
+      const __half* sh0 = reinterpret_cast<const __half*>(&s0);
+      const __half* sh1 = reinterpret_cast<const __half*>(&s1);
+#pragma unroll
+      for (int i = 0; i < CPL; ++i) {
+        const float sc = __half2float(i < 8 ? sh0[i] : sh1[i - 8]);
+#pragma unroll
+        for (int m = 0; m < kM; ++m) acc[m][i] *= sc;
+      }
+    }
+  }
+  __syncthreads();  // X slice no longer needed: the reduction reuses the buffer
+
+  // CTA reduction over the 8 warps, one output row m at a time; the slice's
+  // sums go to Y (single slice) or to partial[sl].
+  const bool single = slices == 1;
+  for (int m = 0; m < a.M && m < kM; ++m) {
+#pragma unroll
+    for (int i = 0; i < CPL; ++i) gsm[warp * kGvChannels + lane * CPL + i] = acc[m][i];
+    __syncthreads();
+    for (int c = threadIdx.x; c < kGvChannels; c += kGvThreads) {
+      const int n = cb * kGvChannels + c;
+      if (n < a.N) {
+        float s = 0.f;
+#pragma unroll
+        for (int w = 0; w < kGvWarps; ++w) s += gsm[w * kGvChannels + c];
+        if (single) {
+          if (kQ == kInt8 && a.scale != nullptr) s *= __half2float(a.scale[n]);
+          a.Y[static_cast<int64_t>(m) * a.ldy + n] = s;
+        } else {
+          a.partial[(static_cast<int64_t>(sl) * a.M + m) * a.N + n] = s;
+        }
+      }
+    }
+    __syncthreads();
+  }
+  if (single) return;
+
+  // The last CTA of this channel block adds the slices in order.
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) is_last = atomicAdd(&a.counters[cb], 1) == slices - 1;
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+  for (int o = threadIdx.x; o < a.M * kGvChannels; o += kGvThreads) {
+    const int m = o / kGvChannels;
+    const int n = cb * kGvChannels + (o % kGvChannels);
+    if (n >= a.N) continue;
+    // Eight slices' loads in flight at a time; the sum order is fixed:
+    // ((s0 + s8 + ...) + (s1 + s9 + ...)) + ... over the eight lanes of v.
+    const float* src = a.partial + static_cast<int64_t>(m) * a.N + n;
+    const int64_t step = static_cast<int64_t>(a.M) * a.N;
+    float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int k = 0; k < slices; k += 8) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        if (k + i < slices) v[i] += __ldcg(src + (k + i) * step);
+      }
+    }
+    float s = ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
+    if (kQ == kInt8 && a.scale != nullptr) s *= __half2float(a.scale[n]);
+    a.Y[static_cast<int64_t>(m) * a.ldy + n] = s;
+  }
+  if (threadIdx.x == 0) a.counters[cb] = 0;  // ready for the next launch on this stream
+}
+
+template <int kQ, int kM>
+int launch_gemv(const QProblem& p, cudaStream_t stream) {
+  GvArgs a{};
+  a.X = static_cast<const __half*>(p.X);
+  a.ldx = p.ldx;
+  a.W = static_cast<const uint8_t*>(p.W);
+  a.ldw = p.ldw;
+  a.scale = static_cast<const __half*>(p.scale);
+  a.lds = p.lds;
+  a.Y = p.Y;
+  a.ldy = p.ldy;
+  a.M = p.M;
+  a.N = p.N;
+  a.rows = kQ == kInt8 ? p.K : p.K / 2;
+  auto kern = wq_gemv_kernel<kQ, kM>;
+  int rc = kernel_setup(reinterpret_cast<const void*>(kern), kGvSmemBytes, nullptr);
+  if (rc != NESO_OK) return rc;
+  // One wave: as many (channel block, K slice) CTAs as fit on the GPU at once.
+  int per_sm = 0;
+  cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kGvThreads, kGvSmemBytes);
+  if (e != cudaSuccess) return cuda_fail(e, "occupancy query");
+  const int resident = std::max(1, per_sm) * sm_count();
+  const int nblk = (p.N + kGvChannels - 1) / kGvChannels;
+  const int want = std::max(1, resident / nblk);
+  int slices;
+  if (kQ == kInt4G128) {
+    // 1, 2, 4 or 8 groups (64 stored rows each) per slice, so that each
+    // warp's rows stay inside one group.
+    const int groups = p.K / 128;
+    int g = 1;
+    while (g < 8 && nblk * ((groups + g - 1) / g) > resident) g *= 2;
+    a.rows_per_slice = 64 * g;
+    slices = (groups + g - 1) / g;
+  } else {
+    int rps = (a.rows + want - 1) / want;
+    rps = std::max(64, (rps + 7) / 8 * 8);
+    a.rows_per_slice = rps;
+    slices = (a.rows + rps - 1) / rps;
+  }
+  if (slices > 65535) return fail(NESO_ERR_UNSUPPORTED, "K too large for the small-M path");
+  if (slices > 1) {
+    void* ws = nullptr;
+    rc = stream_workspace(stream, static_cast<size_t>(slices) * p.M * p.N * sizeof(float), &ws);
+    if (rc != NESO_OK) return rc;
+    a.partial = static_cast<float*>(ws);
+    int* ctr = nullptr;
+    rc = stream_counters(stream, &ctr);
+    if (rc != NESO_OK) return rc;
+    a.counters = ctr + kGemvCounterBase;
+  }
+  kern<<<dim3(nblk, slices, 1), kGvThreads, kGvSmemBytes, stream>>>(a);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "small-M GEMV launch");
+  return ok();
+}
+
+// The small-M path applies when M is small, rows are 16-byte aligned and the
+// channel blocks fit the per-stream counter slots.
+bool gemv_eligible(const QProblem& p) {
+  const int max_m = p.kind == kInt8 ? 4 : 2;
+  const int nblk = (p.N + kGvChannels - 1) / kGvChannels;
+  return p.M <= max_m && p.N % 16 == 0 && p.ldw % 16 == 0 && (reinterpret_cast<uintptr_t>(p.W) & 15u) == 0 &&
+         nblk <= kStreamCounters - kGemvCounterBase;
+}
+
+int run_gemv(const QProblem& p, cudaStream_t stream) {
+  if (p.kind == kInt8) {
+    if (p.M == 1) return launch_gemv<kInt8, 1>(p, stream);
+    if (p.M == 2) return launch_gemv<kInt8, 2>(p, stream);
+    return launch_gemv<kInt8, 4>(p, stream);
+  }
+  if (p.M == 1) return launch_gemv<kInt4G128, 1>(p, stream);
+  return launch_gemv<kInt4G128, 2>(p, stream);
+}
+
 template <int kQ>
 int dispatch_wq(const QProblem& p, cudaStream_t stream) {
   if (p.M <= 16) return launch_wq<kQ, true, 16>(p, stream);
@@ -601,6 +881,7 @@ int run_wq(const QProblem& p, cudaStream_t stream) {
       return fail(NESO_ERR_MISALIGNED, "scale row stride must be >= N, multiple of 8");
     }
   }
+  if (gemv_eligible(p)) return run_gemv(p, stream);
   QProblem q = p;
   int rc = device_status(&q.st);
   if (rc != NESO_OK) return rc;

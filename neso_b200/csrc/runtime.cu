@@ -108,9 +108,9 @@ int stream_counters(cudaStream_t stream, int** out) {
   int*& slot = blocks[{dev, stream}];
   if (slot == nullptr) {
     int* p = nullptr;
-    cudaError_t e = cudaMalloc(&p, 64 * sizeof(int));
+    cudaError_t e = cudaMalloc(&p, kStreamCounters * sizeof(int));
     if (e != cudaSuccess) return cuda_fail(e, "allocating the work counters");
-    e = cudaMemset(p, 0, 64 * sizeof(int));
+    e = cudaMemset(p, 0, kStreamCounters * sizeof(int));
     if (e != cudaSuccess) {
       cudaFree(p);
       return cuda_fail(e, "zeroing the work counters");

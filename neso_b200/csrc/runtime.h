@@ -33,9 +33,13 @@ int device_status(DevStatus* out);
 // per device and stream, grown on demand; growing synchronises the stream
 // first). Stays allocated until the process exits.
 int stream_workspace(cudaStream_t stream, size_t bytes, void** out);
-// 64 zero-initialised ints for kernels queued on `stream` that hand out work
-// through atomic counters (one block per device and stream, allocated and
-// zeroed on first use). A kernel that uses them leaves them zero on exit.
+// kStreamCounters zero-initialised ints for kernels queued on `stream` that
+// hand out or count work through atomics (one block per device and stream,
+// allocated and zeroed on first use). A kernel that uses them leaves them
+// zero on exit. Slots: [0, 2) the FA2 persistent kernel's unit tickets,
+// [kGemvCounterBase, kStreamCounters) the small-M GEMV's channel blocks.
+constexpr int kStreamCounters = 1024;
+constexpr int kGemvCounterBase = 64;
 int stream_counters(cudaStream_t stream, int** out);
 
 // Opt a kernel into `smem_bytes` of dynamic shared memory and return its
