@@ -59,6 +59,9 @@ def load_peaks() -> tuple[dict, str]:
     return dict(FALLBACK_PEAKS), "fallback"
 
 
+_JSON_OUT = sys.stdout  # replaced in main() by a duplicate of the original stdout
+
+
 def load_traffic(kernel_key: str):
     p = ROOT / "profiles" / "traffic.json"
     if not p.exists():
@@ -192,7 +195,7 @@ def run_reference(args, rank: int) -> None:
         "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "gpu_launches": 0,
     }
-    print(json.dumps(line), flush=True)
+    print(json.dumps(line), file=_JSON_OUT, flush=True)
 
 
 def time_steps(fn, steps: int, stream, dist_on: bool) -> float:
@@ -232,8 +235,13 @@ def main() -> None:
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
-    # One JSON line on stdout: keep NCCL's informational banner off it unless
-    # the caller asked for NCCL logging.
+    # One JSON line on stdout: everything else any library writes to file
+    # descriptor 1 (NCCL's version banner, for instance, which the
+    # environment may ask for) is sent to stderr instead.
+    global _JSON_OUT
+    _JSON_OUT = os.fdopen(os.dup(1), "w")
+    sys.stdout.flush()
+    os.dup2(2, 1)
     os.environ.setdefault("NCCL_DEBUG", "WARN")
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -350,7 +358,7 @@ def main() -> None:
             "clocks": clocks, "verified": verified,
         }
         line.update(extras)
-        print(json.dumps(line), flush=True)
+        print(json.dumps(line), file=_JSON_OUT, flush=True)
     if dist_on:
         dist.barrier()
         dist.destroy_process_group()
