@@ -569,20 +569,26 @@ int launch_wq(const QProblem& p, cudaStream_t stream) {
 // straight from HBM with 16-byte streaming loads (lane = 16 channels of one
 // stored row: one k for int8, two k for packed int4), converts in registers
 // and accumulates M dot products per channel in fp32. A CTA covers 512
-// channels x one slice of K; its 8 warps split the slice and reduce through
-// shared memory; the last CTA of a channel block to finish adds the slices in
-// a fixed order (deterministic) and writes Y.
+// channels x one slice of K (one CTA per SM, one wave); its warps split the
+// slice and reduce through shared memory; the last CTA of a channel block to
+// finish adds the slices in a fixed order (deterministic) and writes Y.
 //   int8: fp32(b) = float_bits(0x4B000000 | (b ^ 0x80)) - (2^23 + 128), exact;
 //         the per-channel scale multiplies the final sum (as the reference's
 //         scaled kernel applies it in the epilogue, tests/test_quantized_matmul.py:250-260).
-//   int4: the same on nibbles (q + 8, minus 2^23 + 8); a K slice is one
-//         128-wide group, so its sum is multiplied by that group's scale once
-//         before the slices are added.
-constexpr int kGvThreads = 256;
-constexpr int kGvWarps = kGvThreads / 32;
+//   int4: the same on nibbles (q + 8, minus 2^23 + 8); each warp multiplies
+//         a 128-wide group's sums by the group's scale when the group ends.
 constexpr int kGvChanPerLane = 16;
 constexpr int kGvChannels = 32 * kGvChanPerLane;  // 512 per CTA
-constexpr int kGvSmemBytes = kGvWarps * kGvChannels * 4;
+constexpr int kGvWarpStride = 32 * 17;            // reduction row per warp, padded (bank-conflict free)
+
+template <int kQ, int kM>
+struct GvCfg {
+  // One CTA per SM: 32 warps for int8 M = 1 (64 registers per thread suffice),
+  // else 16 warps with up to 128 registers per thread.
+  static constexpr int kThreads = (kQ == kInt8 && kM == 1) ? 1024 : 512;
+  static constexpr int kWarps = kThreads / 32;
+  static constexpr int kSmemBytes = kWarps * kGvWarpStride * 4;
+};
 
 struct GvArgs {
   const __half* X;
@@ -597,7 +603,7 @@ struct GvArgs {
   int* counters;   // one per channel block, zero between launches
   int M, N;
   int rows;            // stored rows (int8: K, int4: K / 2)
-  int rows_per_slice;  // stored rows per CTA (int4: 64 = one group)
+  int rows_per_slice;  // stored rows per CTA (a multiple of 4 x warps)
 };
 
 // 4 bytes (b ^ 0x80 for int8, q + 8 for int4 nibbles) -> 4 exact fp32 values
@@ -608,11 +614,13 @@ __device__ __forceinline__ void bytes_to_f32(uint32_t t, float bias, float* f) {
 }
 
 template <int kQ, int kM>
-__global__ void __launch_bounds__(kGvThreads) wq_gemv_kernel(GvArgs a) {
+__global__ void __launch_bounds__(GvCfg<kQ, kM>::kThreads, 1) wq_gemv_kernel(GvArgs a) {
+  using Cfg = GvCfg<kQ, kM>;
   constexpr int CPL = kGvChanPerLane;
-  constexpr int U = 4;  // stored rows per batch; two batches in flight per lane
+  constexpr int NW = Cfg::kWarps;
+  constexpr int U = 4;                      // stored rows per batch; two batches in flight per lane
   constexpr int KPR = kQ == kInt8 ? 1 : 2;  // k per stored row
-  extern __shared__ float gsm[];  // [kGvWarps][kGvChannels], and first the slice of X as fp32
+  extern __shared__ float gsm[];  // the slice of X as fp32, later [NW][kGvWarpStride] partial sums
   __shared__ int is_last;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -623,24 +631,25 @@ __global__ void __launch_bounds__(kGvThreads) wq_gemv_kernel(GvArgs a) {
   const bool active = n0 < a.N;  // the host guarantees N % 16 == 0
   const int r0 = sl * a.rows_per_slice;
   const int r1 = min(r0 + a.rows_per_slice, a.rows);
-  const int per_warp = (r1 - r0 + kGvWarps - 1) / kGvWarps;
+  const int per_warp = a.rows_per_slice / NW;  // a multiple of U
   const int wr0 = r0 + warp * per_warp;
   const int wr1 = min(wr0 + per_warp, r1);
 
   // The slice of X (k in [KPR r0, KPR r1)) as fp32 in shared memory.
   float* xs = gsm;  // [kM][KPR * rows_per_slice]
   const int kspan = KPR * a.rows_per_slice;
-  for (int i = threadIdx.x; i < kM * kspan; i += kGvThreads) {
+  for (int i = threadIdx.x; i < kM * kspan; i += Cfg::kThreads) {
     const int m = i / kspan, k = KPR * r0 + (i % kspan);
     xs[i] = (m < a.M && k < KPR * r1) ? __half2float(a.X[static_cast<int64_t>(m) * a.ldx + k]) : 0.f;
   }
   __syncthreads();
 
-  float acc[kM][CPL];
+  float acc[kM][CPL];   // int8: the sums; int4: the current group's sums
+  float tot[kM][CPL];   // int4: scaled sums of finished groups
 #pragma unroll
   for (int m = 0; m < kM; ++m)
 #pragma unroll
-    for (int i = 0; i < CPL; ++i) acc[m][i] = 0.f;
+    for (int i = 0; i < CPL; ++i) acc[m][i] = tot[m][i] = 0.f;
 
   if (active) {
     const uint8_t* wp = a.W + n0;
@@ -652,17 +661,18 @@ __global__ void __launch_bounds__(kGvThreads) wq_gemv_kernel(GvArgs a) {
       }
     };
     uint4 cur[U], nxt[U];
-    load(cur, wr0);
+    if (wr0 < wr1) load(cur, wr0);
     for (int r = wr0; r < wr1; r += U) {
       if (r + U < wr1) load(nxt, r + U);  // next batch in flight while this one is used
 #pragma unroll
       for (int u = 0; u < U; ++u) {
+        const bool row_ok = r + u < wr1;
         const int kl = KPR * (r + u - r0);  // k index within the slice
         const uint32_t words[4] = {cur[u].x, cur[u].y, cur[u].z, cur[u].w};
         if (kQ == kInt8) {
           float xv[kM];
 #pragma unroll
-          for (int m = 0; m < kM; ++m) xv[m] = (r + u < wr1) ? xs[m * kspan + kl] : 0.f;
+          for (int m = 0; m < kM; ++m) xv[m] = row_ok ? xs[m * kspan + kl] : 0.f;
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             float f[4];
@@ -677,8 +687,8 @@ __global__ void __launch_bounds__(kGvThreads) wq_gemv_kernel(GvArgs a) {
           float x0[kM], x1[kM];
 #pragma unroll
           for (int m = 0; m < kM; ++m) {
-            x0[m] = (r + u < wr1) ? xs[m * kspan + kl] : 0.f;
-            x1[m] = (r + u < wr1) ? xs[m * kspan + kl + 1] : 0.f;
+            x0[m] = row_ok ? xs[m * kspan + kl] : 0.f;
+            x1[m] = row_ok ? xs[m * kspan + kl + 1] : 0.f;
           }
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
@@ -693,39 +703,49 @@ __global__ void __launch_bounds__(kGvThreads) wq_gemv_kernel(GvArgs a) {
           }
         }
       }
+      if (kQ == kInt4G128 && ((r + U) % 64 == 0 || r + U >= wr1)) {
+        // A 128-wide group (64 stored rows) ends here: scale its sums.
+        const __half* sg = a.scale + static_cast<int64_t>(r / 64) * a.lds + n0;
+        const uint4 s0 = *reinterpret_cast<const uint4*>(sg);
+        const uint4 s1 = *reinterpret_cast<const uint4*>(sg + 8);
+        const __half* sh0 = reinterpret_cast<const __half*>(&s0);
+        const __half* sh1 = reinterpret_cast<const __half*>(&s1);
+#pragma unroll
+        for (int i = 0; i < CPL; ++i) {
+          const float sc = __half2float(i < 8 ? sh0[i] : sh1[i - 8]);
+#pragma unroll
+          for (int m = 0; m < kM; ++m) {
+            tot[m][i] = fmaf(acc[m][i], sc, tot[m][i]);
+            acc[m][i] = 0.f;
+          }
+        }
+      }
 #pragma unroll
       for (int u = 0; u < U; ++u) cur[u] = nxt[u];
     }
-    if (kQ == kInt4G128 && wr0 < wr1) {
-      // A warp's rows lie in one 128-wide group (64 stored rows): scale its sums.
-      const __half* sg = a.scale + static_cast<int64_t>(wr0 / 64) * a.lds + n0;
-      const uint4 s0 = *reinterpret_cast<const uint4*>(sg);
-      const uint4 s1 = *reinterpret_cast<const uint4*>(sg + 8);
-      const __half* sh0 = reinterpret_cast<const __half*>(&s0);
-      const __half* sh1 = reinterpret_cast<const __half*>(&s1);
+  }
+  if (kQ == kInt4G128) {
 #pragma unroll
-      for (int i = 0; i < CPL; ++i) {
-        const float sc = __half2float(i < 8 ? sh0[i] : sh1[i - 8]);
+    for (int m = 0; m < kM; ++m)
 #pragma unroll
-        for (int m = 0; m < kM; ++m) acc[m][i] *= sc;
-      }
-    }
+      for (int i = 0; i < CPL; ++i) acc[m][i] = tot[m][i];
   }
   __syncthreads();  // X slice no longer needed: the reduction reuses the buffer
 
-  // CTA reduction over the 8 warps, one output row m at a time; the slice's
+  // CTA reduction over the warps, one output row m at a time; the slice's
   // sums go to Y (single slice) or to partial[sl].
   const bool single = slices == 1;
   for (int m = 0; m < a.M && m < kM; ++m) {
 #pragma unroll
-    for (int i = 0; i < CPL; ++i) gsm[warp * kGvChannels + lane * CPL + i] = acc[m][i];
+    for (int i = 0; i < CPL; ++i) gsm[warp * kGvWarpStride + lane * 17 + i] = acc[m][i];
     __syncthreads();
-    for (int c = threadIdx.x; c < kGvChannels; c += kGvThreads) {
+    for (int c = threadIdx.x; c < kGvChannels; c += Cfg::kThreads) {
       const int n = cb * kGvChannels + c;
       if (n < a.N) {
+        const int off = (c / CPL) * 17 + (c % CPL);
         float s = 0.f;
-#pragma unroll
-        for (int w = 0; w < kGvWarps; ++w) s += gsm[w * kGvChannels + c];
+#pragma unroll 8
+        for (int w = 0; w < NW; ++w) s += gsm[w * kGvWarpStride + off];
         if (single) {
           if (kQ == kInt8 && a.scale != nullptr) s *= __half2float(a.scale[n]);
           a.Y[static_cast<int64_t>(m) * a.ldy + n] = s;
@@ -745,22 +765,21 @@ __global__ void __launch_bounds__(kGvThreads) wq_gemv_kernel(GvArgs a) {
   __syncthreads();
   if (!is_last) return;
   __threadfence();
-  for (int o = threadIdx.x; o < a.M * kGvChannels; o += kGvThreads) {
+  for (int o = threadIdx.x; o < a.M * kGvChannels; o += Cfg::kThreads) {
     const int m = o / kGvChannels;
     const int n = cb * kGvChannels + (o % kGvChannels);
     if (n >= a.N) continue;
-    // Eight slices' loads in flight at a time; the sum order is fixed:
-    // ((s0 + s8 + ...) + (s1 + s9 + ...)) + ... over the eight lanes of v.
+    // Eight slices' loads in flight at a time, summed in slice order.
     const float* src = a.partial + static_cast<int64_t>(m) * a.N + n;
     const int64_t step = static_cast<int64_t>(a.M) * a.N;
-    float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    float s = 0.f;
     for (int k = 0; k < slices; k += 8) {
+      float v[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        if (k + i < slices) v[i] += __ldcg(src + (k + i) * step);
-      }
+      for (int i = 0; i < 8; ++i) v[i] = (k + i < slices) ? __ldcg(src + (k + i) * step) : 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) s += v[i];
     }
-    float s = ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
     if (kQ == kInt8 && a.scale != nullptr) s *= __half2float(a.scale[n]);
     a.Y[static_cast<int64_t>(m) * a.ldy + n] = s;
   }
@@ -769,6 +788,7 @@ __global__ void __launch_bounds__(kGvThreads) wq_gemv_kernel(GvArgs a) {
 
 template <int kQ, int kM>
 int launch_gemv(const QProblem& p, cudaStream_t stream) {
+  using Cfg = GvCfg<kQ, kM>;
   GvArgs a{};
   a.X = static_cast<const __half*>(p.X);
   a.ldx = p.ldx;
@@ -782,29 +802,20 @@ int launch_gemv(const QProblem& p, cudaStream_t stream) {
   a.N = p.N;
   a.rows = kQ == kInt8 ? p.K : p.K / 2;
   auto kern = wq_gemv_kernel<kQ, kM>;
-  int rc = kernel_setup(reinterpret_cast<const void*>(kern), kGvSmemBytes, nullptr);
+  int rc = kernel_setup(reinterpret_cast<const void*>(kern), Cfg::kSmemBytes, nullptr);
   if (rc != NESO_OK) return rc;
-  // One wave: as many (channel block, K slice) CTAs as fit on the GPU at once.
-  int per_sm = 0;
-  cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kGvThreads, kGvSmemBytes);
-  if (e != cudaSuccess) return cuda_fail(e, "occupancy query");
-  const int resident = std::max(1, per_sm) * sm_count();
+  // One wave of one CTA per SM: the K slices per channel block fill the SMs,
+  // and few slices keep the final in-order sum short.
   const int nblk = (p.N + kGvChannels - 1) / kGvChannels;
-  const int want = std::max(1, resident / nblk);
-  int slices;
-  if (kQ == kInt4G128) {
-    // 1, 2, 4 or 8 groups (64 stored rows each) per slice, so that each
-    // warp's rows stay inside one group.
-    const int groups = p.K / 128;
-    int g = 1;
-    while (g < 8 && nblk * ((groups + g - 1) / g) > resident) g *= 2;
-    a.rows_per_slice = 64 * g;
-    slices = (groups + g - 1) / g;
-  } else {
-    int rps = (a.rows + want - 1) / want;
-    rps = std::max(64, (rps + 7) / 8 * 8);
-    a.rows_per_slice = rps;
-    slices = (a.rows + rps - 1) / rps;
+  const int want = std::max(1, sm_count() / nblk);
+  const int unit = 4 * Cfg::kWarps;  // rows per slice: a whole number of 4-row batches per warp
+  int rps = (a.rows + want - 1) / want;
+  rps = (rps + unit - 1) / unit * unit;
+  a.rows_per_slice = rps;
+  const int slices = (a.rows + rps - 1) / rps;
+  // The slice of X is staged in the reduction buffer.
+  if (static_cast<int64_t>(kM) * (kQ == kInt8 ? 1 : 2) * rps * 4 > Cfg::kSmemBytes) {
+    return fail(NESO_ERR_UNSUPPORTED, "K slice too long for the small-M path");
   }
   if (slices > 65535) return fail(NESO_ERR_UNSUPPORTED, "K too large for the small-M path");
   if (slices > 1) {
@@ -817,8 +828,8 @@ int launch_gemv(const QProblem& p, cudaStream_t stream) {
     if (rc != NESO_OK) return rc;
     a.counters = ctr + kGemvCounterBase;
   }
-  kern<<<dim3(nblk, slices, 1), kGvThreads, kGvSmemBytes, stream>>>(a);
-  e = cudaGetLastError();
+  kern<<<dim3(nblk, slices, 1), Cfg::kThreads, Cfg::kSmemBytes, stream>>>(a);
+  cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "small-M GEMV launch");
   return ok();
 }
