@@ -839,8 +839,10 @@ int launch_gemv(const QProblem& p, cudaStream_t stream) {
 bool gemv_eligible(const QProblem& p) {
   const int max_m = p.kind == kInt8 ? 4 : 2;
   const int nblk = (p.N + kGvChannels - 1) / kGvChannels;
+  // int4 reads each lane's 16 group scales with two 16-byte loads.
+  const bool scales_ok = p.kind == kInt8 || (reinterpret_cast<uintptr_t>(p.scale) & 15u) == 0;
   return p.M <= max_m && p.N % 16 == 0 && p.ldw % 16 == 0 && (reinterpret_cast<uintptr_t>(p.W) & 15u) == 0 &&
-         nblk <= kStreamCounters - kGemvCounterBase;
+         scales_ok && nblk <= kStreamCounters - kGemvCounterBase;
 }
 
 int run_gemv(const QProblem& p, cudaStream_t stream) {
