@@ -48,7 +48,7 @@ namespace neso {
 namespace {
 
 // Register split: warpgroup 0 (TMA, MMA, TMEM warps) shrinks to
-// FaCfg::kRegsLow, the softmax warpgroups grow to kRegsHigh; the host checks
+// FaCfg::regs_low(), the softmax warpgroups grow to kRegsHigh; the host checks
 // that the split fits the block's launch pool.
 constexpr uint32_t kRegsHigh = 216;
 // The persistent kernel's producer and issuers keep per-unit state across
@@ -66,7 +66,7 @@ enum BiasMode : int { kBiasNone = 0, kBiasTable = 1, kBiasDense = 2 };
 template <int D, int kT = 2>
 struct FaCfg {
   static constexpr int kThreads = 128 * (1 + kT);
-  static constexpr int kMinBlocks = kT == 1 ? 2 : 1;
+  __host__ __device__ static constexpr int min_blocks() { return kT == 1 ? 2 : 1; }
   static constexpr int kChunks = D / 64;           // 128-byte TMA boxes per row
   static constexpr int kTileBytes = 128 * D * 2;   // one Q, K or V tile
   static constexpr int kStages = (D == 64 && kT == 2) ? 3 : 2;
@@ -74,7 +74,7 @@ struct FaCfg {
   static constexpr bool kAliasP = (D > 64);
   // Warpgroup 0 register budget; 128 * kRegsLow + 128 * kT * kRegsHigh must
   // fit the launch pool (kThreads x registers per thread).
-  static constexpr uint32_t kRegsLow = kT == 1 ? 40 : 56;
+  __host__ __device__ static constexpr uint32_t regs_low() { return kT == 1 ? 40 : 56; }
   __host__ __device__ static constexpr uint32_t s_col(int t) { return t ? 128u : 0u; }
   __host__ __device__ static constexpr uint32_t o_col(int t) {
     return kT == 1 ? 128u : (t ? 256u + D : 256u);
@@ -108,7 +108,7 @@ struct FaArgs {
 };
 
 template <int D, int kT, bool kCausal, int kBias>
-__global__ void __launch_bounds__(FaCfg<D, kT>::kThreads, FaCfg<D, kT>::kMinBlocks)
+__global__ void __launch_bounds__(FaCfg<D, kT>::kThreads, FaCfg<D, kT>::min_blocks())
     fa2_tile_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, FaArgs a) {
   using Cfg = FaCfg<D, kT>;
@@ -180,7 +180,7 @@ __global__ void __launch_bounds__(FaCfg<D, kT>::kThreads, FaCfg<D, kT>::kMinBloc
   const uint32_t tmem = *tmem_slot;
   if (warp < 4) {
     // Warpgroup 0: TMA producer, MMA issuer, TMEM allocator.
-    setmaxnreg_dec<Cfg::kRegsLow>();
+    setmaxnreg_dec<Cfg::regs_low()>();
     if (warp == 0 && lane == 0) {
       // ------------------------------------------------------------ producer --
       const uint32_t qbytes = (ntile1 > 0 ? 2 : 1) * Cfg::kTileBytes;
@@ -1168,7 +1168,7 @@ int launch_fa2_t(const FaProblem& p, const CUtensorMap& tq, const CUtensorMap& t
     // 128-row units, two CTAs per SM.
     using Cfg1 = FaCfg<D, 1>;
     args.num_qblocks = (p.S + 127) / 128;
-    return run_fa2_kernel(fa2_tile_kernel<D, 1, kCausal, kBias>, Cfg1::kThreads, Cfg1::kRegsLow,
+    return run_fa2_kernel(fa2_tile_kernel<D, 1, kCausal, kBias>, Cfg1::kThreads, Cfg1::regs_low(),
                           dim3(args.num_qblocks, p.BH, 1), Cfg1::kSmemBytes, tq, tk, tv, args, stream);
   }
 }
