@@ -12,8 +12,9 @@
 //   warp 0      TMA: raw weight tile (int8 [64 k][128 n] or packed int4
 //               [32 byte-rows][128 n], 128-byte swizzled), the fp16
 //               activation tile, and (int4) the group's fp16 scale row.
-//   warps 4-7   dequantise raw -> fp16 directly into the MN-major 128-byte
-//               swizzled layout tcgen05 reads; fence.proxy.async; arrive.
+//   warps 4-7,  dequantise raw -> fp16 directly into the MN-major 128-byte
+//   12-15       swizzled layout tcgen05 reads; fence.proxy.async; arrive. The
+//               two groups take alternate K blocks.
 //                 int8: exact, (b ^ 0x80) | 0x6400 as fp16 is 1024 + b + 128.
 //                 int4: q exact the same way, then w = q * s is split into
 //                 w_hi = fp16(q * s) and w_lo = fma(q, s, -w_hi) (the exact
@@ -33,7 +34,7 @@
 namespace neso {
 namespace {
 
-constexpr int kThreads = 384;
+constexpr int kThreads = 512;  // warps 12-15: second convert group
 constexpr int kBK = 64;
 constexpr int kTileN = 128;  // output channels per tile
 
@@ -52,7 +53,7 @@ struct QCfg {
   static constexpr int kW16Bytes = kBK * kTileN * 2;            // 16 KB per fp16 copy
   static constexpr int kNumW16 = (kQ == kInt8) ? 1 : 2;
   static constexpr int kFBytes = kNumW16 * kW16Bytes;
-  static constexpr int kFStages = 3;
+  static constexpr int kFStages = 4;
   static constexpr int kXStages = kSwap ? 8 : 4;
   static constexpr int kBudget = 220 * 1024;
   static constexpr int kRStagesFit = (kBudget - kFStages * kFBytes - kXStages * kXBytes) / kRawBytes;
@@ -263,14 +264,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     umma_commit(mma_done);
     mbar_wait(mma_done, 0, never_flag, quiet, 0);
-  } else if (warp >= 4 && warp < 8) {
+  } else if ((warp >= 4 && warp < 8) || warp >= 12) {
     // ------------------------------------------------------------- convert --
-    const int ct = threadIdx.x - 128;  // 0..127
+    // Two convert groups (warps 4-7 and 12-15) take alternate K blocks, so
+    // one block is dequantised while the other group's is being stored.
+    const int grp = warp >= 12 ? 1 : 0;
+    const int ct = threadIdx.x - (grp ? 384 : 128);  // 0..127
     int it = 0;
     bool ok_run = true;
     for (int t = blockIdx.x; t < num_units && ok_run; t += gridDim.x) {
       const QUnit u = unit_of(t, args);
       for (int kb = u.kb0; kb < u.kb1; ++kb, ++it) {
+        if ((it & 1) != grp) continue;
         const int rs = it % RS, fs = it % FS;
         if (!mbar_wait(&r_full[rs], (it / RS) & 1, abort_flag, args.st, 0x2300)) { ok_run = false; break; }
         const uint8_t* raw = sR + rs * Cfg::kRawBytes;
@@ -357,7 +362,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) mbar_arrive(&f_full[fs]);
       }
     }
-  } else if (warp >= 8) {
+  } else if (warp >= 8 && warp < 12) {
     // ------------------------------------------------------------ epilogue --
     const uint32_t q = warp & 3;
     const int lrow = q * 32 + lane;  // TMEM lane: m (normal) or n (swap)
@@ -466,9 +471,13 @@ void plan_splits(QProblem& p, int sms) {
   p.kb_per_split = num_k;
   if (base >= sms || num_k < 2) return;
   // Each split writes and re-reads an M x N fp32 partial: keep that traffic
-  // under a tenth of the weight stream.
+  // under a tenth of the weight stream, or, for the swapped small-M layout,
+  // let the partials take up to 48 MB (they stay in L2; measured faster for
+  // M = 16, slower for M = 128 where the extra units and the reduce cost more).
   const double wbytes = (p.kind == kInt8 ? 1.0 : 0.5) * static_cast<double>(p.K) * p.N;
-  const int max_splits = static_cast<int>(0.1 * wbytes / (8.0 * p.M * p.N));
+  const double per_split = 4.0 * p.M * p.N;
+  const int max_splits = static_cast<int>(swap ? std::max(0.1 * wbytes / (2.0 * per_split), 48e6 / per_split)
+                                               : 0.1 * wbytes / (2.0 * per_split));
   if (max_splits < 2) return;
   double best = static_cast<double>(base) / sms;
   for (int sp = 2; sp <= 16 && sp <= num_k && sp <= max_splits; ++sp) {
