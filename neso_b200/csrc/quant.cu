@@ -53,8 +53,10 @@ struct QCfg {
   static constexpr int kW16Bytes = kBK * kTileN * 2;            // 16 KB per fp16 copy
   static constexpr int kNumW16 = (kQ == kInt8) ? 1 : 2;
   static constexpr int kFBytes = kNumW16 * kW16Bytes;
-  static constexpr int kFStages = 4;
-  static constexpr int kXStages = kSwap ? 8 : 4;
+  static constexpr int kFStages = (kQ == kInt4G128 && !kSwap) ? 3 : 4;
+  // X tiles come from L2 with about 2500 cycles of copy latency: a deep
+  // ring keeps the MMAs fed when every K block needs a new 16 KB X tile.
+  static constexpr int kXStages = kSwap ? 8 : 6;
   static constexpr int kBudget = 220 * 1024;
   static constexpr int kRStagesFit = (kBudget - kFStages * kFBytes - kXStages * kXBytes) / kRawBytes;
   static constexpr int kRStages = kRStagesFit > 16 ? 16 : kRStagesFit;
