@@ -283,9 +283,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint8_t* raw = sR + rs * Cfg::kRawBytes;
         uint8_t* w16 = sF + fs * Cfg::kFBytes;
         if (kQ == kInt8) {
-          // thread -> (k row r, n half h); raw unit u of row r sits at unit u ^ (r & 7)
-          const int r = ct >> 1;
-          const int h = ct & 1;
+          // thread -> (k row r, n half h); raw unit u of row r sits at unit u ^ (r & 7).
+          // Each group of 8 consecutive threads takes 8 consecutive rows of one
+          // half, so its 16-byte accesses fall in 8 different bank groups.
+          const int r = (ct & 7) + 8 * (ct >> 4);
+          const int h = (ct >> 3) & 1;
           const int sw = r & 7;
           uint4 o[8];
 #pragma unroll
