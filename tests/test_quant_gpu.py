@@ -96,6 +96,24 @@ def test_w4a16_baseline_shapes(dev, M):
         torch.testing.assert_close(y.cpu(), oracle.w4a16_g128_matmul(x, wq, s), **TOL)
 
 
+@pytest.mark.parametrize("kind", ["w8", "w4"])
+def test_paired_channel_tiles_ragged(dev, kind):
+    # 25 row blocks x 4 channel pairs = 100 paired units (one wave) against
+    # 200 single ones (two waves): the 256-channel unit layout runs, with the
+    # second tile of the last pair only partly inside N = 1008.
+    M, N, K = 3100, 1008, 256
+    if kind == "w8":
+        x, w, s = _w8(M, N, K, seed=7)
+        y = ops.w8a16_matmul(x.to(dev), w.to(dev), s.to(dev))
+        ref = oracle.w8a16_matmul(x, w, s)
+    else:
+        x, q, s = _w4(M, N, K, seed=8)
+        wq = oracle.pack_int4(q)
+        y = ops.w4a16_g128_matmul(x.to(dev), wq.to(dev), s.to(dev))
+        ref = oracle.w4a16_g128_matmul(x, wq, s)
+    torch.testing.assert_close(y.cpu(), ref, **TOL)
+
+
 def test_product_pack_matches_oracle_layout(dev):
     q = torch.randint(-8, 8, (256, 64), dtype=torch.int8)
     assert torch.equal(ops.pack_int4(q), oracle.pack_int4(q))
