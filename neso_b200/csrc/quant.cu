@@ -871,7 +871,7 @@ bool gemv_eligible(const QProblem& p) {
   // int4 reads each lane's 16 group scales with two 16-byte loads.
   const bool scales_ok = p.kind == kInt8 || (reinterpret_cast<uintptr_t>(p.scale) & 15u) == 0;
   return p.M <= max_m && p.N % 16 == 0 && p.ldw % 16 == 0 && (reinterpret_cast<uintptr_t>(p.W) & 15u) == 0 &&
-         scales_ok && nblk <= kStreamCounters - kGemvCounterBase;
+         scales_ok && nblk <= kGemvCounterEnd - kGemvCounterBase;
 }
 
 int run_gemv(const QProblem& p, cudaStream_t stream) {

@@ -37,9 +37,12 @@ int stream_workspace(cudaStream_t stream, size_t bytes, void** out);
 // hand out or count work through atomics (one block per device and stream,
 // allocated and zeroed on first use). A kernel that uses them leaves them
 // zero on exit. Slots: [0, 2) the FA2 persistent kernel's unit tickets,
-// [kGemvCounterBase, kStreamCounters) the small-M GEMV's channel blocks.
-constexpr int kStreamCounters = 1024;
+// [kGemvCounterBase, kGemvCounterEnd) the small-M GEMV's channel blocks,
+// [kGemmCounterBase, kStreamCounters) the GEMM's K-split tail tiles.
+constexpr int kStreamCounters = 4096;
 constexpr int kGemvCounterBase = 64;
+constexpr int kGemvCounterEnd = 1024;
+constexpr int kGemmCounterBase = 2048;
 int stream_counters(cudaStream_t stream, int** out);
 
 // Opt a kernel into `smem_bytes` of dynamic shared memory and return its

@@ -43,6 +43,16 @@ def test_matmul_2048_and_4096(dev):
         torch.testing.assert_close(c.cpu(), oracle.gemm(a, b), **TOL)
 
 
+@pytest.mark.parametrize("M,N,K", [
+    (4000, 4000, 200),   # 256 x 256 tiles: ragged last row tile, column tile and K block
+    (832, 9472, 136),    # 4 x 37 = 148 tiles; the last row tile's second half is entirely past M
+])
+def test_matmul_256_row_tiles_ragged(dev, M, N, K):
+    a, b = _inputs(M, N, K, seed=M)
+    c = ops.matmul(a.to(dev), b.to(dev))
+    torch.testing.assert_close(c.cpu(), oracle.gemm(a, b), **TOL)
+
+
 def test_matmul_8192_sampled(dev):
     # Full BASELINE size; compare a sample of rows against the oracle.
     n = 8192
