@@ -43,7 +43,8 @@ struct GemmCfg {
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kAccBufs = MH == 2 ? 1 : 2;
   static constexpr int kTmemCols = kAccBufs * MH * BN;
-  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int kOutBytes = 4 * MH * 4096;  // C staging: 32 rows x 32 fp32 per epilogue warp
+  static constexpr int kSmemBytes = kStages * kStageBytes + kOutBytes + 1024 /*align*/ + 256 /*barriers*/;
 };
 
 struct GemmArgs {
@@ -52,6 +53,7 @@ struct GemmArgs {
   int M, N, K;
   int num_m, num_n, num_k;
   int b_chunked;  // B tile loaded with one 3-D TMA (all BN/64 column chunks)
+  int c_tma;      // C written by TMA stores (16-byte aligned base and row stride)
   DevStatus st;
 };
 
@@ -68,14 +70,16 @@ __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& mb
 template <int BN, int MH>
 __global__ void __launch_bounds__(GemmCfg<BN, MH>::kThreads, 1)
     gemm_f16_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                            const __grid_constant__ CUtensorMap tmB3, GemmArgs args) {
+                            const __grid_constant__ CUtensorMap tmB3, const __grid_constant__ CUtensorMap tmC,
+                            GemmArgs args) {
   using Cfg = GemmCfg<BN, MH>;
   constexpr int S = Cfg::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;                       // S x MH x 16 KB
   uint8_t* sB = smem + S * Cfg::kABytes;    // S x (BN/64) x 8 KB
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStageBytes);
+  uint8_t* sOut = smem + S * Cfg::kStageBytes;  // 4 KB per epilogue warp
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sOut + Cfg::kOutBytes);
   uint64_t* full = bars;                    // [S]
   uint64_t* empty = bars + S;               // [S]
   uint64_t* acc_full = bars + 2 * S;        // [2]
@@ -105,6 +109,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, MH>::kThreads, 1)
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
     tma_prefetch_desc(&tmB3);
+    if (args.c_tma) tma_prefetch_desc(&tmC);
   }
   if (warp == 2) {
     tmem_alloc(tmem_slot, Cfg::kTmemCols);
@@ -206,6 +211,39 @@ __global__ void __launch_bounds__(GemmCfg<BN, MH>::kThreads, 1)
       // Warp-uniform: every lane must agree before the .sync.aligned TMEM loads.
       if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[buf], use & 1, abort_flag, args.st, 0x300))) break;
       tc_fence_after();
+      if (args.c_tma) {
+        // TMEM -> registers -> this warp's 128-byte-swizzled staging rows ->
+        // one TMA store per 32 x 32 block: full-line writes, and the
+        // accumulator is released as soon as its last columns are loaded.
+        uint8_t* stage = sOut + (warp - 4) * 4096;
+        const int row0 = mb * Cfg::kTileM + h * kBM + q * 32;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(tmem_base + ((q * 32) << 16) + (buf * MH + h) * BN + c * 32, r);
+          tmem_wait_ld();
+          if (c == BN / 32 - 1) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[buf]);
+          }
+          if (lane == 0) bulk_wait_read_all();  // the previous store has read the staging rows
+          __syncwarp();
+#pragma unroll
+          for (int v = 0; v < 8; ++v) {
+            *reinterpret_cast<uint4*>(stage + lane * 128 + ((v ^ (lane & 7)) << 4)) =
+                make_uint4(r[4 * v], r[4 * v + 1], r[4 * v + 2], r[4 * v + 3]);
+          }
+          fence_async_smem();
+          __syncwarp();
+          const int col0 = nb * BN + c * 32;
+          if (lane == 0 && row0 < args.M && col0 < args.N) {
+            tma_store_2d(&tmC, stage, col0, row0);
+            bulk_commit();
+          }
+        }
+        continue;
+      }
       const int grow = mb * Cfg::kTileM + row_in_tile;
       float* crow = args.C + static_cast<int64_t>(grow) * args.ldc;
 #pragma unroll 1
@@ -234,6 +272,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, MH>::kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[buf]);
     }
+    if (lane == 0) bulk_wait_all();  // this warp's C stores are complete before the CTA exits
   }
 
   tc_fence_before();
@@ -288,8 +327,21 @@ int launch_gemm_bn(const void* A, int64_t lda, const void* B, int64_t ldb, float
     if (rc != NESO_OK) return rc;
     b_chunked = 1;
   }
+  // C through TMA stores when its base and row stride are 16-byte aligned.
+  CUtensorMap tmC = tmA;
+  int c_tma = 0;
+  if (ldc % 4 == 0 && (reinterpret_cast<uintptr_t>(C) & 15u) == 0) {
+    uint64_t dims[2] = {static_cast<uint64_t>(N), static_cast<uint64_t>(M)};
+    uint64_t strides[1] = {static_cast<uint64_t>(ldc) * 4};
+    uint32_t box[2] = {32, 32};
+    int rc = encode_tmap(&tmC, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, C, dims, strides, box,
+                         CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc != NESO_OK) return rc;
+    c_tma = 1;
+  }
   GemmArgs args{};
   args.b_chunked = b_chunked;
+  args.c_tma = c_tma;
   args.C = C;
   args.ldc = ldc;
   args.M = M;
@@ -307,7 +359,7 @@ int launch_gemm_bn(const void* A, int64_t lda, const void* B, int64_t ldb, float
     int src = kernel_setup(reinterpret_cast<const void*>(kern), Cfg::kSmemBytes, nullptr);
     if (src != NESO_OK) return src;
   }
-  kern<<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(tmA, tmB, tmB3, args);
+  kern<<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(tmA, tmB, tmB3, tmC, args);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "gemm launch");
   return ok();
