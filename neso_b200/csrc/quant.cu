@@ -63,12 +63,15 @@ struct QCfg {
   // ring keeps the MMAs fed when every K block needs a new 16 KB X tile.
   static constexpr int kXStages = kSwap ? 8 : kNT == 2 ? (kQ == kInt8 ? 4 : 3) : 6;
   static constexpr int kBudget = 220 * 1024;
-  static constexpr int kRStagesFit = (kBudget - kFStages * kFBytes - kXStages * kXBytes) / kRawBytes;
+  // Y staging for TMA stores (M >= 65 layout): 16 rows x 32 fp32 per epilogue warp.
+  static constexpr int kOutBytes = kSwap ? 0 : 4 * 2048;
+  static constexpr int kRStagesFit = (kBudget - kOutBytes - kFStages * kFBytes - kXStages * kXBytes) / kRawBytes;
   static constexpr int kRStages = kRStagesFit > 16 ? 16 : kRStagesFit;
   static constexpr int kOffR = 0;
   static constexpr int kOffX = kRStages * kRawBytes;
   static constexpr int kOffF = kOffX + kXStages * kXBytes;
-  static constexpr int kOffBars = kOffF + kFStages * kFBytes;
+  static constexpr int kOffOut = kOffF + kFStages * kFBytes;
+  static constexpr int kOffBars = kOffOut + kOutBytes;
   static constexpr int kRawTx = kNT * ((kQ == kInt8) ? 64 * 128 : 32 * 128 + 256);
   static constexpr int kAccCols = kSwap ? kNX : kNT * kTileN;   // accumulator columns per buffer
   static constexpr int kTmemCols = (2 * kAccCols <= 32) ? 32 : (2 * kAccCols <= 64) ? 64
@@ -86,6 +89,7 @@ struct QArgs {
   int M, N, K;
   int num_m, num_n, num_k;
   int splits, kb_per_split;  // K blocks are split into `splits` ranges
+  int y_tma;                 // Y written by TMA stores (M >= 65 layout, no split, aligned Y)
   DevStatus st;
 };
 
@@ -130,7 +134,7 @@ __device__ __forceinline__ void dequant_i8x16(uint4 raw, uint4& o0, uint4& o1) {
 template <int kQ, bool kSwap, int kNX, int kNT>
 __global__ void __launch_bounds__(kThreads, 1)
     wq_gemm_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
-                   const __grid_constant__ CUtensorMap tmS, QArgs args) {
+                   const __grid_constant__ CUtensorMap tmS, const __grid_constant__ CUtensorMap tmY, QArgs args) {
   using Cfg = QCfg<kQ, kSwap, kNX, kNT>;
   constexpr int kUnitN = kNT * kTileN;  // output channels per unit
   constexpr int RS = Cfg::kRStages, XS = Cfg::kXStages, FS = Cfg::kFStages;
@@ -181,6 +185,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_prefetch_desc(&tmX);
     tma_prefetch_desc(&tmW);
     if (kQ == kInt4G128) tma_prefetch_desc(&tmS);
+    if (args.y_tma) tma_prefetch_desc(&tmY);
   }
   if (warp == 2) {
     tmem_alloc(tmem_slot, Cfg::kTmemCols);
@@ -425,6 +430,45 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
         }
+      } else if (args.y_tma) {
+        // Rows of 32 channels through 128-byte-swizzled staging (16 rows at a
+        // time) and TMA stores: full-line writes instead of one 4-byte store
+        // per row and channel, which left the L1 busy with the epilogue.
+        uint8_t* stage = smem + Cfg::kOffOut + (warp - 8) * 2048;
+        const int m0 = mb * 128 + static_cast<int>(q) * 32;
+#pragma unroll 1
+        for (int c = 0; c < kUnitN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(acc + c * 32, r);
+          tmem_wait_ld();
+          const int n0 = nb * kUnitN + c * 32;
+          if (csc != nullptr) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const float sc = n0 + i < args.N ? __half2float(__ldg(csc + n0 + i)) : 0.f;
+              r[i] = __float_as_uint(__uint_as_float(r[i]) * sc);
+            }
+          }
+#pragma unroll
+          for (int half = 0; half < 2; ++half) {
+            if (lane == 0) bulk_wait_read_all();  // the previous store has read the staging rows
+            __syncwarp();
+            if ((lane >> 4) == static_cast<uint32_t>(half)) {
+              const uint32_t row = lane & 15;
+#pragma unroll
+              for (int v = 0; v < 8; ++v) {
+                *reinterpret_cast<uint4*>(stage + row * 128 + ((v ^ (row & 7)) << 4)) =
+                    make_uint4(r[4 * v], r[4 * v + 1], r[4 * v + 2], r[4 * v + 3]);
+              }
+            }
+            fence_async_smem();
+            __syncwarp();
+            if (lane == 0 && m0 + 16 * half < args.M && n0 < args.N) {
+              tma_store_2d(&tmY, stage, n0, m0 + 16 * half);
+              bulk_commit();
+            }
+          }
+        }
       } else {
         const int m = mb * 128 + lrow;
         float* yrow = ydst + static_cast<int64_t>(m) * ld;
@@ -450,6 +494,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[buf]);
     }
+    if (lane == 0) bulk_wait_all();  // this warp's Y stores are complete before the CTA exits
   }
 
   tc_fence_before();
@@ -557,7 +602,19 @@ int launch_wq(const QProblem& p, cudaStream_t stream) {
   } else {
     tmS = tmX;  // unused
   }
+  CUtensorMap tmY = tmX;
+  int y_tma = 0;
+  if (!kSwap && p.splits == 1 && p.ldy % 4 == 0 && (reinterpret_cast<uintptr_t>(p.Y) & 15u) == 0) {
+    uint64_t dims[2] = {static_cast<uint64_t>(p.N), static_cast<uint64_t>(p.M)};
+    uint64_t strides[1] = {static_cast<uint64_t>(p.ldy) * 4};
+    uint32_t box[2] = {32, 16};
+    int rc = encode_tmap(&tmY, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, p.Y, dims, strides, box,
+                         CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc != NESO_OK) return rc;
+    y_tma = 1;
+  }
   QArgs args{};
+  args.y_tma = y_tma;
   args.Y = p.Y;
   args.ldy = p.ldy;
   args.chan_scale = kQ == kInt8 ? static_cast<const __half*>(p.scale) : nullptr;
@@ -578,7 +635,7 @@ int launch_wq(const QProblem& p, cudaStream_t stream) {
     int src = kernel_setup(reinterpret_cast<const void*>(kern), Cfg::kSmemBytes, nullptr);
     if (src != NESO_OK) return src;
   }
-  kern<<<grid, kThreads, Cfg::kSmemBytes, stream>>>(tmX, tmW, tmS, args);
+  kern<<<grid, kThreads, Cfg::kSmemBytes, stream>>>(tmX, tmW, tmS, tmY, args);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "wq_gemm launch");
   if (args.partial != nullptr) {
