@@ -110,7 +110,8 @@ struct FaArgs {
 template <int D, int kT, bool kCausal, int kBias>
 __global__ void __launch_bounds__(FaCfg<D, kT>::kThreads, FaCfg<D, kT>::min_blocks())
     fa2_tile_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                    const __grid_constant__ CUtensorMap tmV, FaArgs a) {
+                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
+                    FaArgs a) {
   using Cfg = FaCfg<D, kT>;
   constexpr int KS = Cfg::kStages;
   extern __shared__ uint8_t smem_raw[];
@@ -507,31 +508,75 @@ __global__ void __launch_bounds__(FaCfg<D, kT>::kThreads, FaCfg<D, kT>::min_bloc
         __all_sync(0xffffffffu, mbar_wait(&o_done[t], (n_t - 1) & 1, abort_flag, a.st, 0x1310 + t))) {
       tc_fence_after();
       const float inv_l = 1.f / l;
-      const bool store = qrow < S;
-      uint32_t r[32];
+      if (kT == 1) {
+        // The K ring is idle once the last PV has completed: each warp stages
+        // its 32 rows (128 bytes of O per row and store, 128-byte swizzled)
+        // there and writes them with TMA stores; rows past S are clipped.
+        uint8_t* stage = sK + (warp - 4) * 4096;
+        const int row0 = q0 + static_cast<int>(q) * 32;
+        constexpr int kStores = D / 32;  // fp32: 32 columns per store; fp16: 64
 #pragma unroll 1
-      for (int c = 0; c < D / 32; ++c) {
-        tmem_ld32(lane_base + Cfg::o_col(t) + c * 32, r);
-        tmem_wait_ld();
-        if (store) {
+        for (int c = 0; c < (a.out_f16 ? kStores / 2 : kStores); ++c) {
+          uint32_t w[32];
           if (a.out_f16) {
-            __half* orow = static_cast<__half*>(a.O) + bh * a.o_head + static_cast<int64_t>(qrow) * a.o_row + c * 32;
+            uint32_t r0[32], r1[32];
+            tmem_ld32(lane_base + Cfg::o_col(t) + c * 64, r0);
+            tmem_ld32(lane_base + Cfg::o_col(t) + c * 64 + 32, r1);
+            tmem_wait_ld();
 #pragma unroll
-            for (int v = 0; v < 4; ++v) {
-              uint4 w;
-              w.x = pack_half2(__uint_as_float(r[8 * v + 0]) * inv_l, __uint_as_float(r[8 * v + 1]) * inv_l);
-              w.y = pack_half2(__uint_as_float(r[8 * v + 2]) * inv_l, __uint_as_float(r[8 * v + 3]) * inv_l);
-              w.z = pack_half2(__uint_as_float(r[8 * v + 4]) * inv_l, __uint_as_float(r[8 * v + 5]) * inv_l);
-              w.w = pack_half2(__uint_as_float(r[8 * v + 6]) * inv_l, __uint_as_float(r[8 * v + 7]) * inv_l);
-              *reinterpret_cast<uint4*>(orow + 8 * v) = w;
+            for (int i = 0; i < 16; ++i) {
+              w[i] = pack_half2(__uint_as_float(r0[2 * i]) * inv_l, __uint_as_float(r0[2 * i + 1]) * inv_l);
+              w[16 + i] = pack_half2(__uint_as_float(r1[2 * i]) * inv_l, __uint_as_float(r1[2 * i + 1]) * inv_l);
             }
           } else {
-            float* orow = static_cast<float*>(a.O) + bh * a.o_head + static_cast<int64_t>(qrow) * a.o_row + c * 32;
+            uint32_t r[32];
+            tmem_ld32(lane_base + Cfg::o_col(t) + c * 32, r);
+            tmem_wait_ld();
 #pragma unroll
-            for (int v = 0; v < 8; ++v) {
-              *reinterpret_cast<float4*>(orow + 4 * v) =
-                  make_float4(__uint_as_float(r[4 * v]) * inv_l, __uint_as_float(r[4 * v + 1]) * inv_l,
-                              __uint_as_float(r[4 * v + 2]) * inv_l, __uint_as_float(r[4 * v + 3]) * inv_l);
+            for (int i = 0; i < 32; ++i) w[i] = __float_as_uint(__uint_as_float(r[i]) * inv_l);
+          }
+          if (lane == 0) bulk_wait_read_all();  // the previous store has read the staging rows
+          __syncwarp();
+#pragma unroll
+          for (int v = 0; v < 8; ++v) {
+            *reinterpret_cast<uint4*>(stage + lane * 128 + ((v ^ (lane & 7)) << 4)) =
+                make_uint4(w[4 * v], w[4 * v + 1], w[4 * v + 2], w[4 * v + 3]);
+          }
+          fence_async_smem();
+          __syncwarp();
+          if (lane == 0 && row0 < S) {
+            tma_store_3d(&tmO, stage, c * (a.out_f16 ? 64 : 32), row0, bh);
+            bulk_commit();
+          }
+        }
+        if (lane == 0) bulk_wait_all();
+      } else {
+        const bool store = qrow < S;
+        uint32_t r[32];
+#pragma unroll 1
+        for (int c = 0; c < D / 32; ++c) {
+          tmem_ld32(lane_base + Cfg::o_col(t) + c * 32, r);
+          tmem_wait_ld();
+          if (store) {
+            if (a.out_f16) {
+              __half* orow = static_cast<__half*>(a.O) + bh * a.o_head + static_cast<int64_t>(qrow) * a.o_row + c * 32;
+#pragma unroll
+              for (int v = 0; v < 4; ++v) {
+                uint4 w;
+                w.x = pack_half2(__uint_as_float(r[8 * v + 0]) * inv_l, __uint_as_float(r[8 * v + 1]) * inv_l);
+                w.y = pack_half2(__uint_as_float(r[8 * v + 2]) * inv_l, __uint_as_float(r[8 * v + 3]) * inv_l);
+                w.z = pack_half2(__uint_as_float(r[8 * v + 4]) * inv_l, __uint_as_float(r[8 * v + 5]) * inv_l);
+                w.w = pack_half2(__uint_as_float(r[8 * v + 6]) * inv_l, __uint_as_float(r[8 * v + 7]) * inv_l);
+                *reinterpret_cast<uint4*>(orow + 8 * v) = w;
+              }
+            } else {
+              float* orow = static_cast<float*>(a.O) + bh * a.o_head + static_cast<int64_t>(qrow) * a.o_row + c * 32;
+#pragma unroll
+              for (int v = 0; v < 8; ++v) {
+                *reinterpret_cast<float4*>(orow + 4 * v) =
+                    make_float4(__uint_as_float(r[4 * v]) * inv_l, __uint_as_float(r[4 * v + 1]) * inv_l,
+                                __uint_as_float(r[4 * v + 2]) * inv_l, __uint_as_float(r[4 * v + 3]) * inv_l);
+              }
             }
           }
         }
@@ -582,7 +627,8 @@ __device__ __noinline__ int fetch_unit(uint64_t* full, uint64_t* empty, volatile
 template <int D, bool kCausal, int kBias>
 __global__ void __launch_bounds__(FaCfg<D>::kThreads, 1)
     fa2_persistent_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                          const __grid_constant__ CUtensorMap tmV, FaArgs a) {
+                          const __grid_constant__ CUtensorMap tmV,
+                          const __grid_constant__ CUtensorMap tmO, FaArgs a) {
   using Cfg = FaCfg<D>;
   constexpr int KS = Cfg::kStages;
   constexpr int QB = Cfg::kQBuffers;
@@ -1137,7 +1183,8 @@ struct FaProblem {
 
 template <class Kernel>
 int run_fa2_kernel(Kernel kern, int threads, uint32_t regs_low, dim3 grid, int smem_bytes, const CUtensorMap& tq,
-                   const CUtensorMap& tk, const CUtensorMap& tv, const FaArgs& args, cudaStream_t stream) {
+                   const CUtensorMap& tk, const CUtensorMap& tv, const CUtensorMap& to, const FaArgs& args,
+                   cudaStream_t stream) {
   cudaFuncAttributes fa{};
   int rc = kernel_setup(reinterpret_cast<const void*>(kern), smem_bytes, &fa);
   if (rc != NESO_OK) return rc;
@@ -1145,7 +1192,7 @@ int run_fa2_kernel(Kernel kern, int threads, uint32_t regs_low, dim3 grid, int s
     return fail(NESO_ERR_LAUNCH, "fa2: %d registers/thread cannot fund the %u/%u warpgroup split", fa.numRegs,
                 regs_low, kRegsHigh);
   }
-  kern<<<grid, threads, smem_bytes, stream>>>(tq, tk, tv, args);
+  kern<<<grid, threads, smem_bytes, stream>>>(tq, tk, tv, to, args);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "fa2 launch");
   return ok();
@@ -1155,35 +1202,35 @@ int run_fa2_kernel(Kernel kern, int threads, uint32_t regs_low, dim3 grid, int s
 // persistent kernel, D = 64 one CTA per work unit.
 template <int D, bool kCausal, int kBias>
 int launch_fa2_t(const FaProblem& p, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
-                 FaArgs& args, cudaStream_t stream) {
+                 const CUtensorMap& to, FaArgs& args, cudaStream_t stream) {
   using Cfg = FaCfg<D>;
   if constexpr (D == 128) {
     const int units = args.num_qblocks * p.BH;
     int rc = stream_counters(stream, &args.unit_counter);
     if (rc != NESO_OK) return rc;
     return run_fa2_kernel(fa2_persistent_kernel<D, kCausal, kBias>, Cfg::kThreads, kRegsLowPersistent,
-                          dim3(units < sm_count() ? units : sm_count(), 1, 1), Cfg::kSmemBytes, tq, tk, tv, args,
-                          stream);
+                          dim3(units < sm_count() ? units : sm_count(), 1, 1), Cfg::kSmemBytes, tq, tk, tv, to,
+                          args, stream);
   } else {
     // 128-row units, two CTAs per SM.
     using Cfg1 = FaCfg<D, 1>;
     args.num_qblocks = (p.S + 127) / 128;
     return run_fa2_kernel(fa2_tile_kernel<D, 1, kCausal, kBias>, Cfg1::kThreads, Cfg1::regs_low(),
-                          dim3(args.num_qblocks, p.BH, 1), Cfg1::kSmemBytes, tq, tk, tv, args, stream);
+                          dim3(args.num_qblocks, p.BH, 1), Cfg1::kSmemBytes, tq, tk, tv, to, args, stream);
   }
 }
 
 template <int D>
 int launch_fa2_d(const FaProblem& p, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
-                 FaArgs& args, cudaStream_t stream) {
+                 const CUtensorMap& to, FaArgs& args, cudaStream_t stream) {
   if (p.causal) {
-    if (p.bias_mode == kBiasTable) return launch_fa2_t<D, true, kBiasTable>(p, tq, tk, tv, args, stream);
-    if (p.bias_mode == kBiasDense) return launch_fa2_t<D, true, kBiasDense>(p, tq, tk, tv, args, stream);
-    return launch_fa2_t<D, true, kBiasNone>(p, tq, tk, tv, args, stream);
+    if (p.bias_mode == kBiasTable) return launch_fa2_t<D, true, kBiasTable>(p, tq, tk, tv, to, args, stream);
+    if (p.bias_mode == kBiasDense) return launch_fa2_t<D, true, kBiasDense>(p, tq, tk, tv, to, args, stream);
+    return launch_fa2_t<D, true, kBiasNone>(p, tq, tk, tv, to, args, stream);
   }
-  if (p.bias_mode == kBiasTable) return launch_fa2_t<D, false, kBiasTable>(p, tq, tk, tv, args, stream);
-  if (p.bias_mode == kBiasDense) return launch_fa2_t<D, false, kBiasDense>(p, tq, tk, tv, args, stream);
-  return launch_fa2_t<D, false, kBiasNone>(p, tq, tk, tv, args, stream);
+  if (p.bias_mode == kBiasTable) return launch_fa2_t<D, false, kBiasTable>(p, tq, tk, tv, to, args, stream);
+  if (p.bias_mode == kBiasDense) return launch_fa2_t<D, false, kBiasDense>(p, tq, tk, tv, to, args, stream);
+  return launch_fa2_t<D, false, kBiasNone>(p, tq, tk, tv, to, args, stream);
 }
 
 int make_qkv_map(CUtensorMap* m, const void* base, int D, int S, int BH, int64_t row, int64_t head) {
@@ -1216,6 +1263,18 @@ int launch_fa2(const FaProblem& p, cudaStream_t stream) {
   if (rc == NESO_OK) rc = make_qkv_map(&tk, p.K, p.D, p.S, p.BH, p.k_row, p.k_head);
   if (rc == NESO_OK) rc = make_qkv_map(&tv, p.V, p.D, p.S, p.BH, p.v_row, p.v_head);
   if (rc != NESO_OK) return rc;
+  // O as [BH][S][D] for TMA stores (the alignment checks above make its
+  // strides multiples of 16 bytes): boxes of 32 rows x 128 bytes.
+  CUtensorMap to;
+  {
+    const int esz = p.out_f16 ? 2 : 4;
+    uint64_t dims[3] = {static_cast<uint64_t>(p.D), static_cast<uint64_t>(p.S), static_cast<uint64_t>(p.BH)};
+    uint64_t strides[2] = {static_cast<uint64_t>(p.o_row) * esz, static_cast<uint64_t>(p.o_head) * esz};
+    uint32_t box[3] = {static_cast<uint32_t>(128 / esz), 32, 1};
+    rc = encode_tmap(&to, p.out_f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, p.O, dims,
+                     strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc != NESO_OK) return rc;
+  }
   FaArgs args{};
   args.O = p.O;
   args.o_row = p.o_row;
@@ -1233,8 +1292,8 @@ int launch_fa2(const FaProblem& p, cudaStream_t stream) {
   args.out_f16 = p.out_f16 ? 1 : 0;
   rc = device_status(&args.st);
   if (rc != NESO_OK) return rc;
-  if (p.D == 64) return launch_fa2_d<64>(p, tq, tk, tv, args, stream);
-  return launch_fa2_d<128>(p, tq, tk, tv, args, stream);
+  if (p.D == 64) return launch_fa2_d<64>(p, tq, tk, tv, to, args, stream);
+  return launch_fa2_d<128>(p, tq, tk, tv, to, args, stream);
 }
 
 // The reference's BM is a compile-time tile height (8..128, power of two);
