@@ -84,7 +84,10 @@ struct FaCfg {
   }
   static constexpr uint32_t kPHalfStride = 32u;  // P columns are contiguous (64 per tile)
   static constexpr int kTmemCols = kT == 1 ? 256 : 512;
-  static constexpr int kSmemBytes = (kT * kQBuffers + 2 * kStages) * kTileBytes + 1024 + 512;
+  // Persistent kernel: O staging for TMA stores, 32 rows x 128 bytes per
+  // softmax warp (the K/V ring is busy with the next unit meanwhile).
+  static constexpr int kOutBytes = kT == 2 ? 4 * kT * 4096 : 0;
+  static constexpr int kSmemBytes = (kT * kQBuffers + 2 * kStages) * kTileBytes + kOutBytes + 1024 + 512;
 };
 
 struct FaArgs {
@@ -637,7 +640,8 @@ __global__ void __launch_bounds__(FaCfg<D>::kThreads, 1)
   uint8_t* sQ = smem;                                   // QB x (2 tiles)
   uint8_t* sK = smem + QB * 2 * Cfg::kTileBytes;        // KS tiles
   uint8_t* sV = sK + KS * Cfg::kTileBytes;              // KS tiles
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + KS * Cfg::kTileBytes);
+  uint8_t* sOut = sV + KS * Cfg::kTileBytes;          // 4 KB per softmax warp
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sOut + Cfg::kOutBytes);
   uint64_t* q_full = bars;              // [QB]
   uint64_t* q_empty = q_full + QB;      // [QB] last QK of the unit done
   uint64_t* k_full = q_empty + QB;      // [KS]
@@ -1111,42 +1115,54 @@ __global__ void __launch_bounds__(FaCfg<D>::kThreads, 1)
       }
       tc_fence_after();
       const float inv_l = 1.f / l;
-      const bool store = qrow < S;
-      uint32_t r[32];
+      // 32 rows x 128 bytes per TMA store through this warp's 128-byte-swizzled
+      // staging rows; rows past S are clipped by the store.
+      uint8_t* stage = sOut + (warp - 4) * 4096;
+      const int row0 = q0 + 128 * t + static_cast<int>(q) * 32;
+      constexpr int kStores = D / 32;  // fp32: 32 columns per store; fp16: 64
 #pragma unroll 1
-      for (int c = 0; c < D / 32; ++c) {
-        tmem_ld32(lane_base + Cfg::o_col(t) + c * 32, r);
-        tmem_wait_ld();
-        if (c == D / 32 - 1) {
+      for (int c = 0; c < (a.out_f16 ? kStores / 2 : kStores); ++c) {
+        uint32_t w[32];
+        const bool last_ld = c == (a.out_f16 ? kStores / 2 : kStores) - 1;
+        if (a.out_f16) {
+          uint32_t r0[32], r1[32];
+          tmem_ld32(lane_base + Cfg::o_col(t) + c * 64, r0);
+          tmem_ld32(lane_base + Cfg::o_col(t) + c * 64 + 32, r1);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            w[i] = pack_half2(__uint_as_float(r0[2 * i]) * inv_l, __uint_as_float(r0[2 * i + 1]) * inv_l);
+            w[16 + i] = pack_half2(__uint_as_float(r1[2 * i]) * inv_l, __uint_as_float(r1[2 * i + 1]) * inv_l);
+          }
+        } else {
+          uint32_t r[32];
+          tmem_ld32(lane_base + Cfg::o_col(t) + c * 32, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) w[i] = __float_as_uint(__uint_as_float(r[i]) * inv_l);
+        }
+        if (last_ld) {
           // O_t is in registers: the next unit's first PV may overwrite it.
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&o_free[t]);
         }
-        if (store) {
-          if (a.out_f16) {
-            __half* orow = static_cast<__half*>(a.O) + bh * a.o_head + static_cast<int64_t>(qrow) * a.o_row + c * 32;
+        if (lane == 0) bulk_wait_read_all();  // the previous store has read the staging rows
+        __syncwarp();
 #pragma unroll
-            for (int v = 0; v < 4; ++v) {
-              uint4 wv;
-              wv.x = pack_half2(__uint_as_float(r[8 * v + 0]) * inv_l, __uint_as_float(r[8 * v + 1]) * inv_l);
-              wv.y = pack_half2(__uint_as_float(r[8 * v + 2]) * inv_l, __uint_as_float(r[8 * v + 3]) * inv_l);
-              wv.z = pack_half2(__uint_as_float(r[8 * v + 4]) * inv_l, __uint_as_float(r[8 * v + 5]) * inv_l);
-              wv.w = pack_half2(__uint_as_float(r[8 * v + 6]) * inv_l, __uint_as_float(r[8 * v + 7]) * inv_l);
-              *reinterpret_cast<uint4*>(orow + 8 * v) = wv;
-            }
-          } else {
-            float* orow = static_cast<float*>(a.O) + bh * a.o_head + static_cast<int64_t>(qrow) * a.o_row + c * 32;
-#pragma unroll
-            for (int v = 0; v < 8; ++v) {
-              *reinterpret_cast<float4*>(orow + 4 * v) =
-                  make_float4(__uint_as_float(r[4 * v]) * inv_l, __uint_as_float(r[4 * v + 1]) * inv_l,
-                              __uint_as_float(r[4 * v + 2]) * inv_l, __uint_as_float(r[4 * v + 3]) * inv_l);
-            }
-          }
+        for (int v = 0; v < 8; ++v) {
+          *reinterpret_cast<uint4*>(stage + lane * 128 + ((v ^ (lane & 7)) << 4)) =
+              make_uint4(w[4 * v], w[4 * v + 1], w[4 * v + 2], w[4 * v + 3]);
+        }
+        fence_async_smem();
+        __syncwarp();
+        if (lane == 0 && row0 < S) {
+          tma_store_3d(&tmO, stage, c * (a.out_f16 ? 64 : 32), row0, bh);
+          bulk_commit();
         }
       }
     }
+    if (lane == 0) bulk_wait_all();
   }
 
   tc_fence_before();
