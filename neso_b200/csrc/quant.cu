@@ -946,14 +946,17 @@ int dispatch_wq(const QProblem& p, cudaStream_t stream) {
   if (p.M <= 16) return launch_wq<kQ, true, 16>(p, stream);
   if (p.M <= 32) return launch_wq<kQ, true, 32>(p, stream);
   if (p.M <= 64) return launch_wq<kQ, true, 64>(p, stream);
-  // Pairs of channel tiles per unit (the activation tile is then read once
-  // per 256 channels instead of once per 128, about 5% faster per unit of
-  // work) when that costs no extra wave: a paired unit takes about twice as
-  // long, so 2 x waves(paired) must not exceed waves(single).
+  // Pairs of channel tiles per unit: the activation tile is read once per
+  // 256 channels instead of once per 128 and the two convert groups work on
+  // the same K block. Measured on B200 (K = 4096, N = 11008), a paired unit
+  // takes 1.31x (int8) / 1.82x (int4) the time of a single one, so pairs win
+  // unless they leave too few units to fill the waves.
   const int64_t sms = sm_count();
   const int64_t num_m = (p.M + 127) / 128;
   const int64_t single = num_m * ((p.N + 127) / 128), paired = num_m * ((p.N + 255) / 256);
-  if (p.splits == 1 && 2 * ((paired + sms - 1) / sms) <= (single + sms - 1) / sms) {
+  const double pair_cost = kQ == kInt8 ? 1.35 : 1.85;
+  if (p.splits == 1 &&
+      pair_cost * static_cast<double>((paired + sms - 1) / sms) < static_cast<double>((single + sms - 1) / sms)) {
     return launch_wq<kQ, false, 128, 2>(p, stream);
   }
   return launch_wq<kQ, false, 128>(p, stream);
