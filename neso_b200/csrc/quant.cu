@@ -89,7 +89,7 @@ struct QArgs {
   int M, N, K;
   int num_m, num_n, num_k;
   int splits, kb_per_split;  // K blocks are split into `splits` ranges
-  int y_tma;                 // Y written by TMA stores (M >= 65 layout, no split, aligned Y)
+  int y_tma;                 // Y / partial sums written by TMA stores (M >= 65 layout, aligned rows)
   DevStatus st;
 };
 
@@ -464,7 +464,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             fence_async_smem();
             __syncwarp();
             if (lane == 0 && m0 + 16 * half < args.M && n0 < args.N) {
-              tma_store_2d(&tmY, stage, n0, m0 + 16 * half);
+              tma_store_3d(&tmY, stage, n0, m0 + 16 * half, args.partial != nullptr ? u.ks : 0);
               bulk_commit();
             }
           }
@@ -519,14 +519,55 @@ struct QProblem {
   // split-K plan (filled by plan_splits) and the fp32 partial-sum buffer
   int splits = 1;
   int kb_per_split = 0;
+  int pair = 0;  // M >= 65 layout: two 128-channel tiles per unit
   float* partial = nullptr;
   DevStatus st{};
 };
 
+// M >= 65 layout: choose single or paired channel tiles and a K split from a
+// cost model in units of one single-tile, whole-K unit: waves x unit cost x
+// share of K, plus the split-K cost (a reduce launch and the partial sums'
+// write and read, at HBM speed). Measured on B200 (K = 4096, N = 11008): a
+// paired unit takes 1.31x (int8) / 1.82x (int4) the time of a single one, and
+// a single unit streams a 64-deep K block in about 0.6 us. Split plans whose
+// partial sums exceed max_partial floats are not considered.
+void plan_normal(QProblem& p, int sms, size_t max_partial) {
+  const int num_m = (p.M + 127) / 128;
+  const int num_k = (p.K + kBK - 1) / kBK;
+  const double pair_cost = p.kind == kInt8 ? 1.35 : 1.85;
+  const double unit_us = 0.6 * num_k;
+  // K splits only when even single tiles leave most SMs idle (measured: they
+  // help W8A16 at M = 65..128, N = 11008, and lose once the tiles fill a wave)
+  const int64_t single_units = static_cast<int64_t>(num_m) * ((p.N + kTileN - 1) / kTileN);
+  // (int4 measured no gain at M = 128: its slower dequant already spreads
+  // the weight stream.)
+  const int max_sp = (p.kind == kInt8 && single_units < static_cast<int64_t>(0.6 * sms)) ? 4 : 1;
+  double best = 1e30;
+  for (int pair = 0; pair < 2; ++pair) {
+    const int64_t base = static_cast<int64_t>(num_m) * ((p.N + (kTileN << pair) - 1) / (kTileN << pair));
+    for (int sp = 1; sp <= max_sp && sp <= num_k; ++sp) {
+      const int kbps = (num_k + sp - 1) / sp;
+      const int real = (num_k + kbps - 1) / kbps;
+      if (sp > 1 && real == 1) continue;
+      if (real > 1 && static_cast<size_t>(real) * p.M * p.N > max_partial) continue;
+      if (real > 1 && p.N % 4 != 0) continue;  // partial rows must suit TMA stores
+      const int64_t waves = (base * real + sms - 1) / sms;
+      double t = static_cast<double>(waves) * (pair ? pair_cost : 1.0) * kbps / num_k;
+      if (real > 1) t += (3.0 + real * 8.0 * p.M * p.N / 5e6) / unit_us;
+      if (t < best * 0.98) {
+        best = t;
+        p.pair = pair;
+        p.splits = real;
+        p.kb_per_split = kbps;
+      }
+    }
+  }
+}
+
 // Split K when the output tiles alone cannot fill the SMs (small M): pick the
 // split count whose units fill the persistent grid best, preferring fewer
 // splits (each split adds an M x N fp32 partial write and read).
-void plan_splits(QProblem& p, int sms) {
+void plan_splits(QProblem& p, int sms, size_t max_partial = SIZE_MAX) {
   const bool swap = p.M <= 64;
   const int num_m = swap ? 1 : (p.M + 127) / 128;
   const int num_n = (p.N + kTileN - 1) / kTileN;
@@ -534,15 +575,18 @@ void plan_splits(QProblem& p, int sms) {
   const int base = num_m * num_n;
   p.splits = 1;
   p.kb_per_split = num_k;
+  p.pair = 0;
+  if (!swap) {
+    plan_normal(p, sms, max_partial);
+    return;
+  }
   if (base >= sms || num_k < 2) return;
   // Each split writes and re-reads an M x N fp32 partial: keep that traffic
-  // under a tenth of the weight stream, or, for the swapped small-M layout,
-  // let the partials take up to 48 MB (they stay in L2; measured faster for
-  // M = 16, slower for M = 128 where the extra units and the reduce cost more).
+  // under a tenth of the weight stream, or let the partials take up to 48 MB
+  // (they stay in L2; measured faster for M = 16).
   const double wbytes = (p.kind == kInt8 ? 1.0 : 0.5) * static_cast<double>(p.K) * p.N;
   const double per_split = 4.0 * p.M * p.N;
-  const int max_splits = static_cast<int>(swap ? std::max(0.1 * wbytes / (2.0 * per_split), 48e6 / per_split)
-                                               : 0.1 * wbytes / (2.0 * per_split));
+  const int max_splits = static_cast<int>(std::max(0.1 * wbytes / (2.0 * per_split), 48e6 / per_split));
   if (max_splits < 2) return;
   double best = static_cast<double>(base) / sms;
   for (int sp = 2; sp <= 16 && sp <= num_k && sp <= max_splits; ++sp) {
@@ -602,13 +646,18 @@ int launch_wq(const QProblem& p, cudaStream_t stream) {
   } else {
     tmS = tmX;  // unused
   }
+  // Y (or the split partial sums [splits][M][N]) as a 3-D tensor for TMA
+  // stores of 16 rows x 32 channels.
   CUtensorMap tmY = tmX;
   int y_tma = 0;
-  if (!kSwap && p.splits == 1 && p.ldy % 4 == 0 && (reinterpret_cast<uintptr_t>(p.Y) & 15u) == 0) {
-    uint64_t dims[2] = {static_cast<uint64_t>(p.N), static_cast<uint64_t>(p.M)};
-    uint64_t strides[1] = {static_cast<uint64_t>(p.ldy) * 4};
-    uint32_t box[2] = {32, 16};
-    int rc = encode_tmap(&tmY, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, p.Y, dims, strides, box,
+  const bool split_out = p.splits > 1;
+  float* ybase = split_out ? p.partial : p.Y;
+  const int64_t yld = split_out ? p.N : p.ldy;
+  if (!kSwap && yld % 4 == 0 && (reinterpret_cast<uintptr_t>(ybase) & 15u) == 0) {
+    uint64_t dims[3] = {static_cast<uint64_t>(p.N), static_cast<uint64_t>(p.M), static_cast<uint64_t>(p.splits)};
+    uint64_t strides[2] = {static_cast<uint64_t>(yld) * 4, static_cast<uint64_t>(yld) * 4 * p.M};
+    uint32_t box[3] = {32, 16, 1};
+    int rc = encode_tmap(&tmY, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, ybase, dims, strides, box,
                          CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc != NESO_OK) return rc;
     y_tma = 1;
@@ -946,19 +995,7 @@ int dispatch_wq(const QProblem& p, cudaStream_t stream) {
   if (p.M <= 16) return launch_wq<kQ, true, 16>(p, stream);
   if (p.M <= 32) return launch_wq<kQ, true, 32>(p, stream);
   if (p.M <= 64) return launch_wq<kQ, true, 64>(p, stream);
-  // Pairs of channel tiles per unit: the activation tile is read once per
-  // 256 channels instead of once per 128 and the two convert groups work on
-  // the same K block. Measured on B200 (K = 4096, N = 11008), a paired unit
-  // takes 1.31x (int8) / 1.82x (int4) the time of a single one, so pairs win
-  // unless they leave too few units to fill the waves.
-  const int64_t sms = sm_count();
-  const int64_t num_m = (p.M + 127) / 128;
-  const int64_t single = num_m * ((p.N + 127) / 128), paired = num_m * ((p.N + 255) / 256);
-  const double pair_cost = kQ == kInt8 ? 1.35 : 1.85;
-  if (p.splits == 1 &&
-      pair_cost * static_cast<double>((paired + sms - 1) / sms) < static_cast<double>((single + sms - 1) / sms)) {
-    return launch_wq<kQ, false, 128, 2>(p, stream);
-  }
+  if (p.pair) return launch_wq<kQ, false, 128, 2>(p, stream);
   return launch_wq<kQ, false, 128>(p, stream);
 }
 
@@ -1141,7 +1178,7 @@ int neso_w8a16_matmul_mnk_noalloc(const void* X, const int8_t* W, const void* sc
   q.Y = Y; q.ldy = N;
   q.M = M; q.N = N; q.K = K;
   q.kind = kInt8;
-  plan_splits(q, sm_count());
+  plan_splits(q, sm_count(), kNoAllocScratchFloats);
   const size_t need = q.splits > 1 ? static_cast<size_t>(q.splits) * M * N : 0;
   if (need > kNoAllocScratchFloats) {
     return fail(NESO_ERR_UNSUPPORTED,
