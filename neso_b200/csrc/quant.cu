@@ -22,7 +22,8 @@
 //   warp 1      tcgen05.mma issuer (kind::f16, fp32 accumulator in TMEM,
 //               double-buffered); int4 issues hi and lo MMAs per K step.
 //   warps 8-11  epilogue: TMEM -> registers -> (int8: * f32(scale[n])) -> Y.
-// Orientation: M >= 65 computes Y tiles [128 m x 128 n] with X as the A
+// Orientation: M >= 65 computes Y tiles [128 m x 128 n] (or 128 x 256 with
+// paired channel tiles, 256 x 256 with two accumulators) with X as the A
 // operand; M <= 64 swaps operands (A = dequantised W^T with M' = 128 output
 // channels, B = X with N' = M rounded up to 16/32/64) so decode-sized batches
 // still run on the tensor cores and the weight stream stays at HBM speed.
@@ -44,7 +45,10 @@ template <int kQ, bool kSwap, int kNX, int kNT = 1>
 struct QCfg {
   // kNT = 128-channel weight tiles per unit (2: both convert groups take one
   // tile of every K block and the X tile is used for 256 output channels,
-  // halving the activation traffic per FLOP; large M only).
+  // halving the activation traffic per FLOP; large M only). kNX = activation
+  // rows per unit: 128, or 256 in the M >= 65 layout (two 128-row
+  // accumulators, each fp16 weight stage feeds two MMAs per K step, one
+  // accumulator buffer).
   // Three decoupled rings so weight bytes stay in flight independently of
   // the dequant and MMA rate:
   //   R  raw weight tiles (int8 [64 k][128 n] or packed int4 [32][128] plus
@@ -58,10 +62,13 @@ struct QCfg {
   static constexpr int kNumW16 = (kQ == kInt8) ? 1 : 2;
   static constexpr int kFTileBytes = kNumW16 * kW16Bytes;
   static constexpr int kFBytes = kNT * kFTileBytes;
-  static constexpr int kFStages = kNT == 2 ? (kQ == kInt8 ? 3 : 2) : (kQ == kInt4G128 && !kSwap) ? 3 : 4;
+  // kNX = 256 in the M >= 65 layout: 256-row units, two 128-row accumulators
+  // (every fp16 weight stage feeds two MMAs per K step).
+  static constexpr int kRowHalves = kSwap ? 1 : kNX / 128;
+  static constexpr int kFStages = kRowHalves == 2 ? 2 : kNT == 2 ? (kQ == kInt8 ? 3 : 2) : (kQ == kInt4G128 && !kSwap) ? 3 : 4;
   // X tiles come from L2 with about 2500 cycles of copy latency: a deep
   // ring keeps the MMAs fed when every K block needs a new 16 KB X tile.
-  static constexpr int kXStages = kSwap ? 8 : kNT == 2 ? (kQ == kInt8 ? 4 : 3) : 6;
+  static constexpr int kXStages = kSwap ? 8 : kRowHalves == 2 ? 3 : kNT == 2 ? (kQ == kInt8 ? 4 : 3) : 6;
   static constexpr int kBudget = 220 * 1024;
   // Y staging for TMA stores (M >= 65 layout): 16 rows x 32 fp32 per epilogue warp.
   static constexpr int kOutBytes = kSwap ? 0 : 4 * 2048;
@@ -73,9 +80,10 @@ struct QCfg {
   static constexpr int kOffOut = kOffF + kFStages * kFBytes;
   static constexpr int kOffBars = kOffOut + kOutBytes;
   static constexpr int kRawTx = kNT * ((kQ == kInt8) ? 64 * 128 : 32 * 128 + 256);
-  static constexpr int kAccCols = kSwap ? kNX : kNT * kTileN;   // accumulator columns per buffer
-  static constexpr int kTmemCols = (2 * kAccCols <= 32) ? 32 : (2 * kAccCols <= 64) ? 64
-                                   : (2 * kAccCols <= 128) ? 128 : (2 * kAccCols <= 256) ? 256 : 512;
+  static constexpr int kAccCols = kSwap ? kNX : kRowHalves * kNT * kTileN;  // accumulator columns per buffer
+  static constexpr int kAccBufs = 2 * kAccCols <= 512 ? 2 : 1;
+  static constexpr int kTmemCols = (kAccBufs * kAccCols <= 32) ? 32 : (kAccBufs * kAccCols <= 64) ? 64
+                                   : (kAccBufs * kAccCols <= 128) ? 128 : (kAccBufs * kAccCols <= 256) ? 256 : 512;
   static constexpr int kSmemBytes = kOffBars + 1024 + 1024;
   static_assert(kRStages >= (kNT == 2 ? 3 : 4), "raw ring too shallow");
   static_assert(kXBytes % 1024 == 0 && kRawBytes % 1024 == 0 && kFBytes % 1024 == 0, "1024-aligned stages");
@@ -228,7 +236,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         } else {
           mbar_arrive_expect_tx(&full[s], Cfg::kXBytes);
-          tma_load_2d(sX + s * Cfg::kXBytes, &tmX, &full[s], kb * kBK, kSwap ? 0 : u.mb * 128);
+          tma_load_2d(sX + s * Cfg::kXBytes, &tmX, &full[s], kb * kBK, kSwap ? 0 : u.mb * kNX);
         }
       }
     }
@@ -246,8 +254,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool aborted = false;
     for (int t = blockIdx.x; t < num_units && !aborted; t += gridDim.x, ++tc) {
       const QUnit u = unit_of(t, args);
-      const int buf = tc & 1;
-      const uint32_t use = tc >> 1;
+      const int buf = tc % Cfg::kAccBufs;
+      const uint32_t use = tc / Cfg::kAccBufs;
       if (!mbar_wait(&acc_empty[buf], (use & 1) ^ 1, abort_flag, args.st, 0x2200)) break;
       tc_fence_after();
       const uint32_t d_tmem = tmem + buf * Cfg::kAccCols;
@@ -274,7 +282,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (kSwap) {
               umma_f16_ss(d_tmem, wd, xd, idesc, acc);
             } else {
-              umma_f16_ss(d_tmem, xd, wd, idesc, acc);
+#pragma unroll
+              for (int h = 0; h < Cfg::kRowHalves; ++h) {
+                umma_f16_ss(d_tmem + h * kUnitN, xd + static_cast<uint64_t>((h * 16384) >> 4), wd, idesc, acc);
+              }
             }
           }
         }
@@ -402,8 +413,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       float* ydst = args.partial != nullptr ? args.partial + static_cast<int64_t>(u.ks) * args.M * args.N : args.Y;
       const int64_t ld = args.partial != nullptr ? args.N : args.ldy;
       const __half* csc = args.partial != nullptr ? nullptr : args.chan_scale;
-      const int buf = tc & 1;
-      const uint32_t use = tc >> 1;
+      const int buf = tc % Cfg::kAccBufs;
+      const uint32_t use = tc / Cfg::kAccBufs;
       if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[buf], use & 1, abort_flag, args.st, 0x2400))) break;
       tc_fence_after();
       const uint32_t acc = lane_base + buf * Cfg::kAccCols;
@@ -435,11 +446,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         // time) and TMA stores: full-line writes instead of one 4-byte store
         // per row and channel, which left the L1 busy with the epilogue.
         uint8_t* stage = smem + Cfg::kOffOut + (warp - 8) * 2048;
-        const int m0 = mb * 128 + static_cast<int>(q) * 32;
 #pragma unroll 1
-        for (int c = 0; c < kUnitN / 32; ++c) {
+        for (int hc = 0; hc < Cfg::kRowHalves * (kUnitN / 32); ++hc) {
+          const int h = hc / (kUnitN / 32), c = hc % (kUnitN / 32);
+          const int m0 = mb * kNX + h * 128 + static_cast<int>(q) * 32;
           uint32_t r[32];
-          tmem_ld32(acc + c * 32, r);
+          tmem_ld32(acc + h * kUnitN + c * 32, r);
           tmem_wait_ld();
           const int n0 = nb * kUnitN + c * 32;
           if (csc != nullptr) {
@@ -470,12 +482,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       } else {
-        const int m = mb * 128 + lrow;
-        float* yrow = ydst + static_cast<int64_t>(m) * ld;
 #pragma unroll 1
-        for (int c = 0; c < kUnitN / 32; ++c) {
+        for (int hc = 0; hc < Cfg::kRowHalves * (kUnitN / 32); ++hc) {
+          const int h = hc / (kUnitN / 32), c = hc % (kUnitN / 32);
+          const int m = mb * kNX + h * 128 + lrow;
+          float* yrow = ydst + static_cast<int64_t>(m) * ld;
           uint32_t r[32];
-          tmem_ld32(acc + c * 32, r);
+          tmem_ld32(acc + h * kUnitN + c * 32, r);
           tmem_wait_ld();
           const int n0 = nb * kUnitN + c * 32;
           if (m < args.M) {
@@ -519,44 +532,51 @@ struct QProblem {
   // split-K plan (filled by plan_splits) and the fp32 partial-sum buffer
   int splits = 1;
   int kb_per_split = 0;
-  int pair = 0;  // M >= 65 layout: two 128-channel tiles per unit
+  int pair = 0;   // M >= 65 layout: two 128-channel tiles per unit
+  int rows2 = 0;  // paired units of 256 rows (two accumulators), W8A16 only
   float* partial = nullptr;
   DevStatus st{};
 };
 
-// M >= 65 layout: choose single or paired channel tiles and a K split from a
-// cost model in units of one single-tile, whole-K unit: waves x unit cost x
-// share of K, plus the split-K cost (a reduce launch and the partial sums'
-// write and read, at HBM speed). Measured on B200 (K = 4096, N = 11008): a
-// paired unit takes 1.31x (int8) / 1.82x (int4) the time of a single one, and
-// a single unit streams a 64-deep K block in about 0.6 us. Split plans whose
-// partial sums exceed max_partial floats are not considered.
+// M >= 65 layout: choose the unit shape and a K split from a cost model in
+// units of one 128 x 128, whole-K unit: waves x unit cost x share of K, plus
+// the split-K cost (a reduce launch and the partial sums' write and read, at
+// HBM speed). Measured on B200 (K = 4096, N = 11008) relative to a single
+// unit: 128 rows x 256 channels (paired tiles) 1.31-1.42x (int8) / 1.82x
+// (int4); 256 x 256 (W8A16) 1.9-2.0x; a single unit streams a 64-deep K
+// block in about 0.6 us. Split plans whose partial sums exceed max_partial
+// floats are not considered.
 void plan_normal(QProblem& p, int sms, size_t max_partial) {
-  const int num_m = (p.M + 127) / 128;
   const int num_k = (p.K + kBK - 1) / kBK;
-  const double pair_cost = p.kind == kInt8 ? 1.35 : 1.85;
   const double unit_us = 0.6 * num_k;
   // K splits only when even single tiles leave most SMs idle (measured: they
-  // help W8A16 at M = 65..128, N = 11008, and lose once the tiles fill a wave)
-  const int64_t single_units = static_cast<int64_t>(num_m) * ((p.N + kTileN - 1) / kTileN);
-  // (int4 measured no gain at M = 128: its slower dequant already spreads
-  // the weight stream.)
+  // help W8A16 at M = 65..128, N = 11008, and lose once the tiles fill a
+  // wave; W4A16 measured no gain at M = 128).
+  const int64_t single_units = static_cast<int64_t>((p.M + 127) / 128) * ((p.N + kTileN - 1) / kTileN);
   const int max_sp = (p.kind == kInt8 && single_units < static_cast<int64_t>(0.6 * sms)) ? 4 : 1;
+  // 256-row units keep Y whole-tile TMA stores (aligned Y) and no K split.
+  const bool rows2_ok = p.kind == kInt8 && p.M > 128 && p.ldy % 4 == 0 && (reinterpret_cast<uintptr_t>(p.Y) & 15u) == 0;
+  struct Shape { int rows, chans, pair, rows2; double cost; };
+  const Shape shapes[3] = {{128, 128, 0, 0, 1.0},
+                           {128, 256, 1, 0, p.kind == kInt8 ? 1.35 : 1.85},
+                           {256, 256, 1, 1, 1.95}};
   double best = 1e30;
-  for (int pair = 0; pair < 2; ++pair) {
-    const int64_t base = static_cast<int64_t>(num_m) * ((p.N + (kTileN << pair) - 1) / (kTileN << pair));
-    for (int sp = 1; sp <= max_sp && sp <= num_k; ++sp) {
+  for (const Shape& sh : shapes) {
+    if (sh.rows2 && !rows2_ok) continue;
+    const int64_t base = static_cast<int64_t>((p.M + sh.rows - 1) / sh.rows) * ((p.N + sh.chans - 1) / sh.chans);
+    for (int sp = 1; sp <= (sh.rows2 ? 1 : max_sp) && sp <= num_k; ++sp) {
       const int kbps = (num_k + sp - 1) / sp;
       const int real = (num_k + kbps - 1) / kbps;
       if (sp > 1 && real == 1) continue;
       if (real > 1 && static_cast<size_t>(real) * p.M * p.N > max_partial) continue;
       if (real > 1 && p.N % 4 != 0) continue;  // partial rows must suit TMA stores
       const int64_t waves = (base * real + sms - 1) / sms;
-      double t = static_cast<double>(waves) * (pair ? pair_cost : 1.0) * kbps / num_k;
+      double t = static_cast<double>(waves) * sh.cost * kbps / num_k;
       if (real > 1) t += (3.0 + real * 8.0 * p.M * p.N / 5e6) / unit_us;
       if (t < best * 0.98) {
         best = t;
-        p.pair = pair;
+        p.pair = sh.pair;
+        p.rows2 = sh.rows2;
         p.splits = real;
         p.kb_per_split = kbps;
       }
@@ -576,6 +596,7 @@ void plan_splits(QProblem& p, int sms, size_t max_partial = SIZE_MAX) {
   p.splits = 1;
   p.kb_per_split = num_k;
   p.pair = 0;
+  p.rows2 = 0;
   if (!swap) {
     plan_normal(p, sms, max_partial);
     return;
@@ -671,7 +692,7 @@ int launch_wq(const QProblem& p, cudaStream_t stream) {
   args.M = p.M;
   args.N = p.N;
   args.K = p.K;
-  args.num_m = kSwap ? 1 : (p.M + 127) / 128;
+  args.num_m = kSwap ? 1 : (p.M + kNX - 1) / kNX;
   args.num_n = (p.N + kNT * kTileN - 1) / (kNT * kTileN);
   args.num_k = (p.K + kBK - 1) / kBK;
   args.splits = p.splits;
@@ -995,6 +1016,9 @@ int dispatch_wq(const QProblem& p, cudaStream_t stream) {
   if (p.M <= 16) return launch_wq<kQ, true, 16>(p, stream);
   if (p.M <= 32) return launch_wq<kQ, true, 32>(p, stream);
   if (p.M <= 64) return launch_wq<kQ, true, 64>(p, stream);
+  if constexpr (kQ == kInt8) {
+    if (p.rows2) return launch_wq<kQ, false, 256, 2>(p, stream);
+  }
   if (p.pair) return launch_wq<kQ, false, 128, 2>(p, stream);
   return launch_wq<kQ, false, 128>(p, stream);
 }

@@ -114,6 +114,16 @@ def test_paired_channel_tiles_ragged(dev, kind):
     torch.testing.assert_close(y.cpu(), ref, **TOL)
 
 
+def test_w8a16_256_row_units_ragged(dev):
+    # 5 row blocks of 256 x 29 channel pairs = 145 units (one wave; 128-row
+    # pairs would take two): the two-accumulator layout runs, its last row
+    # block holding 76 rows (second 128-row half empty) and K = 3 blocks.
+    M, N, K = 1100, 7424, 192
+    x, w, s = _w8(M, N, K, seed=11)
+    y = ops.w8a16_matmul(x.to(dev), w.to(dev), s.to(dev))
+    torch.testing.assert_close(y.cpu(), oracle.w8a16_matmul(x, w, s), **TOL)
+
+
 def test_product_pack_matches_oracle_layout(dev):
     q = torch.randint(-8, 8, (256, 64), dtype=torch.int8)
     assert torch.equal(ops.pack_int4(q), oracle.pack_int4(q))
