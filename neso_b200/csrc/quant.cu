@@ -9,22 +9,25 @@
 // grouped dequant of tests/test_advanced12.py:69-84.
 //
 // One persistent CTA per SM; per 64-deep K block ("stage"):
-//   warp 0      TMA: raw weight tile (int8 [64 k][128 n] or packed int4
-//               [32 byte-rows][128 n], 128-byte swizzled), the fp16
-//               activation tile, and (int4) the group's fp16 scale row.
+//   warp 0      TMA: raw weight tile(s) (int8 [64 k][128 n] or packed int4
+//               [32 byte-rows][128 n], 128-byte swizzled) and (int4) the
+//               group's fp16 scale row; warp 3: TMA of the fp16 activation tile.
 //   warps 4-7,  dequantise raw -> fp16 directly into the MN-major 128-byte
 //   12-15       swizzled layout tcgen05 reads; fence.proxy.async; arrive. The
-//               two groups take alternate K blocks.
+//               two groups take alternate K blocks (or, with two channel
+//               tiles per unit, one tile each of every K block).
 //                 int8: exact, (b ^ 0x80) | 0x6400 as fp16 is 1024 + b + 128.
 //                 int4: q exact the same way, then w = q * s is split into
 //                 w_hi = fp16(q * s) and w_lo = fma(q, s, -w_hi) (the exact
 //                 rounding error), so the MMA sums q * s without rounding it.
-//   warp 1      tcgen05.mma issuer (kind::f16, fp32 accumulator in TMEM,
-//               double-buffered); int4 issues hi and lo MMAs per K step.
-//   warps 8-11  epilogue: TMEM -> registers -> (int8: * f32(scale[n])) -> Y.
-// Orientation: M >= 65 computes Y tiles [128 m x 128 n] (or 128 x 256 with
-// paired channel tiles, 256 x 256 with two accumulators) with X as the A
-// operand; M <= 64 swaps operands (A = dequantised W^T with M' = 128 output
+//   warp 1      tcgen05.mma issuer (kind::f16, fp32 accumulators in TMEM);
+//               int4 issues hi and lo MMAs per K step.
+//   warps 8-11  epilogue: TMEM -> registers -> (int8: * f32(scale[n])) ->
+//               swizzled staging -> TMA stores of Y (M >= 65 layout), or
+//               direct coalesced stores (M <= 64 layout).
+// Orientation: M >= 65 computes Y units of 128 or 256 rows x 128 or 256
+// channels (a host cost model picks the shape and any K split) with X as the
+// A operand; M <= 64 swaps operands (A = dequantised W^T with M' = 128 output
 // channels, B = X with N' = M rounded up to 16/32/64) so decode-sized batches
 // still run on the tensor cores and the weight stream stays at HBM speed.
 #include <algorithm>
@@ -533,7 +536,7 @@ struct QProblem {
   int splits = 1;
   int kb_per_split = 0;
   int pair = 0;   // M >= 65 layout: two 128-channel tiles per unit
-  int rows2 = 0;  // paired units of 256 rows (two accumulators), W8A16 only
+  int rows2 = 0;  // units of 256 rows (two accumulators): W8A16 paired, W4A16 single
   float* partial = nullptr;
   DevStatus st{};
 };
@@ -543,8 +546,8 @@ struct QProblem {
 // the split-K cost (a reduce launch and the partial sums' write and read, at
 // HBM speed). Measured on B200 (K = 4096, N = 11008) relative to a single
 // unit: 128 rows x 256 channels (paired tiles) 1.31-1.42x (int8) / 1.82x
-// (int4); 256 x 256 (W8A16) 1.9-2.0x; a single unit streams a 64-deep K
-// block in about 0.6 us. Split plans whose partial sums exceed max_partial
+// (int4); 256 x 256 (W8A16) 1.9-2.0x; 256 x 128 (W4A16) 1.4x; a single unit
+// streams a 64-deep K block in about 0.6 us. Split plans whose partial sums exceed max_partial
 // floats are not considered.
 void plan_normal(QProblem& p, int sms, size_t max_partial) {
   const int num_k = (p.K + kBK - 1) / kBK;
@@ -555,14 +558,16 @@ void plan_normal(QProblem& p, int sms, size_t max_partial) {
   const int64_t single_units = static_cast<int64_t>((p.M + 127) / 128) * ((p.N + kTileN - 1) / kTileN);
   const int max_sp = (p.kind == kInt8 && single_units < static_cast<int64_t>(0.6 * sms)) ? 4 : 1;
   // 256-row units keep Y whole-tile TMA stores (aligned Y) and no K split.
-  const bool rows2_ok = p.kind == kInt8 && p.M > 128 && p.ldy % 4 == 0 && (reinterpret_cast<uintptr_t>(p.Y) & 15u) == 0;
-  struct Shape { int rows, chans, pair, rows2; double cost; };
-  const Shape shapes[3] = {{128, 128, 0, 0, 1.0},
-                           {128, 256, 1, 0, p.kind == kInt8 ? 1.35 : 1.85},
-                           {256, 256, 1, 1, 1.95}};
+  const bool rows2_ok = p.M > 128 && p.ldy % 4 == 0 && (reinterpret_cast<uintptr_t>(p.Y) & 15u) == 0;
+  const bool w8 = p.kind == kInt8;
+  struct Shape { int rows, chans, pair, rows2; double cost; bool ok; };
+  const Shape shapes[4] = {{128, 128, 0, 0, 1.0, true},
+                           {128, 256, 1, 0, w8 ? 1.35 : 1.85, true},
+                           {256, 256, 1, 1, 1.95, w8},
+                           {256, 128, 0, 1, 1.42, !w8}};
   double best = 1e30;
   for (const Shape& sh : shapes) {
-    if (sh.rows2 && !rows2_ok) continue;
+    if (!sh.ok || (sh.rows2 && !rows2_ok)) continue;
     const int64_t base = static_cast<int64_t>((p.M + sh.rows - 1) / sh.rows) * ((p.N + sh.chans - 1) / sh.chans);
     for (int sp = 1; sp <= (sh.rows2 ? 1 : max_sp) && sp <= num_k; ++sp) {
       const int kbps = (num_k + sp - 1) / sp;
@@ -1016,8 +1021,14 @@ int dispatch_wq(const QProblem& p, cudaStream_t stream) {
   if (p.M <= 16) return launch_wq<kQ, true, 16>(p, stream);
   if (p.M <= 32) return launch_wq<kQ, true, 32>(p, stream);
   if (p.M <= 64) return launch_wq<kQ, true, 64>(p, stream);
-  if constexpr (kQ == kInt8) {
-    if (p.rows2) return launch_wq<kQ, false, 256, 2>(p, stream);
+  if (p.rows2) {
+    // 256-row units: W8A16 with paired channel tiles (256 x 256), W4A16 with
+    // one tile (256 x 128; its hi/lo fp16 copies leave no room for pairs).
+    if constexpr (kQ == kInt8) {
+      return launch_wq<kQ, false, 256, 2>(p, stream);
+    } else {
+      return launch_wq<kQ, false, 256, 1>(p, stream);
+    }
   }
   if (p.pair) return launch_wq<kQ, false, 128, 2>(p, stream);
   return launch_wq<kQ, false, 128>(p, stream);

@@ -81,6 +81,20 @@ def test_reference_style_launch_with_strides(dev):
     assert torch.all(c[:, N:] == 0)
 
 
+def test_c_row_stride_not_multiple_of_4_uses_row_stores(dev):
+    # stride_cm = N + 1 floats: C rows are not 16-byte aligned, so the
+    # epilogue cannot use TMA stores and writes rows directly.
+    M, N, K = 384, 512, 256
+    a, b = _inputs(M, N, K, seed=13)
+    c = torch.full((M, N + 1), 5.0, device=dev)
+    grid = lambda meta: ((meta["M"] + meta["BLOCK_M"] - 1) // meta["BLOCK_M"],
+                         (meta["N"] + meta["BLOCK_N"] - 1) // meta["BLOCK_N"], 1)
+    kernels.matmul_kernel[grid](a.to(dev), b.to(dev), c, M, N, K, K, 1, N, 1, N + 1, 1, BLOCK_M=128, BLOCK_N=64,
+                                BLOCK_K=32)
+    torch.testing.assert_close(c[:, :N].cpu(), oracle.gemm(a, b), **TOL)
+    assert torch.all(c[:, N:] == 5.0)
+
+
 def test_matmul_tiled_reference_signature(dev):
     # bench/bench_matmul.py:79-81: matmul_kernel(a, b, c, K, stride_am, stride_bk, stride_cm), grid (M/BM, N/BN)
     M, N, K = 256, 256, 128

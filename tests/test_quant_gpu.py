@@ -124,6 +124,29 @@ def test_w8a16_256_row_units_ragged(dev):
     torch.testing.assert_close(y.cpu(), oracle.w8a16_matmul(x, w, s), **TOL)
 
 
+def test_w4a16_256_row_units_ragged(dev):
+    # 5 row blocks of 256 x 17 channel tiles = 85 units (one wave; 128-row
+    # units would take two): the two-accumulator W4A16 layout, last row
+    # block holding 76 rows, two quantisation groups along K.
+    M, N, K = 1100, 2176, 256
+    x, q, s = _w4(M, N, K, seed=12)
+    wq = oracle.pack_int4(q)
+    y = ops.w4a16_g128_matmul(x.to(dev), wq.to(dev), s.to(dev))
+    torch.testing.assert_close(y.cpu(), oracle.w4a16_g128_matmul(x, wq, s), **TOL)
+
+
+def test_w8a16_c_row_stride_not_multiple_of_4(dev):
+    # Reference launch with stride_cm = N + 1: Y rows are not 16-byte aligned,
+    # so the M >= 65 epilogue writes rows directly instead of TMA stores.
+    M, N, K = 256, 384, 256
+    x, w, s = _w8(M, N, K, seed=21)
+    c = torch.full((M, N + 1), 3.0, device=dev)
+    kernels.w8a16_scaled_matmul[(M // 64, N // 64, 1)](x.to(dev), w.to(dev), c, s.to(dev), K, K, N, N + 1,
+                                                       BM=64, BN=64, BK=32)
+    torch.testing.assert_close(c[:, :N].cpu(), oracle.w8a16_matmul(x, w, s), **TOL)
+    assert torch.all(c[:, N:] == 3.0)
+
+
 def test_product_pack_matches_oracle_layout(dev):
     q = torch.randint(-8, 8, (256, 64), dtype=torch.int8)
     assert torch.equal(ops.pack_int4(q), oracle.pack_int4(q))
