@@ -947,6 +947,30 @@ __global__ void __launch_bounds__(GvCfg<kQ, kM>::kThreads, 1) wq_gemv_kernel(GvA
   if (threadIdx.x == 0) a.counters[cb] = 0;  // ready for the next launch on this stream
 }
 
+// Work split of the small-M path: channel blocks, stored rows per K slice and
+// slices. One wave of one CTA per SM: the K slices per channel block fill the
+// SMs, and few slices keep the final in-order sum short. `fits`: the slice of
+// X staged in the reduction buffer fits in shared memory.
+struct GvPlan {
+  int nblk, rows_per_slice, slices;
+  bool fits;
+};
+template <int kQ, int kM>
+GvPlan gemv_plan(const QProblem& p) {
+  using Cfg = GvCfg<kQ, kM>;
+  GvPlan g{};
+  const int rows = kQ == kInt8 ? p.K : p.K / 2;
+  g.nblk = (p.N + kGvChannels - 1) / kGvChannels;
+  const int want = std::max(1, sm_count() / g.nblk);
+  const int unit = 4 * Cfg::kWarps;  // rows per slice: a whole number of 4-row batches per warp
+  int rps = (rows + want - 1) / want;
+  rps = (rps + unit - 1) / unit * unit;
+  g.rows_per_slice = rps;
+  g.slices = (rows + rps - 1) / rps;
+  g.fits = static_cast<int64_t>(kM) * (kQ == kInt8 ? 1 : 2) * rps * 4 <= Cfg::kSmemBytes && g.slices <= 65535;
+  return g;
+}
+
 template <int kQ, int kM>
 int launch_gemv(const QProblem& p, cudaStream_t stream) {
   using Cfg = GvCfg<kQ, kM>;
@@ -965,20 +989,10 @@ int launch_gemv(const QProblem& p, cudaStream_t stream) {
   auto kern = wq_gemv_kernel<kQ, kM>;
   int rc = kernel_setup(reinterpret_cast<const void*>(kern), Cfg::kSmemBytes, nullptr);
   if (rc != NESO_OK) return rc;
-  // One wave of one CTA per SM: the K slices per channel block fill the SMs,
-  // and few slices keep the final in-order sum short.
-  const int nblk = (p.N + kGvChannels - 1) / kGvChannels;
-  const int want = std::max(1, sm_count() / nblk);
-  const int unit = 4 * Cfg::kWarps;  // rows per slice: a whole number of 4-row batches per warp
-  int rps = (a.rows + want - 1) / want;
-  rps = (rps + unit - 1) / unit * unit;
-  a.rows_per_slice = rps;
-  const int slices = (a.rows + rps - 1) / rps;
-  // The slice of X is staged in the reduction buffer.
-  if (static_cast<int64_t>(kM) * (kQ == kInt8 ? 1 : 2) * rps * 4 > Cfg::kSmemBytes) {
-    return fail(NESO_ERR_UNSUPPORTED, "K slice too long for the small-M path");
-  }
-  if (slices > 65535) return fail(NESO_ERR_UNSUPPORTED, "K too large for the small-M path");
+  const GvPlan g = gemv_plan<kQ, kM>(p);
+  if (!g.fits) return fail(NESO_ERR_UNSUPPORTED, "K slice too long for the small-M path");
+  const int nblk = g.nblk, slices = g.slices;
+  a.rows_per_slice = g.rows_per_slice;
   if (slices > 1) {
     void* ws = nullptr;
     rc = stream_workspace(stream, static_cast<size_t>(slices) * p.M * p.N * sizeof(float), &ws);
@@ -1002,8 +1016,15 @@ bool gemv_eligible(const QProblem& p) {
   const int nblk = (p.N + kGvChannels - 1) / kGvChannels;
   // int4 reads each lane's 16 group scales with two 16-byte loads.
   const bool scales_ok = p.kind == kInt8 || (reinterpret_cast<uintptr_t>(p.scale) & 15u) == 0;
-  return p.M <= max_m && p.N % 16 == 0 && p.ldw % 16 == 0 && (reinterpret_cast<uintptr_t>(p.W) & 15u) == 0 &&
-         scales_ok && nblk <= kGemvCounterEnd - kGemvCounterBase;
+  if (!(p.M <= max_m && p.N % 16 == 0 && p.ldw % 16 == 0 && (reinterpret_cast<uintptr_t>(p.W) & 15u) == 0 &&
+        scales_ok && nblk <= kGemvCounterEnd - kGemvCounterBase)) {
+    return false;
+  }
+  // Long K: a slice of X must fit in shared memory, else the tensor-core path runs.
+  if (p.kind == kInt8) {
+    return p.M == 1 ? gemv_plan<kInt8, 1>(p).fits : p.M == 2 ? gemv_plan<kInt8, 2>(p).fits : gemv_plan<kInt8, 4>(p).fits;
+  }
+  return p.M == 1 ? gemv_plan<kInt4G128, 1>(p).fits : gemv_plan<kInt4G128, 2>(p).fits;
 }
 
 int run_gemv(const QProblem& p, cudaStream_t stream) {

@@ -47,6 +47,22 @@ def test_w4a16_small_m(dev, M, N, K):
     torch.testing.assert_close(y.cpu(), oracle.w4a16_g128_matmul(x, wq, s), **TOL)
 
 
+@pytest.mark.parametrize("kind,M,K", [("w8", 4, 16384), ("w4", 2, 32768)])
+def test_long_k_small_m_falls_back_to_tensor_cores(dev, kind, M, K):
+    # Few channel blocks and a long K make each CTA's slice of X too large to
+    # stage in shared memory; the call must still succeed (tensor-core path).
+    N = 11008
+    if kind == "w8":
+        x, w, s = _w8(M, N, K, seed=K + M)
+        y = ops.w8a16_matmul(x.to(dev), w.to(dev), s.to(dev))
+        ref = oracle.w8a16_matmul(x, w, s)
+    else:
+        x, wq, s = _w4(M, N, K, seed=K + M)
+        y = ops.w4a16_g128_matmul(x.to(dev), wq.to(dev), s.to(dev))
+        ref = oracle.w4a16_g128_matmul(x, wq, s)
+    torch.testing.assert_close(y.cpu(), ref, **TOL)
+
+
 def test_small_m_is_bit_reproducible(dev):
     # The K slices are added in a fixed order by the last CTA of each block.
     x, w, s = _w8(1, 11008, 4096, seed=5)
