@@ -20,6 +20,8 @@
 //            SM (256 TMEM columns, 82 KB of shared memory each): the tiles
 //            of the two CTAs overlap as the ping-pong pair does, and one
 //            CTA's prologue and epilogue run under the other's main loop.
+//            Causal D = 64 runs fa2_pair_kernel: the same one-tile CTA
+//            processing tiles qb and nq-1-qb one after the other.
 //   D = 128  fa2_persistent_kernel: one two-tile CTA per SM walks units
 //            handed out from a per-launch counter.
 // The description below is of the two-tile form; the one-tile form drops
@@ -585,6 +587,452 @@ __global__ void __launch_bounds__(FaCfg<D, kT>::kThreads, FaCfg<D, kT>::min_bloc
         }
       }
     }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem, Cfg::kTmemCols);
+  }
+}
+
+// Two query tiles of one head per CTA, one after the other (tiles bx and
+// nq-1-bx: under causal masking every CTA then has nq+1 key blocks), used
+// for causal attention (measured: S=2048 494 -> 515 TFLOP/s, S=512 214 ->
+// 231; without masking it gains nothing at S=2048 and loses at S=384). Same
+// roles and TMEM layout as the one-tile kernel; the CTA's prologue and
+// launch are paid once per two tiles, the second tile's first QK runs while
+// the first tile's epilogue drains O, and O leaves through a dedicated
+// staging area (the K/V ring is busy with the next tile by then). Every
+// mbarrier phase runs over the CTA's blocks of both tiles (running block
+// index g); q_empty hands the single Q buffer to the next tile's load after
+// the last QK, o_free the O columns to the next tile's first PV after the
+// epilogue has read them.
+template <int D, bool kCausal, int kBias>
+__global__ void __launch_bounds__(FaCfg<D, 1>::kThreads, 2)
+    fa2_pair_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
+                    FaArgs a) {
+  using Cfg = FaCfg<D, 1>;
+  constexpr int kT = 1;
+  constexpr int KS = Cfg::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sK = sQ + Cfg::kTileBytes;                // KS tiles
+  uint8_t* sV = sK + KS * Cfg::kTileBytes;           // KS tiles
+  uint8_t* sOut = sV + KS * Cfg::kTileBytes;         // 4 KB per softmax warp
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sOut + 4 * 4096);
+  uint64_t* q_full = bars;
+  uint64_t* q_empty = bars + 1;
+  uint64_t* k_full = bars + 2;
+  uint64_t* k_empty = k_full + KS;
+  uint64_t* v_full = k_empty + KS;
+  uint64_t* v_empty = v_full + KS;
+  uint64_t* s_full = v_empty + KS;   // [1]
+  uint64_t* p_full = s_full + 1;     // [1]
+  uint64_t* o_done = p_full + 1;     // [1]
+  uint64_t* s_free = o_done + 1;     // [1] softmax has read S (4 warps)
+  uint64_t* o_free = s_free + 1;     // [1] epilogue has read O (4 warps)
+  uint64_t* mma_done = o_free + 1;   // [2] one per MMA issuer
+  uint64_t* turn = mma_done + 2;     // unused (one tile at a time)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(turn + 8);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* never_flag = abort_flag + 1;  // stays 0: drain waits ignore the abort
+
+  const uint32_t warp = warp_id();
+  const uint32_t lane = lane_id();
+  const int S = a.S;
+  const int nq = a.num_qblocks;
+  const int bx = static_cast<int>(blockIdx.x);
+  const int bh = blockIdx.y;
+  const int nkv = (S + 127) / 128;
+  const int ntiles = (nq - 1 - bx != bx) ? 2 : 1;
+  auto tile_qb = [&](int qt) { return qt == 0 ? nq - 1 - bx : bx; };  // heavier tile first under causal
+  auto tile_blocks = [&](int qt) { return kCausal ? min(nkv, tile_qb(qt) + 1) : nkv; };
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    mbar_init(q_empty, 1);
+    for (int s = 0; s < KS; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(p_full, 4);
+    mbar_init(o_done, 1);
+    mbar_init(s_free, 4);
+    mbar_init(o_free, 4);
+    mbar_init(&mma_done[0], 1);
+    mbar_init(&mma_done[1], 1);
+    *abort_flag = 0;
+    *never_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+    tma_prefetch_desc(&tmO);
+  }
+  if (warp == 2) {
+    tmem_alloc(tmem_slot, Cfg::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  DevStatus quiet = a.st;
+  quiet.word = nullptr;
+  if (warp < 4) {
+    setmaxnreg_dec<Cfg::regs_low()>();
+    if (warp == 0 && lane == 0) {
+      // ------------------------------------------------------------ producer --
+      int g = 0;        // K/V blocks issued
+      int q_issued = 0;
+      bool aborted = false;
+      for (int qt = 0; qt < ntiles && !aborted; ++qt) {
+        if (qt > 0 && !mbar_wait(q_empty, (qt - 1) & 1, abort_flag, a.st, 0x1104)) { aborted = true; break; }
+        mbar_arrive_expect_tx(q_full, Cfg::kTileBytes);
+#pragma unroll
+        for (int c = 0; c < Cfg::kChunks; ++c) {
+          tma_load_3d(sQ + c * 16384, &tmQ, q_full, c * 64, tile_qb(qt) * 128, bh);
+        }
+        q_issued = qt + 1;
+        const int n = tile_blocks(qt);
+        for (int j = 0; j < n; ++j, ++g) {
+          const int s = g % KS;
+          const uint32_t ph = (g / KS) & 1;
+          if (!mbar_wait(&k_empty[s], ph ^ 1, abort_flag, a.st, 0x1100)) { aborted = true; break; }
+          mbar_arrive_expect_tx(&k_full[s], Cfg::kTileBytes);
+#pragma unroll
+          for (int c = 0; c < Cfg::kChunks; ++c) {
+            tma_load_3d(sK + s * Cfg::kTileBytes + c * 16384, &tmK, &k_full[s], c * 64, j * 128, bh);
+          }
+          if (!mbar_wait(&v_empty[s], ph ^ 1, abort_flag, a.st, 0x1101)) {
+            mbar_wait(&k_full[s], ph, never_flag, quiet, 0);  // K is in flight; V is not
+            aborted = true;
+            break;
+          }
+          mbar_arrive_expect_tx(&v_full[s], Cfg::kTileBytes);
+#pragma unroll
+          for (int c = 0; c < Cfg::kChunks; ++c) {
+            tma_load_3d(sV + s * Cfg::kTileBytes + c * 16384, &tmV, &v_full[s], c * 64, j * 128, bh);
+          }
+        }
+      }
+      if (aborted) {
+        // Drain this CTA's own copies still in flight before it exits.
+        if (q_issued > 0) mbar_wait(q_full, (q_issued - 1) & 1, never_flag, quiet, 0);
+        for (int i = (g > KS ? g - KS : 0); i < g; ++i) {
+          mbar_wait(&k_full[i % KS], (i / KS) & 1, never_flag, quiet, 0);
+          mbar_wait(&v_full[i % KS], (i / KS) & 1, never_flag, quiet, 0);
+        }
+      }
+    } else if (warp == 1 && lane == 0) {
+      // -------------------------------------------------------- QK issuer --
+      constexpr uint32_t idesc_qk = idesc_f16_f32(128, 128, 0, 0);
+      const uint64_t q_desc0 = sdesc_sw128(smem_u32(sQ), 16, 1024);
+      const uint64_t k_desc0 = sdesc_sw128(smem_u32(sK), 16, 1024);
+      int g = 0;
+      bool ok_run = true;
+      for (int qt = 0; qt < ntiles && ok_run; ++qt) {
+        if (!mbar_wait(q_full, qt & 1, abort_flag, a.st, 0x1200)) break;
+        const int n = tile_blocks(qt);
+        for (int j = 0; j < n; ++j, ++g) {
+          const int s = g % KS;
+          if (!mbar_wait(&k_full[s], (g / KS) & 1, abort_flag, a.st, 0x1213)) { ok_run = false; break; }
+          // S may be overwritten once the softmax holds the previous S in registers.
+          if (g > 0 && !mbar_wait(s_free, (g - 1) & 1, abort_flag, a.st, 0x1218)) { ok_run = false; break; }
+          tc_fence_after();
+          const uint64_t kd = k_desc0 + static_cast<uint64_t>((s * Cfg::kTileBytes) >> 4);
+#pragma unroll
+          for (int k = 0; k < D / 16; ++k) {
+            const uint64_t off = static_cast<uint64_t>(((k >> 2) * 16384 + (k & 3) * 32) >> 4);
+            umma_f16_ss(tmem + Cfg::s_col(0), q_desc0 + off, kd + off, idesc_qk, k > 0 ? 1u : 0u);
+          }
+          umma_commit(s_full);
+          umma_commit(&k_empty[s]);
+        }
+        if (ok_run) umma_commit(q_empty);  // Q buffer free once this tile's QKs finish
+      }
+      umma_commit(&mma_done[0]);
+      mbar_wait(&mma_done[0], 0, never_flag, quiet, 0);
+    } else if (warp == 3 && lane == 0) {
+      // -------------------------------------------------------- PV issuer --
+      constexpr uint32_t idesc_pv = idesc_f16_f32(128, D, 0, 1);
+      const uint64_t v_desc0 = sdesc_sw128(smem_u32(sV), 16384, 1024);
+      int g = 0;
+      bool ok_run = true;
+      for (int qt = 0; qt < ntiles && ok_run; ++qt) {
+        const int n = tile_blocks(qt);
+        for (int j = 0; j < n; ++j, ++g) {
+          const int s = g % KS;
+          if (!mbar_wait(&v_full[s], (g / KS) & 1, abort_flag, a.st, 0x1212)) { ok_run = false; break; }
+          // The first PV of a tile overwrites O: the previous tile's epilogue must have read it.
+          if (j == 0 && qt > 0 && !mbar_wait(o_free, (qt - 1) & 1, abort_flag, a.st, 0x1222)) { ok_run = false; break; }
+          if (!mbar_wait(p_full, g & 1, abort_flag, a.st, 0x1210)) { ok_run = false; break; }
+          tc_fence_after();
+          const uint64_t vd = v_desc0 + static_cast<uint64_t>((s * Cfg::kTileBytes) >> 4);
+          const uint32_t p_tmem = tmem + Cfg::p_col(0);
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            umma_f16_ts(tmem + Cfg::o_col(0), p_tmem + (k >> 2) * Cfg::kPHalfStride + (k & 3) * 8,
+                        vd + static_cast<uint64_t>((k * 2048) >> 4), idesc_pv, (j > 0 || k > 0) ? 1u : 0u);
+          }
+          umma_commit(o_done);
+          umma_commit(&v_empty[s]);
+        }
+      }
+      umma_commit(&mma_done[1]);
+      mbar_wait(&mma_done[1], 0, never_flag, quiet, 0);
+    }
+  } else {
+    // ------------------------------------------------- softmax / epilogue --
+    setmaxnreg_inc<kRegsHigh>();
+    const int t = 0;
+    const uint32_t q = warp & 3;
+    const int row = q * 32 + lane;
+    const uint32_t lane_base = tmem + ((q * 32) << 16);
+    const int h = bh % a.H;
+    const bool fast_path = a.qk_log2 > 0.f;
+    const int ntile0 = 0, ntile1 = 0;  // turn handshake of the two-tile form: not used here
+    (void)ntile0;
+    (void)ntile1;
+    bool ok_run = true;
+    int g = 0;
+    uint8_t* stage = sOut + (warp - 4) * 4096;
+    for (int qt = 0; qt < ntiles && ok_run; ++qt) {
+      const int q0 = tile_qb(qt) * 128;
+      const int qrow = q0 + row;
+      const int n_t = tile_blocks(qt);
+      const float* trow = nullptr;
+      if (kBias == kBiasTable) trow = a.table + static_cast<int64_t>(h) * (2 * S - 1) + (min(qrow, S - 1) + S - 1);
+      const __half* brow = nullptr;
+      if (kBias == kBiasDense) brow = a.bias + bh * a.bias_head + static_cast<int64_t>(min(qrow, S - 1)) * a.bias_row;
+      float m_used = -INFINITY;
+      float l = 0.f;
+      for (int j = 0; j < n_t; ++j, ++g) {
+        // Warp-uniform: every lane must agree before the .sync.aligned TMEM ops.
+        if (!__all_sync(0xffffffffu, mbar_wait(&s_full[t], g & 1, abort_flag, a.st, 0x1300 + t))) {
+          ok_run = false;
+          break;
+        }
+        tc_fence_after();
+        float z[128];
+        {
+          // Four TMEM loads in flight, one wait.
+          uint32_t r0[32], r1[32], r2[32], r3[32];
+          tmem_ld32(lane_base + Cfg::s_col(t) + 0, r0);
+          tmem_ld32(lane_base + Cfg::s_col(t) + 32, r1);
+          tmem_ld32(lane_base + Cfg::s_col(t) + 64, r2);
+          tmem_ld32(lane_base + Cfg::s_col(t) + 96, r3);
+          tmem_wait_ld();
+          if (!Cfg::kAliasP) {
+            // S_t(j) is in registers: the issuer may compute S_t(j+1) now.
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&s_free[t]);
+          }
+  #pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            z[i] = __uint_as_float(r0[i]);
+            z[32 + i] = __uint_as_float(r1[i]);
+            z[64 + i] = __uint_as_float(r2[i]);
+            z[96 + i] = __uint_as_float(r3[i]);
+          }
+        }
+        const int k0 = j * 128;
+        const bool edge = (k0 + 128 > S) || (kCausal && k0 + 127 > qrow);
+        // Without a bias and with a positive scale, max(s) * c = max(s * c): the
+        // row max is taken on the raw scores and each probability costs one FFMA
+        // + one ex2. Otherwise z holds the log2-domain logits.
+        const bool raw_scores = (kBias == kBiasNone) && fast_path;
+        if (kBias == kBiasDense) {
+  #pragma unroll
+          for (int v = 0; v < 16; ++v) {
+            const int key = k0 + v * 8;
+            uint4 raw = make_uint4(0, 0, 0, 0);
+            if (key + 8 <= S) raw = __ldg(reinterpret_cast<const uint4*>(brow + key));
+            const __half2* hp = reinterpret_cast<const __half2*>(&raw);
+  #pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 f = __half22float2(hp[e]);
+              z[v * 8 + 2 * e] = (z[v * 8 + 2 * e] + f.x) * a.qk_log2;
+              z[v * 8 + 2 * e + 1] = (z[v * 8 + 2 * e + 1] + f.y) * a.qk_log2;
+            }
+          }
+        } else if (kBias == kBiasTable) {
+  #pragma unroll
+          for (int col = 0; col < 128; ++col) {
+            const int key = k0 + col;
+            const float tb = (key < S) ? __ldg(trow - key) : 0.f;
+            z[col] = fmaf(z[col], a.qk_log2, tb * kLog2e);
+          }
+        } else if (!raw_scores) {
+  #pragma unroll
+          for (int col = 0; col < 128; ++col) z[col] *= a.qk_log2;
+        }
+        if (edge) {
+  #pragma unroll
+          for (int col = 0; col < 128; ++col) {
+            const int key = k0 + col;
+            if (key >= S || (kCausal && key > qrow)) z[col] = -INFINITY;
+          }
+        }
+        // Row max, 8 independent chains of 3-input max.
+        float pm[8];
+  #pragma unroll
+        for (int i = 0; i < 8; ++i) pm[i] = fmaxf(z[i], z[8 + i]);
+  #pragma unroll
+        for (int c = 16; c < 128; c += 16) {
+  #pragma unroll
+          for (int i = 0; i < 8; ++i) pm[i] = fmax3(pm[i], z[c + i], z[c + 8 + i]);
+        }
+        float rmax = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])),
+                           fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7])));
+        if (raw_scores) rmax *= a.qk_log2;
+        const float m_new = fmaxf(m_used, rmax);
+        const bool need = m_new > m_used + kRescaleThreshold;
+        float alpha = 1.f;
+        if (need) {
+          alpha = ex2_approx(m_used - m_new);
+          m_used = m_new;
+        }
+        const float neg_m = (m_used == -INFINITY) ? 0.f : -m_used;
+        const float zc = raw_scores ? a.qk_log2 : 1.f;
+        // Ping-pong on the exp unit: the two warps that share this SM
+        // sub-partition (same lane quarter q, tiles 0 and 1) take strict turns
+        // for their exp loops, tile 0 first. Everything else a tile does (TMEM
+        // traffic, row max, P store, its MMAs) then hides under the other
+        // tile's exps instead of both tiles stalling at the same time.
+        // Tile 0 block j waits for tile 1's block j-1 (when tile 1 exists);
+        // tile 1 block j waits for tile 0's block j (an existing tile 1 never
+        // has fewer blocks than tile 0).
+        const bool wait_turn = kT == 2 && ((t == 0) ? (j > 0 && ntile1 > 0) : (j < ntile0));
+        if (wait_turn) {
+          const uint32_t par = (t == 0) ? ((j - 1) & 1) : (j & 1);
+          if (!__all_sync(0xffffffffu, mbar_wait(&turn[t * 4 + q], par, abort_flag, a.st, 0x1340 + t))) {
+            ok_run = false;
+            break;
+          }
+        }
+        // p = 2^(z * zc - m), one ex2 per element, fp32 row sums in 8
+        // partials; the exponent arguments and the sums are formed two
+        // lanes per instruction (packed fp32 FMA / add).
+        float ps[8];
+        uint32_t pk[64];
+        const uint64_t zc2 = f2_pack(zc, zc);
+        const uint64_t nm2 = f2_pack(neg_m, neg_m);
+        uint64_t acc2[4] = {0ull, 0ull, 0ull, 0ull};
+  #pragma unroll
+        for (int i = 0; i < 64; ++i) {
+          const uint64_t x2 = ffma2(f2_pack(z[2 * i], z[2 * i + 1]), zc2, nm2);
+          const float p0 = ex2_approx(f2_lo(x2));
+          const float p1 = ex2_approx(f2_hi(x2));
+          acc2[i & 3] = fadd2(acc2[i & 3], f2_pack(p0, p1));
+          pk[i] = pack_half2(p0, p1);
+        }
+  #pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          ps[2 * i] = f2_lo(acc2[i]);
+          ps[2 * i + 1] = f2_hi(acc2[i]);
+        }
+        const float sum = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
+        // Hand the exp unit to the partner warp of the other tile.
+        if (kT == 2) {
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&turn[(1 - t) * 4 + q]);
+        }
+        if (!Cfg::kAliasP && j > 0) {
+          // P_t and O_t are still in use by PV_t(j-1) until it completes.
+          if (!__all_sync(0xffffffffu, mbar_wait(&o_done[t], (g - 1) & 1, abort_flag, a.st, 0x1320 + t))) {
+            ok_run = false;
+            break;
+          }
+          tc_fence_after();
+        }
+  #pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t q16[16];
+  #pragma unroll
+          for (int i = 0; i < 16; ++i) q16[i] = pk[c * 16 + i];
+          tmem_st16(lane_base + Cfg::p_col(t) + c * 16, q16);
+        }
+        l = l * alpha + sum;
+        if (j > 0 && __any_sync(0xffffffffu, need)) {
+          // PV_t(j-1) is complete (waited on above, or implied by s_full when P
+          // aliases S).
+          uint32_t r[32];
+  #pragma unroll 1
+          for (int c = 0; c < D / 32; ++c) {
+            tmem_ld32(lane_base + Cfg::o_col(t) + c * 32, r);
+            tmem_wait_ld();
+  #pragma unroll
+            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+            tmem_st32(lane_base + Cfg::o_col(t) + c * 32, r);
+          }
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[t]);
+      }
+      if (!ok_run) break;
+      // ----------------------------------------------------------- epilogue --
+      if (!__all_sync(0xffffffffu, mbar_wait(o_done, (g - 1) & 1, abort_flag, a.st, 0x1310))) {
+        ok_run = false;
+        break;
+      }
+      tc_fence_after();
+      const float inv_l = 1.f / l;
+      const int row0 = q0 + static_cast<int>(q) * 32;
+      constexpr int kStores = D / 32;  // fp32: 32 columns per store; fp16: 64
+      const int nst = a.out_f16 ? kStores / 2 : kStores;
+#pragma unroll 1
+      for (int c = 0; c < nst; ++c) {
+        uint32_t w[32];
+        if (a.out_f16) {
+          uint32_t r0[32], r1[32];
+          tmem_ld32(lane_base + Cfg::o_col(0) + c * 64, r0);
+          tmem_ld32(lane_base + Cfg::o_col(0) + c * 64 + 32, r1);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            w[i] = pack_half2(__uint_as_float(r0[2 * i]) * inv_l, __uint_as_float(r0[2 * i + 1]) * inv_l);
+            w[16 + i] = pack_half2(__uint_as_float(r1[2 * i]) * inv_l, __uint_as_float(r1[2 * i + 1]) * inv_l);
+          }
+        } else {
+          uint32_t r[32];
+          tmem_ld32(lane_base + Cfg::o_col(0) + c * 32, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) w[i] = __float_as_uint(__uint_as_float(r[i]) * inv_l);
+        }
+        if (c == nst - 1) {
+          // O is in registers: the next tile's first PV may overwrite it.
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(o_free);
+        }
+        if (lane == 0) bulk_wait_read_all();  // the previous store has read the staging rows
+        __syncwarp();
+#pragma unroll
+        for (int v = 0; v < 8; ++v) {
+          *reinterpret_cast<uint4*>(stage + lane * 128 + ((v ^ (lane & 7)) << 4)) =
+              make_uint4(w[4 * v], w[4 * v + 1], w[4 * v + 2], w[4 * v + 3]);
+        }
+        fence_async_smem();
+        __syncwarp();
+        if (lane == 0 && row0 < S) {
+          tma_store_3d(&tmO, stage, c * (a.out_f16 ? 64 : 32), row0, bh);
+          bulk_commit();
+        }
+      }
+    }
+    if (lane == 0) bulk_wait_all();
   }
 
   tc_fence_before();
@@ -1215,7 +1663,8 @@ int run_fa2_kernel(Kernel kern, int threads, uint32_t regs_low, dim3 grid, int s
 }
 
 // Kernel per head dim, the faster one measured on B200: D = 128 runs the
-// persistent kernel, D = 64 one CTA per work unit.
+// persistent kernel, D = 64 one 128-row tile per CTA (two, one after the
+// other, under causal masking).
 template <int D, bool kCausal, int kBias>
 int launch_fa2_t(const FaProblem& p, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                  const CUtensorMap& to, FaArgs& args, cudaStream_t stream) {
@@ -1231,8 +1680,15 @@ int launch_fa2_t(const FaProblem& p, const CUtensorMap& tq, const CUtensorMap& t
     // 128-row units, two CTAs per SM.
     using Cfg1 = FaCfg<D, 1>;
     args.num_qblocks = (p.S + 127) / 128;
-    return run_fa2_kernel(fa2_tile_kernel<D, 1, kCausal, kBias>, Cfg1::kThreads, Cfg1::regs_low(),
-                          dim3(args.num_qblocks, p.BH, 1), Cfg1::kSmemBytes, tq, tk, tv, to, args, stream);
+    if constexpr (kCausal) {
+      // Causal: tiles qb and nq-1-qb share a CTA (nq + 1 key blocks each CTA).
+      return run_fa2_kernel(fa2_pair_kernel<D, kCausal, kBias>, Cfg1::kThreads, Cfg1::regs_low(),
+                            dim3((args.num_qblocks + 1) / 2, p.BH, 1), Cfg1::kSmemBytes + 4 * 4096, tq, tk, tv, to,
+                            args, stream);
+    } else {
+      return run_fa2_kernel(fa2_tile_kernel<D, 1, kCausal, kBias>, Cfg1::kThreads, Cfg1::regs_low(),
+                            dim3(args.num_qblocks, p.BH, 1), Cfg1::kSmemBytes, tq, tk, tv, to, args, stream);
+    }
   }
 }
 
