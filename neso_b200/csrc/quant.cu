@@ -71,7 +71,7 @@ struct QCfg {
   static constexpr int kFStages = kRowHalves == 2 ? 2 : kNT == 2 ? (kQ == kInt8 ? 3 : 2) : (kQ == kInt4G128 && !kSwap) ? 3 : 4;
   // X tiles come from L2 with about 2500 cycles of copy latency: a deep
   // ring keeps the MMAs fed when every K block needs a new 16 KB X tile.
-  static constexpr int kXStages = kSwap ? 8 : kRowHalves == 2 ? 3 : kNT == 2 ? (kQ == kInt8 ? 4 : 3) : 6;
+  static constexpr int kXStages = kSwap ? (kNT == 2 ? 4 : 8) : kRowHalves == 2 ? 3 : kNT == 2 ? (kQ == kInt8 ? 4 : 3) : 6;
   static constexpr int kBudget = 220 * 1024;
   // Y staging for TMA stores (M >= 65 layout): 16 rows x 32 fp32 per epilogue warp.
   static constexpr int kOutBytes = kSwap ? 0 : 4 * 2048;
@@ -83,7 +83,7 @@ struct QCfg {
   static constexpr int kOffOut = kOffF + kFStages * kFBytes;
   static constexpr int kOffBars = kOffOut + kOutBytes;
   static constexpr int kRawTx = kNT * ((kQ == kInt8) ? 64 * 128 : 32 * 128 + 256);
-  static constexpr int kAccCols = kSwap ? kNX : kRowHalves * kNT * kTileN;  // accumulator columns per buffer
+  static constexpr int kAccCols = kSwap ? kNT * kNX : kRowHalves * kNT * kTileN;  // accumulator columns per buffer
   static constexpr int kAccBufs = 2 * kAccCols <= 512 ? 2 : 1;
   static constexpr int kTmemCols = (kAccBufs * kAccCols <= 32) ? 32 : (kAccBufs * kAccCols <= 64) ? 64
                                    : (kAccBufs * kAccCols <= 128) ? 128 : (kAccBufs * kAccCols <= 256) ? 256 : 512;
@@ -283,7 +283,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint64_t wd = wd0 + static_cast<uint64_t>((p * kNT * Cfg::kW16Bytes + k * 2048) >> 4);
             const uint32_t acc = (kb != u.kb0 || k != 0 || p != 0) ? 1u : 0u;
             if (kSwap) {
-              umma_f16_ss(d_tmem, wd, xd, idesc, acc);
+#pragma unroll
+              for (int g = 0; g < kNT; ++g) {
+                umma_f16_ss(d_tmem + g * kNX, wd + static_cast<uint64_t>((g * Cfg::kW16Bytes) >> 4), xd, idesc, acc);
+              }
             } else {
 #pragma unroll
               for (int h = 0; h < Cfg::kRowHalves; ++h) {
@@ -422,25 +425,28 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const uint32_t acc = lane_base + buf * Cfg::kAccCols;
       if (kSwap) {
-        const int n = nb * kTileN + lrow;
-        const float sc = (csc != nullptr && n < args.N) ? __half2float(csc[n]) : 1.f;
+#pragma unroll 1
+        for (int g = 0; g < kNT; ++g) {
+          const int n = nb * kUnitN + g * kTileN + lrow;
+          const float sc = (csc != nullptr && n < args.N) ? __half2float(csc[n]) : 1.f;
 #pragma unroll
-        for (int c = 0; c < (kNX + 31) / 32; ++c) {
-          uint32_t r[32];
-          if (kNX >= 32) {
-            tmem_ld32(acc + c * 32, r);
-          } else {
-            uint32_t r16[16];
-            tmem_ld16(acc, r16);
+          for (int c = 0; c < (kNX + 31) / 32; ++c) {
+            uint32_t r[32];
+            if (kNX >= 32) {
+              tmem_ld32(acc + g * kNX + c * 32, r);
+            } else {
+              uint32_t r16[16];
+              tmem_ld16(acc + g * kNX, r16);
 #pragma unroll
-            for (int i = 0; i < 16; ++i) r[i] = r16[i];
-          }
-          tmem_wait_ld();
-          if (n < args.N) {
+              for (int i = 0; i < 16; ++i) r[i] = r16[i];
+            }
+            tmem_wait_ld();
+            if (n < args.N) {
 #pragma unroll
-            for (int i = 0; i < (kNX >= 32 ? 32 : kNX); ++i) {
-              const int m = c * 32 + i;
-              if (m < args.M) ydst[static_cast<int64_t>(m) * ld + n] = __uint_as_float(r[i]) * sc;
+              for (int i = 0; i < (kNX >= 32 ? 32 : kNX); ++i) {
+                const int m = c * 32 + i;
+                if (m < args.M) ydst[static_cast<int64_t>(m) * ld + n] = __uint_as_float(r[i]) * sc;
+              }
             }
           }
         }
@@ -535,7 +541,7 @@ struct QProblem {
   // split-K plan (filled by plan_splits) and the fp32 partial-sum buffer
   int splits = 1;
   int kb_per_split = 0;
-  int pair = 0;   // M >= 65 layout: two 128-channel tiles per unit
+  int pair = 0;   // two 128-channel tiles per unit (M >= 65 layout, and M <= 16)
   int rows2 = 0;  // units of 256 rows (two accumulators): W8A16 paired, W4A16 single
   float* partial = nullptr;
   DevStatus st{};
@@ -606,7 +612,13 @@ void plan_splits(QProblem& p, int sms, size_t max_partial = SIZE_MAX) {
     plan_normal(p, sms, max_partial);
     return;
   }
-  if (base >= sms || num_k < 2) return;
+  // M <= 16: two 128-channel tiles per unit (both convert groups on every K
+  // block, two MMAs per K step): W8A16 M=16 31 -> 27 us; no gain from M = 32.
+  // (Not in the allocation-free entry, whose split plans keep the single-tile
+  // unit count its fixed scratch was sized for.)
+  p.pair = (p.M <= 16 && max_partial == SIZE_MAX) ? 1 : 0;
+  const int sbase = num_m * ((p.N + (kTileN << p.pair) - 1) / (kTileN << p.pair));
+  if (sbase >= sms || num_k < 2) return;
   // Each split writes and re-reads an M x N fp32 partial: keep that traffic
   // under a tenth of the weight stream, or let the partials take up to 48 MB
   // (they stay in L2; measured faster for M = 16).
@@ -614,11 +626,11 @@ void plan_splits(QProblem& p, int sms, size_t max_partial = SIZE_MAX) {
   const double per_split = 4.0 * p.M * p.N;
   const int max_splits = static_cast<int>(std::max(0.1 * wbytes / (2.0 * per_split), 48e6 / per_split));
   if (max_splits < 2) return;
-  double best = static_cast<double>(base) / sms;
+  double best = static_cast<double>(sbase) / sms;
   for (int sp = 2; sp <= 16 && sp <= num_k && sp <= max_splits; ++sp) {
     const int kbps = (num_k + sp - 1) / sp;
     const int real = (num_k + kbps - 1) / kbps;  // no empty split
-    const int64_t units = static_cast<int64_t>(base) * real;
+    const int64_t units = static_cast<int64_t>(sbase) * real;
     const int64_t waves = (units + sms - 1) / sms;
     const double eff = static_cast<double>(units) / static_cast<double>(waves * sms) * (1.0 - 0.01 * real);
     if (eff > best + 0.02) {
@@ -1039,7 +1051,7 @@ int run_gemv(const QProblem& p, cudaStream_t stream) {
 
 template <int kQ>
 int dispatch_wq(const QProblem& p, cudaStream_t stream) {
-  if (p.M <= 16) return launch_wq<kQ, true, 16>(p, stream);
+  if (p.M <= 16) return p.pair ? launch_wq<kQ, true, 16, 2>(p, stream) : launch_wq<kQ, true, 16>(p, stream);
   if (p.M <= 32) return launch_wq<kQ, true, 32>(p, stream);
   if (p.M <= 64) return launch_wq<kQ, true, 64>(p, stream);
   if (p.rows2) {

@@ -114,6 +114,25 @@ def test_paired_channel_tiles_ragged(dev, kind):
     torch.testing.assert_close(y.cpu(), ref, **TOL)
 
 
+@pytest.mark.parametrize("kind", ["w8", "w4"])
+def test_small_m_paired_channel_tiles_ragged(dev, kind):
+    # M <= 16 (swapped layout) with 256-channel units: N = 400 leaves the last
+    # unit's second tile partly outside N; K ragged for int8.
+    M, N = 12, 400
+    if kind == "w8":
+        K = 1000
+        x, w, s = _w8(M, N, K, seed=31)
+        y = ops.w8a16_matmul(x.to(dev), w.to(dev), s.to(dev))
+        ref = oracle.w8a16_matmul(x, w, s)
+    else:
+        K = 1152
+        x, q, s = _w4(M, N, K, seed=32)
+        wq = oracle.pack_int4(q)
+        y = ops.w4a16_g128_matmul(x.to(dev), wq.to(dev), s.to(dev))
+        ref = oracle.w4a16_g128_matmul(x, wq, s)
+    torch.testing.assert_close(y.cpu(), ref, **TOL)
+
+
 def test_w8a16_256_row_units_ragged(dev):
     # 5 row blocks of 256 x 29 channel pairs = 145 units (one wave; 128-row
     # pairs would take two): the two-accumulator layout runs, its last row
