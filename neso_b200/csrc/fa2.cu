@@ -42,6 +42,11 @@
 //   D = 64: P0/P1 in [384,448)/[448,512); D = 128: P_t aliases the first 64
 //   columns of S_t and the issuer waits for PV_t(j) before QK_t(j+1).
 //   One-tile form (D = 64): S [0,128) O [128,192) P [192,256).
+// Relative-position table: a 128 x 128 block needs 255 consecutive table
+// entries; the tile's first softmax warp stages them in shared memory (its
+// global loads issued one block ahead) and every row reads its 128 values
+// from there (measured S=2048, B=H=16: D=64 152 -> 473 TFLOP/s, D=128 614 ->
+// 737; causal 113 -> 366 and 422 -> 593).
 #include <cmath>
 
 #include "runtime.h"
@@ -62,6 +67,27 @@ constexpr int kUnitRing = 4;      // unit indices the persistent producer may pu
 constexpr int kUnitReaders = 10;  // QK issuer, PV issuer and the 8 softmax warps
 
 enum BiasMode : int { kBiasNone = 0, kBiasTable = 1, kBiasDense = 2 };
+
+// Relative-position table of one 128-row x 128-key block: row i, key c use
+// table[h, d0 + i - c + 127] with d0 = (tile row 0) - (key 0) - 127 + S - 1,
+// a window of 255 consecutive entries. Warp 0 of the tile (the writer) holds
+// the next block's window in registers (lane l: entries l + 32 i), loaded a
+// block ahead so the L2 latency hides under the current block, and stores
+// it, scaled by log2(e), into one of two 256-float buffers; the tile's rows
+// then read entry i - c + 127 (consecutive rows: consecutive banks). Entries
+// outside [0, 2S - 1) only meet rows or keys past S and are 0.
+__device__ __forceinline__ void table_window_load(float (&v)[8], const float* ttab, int d0, int ncols, int lane) {
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int e = lane + 32 * i;
+    const int col = d0 + e;
+    v[i] = (e < 255 && col >= 0 && col < ncols) ? __ldg(ttab + col) : 0.f;
+  }
+}
+__device__ __forceinline__ void table_window_store(float* buf, const float (&v)[8], int lane) {
+#pragma unroll
+  for (int i = 0; i < 8; ++i) buf[lane + 32 * i] = v[i] * kLog2e;
+}
 
 // kT = Q tiles per CTA: 2 (ping-pong pair, one CTA per SM) or 1 (two CTAs
 // per SM, each with half the TMEM and shared memory).
@@ -89,7 +115,11 @@ struct FaCfg {
   // Persistent kernel: O staging for TMA stores, 32 rows x 128 bytes per
   // softmax warp (the K/V ring is busy with the next unit meanwhile).
   static constexpr int kOutBytes = kT == 2 ? 4 * kT * 4096 : 0;
-  static constexpr int kSmemBytes = (kT * kQBuffers + 2 * kStages) * kTileBytes + kOutBytes + 1024 + 512;
+  // One-tile kernels: relative-position table staging, two 256-float
+  // buffers (the persistent kernel stages it in its O staging blocks).
+  static constexpr int kTableBytes = kT == 1 ? 2 * 256 * 4 : 0;
+  static constexpr int kSmemBytes =
+      (kT * kQBuffers + 2 * kStages) * kTileBytes + kOutBytes + kTableBytes + 1024 + 512;
 };
 
 struct FaArgs {
@@ -124,7 +154,8 @@ __global__ void __launch_bounds__(FaCfg<D, kT>::kThreads, FaCfg<D, kT>::min_bloc
   uint8_t* sQ = smem;                                // kT tiles
   uint8_t* sK = smem + kT * Cfg::kTileBytes;         // KS tiles
   uint8_t* sV = sK + KS * Cfg::kTileBytes;           // KS tiles
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + KS * Cfg::kTileBytes);
+  float* tb_base = reinterpret_cast<float*>(sV + KS * Cfg::kTileBytes);  // table window buffers (kT = 1)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + KS * Cfg::kTileBytes + Cfg::kTableBytes);
   uint64_t* q_full = bars;
   uint64_t* k_full = bars + 1;
   uint64_t* k_empty = k_full + KS;
@@ -136,7 +167,8 @@ __global__ void __launch_bounds__(FaCfg<D, kT>::kThreads, FaCfg<D, kT>::min_bloc
   uint64_t* s_free = o_done + 2;     // [2] softmax has read S_t (4 warps)
   uint64_t* mma_done = s_free + 2;   // [2] one per MMA issuer
   uint64_t* turn = mma_done + 2;     // [2][4] exp-loop turn of tile t, lane quarter q
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(turn + 8);
+  uint64_t* tb_full = turn + 8;      // table window staged (writer warp)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tb_full + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* never_flag = abort_flag + 1;  // stays 0: drain waits ignore the abort
 
@@ -169,6 +201,7 @@ __global__ void __launch_bounds__(FaCfg<D, kT>::kThreads, FaCfg<D, kT>::min_bloc
     mbar_init(&mma_done[0], 1);
     mbar_init(&mma_done[1], 1);
     for (int i = 0; i < 8; ++i) mbar_init(&turn[i], 1);
+    mbar_init(tb_full, 1);
     *abort_flag = 0;
     *never_flag = 0;
     fence_mbar_init();
@@ -334,8 +367,10 @@ __global__ void __launch_bounds__(FaCfg<D, kT>::kThreads, FaCfg<D, kT>::min_bloc
     const uint32_t lane_base = tmem + ((q * 32) << 16);
     const int n_t = t ? ntile1 : ntile0;
     const int h = bh % a.H;
-    const float* trow = nullptr;
-    if (kBias == kBiasTable) trow = a.table + static_cast<int64_t>(h) * (2 * S - 1) + (min(qrow, S - 1) + S - 1);
+    const float* ttab = kBias == kBiasTable ? a.table + static_cast<int64_t>(h) * (2 * S - 1) : nullptr;
+    const int d0 = (qrow - row) - 127 + S - 1;  // window start of block 0
+    float tpre[8];
+    if (kBias == kBiasTable && q == 0 && n_t > 0) table_window_load(tpre, ttab, d0, 2 * S - 1, static_cast<int>(lane));
     const __half* brow = nullptr;
     if (kBias == kBiasDense) brow = a.bias + bh * a.bias_head + static_cast<int64_t>(min(qrow, S - 1)) * a.bias_row;
 
@@ -394,12 +429,25 @@ __global__ void __launch_bounds__(FaCfg<D, kT>::kThreads, FaCfg<D, kT>::min_bloc
           }
         }
       } else if (kBias == kBiasTable) {
-#pragma unroll
-        for (int col = 0; col < 128; ++col) {
-          const int key = k0 + col;
-          const float tb = (key < S) ? __ldg(trow - key) : 0.f;
-          z[col] = fmaf(z[col], a.qk_log2, tb * kLog2e);
+        // Buffer reuse needs no extra barrier: this block's s_full implies
+        // every row has finished the block two back (its S or P columns were
+        // released after that block's softmax), so the buffer written here is
+        // free; the epilogue writes staging only after o_done, which implies
+        // every row's last P, hence its last table read.
+        float* tbuf = tb_base + (j & 1) * 256;
+        if (q == 0) {
+          table_window_store(tbuf, tpre, static_cast<int>(lane));
+          __syncwarp();
+          if (lane == 0) mbar_arrive(tb_full);
+          if (j + 1 < n_t) table_window_load(tpre, ttab, d0 - 128 * (j + 1), 2 * S - 1, static_cast<int>(lane));
         }
+        if (!__all_sync(0xffffffffu, mbar_wait(tb_full, j & 1, abort_flag, a.st, 0x1360))) {
+          ok_run = false;
+          break;
+        }
+        const float* trow = tbuf + row + 127;
+#pragma unroll
+        for (int col = 0; col < 128; ++col) z[col] = fmaf(z[col], a.qk_log2, trow[-col]);
       } else if (!raw_scores) {
 #pragma unroll
         for (int col = 0; col < 128; ++col) z[col] *= a.qk_log2;
@@ -623,7 +671,8 @@ __global__ void __launch_bounds__(FaCfg<D, 1>::kThreads, 2)
   uint8_t* sK = sQ + Cfg::kTileBytes;                // KS tiles
   uint8_t* sV = sK + KS * Cfg::kTileBytes;           // KS tiles
   uint8_t* sOut = sV + KS * Cfg::kTileBytes;         // 4 KB per softmax warp
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sOut + 4 * 4096);
+  float* tb_base = reinterpret_cast<float*>(sOut + 4 * 4096);  // table window buffers
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sOut + 4 * 4096 + Cfg::kTableBytes);
   uint64_t* q_full = bars;
   uint64_t* q_empty = bars + 1;
   uint64_t* k_full = bars + 2;
@@ -637,7 +686,8 @@ __global__ void __launch_bounds__(FaCfg<D, 1>::kThreads, 2)
   uint64_t* o_free = s_free + 1;     // [1] epilogue has read O (4 warps)
   uint64_t* mma_done = o_free + 1;   // [2] one per MMA issuer
   uint64_t* turn = mma_done + 2;     // unused (one tile at a time)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(turn + 8);
+  uint64_t* tb_full = turn + 8;      // table window staged (writer warp)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tb_full + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* never_flag = abort_flag + 1;  // stays 0: drain waits ignore the abort
 
@@ -666,6 +716,7 @@ __global__ void __launch_bounds__(FaCfg<D, 1>::kThreads, 2)
     mbar_init(o_done, 1);
     mbar_init(s_free, 4);
     mbar_init(o_free, 4);
+    mbar_init(tb_full, 1);
     mbar_init(&mma_done[0], 1);
     mbar_init(&mma_done[1], 1);
     *abort_flag = 0;
@@ -808,8 +859,10 @@ __global__ void __launch_bounds__(FaCfg<D, 1>::kThreads, 2)
       const int q0 = tile_qb(qt) * 128;
       const int qrow = q0 + row;
       const int n_t = tile_blocks(qt);
-      const float* trow = nullptr;
-      if (kBias == kBiasTable) trow = a.table + static_cast<int64_t>(h) * (2 * S - 1) + (min(qrow, S - 1) + S - 1);
+      const float* ttab = kBias == kBiasTable ? a.table + static_cast<int64_t>(h) * (2 * S - 1) : nullptr;
+      const int d0 = (qrow - row) - 127 + S - 1;  // window start of block 0
+      float tpre[8];
+      if (kBias == kBiasTable && q == 0) table_window_load(tpre, ttab, d0, 2 * S - 1, static_cast<int>(lane));
       const __half* brow = nullptr;
       if (kBias == kBiasDense) brow = a.bias + bh * a.bias_head + static_cast<int64_t>(min(qrow, S - 1)) * a.bias_row;
       float m_used = -INFINITY;
@@ -865,12 +918,25 @@ __global__ void __launch_bounds__(FaCfg<D, 1>::kThreads, 2)
             }
           }
         } else if (kBias == kBiasTable) {
-  #pragma unroll
-          for (int col = 0; col < 128; ++col) {
-            const int key = k0 + col;
-            const float tb = (key < S) ? __ldg(trow - key) : 0.f;
-            z[col] = fmaf(z[col], a.qk_log2, tb * kLog2e);
+          // Buffer reuse needs no extra barrier: this block's s_full implies
+          // every row has finished the block two back (its S or P columns were
+          // released after that block's softmax), so the buffer written here is
+          // free; the epilogue writes staging only after o_done, which implies
+          // every row's last P, hence its last table read.
+          float* tbuf = tb_base + (g & 1) * 256;
+          if (q == 0) {
+            table_window_store(tbuf, tpre, static_cast<int>(lane));
+            __syncwarp();
+            if (lane == 0) mbar_arrive(tb_full);
+            if (j + 1 < n_t) table_window_load(tpre, ttab, d0 - 128 * (j + 1), 2 * S - 1, static_cast<int>(lane));
           }
+          if (!__all_sync(0xffffffffu, mbar_wait(tb_full, g & 1, abort_flag, a.st, 0x1360))) {
+            ok_run = false;
+            break;
+          }
+          const float* trow = tbuf + row + 127;
+#pragma unroll
+          for (int col = 0; col < 128; ++col) z[col] = fmaf(z[col], a.qk_log2, trow[-col]);
         } else if (!raw_scores) {
   #pragma unroll
           for (int col = 0; col < 128; ++col) z[col] *= a.qk_log2;
@@ -1105,8 +1171,9 @@ __global__ void __launch_bounds__(FaCfg<D>::kThreads, 1)
   uint64_t* turn = mma_done + 2;        // [2][4] exp-loop turn of tile t, lane quarter q
   uint64_t* unit_full = turn + 8;       // [kUnitRing] unit index published
   uint64_t* unit_empty = unit_full + kUnitRing;  // [kUnitRing] read by all consumers
-  volatile int* unit_ring = reinterpret_cast<volatile int*>(unit_empty + kUnitRing);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(unit_empty + kUnitRing) + kUnitRing;
+  uint64_t* tb_full = unit_empty + kUnitRing;    // [2] table window of tile t staged
+  volatile int* unit_ring = reinterpret_cast<volatile int*>(tb_full + 2);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tb_full + 2) + kUnitRing;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* never_flag = abort_flag + 1;  // stays 0: drain waits ignore the abort
 
@@ -1145,6 +1212,8 @@ __global__ void __launch_bounds__(FaCfg<D>::kThreads, 1)
       mbar_init(&unit_full[i], 1);
       mbar_init(&unit_empty[i], kUnitReaders);
     }
+    mbar_init(&tb_full[0], 1);
+    mbar_init(&tb_full[1], 1);
     *abort_flag = 0;
     *never_flag = 0;
     fence_mbar_init();
@@ -1380,12 +1449,16 @@ __global__ void __launch_bounds__(FaCfg<D>::kThreads, 1)
       if (n_t == 0) continue;
       const int qrow = q0 + 128 * t + row;
       const int h = bh % a.H;
-      const float* trow = nullptr;
-      if (kBias == kBiasTable) trow = a.table + static_cast<int64_t>(h) * (2 * S - 1) + (min(qrow, S - 1) + S - 1);
+      const float* ttab = kBias == kBiasTable ? a.table + static_cast<int64_t>(h) * (2 * S - 1) : nullptr;
+      const int d0 = (qrow - row) - 127 + S - 1;  // window start of block 0
+      float tpre[8];
+      if (kBias == kBiasTable && q == 0) table_window_load(tpre, ttab, d0, 2 * S - 1, static_cast<int>(lane));
       const __half* brow = nullptr;
       if (kBias == kBiasDense) brow = a.bias + bh * a.bias_head + static_cast<int64_t>(min(qrow, S - 1)) * a.bias_row;
       float m_used = -INFINITY;
       float l = 0.f;
+      // Table window buffers: the first 2 KB of the writer warp's O staging block.
+      float* tb_base = reinterpret_cast<float*>(sOut + t * 16384);
       for (int j = 0; j < n_t; ++j, ph ^= 1u) {
         // Warp-uniform: every lane must agree before the .sync.aligned TMEM ops.
         if (!__all_sync(0xffffffffu, mbar_wait(&s_full[t], ph & 1u, abort_flag, a.st, 0x1300 + t))) {
@@ -1437,12 +1510,31 @@ __global__ void __launch_bounds__(FaCfg<D>::kThreads, 1)
             }
           }
         } else if (kBias == kBiasTable) {
-#pragma unroll
-          for (int col = 0; col < 128; ++col) {
-            const int key = k0 + col;
-            const float tb = (key < S) ? __ldg(trow - key) : 0.f;
-            z[col] = fmaf(z[col], a.qk_log2, tb * kLog2e);
+          // Buffer reuse needs no extra barrier: this block's s_full implies
+          // every row has finished the block two back (its S or P columns were
+          // released after that block's softmax), so the buffer written here is
+          // free; the epilogue writes staging only after o_done, which implies
+          // every row's last P, hence its last table read.
+          float* tbuf = tb_base + (ph & 1) * 256;
+          if (q == 0) {
+            if (j == 0) {
+              // The window shares this warp's O staging block: the previous
+              // unit's stores must have read it.
+              if (lane == 0) bulk_wait_read_all();
+              __syncwarp();
+            }
+            table_window_store(tbuf, tpre, static_cast<int>(lane));
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tb_full[t]);
+            if (j + 1 < n_t) table_window_load(tpre, ttab, d0 - 128 * (j + 1), 2 * S - 1, static_cast<int>(lane));
           }
+          if (!__all_sync(0xffffffffu, mbar_wait(&tb_full[t], ph & 1, abort_flag, a.st, 0x1360))) {
+            ok_run = false;
+            break;
+          }
+          const float* trow = tbuf + row + 127;
+#pragma unroll
+          for (int col = 0; col < 128; ++col) z[col] = fmaf(z[col], a.qk_log2, trow[-col]);
         } else if (!raw_scores) {
 #pragma unroll
           for (int col = 0; col < 128; ++col) z[col] *= a.qk_log2;
