@@ -42,11 +42,12 @@
 //   D = 64: P0/P1 in [384,448)/[448,512); D = 128: P_t aliases the first 64
 //   columns of S_t and the issuer waits for PV_t(j) before QK_t(j+1).
 //   One-tile form (D = 64): S [0,128) O [128,192) P [192,256).
-// Relative-position table: a 128 x 128 block needs 255 consecutive table
-// entries; the tile's first softmax warp stages them in shared memory (its
-// global loads issued one block ahead) and every row reads its 128 values
-// from there (measured S=2048, B=H=16: D=64 152 -> 473 TFLOP/s, D=128 614 ->
-// 737; causal 113 -> 366 and 422 -> 593).
+// Relative-position table: the 32 rows of a softmax warp need 159
+// consecutive table entries per 128-key block; the warp stages them in its
+// own shared-memory window (global loads issued one block ahead) and each row
+// reads its 128 values from there (measured S=2048, B=H=16 against 128
+// scattered global loads per row and block: D=64 152 -> 499 TFLOP/s, D=128
+// 614 -> 740; causal 113 -> 384 and 422 -> 534-593).
 #include <cmath>
 
 #include "runtime.h"
@@ -69,24 +70,28 @@ constexpr int kUnitReaders = 10;  // QK issuer, PV issuer and the 8 softmax warp
 enum BiasMode : int { kBiasNone = 0, kBiasTable = 1, kBiasDense = 2 };
 
 // Relative-position table of one 128-row x 128-key block: row i, key c use
-// table[h, d0 + i - c + 127] with d0 = (tile row 0) - (key 0) - 127 + S - 1,
-// a window of 255 consecutive entries. Warp 0 of the tile (the writer) holds
-// the next block's window in registers (lane l: entries l + 32 i), loaded a
-// block ahead so the L2 latency hides under the current block, and stores
-// it, scaled by log2(e), into one of two 256-float buffers; the tile's rows
-// then read entry i - c + 127 (consecutive rows: consecutive banks). Entries
-// outside [0, 2S - 1) only meet rows or keys past S and are 0.
-__device__ __forceinline__ void table_window_load(float (&v)[8], const float* ttab, int d0, int ncols, int lane) {
+// table[h, d0 + i - c + 127] with d0 = (tile row 0) - (key 0) - 127 + S - 1.
+// The 32 rows of softmax warp q need the 159 consecutive entries from
+// d0 + 32 q: the warp stages them, scaled by log2(e), in its own 160-float
+// window (lane l row: window[l + 127 - c], consecutive lanes on consecutive
+// banks), from registers loaded one block ahead so the L2 latency hides
+// under the current block. Nothing is shared between warps. Entries outside
+// [0, 2S - 1) only meet rows or keys past S and are 0.
+__device__ __forceinline__ void table_window_load(float (&v)[5], const float* ttab, int d0, int ncols, int lane) {
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int e = lane + 32 * i;
-    const int col = d0 + e;
-    v[i] = (e < 255 && col >= 0 && col < ncols) ? __ldg(ttab + col) : 0.f;
+  for (int i = 0; i < 5; ++i) {
+    const int u = lane + 32 * i;
+    const int col = d0 + u;
+    v[i] = (u < 159 && col >= 0 && col < ncols) ? __ldg(ttab + col) : 0.f;
   }
 }
-__device__ __forceinline__ void table_window_store(float* buf, const float (&v)[8], int lane) {
+// Stores the window and returns this lane's row pointer (read at [-c]).
+__device__ __forceinline__ const float* table_window_store(float* win, const float (&v)[5], int lane) {
+  __syncwarp();  // every lane has read the previous block's window
 #pragma unroll
-  for (int i = 0; i < 8; ++i) buf[lane + 32 * i] = v[i] * kLog2e;
+  for (int i = 0; i < 5; ++i) win[lane + 32 * i] = v[i] * kLog2e;
+  __syncwarp();
+  return win + lane + 127;
 }
 
 // kT = Q tiles per CTA: 2 (ping-pong pair, one CTA per SM) or 1 (two CTAs
@@ -115,9 +120,9 @@ struct FaCfg {
   // Persistent kernel: O staging for TMA stores, 32 rows x 128 bytes per
   // softmax warp (the K/V ring is busy with the next unit meanwhile).
   static constexpr int kOutBytes = kT == 2 ? 4 * kT * 4096 : 0;
-  // One-tile kernels: relative-position table staging, two 256-float
-  // buffers (the persistent kernel stages it in its O staging blocks).
-  static constexpr int kTableBytes = kT == 1 ? 2 * 256 * 4 : 0;
+  // One-tile kernels: relative-position table windows, 160 floats per
+  // softmax warp (the persistent kernel uses its O staging blocks).
+  static constexpr int kTableBytes = kT == 1 ? 4 * 160 * 4 : 0;
   static constexpr int kSmemBytes =
       (kT * kQBuffers + 2 * kStages) * kTileBytes + kOutBytes + kTableBytes + 1024 + 512;
 };
@@ -154,7 +159,7 @@ __global__ void __launch_bounds__(FaCfg<D, kT>::kThreads, FaCfg<D, kT>::min_bloc
   uint8_t* sQ = smem;                                // kT tiles
   uint8_t* sK = smem + kT * Cfg::kTileBytes;         // KS tiles
   uint8_t* sV = sK + KS * Cfg::kTileBytes;           // KS tiles
-  float* tb_base = reinterpret_cast<float*>(sV + KS * Cfg::kTileBytes);  // table window buffers (kT = 1)
+  float* tb_base = reinterpret_cast<float*>(sV + KS * Cfg::kTileBytes);  // table windows (kT = 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(sV + KS * Cfg::kTileBytes + Cfg::kTableBytes);
   uint64_t* q_full = bars;
   uint64_t* k_full = bars + 1;
@@ -167,8 +172,7 @@ __global__ void __launch_bounds__(FaCfg<D, kT>::kThreads, FaCfg<D, kT>::min_bloc
   uint64_t* s_free = o_done + 2;     // [2] softmax has read S_t (4 warps)
   uint64_t* mma_done = s_free + 2;   // [2] one per MMA issuer
   uint64_t* turn = mma_done + 2;     // [2][4] exp-loop turn of tile t, lane quarter q
-  uint64_t* tb_full = turn + 8;      // table window staged (writer warp)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tb_full + 1);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(turn + 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* never_flag = abort_flag + 1;  // stays 0: drain waits ignore the abort
 
@@ -201,7 +205,6 @@ __global__ void __launch_bounds__(FaCfg<D, kT>::kThreads, FaCfg<D, kT>::min_bloc
     mbar_init(&mma_done[0], 1);
     mbar_init(&mma_done[1], 1);
     for (int i = 0; i < 8; ++i) mbar_init(&turn[i], 1);
-    mbar_init(tb_full, 1);
     *abort_flag = 0;
     *never_flag = 0;
     fence_mbar_init();
@@ -368,9 +371,10 @@ __global__ void __launch_bounds__(FaCfg<D, kT>::kThreads, FaCfg<D, kT>::min_bloc
     const int n_t = t ? ntile1 : ntile0;
     const int h = bh % a.H;
     const float* ttab = kBias == kBiasTable ? a.table + static_cast<int64_t>(h) * (2 * S - 1) : nullptr;
-    const int d0 = (qrow - row) - 127 + S - 1;  // window start of block 0
-    float tpre[8];
-    if (kBias == kBiasTable && q == 0 && n_t > 0) table_window_load(tpre, ttab, d0, 2 * S - 1, static_cast<int>(lane));
+    const int d0 = (qrow - lane) - 127 + S - 1;  // this warp's window start, block 0
+    float* tb_win = tb_base + q * 160;
+    float tpre[5];
+    if (kBias == kBiasTable && n_t > 0) table_window_load(tpre, ttab, d0, 2 * S - 1, static_cast<int>(lane));
     const __half* brow = nullptr;
     if (kBias == kBiasDense) brow = a.bias + bh * a.bias_head + static_cast<int64_t>(min(qrow, S - 1)) * a.bias_row;
 
@@ -429,23 +433,8 @@ __global__ void __launch_bounds__(FaCfg<D, kT>::kThreads, FaCfg<D, kT>::min_bloc
           }
         }
       } else if (kBias == kBiasTable) {
-        // Buffer reuse needs no extra barrier: this block's s_full implies
-        // every row has finished the block two back (its S or P columns were
-        // released after that block's softmax), so the buffer written here is
-        // free; the epilogue writes staging only after o_done, which implies
-        // every row's last P, hence its last table read.
-        float* tbuf = tb_base + (j & 1) * 256;
-        if (q == 0) {
-          table_window_store(tbuf, tpre, static_cast<int>(lane));
-          __syncwarp();
-          if (lane == 0) mbar_arrive(tb_full);
-          if (j + 1 < n_t) table_window_load(tpre, ttab, d0 - 128 * (j + 1), 2 * S - 1, static_cast<int>(lane));
-        }
-        if (!__all_sync(0xffffffffu, mbar_wait(tb_full, j & 1, abort_flag, a.st, 0x1360))) {
-          ok_run = false;
-          break;
-        }
-        const float* trow = tbuf + row + 127;
+        const float* trow = table_window_store(tb_win, tpre, static_cast<int>(lane));
+        if (j + 1 < n_t) table_window_load(tpre, ttab, d0 - 128 * (j + 1), 2 * S - 1, static_cast<int>(lane));
 #pragma unroll
         for (int col = 0; col < 128; ++col) z[col] = fmaf(z[col], a.qk_log2, trow[-col]);
       } else if (!raw_scores) {
@@ -671,7 +660,7 @@ __global__ void __launch_bounds__(FaCfg<D, 1>::kThreads, 2)
   uint8_t* sK = sQ + Cfg::kTileBytes;                // KS tiles
   uint8_t* sV = sK + KS * Cfg::kTileBytes;           // KS tiles
   uint8_t* sOut = sV + KS * Cfg::kTileBytes;         // 4 KB per softmax warp
-  float* tb_base = reinterpret_cast<float*>(sOut + 4 * 4096);  // table window buffers
+  float* tb_base = reinterpret_cast<float*>(sOut + 4 * 4096);  // table windows
   uint64_t* bars = reinterpret_cast<uint64_t*>(sOut + 4 * 4096 + Cfg::kTableBytes);
   uint64_t* q_full = bars;
   uint64_t* q_empty = bars + 1;
@@ -686,8 +675,7 @@ __global__ void __launch_bounds__(FaCfg<D, 1>::kThreads, 2)
   uint64_t* o_free = s_free + 1;     // [1] epilogue has read O (4 warps)
   uint64_t* mma_done = o_free + 1;   // [2] one per MMA issuer
   uint64_t* turn = mma_done + 2;     // unused (one tile at a time)
-  uint64_t* tb_full = turn + 8;      // table window staged (writer warp)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tb_full + 1);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(turn + 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* never_flag = abort_flag + 1;  // stays 0: drain waits ignore the abort
 
@@ -716,7 +704,6 @@ __global__ void __launch_bounds__(FaCfg<D, 1>::kThreads, 2)
     mbar_init(o_done, 1);
     mbar_init(s_free, 4);
     mbar_init(o_free, 4);
-    mbar_init(tb_full, 1);
     mbar_init(&mma_done[0], 1);
     mbar_init(&mma_done[1], 1);
     *abort_flag = 0;
@@ -860,9 +847,10 @@ __global__ void __launch_bounds__(FaCfg<D, 1>::kThreads, 2)
       const int qrow = q0 + row;
       const int n_t = tile_blocks(qt);
       const float* ttab = kBias == kBiasTable ? a.table + static_cast<int64_t>(h) * (2 * S - 1) : nullptr;
-      const int d0 = (qrow - row) - 127 + S - 1;  // window start of block 0
-      float tpre[8];
-      if (kBias == kBiasTable && q == 0) table_window_load(tpre, ttab, d0, 2 * S - 1, static_cast<int>(lane));
+      const int d0 = (qrow - lane) - 127 + S - 1;  // this warp's window start, block 0
+      float* tb_win = tb_base + q * 160;
+      float tpre[5];
+      if (kBias == kBiasTable) table_window_load(tpre, ttab, d0, 2 * S - 1, static_cast<int>(lane));
       const __half* brow = nullptr;
       if (kBias == kBiasDense) brow = a.bias + bh * a.bias_head + static_cast<int64_t>(min(qrow, S - 1)) * a.bias_row;
       float m_used = -INFINITY;
@@ -918,23 +906,8 @@ __global__ void __launch_bounds__(FaCfg<D, 1>::kThreads, 2)
             }
           }
         } else if (kBias == kBiasTable) {
-          // Buffer reuse needs no extra barrier: this block's s_full implies
-          // every row has finished the block two back (its S or P columns were
-          // released after that block's softmax), so the buffer written here is
-          // free; the epilogue writes staging only after o_done, which implies
-          // every row's last P, hence its last table read.
-          float* tbuf = tb_base + (g & 1) * 256;
-          if (q == 0) {
-            table_window_store(tbuf, tpre, static_cast<int>(lane));
-            __syncwarp();
-            if (lane == 0) mbar_arrive(tb_full);
-            if (j + 1 < n_t) table_window_load(tpre, ttab, d0 - 128 * (j + 1), 2 * S - 1, static_cast<int>(lane));
-          }
-          if (!__all_sync(0xffffffffu, mbar_wait(tb_full, g & 1, abort_flag, a.st, 0x1360))) {
-            ok_run = false;
-            break;
-          }
-          const float* trow = tbuf + row + 127;
+          const float* trow = table_window_store(tb_win, tpre, static_cast<int>(lane));
+          if (j + 1 < n_t) table_window_load(tpre, ttab, d0 - 128 * (j + 1), 2 * S - 1, static_cast<int>(lane));
 #pragma unroll
           for (int col = 0; col < 128; ++col) z[col] = fmaf(z[col], a.qk_log2, trow[-col]);
         } else if (!raw_scores) {
@@ -1171,9 +1144,8 @@ __global__ void __launch_bounds__(FaCfg<D>::kThreads, 1)
   uint64_t* turn = mma_done + 2;        // [2][4] exp-loop turn of tile t, lane quarter q
   uint64_t* unit_full = turn + 8;       // [kUnitRing] unit index published
   uint64_t* unit_empty = unit_full + kUnitRing;  // [kUnitRing] read by all consumers
-  uint64_t* tb_full = unit_empty + kUnitRing;    // [2] table window of tile t staged
-  volatile int* unit_ring = reinterpret_cast<volatile int*>(tb_full + 2);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tb_full + 2) + kUnitRing;
+  volatile int* unit_ring = reinterpret_cast<volatile int*>(unit_empty + kUnitRing);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(unit_empty + kUnitRing) + kUnitRing;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* never_flag = abort_flag + 1;  // stays 0: drain waits ignore the abort
 
@@ -1212,8 +1184,6 @@ __global__ void __launch_bounds__(FaCfg<D>::kThreads, 1)
       mbar_init(&unit_full[i], 1);
       mbar_init(&unit_empty[i], kUnitReaders);
     }
-    mbar_init(&tb_full[0], 1);
-    mbar_init(&tb_full[1], 1);
     *abort_flag = 0;
     *never_flag = 0;
     fence_mbar_init();
@@ -1450,15 +1420,14 @@ __global__ void __launch_bounds__(FaCfg<D>::kThreads, 1)
       const int qrow = q0 + 128 * t + row;
       const int h = bh % a.H;
       const float* ttab = kBias == kBiasTable ? a.table + static_cast<int64_t>(h) * (2 * S - 1) : nullptr;
-      const int d0 = (qrow - row) - 127 + S - 1;  // window start of block 0
-      float tpre[8];
-      if (kBias == kBiasTable && q == 0) table_window_load(tpre, ttab, d0, 2 * S - 1, static_cast<int>(lane));
+      const int d0 = (qrow - lane) - 127 + S - 1;  // this warp's window start, block 0
+      float* tb_win = reinterpret_cast<float*>(sOut + (warp - 4) * 4096);  // in this warp's O staging block
+      float tpre[5];
+      if (kBias == kBiasTable) table_window_load(tpre, ttab, d0, 2 * S - 1, static_cast<int>(lane));
       const __half* brow = nullptr;
       if (kBias == kBiasDense) brow = a.bias + bh * a.bias_head + static_cast<int64_t>(min(qrow, S - 1)) * a.bias_row;
       float m_used = -INFINITY;
       float l = 0.f;
-      // Table window buffers: the first 2 KB of the writer warp's O staging block.
-      float* tb_base = reinterpret_cast<float*>(sOut + t * 16384);
       for (int j = 0; j < n_t; ++j, ph ^= 1u) {
         // Warp-uniform: every lane must agree before the .sync.aligned TMEM ops.
         if (!__all_sync(0xffffffffu, mbar_wait(&s_full[t], ph & 1u, abort_flag, a.st, 0x1300 + t))) {
@@ -1510,29 +1479,13 @@ __global__ void __launch_bounds__(FaCfg<D>::kThreads, 1)
             }
           }
         } else if (kBias == kBiasTable) {
-          // Buffer reuse needs no extra barrier: this block's s_full implies
-          // every row has finished the block two back (its S or P columns were
-          // released after that block's softmax), so the buffer written here is
-          // free; the epilogue writes staging only after o_done, which implies
-          // every row's last P, hence its last table read.
-          float* tbuf = tb_base + (ph & 1) * 256;
-          if (q == 0) {
-            if (j == 0) {
-              // The window shares this warp's O staging block: the previous
-              // unit's stores must have read it.
-              if (lane == 0) bulk_wait_read_all();
-              __syncwarp();
-            }
-            table_window_store(tbuf, tpre, static_cast<int>(lane));
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&tb_full[t]);
-            if (j + 1 < n_t) table_window_load(tpre, ttab, d0 - 128 * (j + 1), 2 * S - 1, static_cast<int>(lane));
+          if (j == 0) {
+            // The window shares this warp's O staging block: the previous unit's
+            // stores must have read it.
+            if (lane == 0) bulk_wait_read_all();
           }
-          if (!__all_sync(0xffffffffu, mbar_wait(&tb_full[t], ph & 1, abort_flag, a.st, 0x1360))) {
-            ok_run = false;
-            break;
-          }
-          const float* trow = tbuf + row + 127;
+          const float* trow = table_window_store(tb_win, tpre, static_cast<int>(lane));
+          if (j + 1 < n_t) table_window_load(tpre, ttab, d0 - 128 * (j + 1), 2 * S - 1, static_cast<int>(lane));
 #pragma unroll
           for (int col = 0; col < 128; ++col) z[col] = fmaf(z[col], a.qk_log2, trow[-col]);
         } else if (!raw_scores) {
