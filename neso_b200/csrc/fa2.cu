@@ -45,9 +45,10 @@
 // Relative-position table: the 32 rows of a softmax warp need 159
 // consecutive table entries per 128-key block; the warp stages them in its
 // own shared-memory window (global loads issued one block ahead) and each row
-// reads its 128 values from there (measured S=2048, B=H=16 against 128
-// scattered global loads per row and block: D=64 152 -> 499 TFLOP/s, D=128
-// 614 -> 740; causal 113 -> 384 and 422 -> 534-593).
+// reads its 128 values from there, adding them two keys per packed FMA
+// (measured S=2048, B=H=16 against 128 scattered global loads per row and
+// block: D=64 152 -> 506 TFLOP/s, D=128 614 -> 720-740; causal 113 -> 399 and
+// 422 -> 514-593).
 #include <cmath>
 
 #include "runtime.h"
@@ -435,8 +436,13 @@ __global__ void __launch_bounds__(FaCfg<D, kT>::kThreads, FaCfg<D, kT>::min_bloc
       } else if (kBias == kBiasTable) {
         const float* trow = table_window_store(tb_win, tpre, static_cast<int>(lane));
         if (j + 1 < n_t) table_window_load(tpre, ttab, d0 - 128 * (j + 1), 2 * S - 1, static_cast<int>(lane));
+        const uint64_t qk2 = f2_pack(a.qk_log2, a.qk_log2);
 #pragma unroll
-        for (int col = 0; col < 128; ++col) z[col] = fmaf(z[col], a.qk_log2, trow[-col]);
+        for (int col = 0; col < 128; col += 2) {
+          const uint64_t r2 = ffma2(f2_pack(z[col], z[col + 1]), qk2, f2_pack(trow[-col], trow[-col - 1]));
+          z[col] = f2_lo(r2);
+          z[col + 1] = f2_hi(r2);
+        }
       } else if (!raw_scores) {
 #pragma unroll
         for (int col = 0; col < 128; ++col) z[col] *= a.qk_log2;
@@ -908,8 +914,13 @@ __global__ void __launch_bounds__(FaCfg<D, 1>::kThreads, 2)
         } else if (kBias == kBiasTable) {
           const float* trow = table_window_store(tb_win, tpre, static_cast<int>(lane));
           if (j + 1 < n_t) table_window_load(tpre, ttab, d0 - 128 * (j + 1), 2 * S - 1, static_cast<int>(lane));
+          const uint64_t qk2 = f2_pack(a.qk_log2, a.qk_log2);
 #pragma unroll
-          for (int col = 0; col < 128; ++col) z[col] = fmaf(z[col], a.qk_log2, trow[-col]);
+          for (int col = 0; col < 128; col += 2) {
+            const uint64_t r2 = ffma2(f2_pack(z[col], z[col + 1]), qk2, f2_pack(trow[-col], trow[-col - 1]));
+            z[col] = f2_lo(r2);
+            z[col + 1] = f2_hi(r2);
+          }
         } else if (!raw_scores) {
   #pragma unroll
           for (int col = 0; col < 128; ++col) z[col] *= a.qk_log2;
@@ -1486,8 +1497,13 @@ __global__ void __launch_bounds__(FaCfg<D>::kThreads, 1)
           }
           const float* trow = table_window_store(tb_win, tpre, static_cast<int>(lane));
           if (j + 1 < n_t) table_window_load(tpre, ttab, d0 - 128 * (j + 1), 2 * S - 1, static_cast<int>(lane));
+          const uint64_t qk2 = f2_pack(a.qk_log2, a.qk_log2);
 #pragma unroll
-          for (int col = 0; col < 128; ++col) z[col] = fmaf(z[col], a.qk_log2, trow[-col]);
+          for (int col = 0; col < 128; col += 2) {
+            const uint64_t r2 = ffma2(f2_pack(z[col], z[col + 1]), qk2, f2_pack(trow[-col], trow[-col - 1]));
+            z[col] = f2_lo(r2);
+            z[col + 1] = f2_hi(r2);
+          }
         } else if (!raw_scores) {
 #pragma unroll
           for (int col = 0; col < 128; ++col) z[col] *= a.qk_log2;
