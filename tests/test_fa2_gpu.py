@@ -102,6 +102,38 @@ def test_relpos_table(dev, D, causal):
 
 
 @pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("S", [1, 77, 300])
+def test_relpos_table_ragged_unit_scale(dev, D, causal, S):
+    # Ragged S (the last query tile and key block partly past S) and a table of
+    # unit scale, so a table entry read at the wrong offset moves the output
+    # far past the tolerance; entries past S must be ignored.
+    B, H = 2, 3
+    g = torch.Generator().manual_seed(S + D)
+    table = torch.randn(H, 2 * S - 1, generator=g)
+    _check(dev, B, H, S, D, causal=causal, table=table, seed=S)
+
+
+@pytest.mark.parametrize("D", [64, 128])
+def test_relpos_table_many_units_sampled(dev, D):
+    # 8 x 16 heads at S = 1000: the D = 128 persistent CTAs each take several
+    # work units, so every warp re-stages its table window in its O staging
+    # block after the previous unit's stores; causal D = 64 runs two query
+    # tiles per CTA. A sample of heads against the oracle.
+    B, H, S = 8, 16, 1000
+    g = torch.Generator().manual_seed(100 + D)
+    q, k, v = (torch.randn(B, H, S, D, generator=g).half() for _ in range(3))
+    table = torch.randn(H, 2 * S - 1, generator=g)
+    qd, kd, vd, td = q.to(dev), k.to(dev), v.to(dev), table.to(dev)
+    for causal in (False, True):
+        o = ops.flash_attention(qd, kd, vd, 1 / math.sqrt(D), causal=causal, table=td)
+        for (b, h) in [(0, 0), (3, 7), (7, 15)]:
+            ref = oracle.attention(q[b, h], k[b, h], v[b, h], 1 / math.sqrt(D), causal=causal,
+                                   table=table[h:h + 1])
+            torch.testing.assert_close(o[b, h].cpu(), ref, **TOL)
+
+
+@pytest.mark.parametrize("D", [64, 128])
 def test_baseline_sweep_s2048_sampled(dev, D):
     # Full BASELINE shape B = H = 16, S = 2048; a sample of heads against the oracle.
     B, H, S = 16, 16, 2048
