@@ -420,6 +420,7 @@ __global__ void __launch_bounds__(FaCfg<D, kT>::kThreads, FaCfg<D, kT>::min_bloc
       // + one ex2. Otherwise z holds the log2-domain logits.
       const bool raw_scores = (kBias == kBiasNone) && fast_path;
       if (kBias == kBiasDense) {
+        const uint64_t qk2 = f2_pack(a.qk_log2, a.qk_log2);
 #pragma unroll
         for (int v = 0; v < 16; ++v) {
           const int key = k0 + v * 8;
@@ -429,8 +430,9 @@ __global__ void __launch_bounds__(FaCfg<D, kT>::kThreads, FaCfg<D, kT>::min_bloc
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const float2 f = __half22float2(hp[e]);
-            z[v * 8 + 2 * e] = (z[v * 8 + 2 * e] + f.x) * a.qk_log2;
-            z[v * 8 + 2 * e + 1] = (z[v * 8 + 2 * e + 1] + f.y) * a.qk_log2;
+            const uint64_t r2 = fmul2(fadd2(f2_pack(z[v * 8 + 2 * e], z[v * 8 + 2 * e + 1]), f2_pack(f.x, f.y)), qk2);
+            z[v * 8 + 2 * e] = f2_lo(r2);
+            z[v * 8 + 2 * e + 1] = f2_hi(r2);
           }
         }
       } else if (kBias == kBiasTable) {
@@ -883,7 +885,7 @@ __global__ void __launch_bounds__(FaCfg<D, 1>::kThreads, 2)
             __syncwarp();
             if (lane == 0) mbar_arrive(&s_free[t]);
           }
-  #pragma unroll
+#pragma unroll
           for (int i = 0; i < 32; ++i) {
             z[i] = __uint_as_float(r0[i]);
             z[32 + i] = __uint_as_float(r1[i]);
@@ -898,17 +900,19 @@ __global__ void __launch_bounds__(FaCfg<D, 1>::kThreads, 2)
         // + one ex2. Otherwise z holds the log2-domain logits.
         const bool raw_scores = (kBias == kBiasNone) && fast_path;
         if (kBias == kBiasDense) {
-  #pragma unroll
+          const uint64_t qk2 = f2_pack(a.qk_log2, a.qk_log2);
+#pragma unroll
           for (int v = 0; v < 16; ++v) {
             const int key = k0 + v * 8;
             uint4 raw = make_uint4(0, 0, 0, 0);
             if (key + 8 <= S) raw = __ldg(reinterpret_cast<const uint4*>(brow + key));
             const __half2* hp = reinterpret_cast<const __half2*>(&raw);
-  #pragma unroll
+#pragma unroll
             for (int e = 0; e < 4; ++e) {
               const float2 f = __half22float2(hp[e]);
-              z[v * 8 + 2 * e] = (z[v * 8 + 2 * e] + f.x) * a.qk_log2;
-              z[v * 8 + 2 * e + 1] = (z[v * 8 + 2 * e + 1] + f.y) * a.qk_log2;
+              const uint64_t r2 = fmul2(fadd2(f2_pack(z[v * 8 + 2 * e], z[v * 8 + 2 * e + 1]), f2_pack(f.x, f.y)), qk2);
+              z[v * 8 + 2 * e] = f2_lo(r2);
+              z[v * 8 + 2 * e + 1] = f2_hi(r2);
             }
           }
         } else if (kBias == kBiasTable) {
@@ -922,11 +926,11 @@ __global__ void __launch_bounds__(FaCfg<D, 1>::kThreads, 2)
             z[col + 1] = f2_hi(r2);
           }
         } else if (!raw_scores) {
-  #pragma unroll
+#pragma unroll
           for (int col = 0; col < 128; ++col) z[col] *= a.qk_log2;
         }
         if (edge) {
-  #pragma unroll
+#pragma unroll
           for (int col = 0; col < 128; ++col) {
             const int key = k0 + col;
             if (key >= S || (kCausal && key > qrow)) z[col] = -INFINITY;
@@ -934,11 +938,11 @@ __global__ void __launch_bounds__(FaCfg<D, 1>::kThreads, 2)
         }
         // Row max, 8 independent chains of 3-input max.
         float pm[8];
-  #pragma unroll
+#pragma unroll
         for (int i = 0; i < 8; ++i) pm[i] = fmaxf(z[i], z[8 + i]);
-  #pragma unroll
+#pragma unroll
         for (int c = 16; c < 128; c += 16) {
-  #pragma unroll
+#pragma unroll
           for (int i = 0; i < 8; ++i) pm[i] = fmax3(pm[i], z[c + i], z[c + 8 + i]);
         }
         float rmax = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])),
@@ -977,7 +981,7 @@ __global__ void __launch_bounds__(FaCfg<D, 1>::kThreads, 2)
         const uint64_t zc2 = f2_pack(zc, zc);
         const uint64_t nm2 = f2_pack(neg_m, neg_m);
         uint64_t acc2[4] = {0ull, 0ull, 0ull, 0ull};
-  #pragma unroll
+#pragma unroll
         for (int i = 0; i < 64; ++i) {
           const uint64_t x2 = ffma2(f2_pack(z[2 * i], z[2 * i + 1]), zc2, nm2);
           const float p0 = ex2_approx(f2_lo(x2));
@@ -985,7 +989,7 @@ __global__ void __launch_bounds__(FaCfg<D, 1>::kThreads, 2)
           acc2[i & 3] = fadd2(acc2[i & 3], f2_pack(p0, p1));
           pk[i] = pack_half2(p0, p1);
         }
-  #pragma unroll
+#pragma unroll
         for (int i = 0; i < 4; ++i) {
           ps[2 * i] = f2_lo(acc2[i]);
           ps[2 * i + 1] = f2_hi(acc2[i]);
@@ -1004,10 +1008,10 @@ __global__ void __launch_bounds__(FaCfg<D, 1>::kThreads, 2)
           }
           tc_fence_after();
         }
-  #pragma unroll
+#pragma unroll
         for (int c = 0; c < 4; ++c) {
           uint32_t q16[16];
-  #pragma unroll
+#pragma unroll
           for (int i = 0; i < 16; ++i) q16[i] = pk[c * 16 + i];
           tmem_st16(lane_base + Cfg::p_col(t) + c * 16, q16);
         }
@@ -1020,7 +1024,7 @@ __global__ void __launch_bounds__(FaCfg<D, 1>::kThreads, 2)
           for (int c = 0; c < D / 32; ++c) {
             tmem_ld32(lane_base + Cfg::o_col(t) + c * 32, r);
             tmem_wait_ld();
-  #pragma unroll
+#pragma unroll
             for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
             tmem_st32(lane_base + Cfg::o_col(t) + c * 32, r);
           }
@@ -1476,6 +1480,7 @@ __global__ void __launch_bounds__(FaCfg<D>::kThreads, 1)
         // + one ex2. Otherwise z holds the log2-domain logits.
         const bool raw_scores = (kBias == kBiasNone) && fast_path;
         if (kBias == kBiasDense) {
+          const uint64_t qk2 = f2_pack(a.qk_log2, a.qk_log2);
 #pragma unroll
           for (int v = 0; v < 16; ++v) {
             const int key = k0 + v * 8;
@@ -1485,8 +1490,9 @@ __global__ void __launch_bounds__(FaCfg<D>::kThreads, 1)
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
               const float2 f = __half22float2(hp[e]);
-              z[v * 8 + 2 * e] = (z[v * 8 + 2 * e] + f.x) * a.qk_log2;
-              z[v * 8 + 2 * e + 1] = (z[v * 8 + 2 * e + 1] + f.y) * a.qk_log2;
+              const uint64_t r2 = fmul2(fadd2(f2_pack(z[v * 8 + 2 * e], z[v * 8 + 2 * e + 1]), f2_pack(f.x, f.y)), qk2);
+              z[v * 8 + 2 * e] = f2_lo(r2);
+              z[v * 8 + 2 * e + 1] = f2_hi(r2);
             }
           }
         } else if (kBias == kBiasTable) {
