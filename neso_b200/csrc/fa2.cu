@@ -17,7 +17,7 @@
 // kernels share this design and the host picks the faster one per head dim
 // (measured on B200):
 //   D = 64   fa2_tile_kernel with one 128-row tile per CTA and two CTAs per
-//            SM (256 TMEM columns, 82 KB of shared memory each): the tiles
+//            SM (256 TMEM columns, 86 KB of shared memory each): the tiles
 //            of the two CTAs overlap as the ping-pong pair does, and one
 //            CTA's prologue and epilogue run under the other's main loop.
 //            Causal D = 64 runs fa2_pair_kernel: the same one-tile CTA
