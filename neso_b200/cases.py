@@ -9,6 +9,8 @@
 Each case launches the op ``--warmup`` times, then ``--iters`` times between
 CUDA events on the current stream, and prints one JSON line with the mean
 time and the achieved TFLOP/s or GB/s (algorithmic work, as in bench.py).
+With ``--graph`` the timed calls are replayed from one CUDA graph instead, so
+small problems show their device time rather than the host's per-call cost.
 Weights rotate over three copies for the quantized cases so small-M runs
 read HBM rather than L2.
 """
@@ -23,7 +25,12 @@ import torch
 from . import ops
 
 
+GRAPH = False
+
+
 def _time(fn, warmup: int, iters: int) -> float:
+    if GRAPH:
+        return _time_graph(fn, warmup, iters)
     for i in range(warmup):
         fn(i)
     torch.cuda.synchronize()
@@ -32,6 +39,30 @@ def _time(fn, warmup: int, iters: int) -> float:
     for i in range(iters):
         fn(i)
     en.record()
+    torch.cuda.synchronize()
+    return st.elapsed_time(en) / iters * 1e-3
+
+
+def _time_graph(fn, warmup: int, iters: int) -> float:
+    """Device time per call without the host's per-call cost: the warm-up runs
+    on the capture stream (so per-stream work counters exist before capture),
+    then ``iters`` calls are captured in one CUDA graph and replayed."""
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        for i in range(max(warmup, 1)):
+            fn(i)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        for i in range(iters):
+            fn(i)
+    g.replay()
+    torch.cuda.synchronize()
+    st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(s):
+        st.record()
+        g.replay()
+        en.record()
     torch.cuda.synchronize()
     return st.elapsed_time(en) / iters * 1e-3
 
@@ -51,7 +82,11 @@ def main() -> None:
     ap.add_argument("--n", type=int, default=1 << 28)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--iters", type=int, default=5)
+    ap.add_argument("--graph", action="store_true",
+                    help="time the calls replayed from one CUDA graph (device time, no per-call host cost)")
     a = ap.parse_args()
+    global GRAPH
+    GRAPH = a.graph
     dev = torch.device("cuda", 0)
     g = torch.Generator(device=dev).manual_seed(0)
     res: dict = {"case": a.case}
@@ -96,6 +131,7 @@ def main() -> None:
             t = _time(lambda i: ops.scale(x, 0.5, out=z), a.warmup, a.iters)
             nbytes = 8 * a.n
         res.update(n=a.n, us=t * 1e6, gbs=nbytes / t / 1e9)
+    res["timing"] = "cuda_graph" if a.graph else "eager"
     print(json.dumps(res), flush=True)
 
 

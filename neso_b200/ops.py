@@ -18,7 +18,7 @@ from .kernels import current_stream_and_device
 def _need(t: torch.Tensor, name: str, dtype: torch.dtype, contiguous: bool = True) -> None:
     if not isinstance(t, torch.Tensor):
         raise TypeError(f"{name} must be a torch.Tensor")
-    if t.device.type != "cuda":
+    if not t.is_cuda:
         raise ValueError(f"{name} must be a CUDA tensor (got {t.device})")
     if t.dtype != dtype:
         raise TypeError(f"{name} must be {dtype} (got {t.dtype})")
