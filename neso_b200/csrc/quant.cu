@@ -71,7 +71,10 @@ struct QCfg {
   static constexpr int kFStages = kRowHalves == 2 ? 2 : kNT == 2 ? (kQ == kInt8 ? 3 : 2) : (kQ == kInt4G128 && !kSwap) ? 3 : 4;
   // X tiles come from L2 with about 2500 cycles of copy latency: a deep
   // ring keeps the MMAs fed when every K block needs a new 16 KB X tile.
-  static constexpr int kXStages = kSwap ? (kNT == 2 ? 4 : 8) : kRowHalves == 2 ? 3 : kNT == 2 ? (kQ == kInt8 ? 4 : 3) : 6;
+  // Swapped layout: X tiles are 2-8 KB and the X ring moves in step with the
+  // F ring (same depth, released by the same commit; deeper X rings measured
+  // no faster at M = 16).
+  static constexpr int kXStages = kSwap ? kFStages : kRowHalves == 2 ? 3 : kNT == 2 ? (kQ == kInt8 ? 4 : 3) : 6;
   static constexpr int kBudget = 220 * 1024;
   // Y staging for TMA stores (M >= 65 layout): 16 rows x 32 fp32 per epilogue warp.
   static constexpr int kOutBytes = kSwap ? 0 : 4 * 2048;
@@ -214,7 +217,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const bool raw = warp == 0;
     const int depth = raw ? RS : XS;
     uint64_t* full = raw ? r_full : x_full;
-    uint64_t* empty = raw ? r_empty : x_empty;
+    // Swapped layout: an X slot is free when the F slot of the same K block is
+    // (same ring depth and order, one commit per stage).
+    uint64_t* empty = raw ? r_empty : (kSwap ? f_empty : x_empty);
     int it = 0;
     bool aborted = false;
     for (int t = blockIdx.x; t < num_units && !aborted; t += gridDim.x) {
@@ -296,7 +301,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         umma_commit(&f_empty[fs]);
-        umma_commit(&x_empty[xs]);
+        if (!kSwap) umma_commit(&x_empty[xs]);
       }
       if (!aborted) umma_commit(&acc_full[buf]);
     }
