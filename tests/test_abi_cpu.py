@@ -111,3 +111,47 @@ def test_status_codes_match_header():
                  "NESO_ERR_LAUNCH", "NESO_ERR_DEVICE_TIMEOUT", "NESO_ERR_NO_DEVICE"]:
         val = getattr(_lib, name)
         assert f"#define {name} ({val})" in text or f"#define {name} {val}" in text
+
+
+class _FakeCudaTensor:
+    def __init__(self, index):
+        self.is_cuda = True
+        self._index = index
+
+    def get_device(self):
+        return self._index
+
+
+class _FakeCpuTensor:
+    is_cuda = False
+
+    def get_device(self):
+        return -1
+
+
+def test_launch_stream_and_device_selection(monkeypatch):
+    # Host logic of every launch: the first CUDA tensor picks the device, the
+    # library is switched to it, and torch's current stream on that device is
+    # passed as a raw handle (falling back to the Stream object without the
+    # raw query).
+    import torch
+
+    from neso_b200 import kernels
+
+    calls = []
+    monkeypatch.setattr(_lib, "call", lambda name, *args: calls.append((name, args)))
+    monkeypatch.setattr(torch._C, "_cuda_getCurrentRawStream", lambda dev: 0x1000 + dev, raising=False)
+    assert kernels.current_stream_and_device([3, _FakeCpuTensor(), _FakeCudaTensor(2), _FakeCudaTensor(5)]) == 0x1002
+    assert calls == [("neso_set_device", (2,))]
+
+    calls.clear()
+    monkeypatch.setattr(torch.cuda, "current_device", lambda: 1)
+    assert kernels.current_stream_and_device([_FakeCpuTensor()]) == 0x1001
+    assert calls == [("neso_set_device", (1,))]
+
+    class _Stream:
+        cuda_stream = 0xBEEF
+
+    monkeypatch.delattr(torch._C, "_cuda_getCurrentRawStream")
+    monkeypatch.setattr(torch.cuda, "current_stream", lambda dev: _Stream())
+    assert kernels.current_stream_and_device([_FakeCudaTensor(0)]) == 0xBEEF
