@@ -83,6 +83,32 @@ NESO_API int neso_add_kernel(const float* x_ptr, const float* y_ptr, float* z_pt
 NESO_API int neso_scale(const float* x, float* output, float factor, int32_t n_elements, int32_t BLOCK_SIZE,
                uint32_t grid_x, uint32_t grid_y, uint32_t grid_z, neso_stream_t stream);
 
+/* ----------------------------------------- LLM building blocks (rowops) -- */
+/* tests/test_advanced12.py:104-120  rmsnorm_kernel(x_ptr, weight_ptr, out_ptr,
+ *   row_stride, n_cols, eps, BLOCK_SIZE). Reference grid: (M, 1, 1), one row per
+ *   program: out = x / sqrt(sum(x^2) / n_cols + eps) * w over the first
+ *   min(BLOCK_SIZE, n_cols) columns of each row. fp32. */
+NESO_API int neso_rmsnorm_kernel(const float* x_ptr, const float* weight_ptr, float* out_ptr, int32_t row_stride,
+                        int32_t n_cols, float eps, int32_t BLOCK_SIZE, uint32_t grid_x, uint32_t grid_y,
+                        uint32_t grid_z, neso_stream_t stream);
+/* tests/test_advanced12.py:135-153  residual_rmsnorm_kernel(x_ptr, residual_ptr,
+ *   weight_ptr, out_ptr, row_stride, n_cols, eps, BLOCK_SIZE): RMSNorm of
+ *   h = x + residual. Reference grid: (M, 1, 1). */
+NESO_API int neso_residual_rmsnorm_kernel(const float* x_ptr, const float* residual_ptr, const float* weight_ptr,
+                                 float* out_ptr, int32_t row_stride, int32_t n_cols, float eps, int32_t BLOCK_SIZE,
+                                 uint32_t grid_x, uint32_t grid_y, uint32_t grid_z, neso_stream_t stream);
+/* tests/test_advanced12.py:156-176  rope_kernel(x_ptr, cos_ptr, sin_ptr, out_ptr,
+ *   seq_len, head_dim, BLOCK_D). x, out [seq_len, head_dim], cos/sin
+ *   [seq_len, head_dim/2]; rotates pairs (d, d + head_dim/2) for
+ *   d < min(BLOCK_D, head_dim/2). Reference grid: (seq_len, 1, 1). */
+NESO_API int neso_rope_kernel(const float* x_ptr, const float* cos_ptr, const float* sin_ptr, float* out_ptr,
+                     int32_t seq_len, int32_t head_dim, int32_t BLOCK_D, uint32_t grid_x, uint32_t grid_y,
+                     uint32_t grid_z, neso_stream_t stream);
+/* tests/test_advanced12.py:123-132  silu_kernel(x_ptr, out_ptr, n, BLOCK):
+ *   out = x * sigmoid(x). Reference grid: (cdiv(n, BLOCK), 1, 1). */
+NESO_API int neso_silu_kernel(const float* x_ptr, float* out_ptr, int32_t n, int32_t BLOCK, uint32_t grid_x,
+                     uint32_t grid_y, uint32_t grid_z, neso_stream_t stream);
+
 /* ------------------------------------------------------ flash attention -- */
 /* tests/test_flash_attention.py:149-152
  *   flash_attention_fwd(Q, K, V, O, N, stride_qo, stride_kv, scale), constexpr d.

@@ -70,6 +70,10 @@ SIGNATURES: dict[str, tuple[object, list]] = {
     "neso_vector_add": (_int, [_p, _p, _p, _i32, _i32, *_GRID, _p]),
     "neso_add_kernel": (_int, [_p, _p, _p, _i32, _i32, *_GRID, _p]),
     "neso_scale": (_int, [_p, _p, _f32, _i32, _i32, *_GRID, _p]),
+    "neso_rmsnorm_kernel": (_int, [_p, _p, _p, _i32, _i32, _f32, _i32, *_GRID, _p]),
+    "neso_residual_rmsnorm_kernel": (_int, [_p, _p, _p, _p, _i32, _i32, _f32, _i32, *_GRID, _p]),
+    "neso_rope_kernel": (_int, [_p, _p, _p, _p, _i32, _i32, _i32, *_GRID, _p]),
+    "neso_silu_kernel": (_int, [_p, _p, _i32, _i32, *_GRID, _p]),
     "neso_flash_attention_fwd": (_int, [_p, _p, _p, _p, _i32, _i32, _i32, _f32, _i32, *_GRID, _p]),
     "neso_rel_pos_fa2_fwd": (_int, [_p, _p, _p, _p, _p, _i32, _i32, _f32, _i32, _i32, _i32, *_GRID, _p]),
     "neso_fa2_fwd": (_int, [_p, _p, _p, _p, _i32, _i32, _i32, _i32, _f32, _i32, _p]),

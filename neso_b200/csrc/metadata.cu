@@ -114,6 +114,22 @@ const std::unordered_map<std::string, std::string>& table() {
          {{"X", "*fp16", F16P}, {"Wq", "*u8", "const uint8_t*"}, {"scales", "*fp16", F16P},
           {"Y", "*fp32", "float*"}, {"M", "i32", "int32_t"}, {"N", "i32", "int32_t"}, {"K", "i32", "int32_t"}},
          "{\"GROUP\": 128}", 256, {"internal", "1", "1"}},
+        {"rmsnorm_kernel",
+         {{"x_ptr", "*fp32", "const float*"}, {"weight_ptr", "*fp32", "const float*"}, {"out_ptr", "*fp32", "float*"},
+          {"row_stride", "i32", "int32_t"}, {"n_cols", "i32", "int32_t"}, {"eps", "fp32", "float"}},
+         "{\"BLOCK_SIZE\": 128}", 256, {"M", "1", "1"}},
+        {"residual_rmsnorm_kernel",
+         {{"x_ptr", "*fp32", "const float*"}, {"residual_ptr", "*fp32", "const float*"},
+          {"weight_ptr", "*fp32", "const float*"}, {"out_ptr", "*fp32", "float*"}, {"row_stride", "i32", "int32_t"},
+          {"n_cols", "i32", "int32_t"}, {"eps", "fp32", "float"}},
+         "{\"BLOCK_SIZE\": 128}", 256, {"M", "1", "1"}},
+        {"rope_kernel",
+         {{"x_ptr", "*fp32", "const float*"}, {"cos_ptr", "*fp32", "const float*"}, {"sin_ptr", "*fp32", "const float*"},
+          {"out_ptr", "*fp32", "float*"}, {"seq_len", "i32", "int32_t"}, {"head_dim", "i32", "int32_t"}},
+         "{\"BLOCK_D\": 32}", 256, {"seq_len", "1", "1"}},
+        {"silu_kernel",
+         {{"x_ptr", "*fp32", "const float*"}, {"out_ptr", "*fp32", "float*"}, {"n", "i32", "int32_t"}},
+         "{\"BLOCK\": 256}", 256, {"cdiv(n, BLOCK)", "1", "1"}},
     };
     std::unordered_map<std::string, std::string> m;
     for (const KernelMeta& k : ks) m.emplace(k.name, to_json(k));

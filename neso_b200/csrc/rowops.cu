@@ -1,0 +1,227 @@
+// LLM building-block kernels the reference compiles and tests next to the hot
+// path (tests/test_advanced12.py:104-177): RMSNorm, residual + RMSNorm, RoPE
+// and SiLU, fp32, under the reference names, argument orders and grids.
+//
+// All four are HBM-bound streams:
+//   rmsnorm / residual_rmsnorm  one warp per row (8 rows per 256-thread CTA,
+//       grid-stride over rows), 16-byte loads when the row starts and the
+//       column count allow it; pass 1 sums h^2 in registers and reduces with
+//       warp shuffles in a fixed order, pass 2 re-reads the row (L1/L2 hit)
+//       and writes h / rms * w. Per row the reference touches the first
+//       min(BLOCK_SIZE, n_cols) columns and divides by n_cols
+//       (:110-120, :137-153); so does this kernel.
+//   rope  one thread per rotated pair (pos, d), d < min(BLOCK_D, head_dim/2)
+//       (:158-176); products and sums are rounded separately (no FMA
+//       contraction), so results equal a plain fp32 evaluation bit for bit.
+//   silu  x * sigmoid(x), 16-byte grid-stride stream (:124-132).
+// Every element is read and written by the same thread, so in-place calls
+// (out == x) are safe as in the reference.
+#include "runtime.h"
+
+namespace neso {
+namespace {
+
+constexpr int kRowWarps = 8;
+constexpr int kRowThreads = kRowWarps * 32;
+constexpr int kStreamThreads = 256;
+
+bool pow2(int v) { return v >= 1 && v <= (1 << 20) && (v & (v - 1)) == 0; }
+
+template <bool kResidual, bool kVec>
+__global__ void __launch_bounds__(kRowThreads)
+    rmsnorm_rows_kernel(const float* x, const float* r, const float* w, float* out, int64_t rows, int64_t stride,
+                        int ncols, float n_div, float eps) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp0 = static_cast<int64_t>(blockIdx.x) * kRowWarps + (threadIdx.x >> 5);
+  const int64_t wstep = static_cast<int64_t>(gridDim.x) * kRowWarps;
+  for (int64_t row = warp0; row < rows; row += wstep) {
+    const float* xr = x + row * stride;
+    const float* rr = kResidual ? r + row * stride : nullptr;
+    float* orow = out + row * stride;
+    float acc = 0.f;
+    if (kVec) {
+      const int n4 = ncols >> 2;
+      for (int c = lane; c < n4; c += 32) {
+        float4 a = reinterpret_cast<const float4*>(xr)[c];
+        if (kResidual) {
+          const float4 b = reinterpret_cast<const float4*>(rr)[c];
+          a = make_float4(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y), __fadd_rn(a.z, b.z), __fadd_rn(a.w, b.w));
+        }
+        acc = fmaf(a.x, a.x, acc);
+        acc = fmaf(a.y, a.y, acc);
+        acc = fmaf(a.z, a.z, acc);
+        acc = fmaf(a.w, a.w, acc);
+      }
+    } else {
+      for (int c = lane; c < ncols; c += 32) {
+        const float a = kResidual ? __fadd_rn(xr[c], rr[c]) : xr[c];
+        acc = fmaf(a, a, acc);
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    const float rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(acc, n_div), eps));
+    if (kVec) {
+      const int n4 = ncols >> 2;
+      for (int c = lane; c < n4; c += 32) {
+        float4 a = reinterpret_cast<const float4*>(xr)[c];
+        if (kResidual) {
+          const float4 b = reinterpret_cast<const float4*>(rr)[c];
+          a = make_float4(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y), __fadd_rn(a.z, b.z), __fadd_rn(a.w, b.w));
+        }
+        const float4 g = reinterpret_cast<const float4*>(w)[c];
+        reinterpret_cast<float4*>(orow)[c] =
+            make_float4(__fmul_rn(__fdiv_rn(a.x, rms), g.x), __fmul_rn(__fdiv_rn(a.y, rms), g.y),
+                        __fmul_rn(__fdiv_rn(a.z, rms), g.z), __fmul_rn(__fdiv_rn(a.w, rms), g.w));
+      }
+    } else {
+      for (int c = lane; c < ncols; c += 32) {
+        const float a = kResidual ? __fadd_rn(xr[c], rr[c]) : xr[c];
+        orow[c] = __fmul_rn(__fdiv_rn(a, rms), w[c]);
+      }
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kStreamThreads)
+    rope_kernel_impl(const float* x, const float* cs, const float* sn, float* out, int64_t pairs, int hd, int half,
+                     int head_dim) {
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < pairs;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t pos = i / hd;
+    const int d = static_cast<int>(i - pos * hd);
+    const int64_t xo = pos * head_dim + d;
+    const int64_t to = pos * half + d;
+    const float x1 = x[xo], x2 = x[xo + half];
+    const float c = cs[to], s = sn[to];
+    out[xo] = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s));
+    out[xo + half] = __fadd_rn(__fmul_rn(x1, s), __fmul_rn(x2, c));
+  }
+}
+
+__device__ __forceinline__ float silu1(float v) { return v * (1.0f / (1.0f + expf(-v))); }
+
+__global__ void __launch_bounds__(kStreamThreads)
+    silu_vec4_kernel(const float4* x, float4* out, int64_t n4) {
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n4;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const float4 v = x[i];
+    out[i] = make_float4(silu1(v.x), silu1(v.y), silu1(v.z), silu1(v.w));
+  }
+}
+
+__global__ void __launch_bounds__(kStreamThreads)
+    silu_scalar_kernel(const float* x, float* out, int64_t begin, int64_t n) {
+  for (int64_t i = begin + static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    out[i] = silu1(x[i]);
+  }
+}
+
+int stream_blocks(int64_t work) {
+  const int64_t cap = static_cast<int64_t>(sm_count()) * (2048 / kStreamThreads);
+  const int64_t want = (work + kStreamThreads - 1) / kStreamThreads;
+  return static_cast<int>(want < cap ? (want < 1 ? 1 : want) : cap);
+}
+
+template <bool kResidual>
+int launch_rmsnorm(const float* x, const float* r, const float* w, float* out, int32_t row_stride, int32_t n_cols,
+                   float eps, int32_t block, uint32_t gx, uint32_t gy, uint32_t gz, cudaStream_t stream) {
+  if (!pow2(block)) return fail(NESO_ERR_INVALID_ARG, "BLOCK_SIZE must be a power of two (got %d)", block);
+  if (gy != 1 || gz != 1) return fail(NESO_ERR_GRID, "grid (%u,%u,%u) must be (rows, 1, 1)", gx, gy, gz);
+  if (n_cols < 0 || row_stride < 0) return fail(NESO_ERR_INVALID_ARG, "n_cols and row_stride must be >= 0");
+  const int ncols = n_cols < block ? n_cols : block;  // columns the reference's one block covers
+  if (gx == 0 || ncols == 0) return ok();
+  if (x == nullptr || w == nullptr || out == nullptr || (kResidual && r == nullptr)) {
+    return fail(NESO_ERR_INVALID_ARG, "null pointer");
+  }
+  const bool vec = aligned16(x) && aligned16(w) && aligned16(out) && (!kResidual || aligned16(r)) &&
+                   row_stride % 4 == 0 && ncols % 4 == 0;
+  const int64_t rows = gx;
+  const int64_t cap = static_cast<int64_t>(sm_count()) * (2048 / kRowThreads);
+  const int64_t want = (rows + kRowWarps - 1) / kRowWarps;
+  const int blocks = static_cast<int>(want < cap ? want : cap);
+  const float n_div = static_cast<float>(n_cols);
+  if (vec) {
+    rmsnorm_rows_kernel<kResidual, true><<<blocks, kRowThreads, 0, stream>>>(x, r, w, out, rows, row_stride, ncols,
+                                                                               n_div, eps);
+  } else {
+    rmsnorm_rows_kernel<kResidual, false><<<blocks, kRowThreads, 0, stream>>>(x, r, w, out, rows, row_stride, ncols,
+                                                                                n_div, eps);
+  }
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "rmsnorm launch");
+  return ok();
+}
+
+}  // namespace
+}  // namespace neso
+
+using namespace neso;
+
+extern "C" {
+
+int neso_rmsnorm_kernel(const float* x_ptr, const float* weight_ptr, float* out_ptr, int32_t row_stride,
+                        int32_t n_cols, float eps, int32_t BLOCK_SIZE, uint32_t grid_x, uint32_t grid_y,
+                        uint32_t grid_z, neso_stream_t stream) {
+  return launch_rmsnorm<false>(x_ptr, nullptr, weight_ptr, out_ptr, row_stride, n_cols, eps, BLOCK_SIZE, grid_x,
+                               grid_y, grid_z, as_stream(stream));
+}
+
+int neso_residual_rmsnorm_kernel(const float* x_ptr, const float* residual_ptr, const float* weight_ptr,
+                                 float* out_ptr, int32_t row_stride, int32_t n_cols, float eps, int32_t BLOCK_SIZE,
+                                 uint32_t grid_x, uint32_t grid_y, uint32_t grid_z, neso_stream_t stream) {
+  return launch_rmsnorm<true>(x_ptr, residual_ptr, weight_ptr, out_ptr, row_stride, n_cols, eps, BLOCK_SIZE, grid_x,
+                              grid_y, grid_z, as_stream(stream));
+}
+
+int neso_rope_kernel(const float* x_ptr, const float* cos_ptr, const float* sin_ptr, float* out_ptr, int32_t seq_len,
+                     int32_t head_dim, int32_t BLOCK_D, uint32_t grid_x, uint32_t grid_y, uint32_t grid_z,
+                     neso_stream_t stream) {
+  if (!pow2(BLOCK_D)) return fail(NESO_ERR_INVALID_ARG, "BLOCK_D must be a power of two (got %d)", BLOCK_D);
+  if (seq_len < 0 || head_dim < 0) return fail(NESO_ERR_INVALID_ARG, "seq_len and head_dim must be >= 0");
+  if (grid_x != static_cast<uint32_t>(seq_len) || grid_y != 1 || grid_z != 1) {
+    return fail(NESO_ERR_GRID, "grid (%u,%u,%u) != (seq_len=%d,1,1)", grid_x, grid_y, grid_z, seq_len);
+  }
+  const int half = head_dim / 2;
+  const int hd = half < BLOCK_D ? half : BLOCK_D;
+  const int64_t pairs = static_cast<int64_t>(seq_len) * hd;
+  if (pairs == 0) return ok();
+  if (x_ptr == nullptr || cos_ptr == nullptr || sin_ptr == nullptr || out_ptr == nullptr) {
+    return fail(NESO_ERR_INVALID_ARG, "null pointer");
+  }
+  cudaStream_t st = as_stream(stream);
+  rope_kernel_impl<<<stream_blocks(pairs), kStreamThreads, 0, st>>>(x_ptr, cos_ptr, sin_ptr, out_ptr, pairs, hd,
+                                                                      half, head_dim);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "rope launch");
+  return ok();
+}
+
+int neso_silu_kernel(const float* x_ptr, float* out_ptr, int32_t n, int32_t BLOCK, uint32_t grid_x, uint32_t grid_y,
+                     uint32_t grid_z, neso_stream_t stream) {
+  if (n < 0) return fail(NESO_ERR_INVALID_ARG, "n must be >= 0 (got %d)", n);
+  if (!pow2(BLOCK)) return fail(NESO_ERR_INVALID_ARG, "BLOCK must be a power of two (got %d)", BLOCK);
+  const uint32_t want = static_cast<uint32_t>((static_cast<int64_t>(n) + BLOCK - 1) / BLOCK);
+  if (grid_x != want || grid_y != 1 || grid_z != 1) {
+    return fail(NESO_ERR_GRID, "grid (%u,%u,%u) != (cdiv(%d,%d)=%u,1,1)", grid_x, grid_y, grid_z, n, BLOCK, want);
+  }
+  if (n == 0) return ok();
+  if (x_ptr == nullptr || out_ptr == nullptr) return fail(NESO_ERR_INVALID_ARG, "null pointer");
+  cudaStream_t st = as_stream(stream);
+  int64_t done = 0;
+  if (aligned16(x_ptr) && aligned16(out_ptr)) {
+    const int64_t n4 = n / 4;
+    if (n4 > 0) {
+      silu_vec4_kernel<<<stream_blocks(n4), kStreamThreads, 0, st>>>(reinterpret_cast<const float4*>(x_ptr),
+                                                                      reinterpret_cast<float4*>(out_ptr), n4);
+    }
+    done = n4 * 4;
+  }
+  if (done < n) silu_scalar_kernel<<<stream_blocks(n - done), kStreamThreads, 0, st>>>(x_ptr, out_ptr, done, n);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "silu launch");
+  return ok();
+}
+
+}  // extern "C"

@@ -172,5 +172,22 @@ w8a16_scaled_matmul = Kernel(
      ("stride_cm", I)],
     {"BM": 64, "BN": 64, "BK": 32})
 
+# LLM building blocks (tests/test_advanced12.py:104-177)
+rmsnorm_kernel = Kernel(
+    "rmsnorm_kernel", "neso_rmsnorm_kernel",
+    [("x_ptr", P), ("weight_ptr", P), ("out_ptr", P), ("row_stride", I), ("n_cols", I), ("eps", F)],
+    {"BLOCK_SIZE": None})
+residual_rmsnorm_kernel = Kernel(
+    "residual_rmsnorm_kernel", "neso_residual_rmsnorm_kernel",
+    [("x_ptr", P), ("residual_ptr", P), ("weight_ptr", P), ("out_ptr", P), ("row_stride", I), ("n_cols", I),
+     ("eps", F)],
+    {"BLOCK_SIZE": None})
+rope_kernel = Kernel(
+    "rope_kernel", "neso_rope_kernel",
+    [("x_ptr", P), ("cos_ptr", P), ("sin_ptr", P), ("out_ptr", P), ("seq_len", I), ("head_dim", I)],
+    {"BLOCK_D": None})
+silu_kernel = Kernel("silu_kernel", "neso_silu_kernel", [("x_ptr", P), ("out_ptr", P), ("n", I)], {"BLOCK": None})
+
 KERNELS = {k.name: k for k in (vector_add, add_kernel, scale, flash_attention_fwd, rel_pos_fa2_fwd, matmul_kernel,
-                                matmul_tiled, w8a16_matmul, w8a16_scaled_matmul)}
+                                matmul_tiled, w8a16_matmul, w8a16_scaled_matmul, rmsnorm_kernel,
+                                residual_rmsnorm_kernel, rope_kernel, silu_kernel)}

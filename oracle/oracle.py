@@ -22,6 +22,9 @@ Parity pins and where they come from:
   * W8A16: (X @ f16(W)) * scale[n] (tests/test_quantized_matmul.py:288-311).
   * W4A16 g128: sum_g s[g,n] * sum_{k in g} X[m,k] q[k,n], group semantics of
     tests/test_advanced12.py:69-84 (offs // group_size), packing pinned below.
+  * RMSNorm / residual RMSNorm, RoPE, SiLU: tests/test_advanced12.py:104-177
+    (their own checks :243-298); RoPE is compared bit for bit (plain fp32
+    products and sums), the others with a tolerance.
 """
 from __future__ import annotations
 
@@ -33,6 +36,7 @@ import torch
 __all__ = [
     "vector_add", "scale", "attention", "attention_rows", "gemm", "w8a16_matmul", "pack_int4",
     "unpack_int4", "w4a16_g128_matmul", "harness_elementwise_inputs", "harness_fa2_values",
+    "rmsnorm", "rope", "silu",
 ]
 
 
@@ -170,6 +174,37 @@ def w4a16_g128_matmul(x: torch.Tensor, wq: torch.Tensor, scales: torch.Tensor, g
     q = unpack_int4(wq).float()
     s = scales.float().repeat_interleave(group, dim=0)
     return torch.matmul(x.float(), q * s)
+
+
+def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float, residual: torch.Tensor | None = None,
+            block: int | None = None) -> torch.Tensor:
+    """h / sqrt(sum(h^2) / n_cols + eps) * w, h = x (+ residual), row-wise over
+    the first min(block, n_cols) columns, divided by the full n_cols
+    (tests/test_advanced12.py:104-120, :135-153; reference check :243-254)."""
+    h = x.float() if residual is None else x.float() + residual.float()
+    n_cols = h.shape[-1]
+    c = n_cols if block is None else min(block, n_cols)
+    hc = h[..., :c]
+    rms = ((hc * hc).sum(dim=-1, keepdim=True) / n_cols + eps).sqrt()
+    return hc / rms * w.float()[:c]  # the columns the kernel writes
+
+
+def rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
+         block_d: int | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """Rotate pairs (d, d + head_dim/2) of x [seq, head_dim] by cos/sin
+    [seq, head_dim/2] (tests/test_advanced12.py:156-176; check :281-298); only
+    d < min(block_d, head_dim/2) is rotated and returned."""
+    half = x.shape[-1] // 2
+    hd = half if block_d is None else min(block_d, half)
+    x1, x2 = x[:, :hd].float(), x[:, half:half + hd].float()
+    c, s = cos[:, :hd].float(), sin[:, :hd].float()
+    return x1 * c - x2 * s, x1 * s + x2 * c  # columns [0, hd) and [half, half + hd)
+
+
+def silu(x: torch.Tensor) -> torch.Tensor:
+    """x * sigmoid(x) (tests/test_advanced12.py:123-132; check :257-265)."""
+    xf = x.float()
+    return xf * torch.sigmoid(xf)
 
 
 def fa2_flops(B: int, H: int, S: int, D: int, causal: bool = False) -> float:

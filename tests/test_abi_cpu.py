@@ -155,3 +155,22 @@ def test_launch_stream_and_device_selection(monkeypatch):
     monkeypatch.delattr(torch._C, "_cuda_getCurrentRawStream")
     monkeypatch.setattr(torch.cuda, "current_stream", lambda dev: _Stream())
     assert kernels.current_stream_and_device([_FakeCudaTensor(0)]) == 0xBEEF
+
+
+def test_rowops_reject_bad_launch_before_the_device():
+    lib = _lib.lib()
+    G, I = _lib.NESO_ERR_GRID, _lib.NESO_ERR_INVALID_ARG
+    assert lib.neso_rmsnorm_kernel(None, None, None, 128, 128, 1e-5, 100, 32, 1, 1, None) == I  # BLOCK not 2^k
+    assert lib.neso_rmsnorm_kernel(None, None, None, 128, 128, 1e-5, 128, 32, 2, 1, None) == G
+    assert lib.neso_residual_rmsnorm_kernel(None, None, None, None, 128, 128, 1e-5, 128, 32, 1, 3, None) == G
+    assert lib.neso_rope_kernel(None, None, None, None, 16, 64, 32, 15, 1, 1, None) == G   # grid != seq_len
+    assert lib.neso_rope_kernel(None, None, None, None, 16, 64, 24, 16, 1, 1, None) == I   # BLOCK_D not 2^k
+    assert lib.neso_silu_kernel(None, None, 2048, 256, 9, 1, 1, None) == G                 # cdiv(2048, 256) = 8
+    assert lib.neso_silu_kernel(None, None, 2048, 300, 7, 1, 1, None) == I
+    # empty problems are no-ops
+    assert lib.neso_rmsnorm_kernel(None, None, None, 128, 128, 1e-5, 128, 0, 1, 1, None) == _lib.NESO_OK
+    assert lib.neso_rope_kernel(None, None, None, None, 0, 64, 32, 0, 1, 1, None) == _lib.NESO_OK
+    assert lib.neso_silu_kernel(None, None, 0, 256, 0, 1, 1, None) == _lib.NESO_OK
+    for name in ("rmsnorm_kernel", "residual_rmsnorm_kernel", "rope_kernel", "silu_kernel"):
+        meta = json.loads(lib.neso_kernel_metadata(name.encode()).decode())
+        assert meta["kernel_name"] == name
