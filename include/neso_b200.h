@@ -108,6 +108,30 @@ NESO_API int neso_rope_kernel(const float* x_ptr, const float* cos_ptr, const fl
  *   out = x * sigmoid(x). Reference grid: (cdiv(n, BLOCK), 1, 1). */
 NESO_API int neso_silu_kernel(const float* x_ptr, float* out_ptr, int32_t n, int32_t BLOCK, uint32_t grid_x,
                      uint32_t grid_y, uint32_t grid_z, neso_stream_t stream);
+/* tests/test_triton_jit.py:55-70  softmax_kernel(output_ptr, input_ptr,
+ *   input_row_stride, output_row_stride, n_cols, BLOCK_SIZE): row-wise softmax
+ *   over the first min(BLOCK_SIZE, n_cols) columns. Reference grid: (M, 1, 1). */
+NESO_API int neso_softmax_kernel(float* output_ptr, const float* input_ptr, int32_t input_row_stride,
+                        int32_t output_row_stride, int32_t n_cols, int32_t BLOCK_SIZE, uint32_t grid_x,
+                        uint32_t grid_y, uint32_t grid_z, neso_stream_t stream);
+/* tests/test_advanced12.py:54-67  per_channel_dequant_kernel(x_int8_ptr,
+ *   scale_ptr, zero_ptr, out_ptr, n_rows, n_cols, BLOCK_M, BLOCK_N):
+ *   out = (x - zero[col]) * scale[col]; x held as int32 (the reference test
+ *   passes int32, :222). Reference grid: (cdiv(n_rows, BLOCK_M), cdiv(n_cols, BLOCK_N), 1). */
+NESO_API int neso_per_channel_dequant_kernel(const int32_t* x_int8_ptr, const float* scale_ptr, const float* zero_ptr,
+                                    float* out_ptr, int32_t n_rows, int32_t n_cols, int32_t BLOCK_M, int32_t BLOCK_N,
+                                    uint32_t grid_x, uint32_t grid_y, uint32_t grid_z, neso_stream_t stream);
+/* tests/test_advanced12.py:69-84  grouped_dequant_kernel(x_int8_ptr, scale_ptr,
+ *   zero_ptr, out_ptr, n, group_size, BLOCK): out[i] = (x[i] - zero[i / gs]) *
+ *   scale[i / gs]; x held as int32. Reference grid: (cdiv(n, BLOCK), 1, 1). */
+NESO_API int neso_grouped_dequant_kernel(const int32_t* x_int8_ptr, const float* scale_ptr, const float* zero_ptr,
+                                float* out_ptr, int32_t n, int32_t group_size, int32_t BLOCK, uint32_t grid_x,
+                                uint32_t grid_y, uint32_t grid_z, neso_stream_t stream);
+/* tests/test_advanced12.py:87-101  quantize_kernel(x_ptr, scale_ptr, out_ptr, n,
+ *   BLOCK): q = x / scale[0], rounded as q +/- 0.5 truncated toward zero,
+ *   clamped to [-128, 127], stored as int32. Reference grid: (cdiv(n, BLOCK), 1, 1). */
+NESO_API int neso_quantize_kernel(const float* x_ptr, const float* scale_ptr, int32_t* out_ptr, int32_t n, int32_t BLOCK,
+                         uint32_t grid_x, uint32_t grid_y, uint32_t grid_z, neso_stream_t stream);
 
 /* ------------------------------------------------------ flash attention -- */
 /* tests/test_flash_attention.py:149-152

@@ -74,6 +74,10 @@ SIGNATURES: dict[str, tuple[object, list]] = {
     "neso_residual_rmsnorm_kernel": (_int, [_p, _p, _p, _p, _i32, _i32, _f32, _i32, *_GRID, _p]),
     "neso_rope_kernel": (_int, [_p, _p, _p, _p, _i32, _i32, _i32, *_GRID, _p]),
     "neso_silu_kernel": (_int, [_p, _p, _i32, _i32, *_GRID, _p]),
+    "neso_softmax_kernel": (_int, [_p, _p, _i32, _i32, _i32, _i32, *_GRID, _p]),
+    "neso_per_channel_dequant_kernel": (_int, [_p, _p, _p, _p, _i32, _i32, _i32, _i32, *_GRID, _p]),
+    "neso_grouped_dequant_kernel": (_int, [_p, _p, _p, _p, _i32, _i32, _i32, *_GRID, _p]),
+    "neso_quantize_kernel": (_int, [_p, _p, _p, _i32, _i32, *_GRID, _p]),
     "neso_flash_attention_fwd": (_int, [_p, _p, _p, _p, _i32, _i32, _i32, _f32, _i32, *_GRID, _p]),
     "neso_rel_pos_fa2_fwd": (_int, [_p, _p, _p, _p, _p, _i32, _i32, _f32, _i32, _i32, _i32, *_GRID, _p]),
     "neso_fa2_fwd": (_int, [_p, _p, _p, _p, _i32, _i32, _i32, _i32, _f32, _i32, _p]),

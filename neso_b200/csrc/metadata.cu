@@ -130,6 +130,24 @@ const std::unordered_map<std::string, std::string>& table() {
         {"silu_kernel",
          {{"x_ptr", "*fp32", "const float*"}, {"out_ptr", "*fp32", "float*"}, {"n", "i32", "int32_t"}},
          "{\"BLOCK\": 256}", 256, {"cdiv(n, BLOCK)", "1", "1"}},
+        {"softmax_kernel",
+         {{"output_ptr", "*fp32", "float*"}, {"input_ptr", "*fp32", "const float*"},
+          {"input_row_stride", "i32", "int32_t"}, {"output_row_stride", "i32", "int32_t"}, {"n_cols", "i32", "int32_t"}},
+         "{\"BLOCK_SIZE\": 128}", 256, {"M", "1", "1"}},
+        {"per_channel_dequant_kernel",
+         {{"x_int8_ptr", "*i32", "const int32_t*"}, {"scale_ptr", "*fp32", "const float*"},
+          {"zero_ptr", "*fp32", "const float*"}, {"out_ptr", "*fp32", "float*"}, {"n_rows", "i32", "int32_t"},
+          {"n_cols", "i32", "int32_t"}},
+         "{\"BLOCK_M\": 32, \"BLOCK_N\": 32}", 256, {"cdiv(n_rows, BLOCK_M)", "cdiv(n_cols, BLOCK_N)", "1"}},
+        {"grouped_dequant_kernel",
+         {{"x_int8_ptr", "*i32", "const int32_t*"}, {"scale_ptr", "*fp32", "const float*"},
+          {"zero_ptr", "*fp32", "const float*"}, {"out_ptr", "*fp32", "float*"}, {"n", "i32", "int32_t"},
+          {"group_size", "i32", "int32_t"}},
+         "{\"BLOCK\": 256}", 256, {"cdiv(n, BLOCK)", "1", "1"}},
+        {"quantize_kernel",
+         {{"x_ptr", "*fp32", "const float*"}, {"scale_ptr", "*fp32", "const float*"}, {"out_ptr", "*i32", "int32_t*"},
+          {"n", "i32", "int32_t"}},
+         "{\"BLOCK\": 256}", 256, {"cdiv(n, BLOCK)", "1", "1"}},
     };
     std::unordered_map<std::string, std::string> m;
     for (const KernelMeta& k : ks) m.emplace(k.name, to_json(k));

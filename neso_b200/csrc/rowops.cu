@@ -14,6 +14,14 @@
 //       (:158-176); products and sums are rounded separately (no FMA
 //       contraction), so results equal a plain fp32 evaluation bit for bit.
 //   silu  x * sigmoid(x), 16-byte grid-stride stream (:124-132).
+//   softmax (tests/test_triton_jit.py:55-70)  one warp per row over the first
+//       min(BLOCK_SIZE, n_cols) columns: max, sum of exp, then exp / sum, each
+//       a pass over the row with a fixed-order shuffle reduction.
+//   per_channel_dequant, grouped_dequant, quantize (tests/test_advanced12.py:
+//       54-101)  grid-stride streams. As in the reference's tests (:222,
+//       :238, :243) the "int8" values are held in int32 storage; quantize
+//       rounds as that kernel does (q +/- 0.5, truncated toward zero) and
+//       clamps to [-128, 127].
 // Every element is read and written by the same thread, so in-place calls
 // (out == x) are safe as in the reference.
 #include "runtime.h"
@@ -115,6 +123,58 @@ __global__ void __launch_bounds__(kStreamThreads)
   for (int64_t i = begin + static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     out[i] = silu1(x[i]);
+  }
+}
+
+__global__ void __launch_bounds__(kRowThreads)
+    softmax_rows_kernel(float* out, const float* in, int64_t rows, int64_t in_stride, int64_t out_stride,
+                        int ncols) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp0 = static_cast<int64_t>(blockIdx.x) * kRowWarps + (threadIdx.x >> 5);
+  const int64_t wstep = static_cast<int64_t>(gridDim.x) * kRowWarps;
+  for (int64_t row = warp0; row < rows; row += wstep) {
+    const float* xr = in + row * in_stride;
+    float* orow = out + row * out_stride;
+    float m = -INFINITY;
+    for (int c = lane; c < ncols; c += 32) m = fmaxf(m, xr[c]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float sum = 0.f;
+    for (int c = lane; c < ncols; c += 32) sum += expf(xr[c] - m);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    for (int c = lane; c < ncols; c += 32) orow[c] = __fdiv_rn(expf(xr[c] - m), sum);
+  }
+}
+
+__global__ void __launch_bounds__(kStreamThreads)
+    per_channel_dequant_impl(const int32_t* x, const float* scale, const float* zero, float* out, int64_t total,
+                             int ncols) {
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int c = static_cast<int>(i % ncols);
+    out[i] = __fmul_rn(__fsub_rn(static_cast<float>(x[i]), zero[c]), scale[c]);
+  }
+}
+
+__global__ void __launch_bounds__(kStreamThreads)
+    grouped_dequant_impl(const int32_t* x, const float* scale, const float* zero, float* out, int64_t n, int gs) {
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t g = i / gs;
+    out[i] = __fmul_rn(__fsub_rn(static_cast<float>(x[i]), zero[g]), scale[g]);
+  }
+}
+
+__global__ void __launch_bounds__(kStreamThreads)
+    quantize_impl(const float* x, const float* scale, int32_t* out, int64_t n) {
+  const float s = *scale;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const float q = __fdiv_rn(x[i], s);
+    int v = __float2int_rz(q >= 0.f ? __fadd_rn(q, 0.5f) : __fsub_rn(q, 0.5f));
+    v = v > 127 ? 127 : (v < -128 ? -128 : v);
+    out[i] = v;
   }
 }
 
@@ -221,6 +281,87 @@ int neso_silu_kernel(const float* x_ptr, float* out_ptr, int32_t n, int32_t BLOC
   if (done < n) silu_scalar_kernel<<<stream_blocks(n - done), kStreamThreads, 0, st>>>(x_ptr, out_ptr, done, n);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "silu launch");
+  return ok();
+}
+
+int neso_softmax_kernel(float* output_ptr, const float* input_ptr, int32_t input_row_stride,
+                        int32_t output_row_stride, int32_t n_cols, int32_t BLOCK_SIZE, uint32_t grid_x,
+                        uint32_t grid_y, uint32_t grid_z, neso_stream_t stream) {
+  if (!pow2(BLOCK_SIZE)) return fail(NESO_ERR_INVALID_ARG, "BLOCK_SIZE must be a power of two (got %d)", BLOCK_SIZE);
+  if (grid_y != 1 || grid_z != 1) return fail(NESO_ERR_GRID, "grid (%u,%u,%u) must be (rows, 1, 1)", grid_x, grid_y, grid_z);
+  if (n_cols < 0 || input_row_stride < 0 || output_row_stride < 0) {
+    return fail(NESO_ERR_INVALID_ARG, "n_cols and row strides must be >= 0");
+  }
+  const int ncols = n_cols < BLOCK_SIZE ? n_cols : BLOCK_SIZE;
+  if (grid_x == 0 || ncols == 0) return ok();
+  if (output_ptr == nullptr || input_ptr == nullptr) return fail(NESO_ERR_INVALID_ARG, "null pointer");
+  const int64_t rows = grid_x;
+  const int64_t cap = static_cast<int64_t>(sm_count()) * (2048 / kRowThreads);
+  const int64_t want = (rows + kRowWarps - 1) / kRowWarps;
+  softmax_rows_kernel<<<static_cast<int>(want < cap ? want : cap), kRowThreads, 0, as_stream(stream)>>>(
+      output_ptr, input_ptr, rows, input_row_stride, output_row_stride, ncols);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "softmax launch");
+  return ok();
+}
+
+int neso_per_channel_dequant_kernel(const int32_t* x_int8_ptr, const float* scale_ptr, const float* zero_ptr,
+                                    float* out_ptr, int32_t n_rows, int32_t n_cols, int32_t BLOCK_M, int32_t BLOCK_N,
+                                    uint32_t grid_x, uint32_t grid_y, uint32_t grid_z, neso_stream_t stream) {
+  if (!pow2(BLOCK_M) || !pow2(BLOCK_N)) return fail(NESO_ERR_INVALID_ARG, "BLOCK_M and BLOCK_N must be powers of two");
+  if (n_rows < 0 || n_cols < 0) return fail(NESO_ERR_INVALID_ARG, "n_rows and n_cols must be >= 0");
+  const uint32_t gx = static_cast<uint32_t>((static_cast<int64_t>(n_rows) + BLOCK_M - 1) / BLOCK_M);
+  const uint32_t gy = static_cast<uint32_t>((static_cast<int64_t>(n_cols) + BLOCK_N - 1) / BLOCK_N);
+  if (grid_x != gx || grid_y != gy || grid_z != 1) {
+    return fail(NESO_ERR_GRID, "grid (%u,%u,%u) != (cdiv(n_rows, BLOCK_M)=%u, cdiv(n_cols, BLOCK_N)=%u, 1)", grid_x,
+                grid_y, grid_z, gx, gy);
+  }
+  const int64_t total = static_cast<int64_t>(n_rows) * n_cols;
+  if (total == 0) return ok();
+  if (x_int8_ptr == nullptr || scale_ptr == nullptr || zero_ptr == nullptr || out_ptr == nullptr) {
+    return fail(NESO_ERR_INVALID_ARG, "null pointer");
+  }
+  per_channel_dequant_impl<<<stream_blocks(total), kStreamThreads, 0, as_stream(stream)>>>(x_int8_ptr, scale_ptr,
+                                                                                          zero_ptr, out_ptr, total,
+                                                                                          n_cols);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "per_channel_dequant launch");
+  return ok();
+}
+
+int neso_grouped_dequant_kernel(const int32_t* x_int8_ptr, const float* scale_ptr, const float* zero_ptr,
+                                float* out_ptr, int32_t n, int32_t group_size, int32_t BLOCK, uint32_t grid_x,
+                                uint32_t grid_y, uint32_t grid_z, neso_stream_t stream) {
+  if (!pow2(BLOCK)) return fail(NESO_ERR_INVALID_ARG, "BLOCK must be a power of two (got %d)", BLOCK);
+  if (n < 0 || group_size <= 0) return fail(NESO_ERR_INVALID_ARG, "n must be >= 0 and group_size > 0");
+  const uint32_t want = static_cast<uint32_t>((static_cast<int64_t>(n) + BLOCK - 1) / BLOCK);
+  if (grid_x != want || grid_y != 1 || grid_z != 1) {
+    return fail(NESO_ERR_GRID, "grid (%u,%u,%u) != (cdiv(%d,%d)=%u,1,1)", grid_x, grid_y, grid_z, n, BLOCK, want);
+  }
+  if (n == 0) return ok();
+  if (x_int8_ptr == nullptr || scale_ptr == nullptr || zero_ptr == nullptr || out_ptr == nullptr) {
+    return fail(NESO_ERR_INVALID_ARG, "null pointer");
+  }
+  grouped_dequant_impl<<<stream_blocks(n), kStreamThreads, 0, as_stream(stream)>>>(x_int8_ptr, scale_ptr, zero_ptr,
+                                                                                   out_ptr, n, group_size);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "grouped_dequant launch");
+  return ok();
+}
+
+int neso_quantize_kernel(const float* x_ptr, const float* scale_ptr, int32_t* out_ptr, int32_t n, int32_t BLOCK,
+                         uint32_t grid_x, uint32_t grid_y, uint32_t grid_z, neso_stream_t stream) {
+  if (!pow2(BLOCK)) return fail(NESO_ERR_INVALID_ARG, "BLOCK must be a power of two (got %d)", BLOCK);
+  if (n < 0) return fail(NESO_ERR_INVALID_ARG, "n must be >= 0 (got %d)", n);
+  const uint32_t want = static_cast<uint32_t>((static_cast<int64_t>(n) + BLOCK - 1) / BLOCK);
+  if (grid_x != want || grid_y != 1 || grid_z != 1) {
+    return fail(NESO_ERR_GRID, "grid (%u,%u,%u) != (cdiv(%d,%d)=%u,1,1)", grid_x, grid_y, grid_z, n, BLOCK, want);
+  }
+  if (n == 0) return ok();
+  if (x_ptr == nullptr || scale_ptr == nullptr || out_ptr == nullptr) return fail(NESO_ERR_INVALID_ARG, "null pointer");
+  quantize_impl<<<stream_blocks(n), kStreamThreads, 0, as_stream(stream)>>>(x_ptr, scale_ptr, out_ptr, n);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "quantize launch");
   return ok();
 }
 

@@ -187,7 +187,25 @@ rope_kernel = Kernel(
     [("x_ptr", P), ("cos_ptr", P), ("sin_ptr", P), ("out_ptr", P), ("seq_len", I), ("head_dim", I)],
     {"BLOCK_D": None})
 silu_kernel = Kernel("silu_kernel", "neso_silu_kernel", [("x_ptr", P), ("out_ptr", P), ("n", I)], {"BLOCK": None})
+# tests/test_triton_jit.py:55-70
+softmax_kernel = Kernel(
+    "softmax_kernel", "neso_softmax_kernel",
+    [("output_ptr", P), ("input_ptr", P), ("input_row_stride", I), ("output_row_stride", I), ("n_cols", I)],
+    {"BLOCK_SIZE": None})
+# tests/test_advanced12.py:54-101 (int8 values held in int32 tensors, as the reference's tests pass them)
+per_channel_dequant_kernel = Kernel(
+    "per_channel_dequant_kernel", "neso_per_channel_dequant_kernel",
+    [("x_int8_ptr", P), ("scale_ptr", P), ("zero_ptr", P), ("out_ptr", P), ("n_rows", I), ("n_cols", I)],
+    {"BLOCK_M": None, "BLOCK_N": None})
+grouped_dequant_kernel = Kernel(
+    "grouped_dequant_kernel", "neso_grouped_dequant_kernel",
+    [("x_int8_ptr", P), ("scale_ptr", P), ("zero_ptr", P), ("out_ptr", P), ("n", I), ("group_size", I)],
+    {"BLOCK": None})
+quantize_kernel = Kernel(
+    "quantize_kernel", "neso_quantize_kernel", [("x_ptr", P), ("scale_ptr", P), ("out_ptr", P), ("n", I)],
+    {"BLOCK": None})
 
 KERNELS = {k.name: k for k in (vector_add, add_kernel, scale, flash_attention_fwd, rel_pos_fa2_fwd, matmul_kernel,
                                 matmul_tiled, w8a16_matmul, w8a16_scaled_matmul, rmsnorm_kernel,
-                                residual_rmsnorm_kernel, rope_kernel, silu_kernel)}
+                                residual_rmsnorm_kernel, rope_kernel, silu_kernel, softmax_kernel,
+                                per_channel_dequant_kernel, grouped_dequant_kernel, quantize_kernel)}

@@ -36,7 +36,7 @@ import torch
 __all__ = [
     "vector_add", "scale", "attention", "attention_rows", "gemm", "w8a16_matmul", "pack_int4",
     "unpack_int4", "w4a16_g128_matmul", "harness_elementwise_inputs", "harness_fa2_values",
-    "rmsnorm", "rope", "silu",
+    "rmsnorm", "rope", "silu", "softmax_rows", "per_channel_dequant", "grouped_dequant", "quantize_int8",
 ]
 
 
@@ -205,6 +205,32 @@ def silu(x: torch.Tensor) -> torch.Tensor:
     """x * sigmoid(x) (tests/test_advanced12.py:123-132; check :257-265)."""
     xf = x.float()
     return xf * torch.sigmoid(xf)
+
+
+def softmax_rows(x: torch.Tensor, block: int | None = None) -> torch.Tensor:
+    """Row softmax over the first min(block, n_cols) columns
+    (tests/test_triton_jit.py:55-70; check :307-325)."""
+    c = x.shape[-1] if block is None else min(block, x.shape[-1])
+    return torch.softmax(x[..., :c].float(), dim=-1)
+
+
+def per_channel_dequant(x: torch.Tensor, scale: torch.Tensor, zero: torch.Tensor) -> torch.Tensor:
+    """(x - zero[col]) * scale[col] (tests/test_advanced12.py:54-67; check :216-226)."""
+    return (x.float() - zero.float()[None, :]) * scale.float()[None, :]
+
+
+def grouped_dequant(x: torch.Tensor, scale: torch.Tensor, zero: torch.Tensor, group_size: int) -> torch.Tensor:
+    """(x[i] - zero[i // gs]) * scale[i // gs] (tests/test_advanced12.py:69-84; check :229-241)."""
+    g = torch.arange(x.numel()) // group_size
+    return (x.float() - zero.float()[g]) * scale.float()[g]
+
+
+def quantize_int8(x: torch.Tensor, scale: torch.Tensor) -> torch.Tensor:
+    """The kernel's rounding (tests/test_advanced12.py:87-101): q = x / scale,
+    q + 0.5 or q - 0.5 by sign, truncated toward zero, clamped to [-128, 127]."""
+    q = x.float() / scale.float()[0]
+    r = torch.where(q >= 0, (q + 0.5).to(torch.int32), (q - 0.5).to(torch.int32))
+    return r.clamp(-128, 127).to(torch.int32)
 
 
 def fa2_flops(B: int, H: int, S: int, D: int, causal: bool = False) -> float:

@@ -171,6 +171,11 @@ def test_rowops_reject_bad_launch_before_the_device():
     assert lib.neso_rmsnorm_kernel(None, None, None, 128, 128, 1e-5, 128, 0, 1, 1, None) == _lib.NESO_OK
     assert lib.neso_rope_kernel(None, None, None, None, 0, 64, 32, 0, 1, 1, None) == _lib.NESO_OK
     assert lib.neso_silu_kernel(None, None, 0, 256, 0, 1, 1, None) == _lib.NESO_OK
-    for name in ("rmsnorm_kernel", "residual_rmsnorm_kernel", "rope_kernel", "silu_kernel"):
+    assert lib.neso_softmax_kernel(None, None, 128, 128, 128, 96, 16, 1, 1, None) == I              # BLOCK not 2^k
+    assert lib.neso_per_channel_dequant_kernel(None, None, None, None, 32, 64, 32, 32, 1, 1, 1, None) == G  # want (1, 2, 1)
+    assert lib.neso_grouped_dequant_kernel(None, None, None, None, 1024, 0, 256, 4, 1, 1, None) == I  # group 0
+    assert lib.neso_quantize_kernel(None, None, None, 1024, 256, 5, 1, 1, None) == G
+    for name in ("rmsnorm_kernel", "residual_rmsnorm_kernel", "rope_kernel", "silu_kernel", "softmax_kernel",
+                 "per_channel_dequant_kernel", "grouped_dequant_kernel", "quantize_kernel"):
         meta = json.loads(lib.neso_kernel_metadata(name.encode()).decode())
         assert meta["kernel_name"] == name

@@ -43,7 +43,7 @@ def test_signature_errors_match_reference():
     with pytest.raises(ValueError, match="expected a Neso target"):
         aot.compile_kernel("vector_add", "*fp32, *fp32, *fp32, i32, 1024", target="cuda:100:32")
     with pytest.raises(KeyError):
-        aot.compile_kernel("softmax_kernel", "*fp32, *fp32, i32, 1024")
+        aot.compile_kernel("square_kernel", "*fp32, *fp32, i32, 1024")
     with pytest.raises(ValueError, match="constexpr"):
         aot.compile_kernel("vector_add", "*fp32, *fp32, *fp32, i32, i32")
 

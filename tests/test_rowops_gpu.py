@@ -125,3 +125,46 @@ def test_silu_ragged_and_unaligned(dev):
     out2 = torch.empty(n + 1, device=dev)
     kernels.silu_kernel[(_cdiv(n, 1024),)](xd[1:], out2[1:], n, BLOCK=1024)  # 4-byte offset: scalar path
     torch.testing.assert_close(out2[1:].cpu(), oracle.silu(x[1:]), atol=1e-6, rtol=1e-5)
+
+
+@pytest.mark.parametrize("M,N,block", [(16, 128, 128), (8, 256, 256), (300, 1000, 1024), (5, 300, 128)])
+def test_softmax_rows(dev, M, N, block):
+    # tests/test_triton_jit.py:307-325 launches, plus long, strided-output and
+    # partial-row (BLOCK_SIZE < n_cols: the columns past BLOCK_SIZE untouched) cases.
+    g = torch.Generator().manual_seed(M + N)
+    x = torch.randn(M, N, generator=g) * 4
+    out = torch.full((M, N + 3), 7.0, device=dev)
+    kernels.softmax_kernel[(M,)](out, x.to(dev), N, N + 3, N, BLOCK_SIZE=block)
+    c = min(block, N)
+    torch.testing.assert_close(out[:, :c].cpu(), oracle.softmax_rows(x, block), atol=1e-6, rtol=1e-5)
+    assert torch.all(out[:, c:] == 7.0)
+
+
+def test_dequant_and_quantize(dev):
+    # tests/test_advanced12.py:216-241 launches (int8 values in int32 tensors) plus ragged sizes;
+    # quantize follows the kernel's own rounding bit for bit.
+    g = torch.Generator().manual_seed(9)
+    for (M, N) in [(32, 64), (77, 1001)]:
+        x = torch.randint(-128, 127, (M, N), generator=g, dtype=torch.int32)
+        sc = torch.rand(N, generator=g) * 0.1 + 0.01
+        zr = torch.randint(-5, 5, (N,), generator=g).float()
+        out = torch.zeros(M, N, device=dev)
+        kernels.per_channel_dequant_kernel[(_cdiv(M, 32), _cdiv(N, 32))](x.to(dev), sc.to(dev), zr.to(dev), out, M, N,
+                                                                         BLOCK_M=32, BLOCK_N=32)
+        assert torch.equal(out.cpu(), oracle.per_channel_dequant(x, sc, zr))
+    for (n, gs) in [(1024, 128), (100_003, 64)]:
+        x = torch.randint(-128, 127, (n,), generator=g, dtype=torch.int32)
+        ng = _cdiv(n, gs)
+        sc = torch.rand(ng, generator=g) * 0.1 + 0.01
+        zr = torch.randint(-5, 5, (ng,), generator=g).float()
+        out = torch.zeros(n, device=dev)
+        kernels.grouped_dequant_kernel[lambda m: (_cdiv(n, m["BLOCK"]),)](x.to(dev), sc.to(dev), zr.to(dev), out, n,
+                                                                          gs, BLOCK=256)
+        assert torch.equal(out.cpu(), oracle.grouped_dequant(x, sc, zr, gs))
+    for n in (1024, 50_001):
+        x = torch.randn(n, generator=g) * 10
+        x[:4] = torch.tensor([1e6, -1e6, 0.5, -0.5])  # clamping and ties
+        scale = torch.tensor([x[4:].abs().max().item() / 127.0])
+        out = torch.zeros(n, device=dev, dtype=torch.int32)
+        kernels.quantize_kernel[(_cdiv(n, 256),)](x.to(dev), scale.to(dev), out, n, BLOCK=256)
+        assert torch.equal(out.cpu(), oracle.quantize_int8(x, scale))
