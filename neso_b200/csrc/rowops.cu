@@ -1,8 +1,10 @@
 // LLM building-block kernels the reference compiles and tests next to the hot
-// path (tests/test_advanced12.py:104-177): RMSNorm, residual + RMSNorm, RoPE
-// and SiLU, fp32, under the reference names, argument orders and grids.
+// path (tests/test_advanced12.py:54-177, tests/test_triton_jit.py:55-70):
+// RMSNorm, residual + RMSNorm, RoPE, SiLU, softmax, per-channel and grouped
+// dequant, quantize; fp32 (int32 for the int8 values, as the reference's tests
+// hold them), under the reference names, argument orders and grids.
 //
-// All four are HBM-bound streams:
+// All of them are HBM-bound streams:
 //   rmsnorm / residual_rmsnorm  one warp per row (8 rows per 256-thread CTA,
 //       grid-stride over rows), 16-byte loads when the row starts and the
 //       column count allow it; pass 1 sums h^2 in registers and reduces with
