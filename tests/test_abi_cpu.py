@@ -179,3 +179,24 @@ def test_rowops_reject_bad_launch_before_the_device():
                  "per_channel_dequant_kernel", "grouped_dequant_kernel", "quantize_kernel"):
         meta = json.loads(lib.neso_kernel_metadata(name.encode()).decode())
         assert meta["kernel_name"] == name
+
+
+def test_row_kernel_handles_bind_like_the_reference_launcher():
+    # Reference launches (tests/test_advanced12.py:249, :275, :295; tests/test_triton_jit.py:311):
+    # runtime arguments in order, BLOCK constexprs by name and required (no default is invented).
+    from neso_b200 import kernels
+
+    b = kernels.rmsnorm_kernel.bind("x", "w", "out", 128, 128, 1e-5, BLOCK_SIZE=128)
+    assert list(b) == ["x_ptr", "weight_ptr", "out_ptr", "row_stride", "n_cols", "eps", "BLOCK_SIZE"]
+    b = kernels.softmax_kernel.bind("out", "x", 128, 128, 128, BLOCK_SIZE=256)
+    assert b["output_ptr"] == "out" and b["input_ptr"] == "x" and b["BLOCK_SIZE"] == 256
+    b = kernels.per_channel_dequant_kernel.bind("x", "s", "z", "o", 32, 64, BLOCK_M=32, BLOCK_N=32)
+    assert (b["n_rows"], b["n_cols"], b["BLOCK_M"], b["BLOCK_N"]) == (32, 64, 32, 32)
+    for k, args in ((kernels.rope_kernel, ("x", "c", "s", "o", 16, 64)), (kernels.silu_kernel, ("x", "o", 2048)),
+                    (kernels.quantize_kernel, ("x", "s", "o", 1024)),
+                    (kernels.grouped_dequant_kernel, ("x", "s", "z", "o", 1024, 128))):
+        with pytest.raises(TypeError, match="constexpr"):
+            k.bind(*args)
+    assert set(kernels.KERNELS) >= {"rmsnorm_kernel", "residual_rmsnorm_kernel", "rope_kernel", "silu_kernel",
+                                    "softmax_kernel", "per_channel_dequant_kernel", "grouped_dequant_kernel",
+                                    "quantize_kernel"}
