@@ -220,14 +220,18 @@ NESO_API int neso_w4a16_g128_matmul(const void* X, const uint8_t* Wq, const void
  * neso_w8a16_matmul_mnk for callers that cannot call cudaMalloc (for example
  * code running inside a host allocator callback, a pre-reserved memory pool
  * manager, or an environment whose device memory is fully budgeted before
- * launch). Same arguments and result. Its split-K scratch is a fixed array of
- * 2^20 floats (4 MiB) compiled into the library, which every GPU that loads
- * the library keeps until the process exits; a problem whose partial sums
- * would exceed it (split count x M x N > 2^20) returns NESO_ERR_UNSUPPORTED.
- * The first call on a device resolves the array's address and should come
- * before any stream capture. All calls on a device share the array: calls
- * that overlap on the GPU (different streams, or concurrent host threads)
- * race and must be serialised by the caller. */
+ * launch). Same arguments and result (K = 0 writes zeros). It always runs the
+ * tensor-core kernel (decode batches of M <= 4 do not take the GEMV path,
+ * which keeps per-launch counters in allocated memory). Its split-K scratch is
+ * a fixed array of 2^20 floats (4 MiB) compiled into the library, which every
+ * GPU that loads the library keeps until the process exits; the K split is
+ * chosen among those whose partial sums (splits x M x N floats) fit it, down
+ * to no split at all, so no problem is refused for want of scratch. The first
+ * call on a device resolves the array's address and should come before any
+ * stream capture. All calls on a device share the array: calls that overlap
+ * on the GPU (different streams, or concurrent host threads) race and must be
+ * serialised by the caller. A timed-out device wait inside it is reported by
+ * neso_device_status until neso_clear_device_status. */
 NESO_API int neso_w8a16_matmul_mnk_noalloc(const void* X, const int8_t* W, const void* scale, float* Y, int32_t M,
                                            int32_t N, int32_t K, neso_stream_t stream);
 

@@ -635,6 +635,7 @@ void plan_splits(QProblem& p, int sms, size_t max_partial = SIZE_MAX) {
   for (int sp = 2; sp <= 16 && sp <= num_k && sp <= max_splits; ++sp) {
     const int kbps = (num_k + sp - 1) / sp;
     const int real = (num_k + kbps - 1) / kbps;  // no empty split
+    if (static_cast<size_t>(real) * p.M * p.N > max_partial) continue;  // partial sums must fit the scratch
     const int64_t units = static_cast<int64_t>(sbase) * real;
     const int64_t waves = (units + sms - 1) / sms;
     const double eff = static_cast<double>(units) / static_cast<double>(waves * sms) * (1.0 - 0.01 * real);
@@ -1172,6 +1173,16 @@ int noalloc_status_read(int* host4) {
   return e == cudaSuccess ? NESO_OK : cuda_fail(e, "reading the no-allocation status block");
 }
 
+// Zeroes that status block on the current device (neso_clear_device_status).
+int noalloc_status_clear() {
+  float* partial = nullptr;
+  int* status = nullptr;
+  int rc = noalloc_scratch(&partial, &status);
+  if (rc != NESO_OK) return rc;
+  cudaError_t e = cudaMemset(status, 0, 16 * sizeof(int));
+  return e == cudaSuccess ? NESO_OK : cuda_fail(e, "clearing the no-allocation status block");
+}
+
 }  // namespace neso
 
 using namespace neso;
@@ -1239,11 +1250,16 @@ int neso_w8a16_matmul_mnk_noalloc(const void* X, const int8_t* W, const void* sc
   // array's address, see noalloc_scratch).
   if (M < 0 || N < 0 || K < 0) return fail(NESO_ERR_INVALID_ARG, "negative size");
   if (M == 0 || N == 0) return ok();
-  if (X == nullptr || W == nullptr || Y == nullptr) return fail(NESO_ERR_INVALID_ARG, "null pointer");
+  if (Y == nullptr) return fail(NESO_ERR_INVALID_ARG, "null output");
+  if (K == 0) {  // an empty sum: Y = 0, as the allocating entry point writes it
+    zero_y_kernel<<<256, 256, 0, as_stream(stream)>>>(Y, N, M, N);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? ok() : cuda_fail(e, "zero launch");
+  }
+  if (X == nullptr || W == nullptr) return fail(NESO_ERR_INVALID_ARG, "null input");
   if (K % 8 != 0 || N % 16 != 0) {
     return fail(NESO_ERR_MISALIGNED, "noalloc W8A16 needs K %% 8 == 0 and N %% 16 == 0 (K=%d N=%d)", K, N);
   }
-  if (K == 0) return fail(NESO_ERR_UNSUPPORTED, "noalloc W8A16 needs K > 0");
   QProblem q{};
   q.X = X; q.ldx = K;
   q.W = W; q.ldw = N;
@@ -1251,9 +1267,11 @@ int neso_w8a16_matmul_mnk_noalloc(const void* X, const int8_t* W, const void* sc
   q.Y = Y; q.ldy = N;
   q.M = M; q.N = N; q.K = K;
   q.kind = kInt8;
+  // The planner only considers K splits whose partial sums fit the fixed
+  // scratch, falling back to fewer splits (one split needs none).
   plan_splits(q, sm_count(), kNoAllocScratchFloats);
   const size_t need = q.splits > 1 ? static_cast<size_t>(q.splits) * M * N : 0;
-  if (need > kNoAllocScratchFloats) {
+  if (need > kNoAllocScratchFloats) {  // guard: the planner above never returns such a plan
     return fail(NESO_ERR_UNSUPPORTED,
                 "noalloc W8A16: M=%d N=%d needs %zu split-K partial floats (%d splits), above the fixed scratch "
                 "of %zu floats; use neso_w8a16_matmul_mnk", M, N, need, q.splits, kNoAllocScratchFloats);
@@ -1262,10 +1280,9 @@ int neso_w8a16_matmul_mnk_noalloc(const void* X, const int8_t* W, const void* sc
   int* status = nullptr;
   int rc = noalloc_scratch(&partial, &status);
   if (rc != NESO_OK) return rc;
-  // The status block must start at zero for each call; the partial sums need
-  // no clearing (every split writes all of its M x N entries).
-  cudaError_t e = cudaMemsetAsync(status, 0, 16 * sizeof(int), as_stream(stream));
-  if (e != cudaSuccess) return cuda_fail(e, "clearing the no-allocation status block");
+  // The partial sums need no clearing: every split writes all of its M x N
+  // entries. The status block records the first timed-out wait since the last
+  // neso_clear_device_status, like the main status word.
   q.st.word = status;
   q.st.budget_ns = kWaitBudgetNs;
   q.partial = need > 0 ? partial : nullptr;

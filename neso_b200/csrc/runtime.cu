@@ -169,6 +169,7 @@ int kernel_setup(const void* kern, int smem_bytes, cudaFuncAttributes* attrs) {
 }
 
 int noalloc_status_read(int* host4);  // quant.cu
+int noalloc_status_clear();           // quant.cu
 
 int sm_count() {
   int dev = 0;
@@ -315,6 +316,8 @@ int neso_clear_device_status(int device) {
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
     if (e != cudaSuccess) rc = cuda_fail(e, "clearing the device status word");
   }
+  // The allocation-free entry point's waits report to their own block.
+  if (rc == NESO_OK) rc = noalloc_status_clear();
   cudaSetDevice(prev);
   return rc == NESO_OK ? ok() : rc;
 }

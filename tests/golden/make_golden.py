@@ -7,11 +7,12 @@ tests/test_quantized_matmul.py:288-311). Those scripts import PyObjC's
 stand-in ``Metal`` module (no GPU work is ever dispatched through it) and then
 calls the reference functions on the reference's own seeded inputs.
 
-This script needs the reference checkout (default ``/root/reference``,
-override with NESO_REFERENCE); the GPU box never runs it. The generated
-``.npz`` files are committed and read by tests/test_oracle_golden.py.
+This script needs a checkout of the reference, named by the NESO_REFERENCE
+environment variable or the first command-line argument; the GPU box never
+runs it. The generated ``.npz`` files are committed and read by
+tests/test_oracle_golden.py.
 
-Run: python tests/golden/make_golden.py
+Run: NESO_REFERENCE=<path to the reference checkout> python tests/golden/make_golden.py
 """
 from __future__ import annotations
 
@@ -27,7 +28,17 @@ from unittest import mock
 import numpy as np
 
 OUT = Path(__file__).resolve().parent
-REF = Path(os.environ.get("NESO_REFERENCE", "/root/reference"))
+REF: Path | None = None
+
+
+def _reference_root() -> Path:
+    arg = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("NESO_REFERENCE")
+    if not arg:
+        raise SystemExit("name the reference checkout: NESO_REFERENCE=<path> or the first argument")
+    root = Path(arg)
+    if not (root / "tests" / "test_rel_pos_fa2.py").exists():
+        raise SystemExit(f"{root} does not look like the reference checkout (no tests/test_rel_pos_fa2.py)")
+    return root
 
 
 def _import_reference():
@@ -113,6 +124,8 @@ def quant_case(quant, kind: str, M: int, N: int, K: int) -> dict:
 
 
 def main() -> None:
+    global REF
+    REF = _reference_root()
     relpos, quant = _import_reference()
     cases = {
         # tests/test_rel_pos_fa2.py:435-437 configs (T, d, nh)
