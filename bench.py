@@ -4,26 +4,31 @@
 Headline workload (BASELINE.json metric "FA2 fwd TFLOP/s (D=64,S=2048)"):
 Flash Attention 2 forward, fp16 Q/K/V [B=16, H=16, S=2048, D=64] drawn N(0,1)
 from a seed, softmax scale 1/8, fp32 accumulation and fp32 O, non-causal.
-One step = one FA2 forward over that batch (one kernel launch). The inputs
-(3 x 64 MiB fp16 + 128 MiB fp32 out) are larger than the 126 MB L2, so no L2
-flush is needed between steps.
+One step = one FA2 forward over the whole batch. The inputs (3 x 64 MiB fp16
++ 128 MiB fp32 out at N=1) are larger than the 126 MB L2, so no L2 flush is
+needed between steps.
 
-Multi-GPU (``torchrun --nproc-per-node N``): every rank owns its own
-B x H = 16 x 16 slice of a global batch of 16 N sequences (sharding along
-batch x heads, no cross-GPU reduction) -> "scaling": "weak". The step time is
-the max over ranks of the CUDA-event time (NCCL all-reduce MAX); after timing,
-each rank's first head is all-gathered to rank 0 over NCCL and checked against
-the CPU oracle (``verified``).
+Multi-GPU (``torchrun --nproc-per-node N``): the fixed 16 x 16 heads are
+partitioned along flattened batch x heads (``neso_b200.shard``), 256/N heads
+per rank, one launch per rank and step, no collective in the step ->
+"scaling": "strong". ``value`` = total FLOPs / the step time, the max over
+ranks of the CUDA-event time. After timing, the ranks' outputs are
+all-gathered over NCCL and rank 0 checks sampled heads against the CPU oracle
+(``verified``). The timed region (K steps between barrier + synchronize) is
+repeated until about a third of a second of device time has been sampled, so
+the clock sampler sees the kernel; ``ms_per_step`` is the median region.
 
 ``--impl reference`` times the reference algorithm's CPU implementation (the
 torch-fp32 oracle port: the reference's own kernels are Metal/HLSL and cannot
-run here) on the host cores, one bounded sample per step.
+run here) on the host cores, one bounded sample per step; under torchrun only
+rank 0 runs it.
 
-Also reported (not part of ``value``): the quantized GEMM (W8A16 / W4A16,
-K=4096, N=11008, M in {1, 16, 128, 2048}) TFLOP/s, the e2e number through the
-public API with host buffers (each step copies its Q/K/V in from pinned host
-memory and reads O back; consecutive steps overlap on separate copy and compute
-streams), the roofline of the FA2 kernel and the CPU baseline.
+Also reported (not part of ``value``), each sharded over the ranks the same
+way as the headline (heads for attention, output columns for the matmuls,
+element ranges for the elementwise kernels) and timed as the max over ranks:
+every BASELINE config with its roofline fraction (``baseline_configs``), the
+e2e number through the public API with pinned host buffers, the roofline of
+the headline kernel and the CPU baseline.
 """
 from __future__ import annotations
 
@@ -44,6 +49,8 @@ B, H, S, D = 16, 16, 2048, 64
 SEED = 1234
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 METRIC = "FA2 fwd TFLOP/s (D=64,S=2048) & quant-GEMM TFLOP/s at 1/2/4/8 B200"
+L2_FLOOR = 256 << 20  # rotate input sets until they exceed twice the 126 MB L2
+QK, QN = 4096, 11008   # quantized matmul weight shape
 
 
 def fa2_flops(b=B, h=H, s=S, d=D, causal=False) -> float:
@@ -164,9 +171,10 @@ def host_threads() -> int:
         return os.cpu_count() or 1
 
 
-def run_reference(args, rank: int) -> None:
+def run_reference(args, rank: int, world: int) -> None:
     """--impl reference: the reference algorithm's CPU implementation (torch
-    fp32 oracle port) on the host cores, one head of the workload per step."""
+    fp32 oracle port) on the host cores, one head of the workload per step.
+    Under torchrun rank 0 alone runs it."""
     if rank != 0:
         return
     import torch
@@ -186,11 +194,11 @@ def run_reference(args, rank: int) -> None:
     per = statistics.median(times)
     value = fa2_flops(1, 1, S, D) / per / 1e12
     line = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus,
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": per * 1e3, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
+        "scaling": "strong", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
         "config": {"workload": f"FA2 fwd B={B} H={H} S={S} D={D} non-causal (one head per step on CPU)",
-                   "global_batch": B * args.gpus, "seq_len": S, "parallelism": f"dp{args.gpus}"},
+                   "global_batch": B, "heads": H, "seq_len": S, "head_dim": D, "parallelism": "cpu"},
         "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": "port",
                          "sample": f"1 head [S={S}, D={D}] per step, torch CPU fp32 oracle (reference kernels "
                                    f"are Metal/HLSL: unavailable on this box)"},
@@ -200,40 +208,202 @@ def run_reference(args, rank: int) -> None:
     print(json.dumps(line), file=_JSON_OUT, flush=True)
 
 
-def time_steps(fn, steps: int, stream, dist_on: bool) -> float:
-    """Barrier + sync, K steps between CUDA events on `stream`, barrier + sync.
-    Returns the step time in ms (max over ranks)."""
-    import torch
-    import torch.distributed as dist
+class Ctx:
+    """Rank, world, device, stream and the cross-rank max of a time."""
 
-    if dist_on:
-        dist.barrier()
+    def __init__(self, world: int, rank: int, dev, stream):
+        self.world, self.rank, self.dev, self.stream = world, rank, dev, stream
+
+    @property
+    def dist_on(self) -> bool:
+        return self.world > 1
+
+    def max_over_ranks(self, ms: float) -> float:
+        if not self.dist_on:
+            return ms
+        import torch
+        import torch.distributed as dist
+        t = torch.tensor([ms], device=self.dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def barrier(self) -> None:
+        if self.dist_on:
+            import torch.distributed as dist
+            dist.barrier()
+
+
+def time_region(ctx: Ctx, fn, steps: int) -> float:
+    """Barrier + sync, `steps` calls between CUDA events on the launching
+    stream, barrier + sync. Returns ms per step, max over ranks."""
+    import torch
+
+    ctx.barrier()
     torch.cuda.synchronize()
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
-    start.record(stream)
+    start.record(ctx.stream)
     for _ in range(steps):
         fn()
-    end.record(stream)
+    end.record(ctx.stream)
     torch.cuda.synchronize()
-    if dist_on:
-        dist.barrier()
-    ms = start.elapsed_time(end) / steps
-    if dist_on:
-        t = torch.tensor([ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    return ms
+    ctx.barrier()
+    return ctx.max_over_ranks(start.elapsed_time(end) / steps)
+
+
+def time_rotating(ctx: Ctx, sets: list, launch, iters: int = 20) -> float:
+    """ms per launch of `launch(set)` over rotating input sets (their total
+    size exceeds L2, so every launch reads HBM), after one warm-up launch per
+    set; max over ranks."""
+    import torch
+
+    for st in sets:
+        launch(st)
+    torch.cuda.synchronize()
+    return time_region(ctx, _Rotor(sets, launch), iters)
+
+
+class _Rotor:
+    def __init__(self, sets, launch):
+        self.sets, self.launch, self.i = sets, launch, 0
+
+    def __call__(self):
+        self.launch(self.sets[self.i % len(self.sets)])
+        self.i += 1
+
+
+def copies(bytes_per_set: int) -> int:
+    return max(1, -(-L2_FLOOR // max(1, bytes_per_set)))
+
+
+def roofline(flops: float | None, nbytes: float, t_s: float, peaks: dict) -> dict:
+    """Per-GPU achieved rate against min(tensor peak, AI x HBM) (tensor-bound
+    work) or the HBM peak (byte work)."""
+    hbm = float(peaks["hbm_gbs"]) * 1e9
+    ten = float(peaks["bf16_tflops"]) * 1e12
+    if flops is None:
+        ach = nbytes / t_s
+        return {"bound": "hbm", "achieved_gbs": ach / 1e9, "frac": ach / hbm}
+    ach = flops / t_s
+    roof = min(ten, flops / nbytes * hbm)
+    return {"bound": "tensor" if roof >= ten else "hbm", "achieved_tflops": ach / 1e12,
+            "roof_tflops": roof / 1e12, "frac": ach / roof, "frac_of_tensor_peak": ach / ten}
+
+
+def baseline_configs(ctx: Ctx, peaks: dict) -> dict:
+    """Every BASELINE config, sharded over the ranks like the headline; each
+    entry has the aggregate rate, the per-launch time (max over ranks) and the
+    per-GPU roofline fraction."""
+    import torch
+    from neso_b200 import ops, shard
+
+    dev, world, rank = ctx.dev, ctx.world, ctx.rank
+    g = torch.Generator(device=dev).manual_seed(SEED + 17)
+    out: dict = {}
+
+    # config 2: elementwise, n = 2^28 fp32 (contiguous element ranges)
+    n = 1 << 28
+    sh = shard.shard_range(n, world, rank, 1024)
+    x = torch.rand(sh.size, device=dev, generator=g) * 2 - 1
+    y = torch.rand(sh.size, device=dev, generator=g) * 2 - 1
+    z = torch.empty_like(x)
+    for name, fn, per_el in (("vector_add", lambda _: ops.vector_add(x, y, out=z), 12),
+                             ("scale", lambda _: ops.scale(x, 0.5, out=z), 8)):
+        ms = time_rotating(ctx, [None], fn, 10)
+        r = roofline(None, per_el * sh.size, ms * 1e-3, peaks)
+        out[name] = {"n": n, "gbs": per_el * n / (ms * 1e-3) / 1e9, "ms": ms, **r}
+    del x, y, z
+
+    # config 4: dense GEMM M = N = K, output columns sharded (16-column groups)
+    for m in (1024, 2048, 4096, 8192):
+        sh = shard.shard_columns(m, world, rank, 16)
+        a = (torch.randn(m, m, device=dev, generator=g) / math.sqrt(m)).half()
+        bfull = (torch.randn(m, m, device=dev, generator=g) / math.sqrt(m)).half()
+        b = bfull[:, sh.slice()].contiguous()
+        del bfull
+        set_bytes = 2 * m * m + 2 * m * sh.size + 4 * m * sh.size
+        sets = [(a, b, torch.empty(m, sh.size, device=dev))]
+        for _ in range(copies(set_bytes) - 1):
+            sets.append((a.clone(), b.clone(), torch.empty(m, sh.size, device=dev)))
+        ms = time_rotating(ctx, sets, lambda s: ops.matmul(s[0], s[1], out=s[2]))
+        fl = 2.0 * m * sh.size * m
+        r = roofline(fl, set_bytes, ms * 1e-3, peaks)
+        out[f"gemm_{m}"] = {"tflops": 2.0 * m ** 3 / (ms * 1e-3) / 1e12, "ms": ms, "cols_per_rank": sh.size, **r}
+        del sets, a, b
+
+    # configs 1 and 3: FA2, heads sharded
+    fa2_cases = [("fa2_b1h8s512d64", 1, 8, 512, 64, False, False)]
+    for d in (64, 128):
+        for s_ in (128, 256, 512, 1024, 2048):
+            fa2_cases.append((f"fa2_s{s_}_d{d}", 16, 16, s_, d, False, False))
+        fa2_cases.append((f"fa2_s2048_d{d}_causal", 16, 16, 2048, d, True, False))
+        fa2_cases.append((f"fa2_s2048_d{d}_table", 16, 16, 2048, d, False, True))
+        fa2_cases.append((f"fa2_s2048_d{d}_causal_table", 16, 16, 2048, d, True, True))
+    for name, b_, h_, s_, d_, causal, tab in fa2_cases:
+        if any(shard.shard_heads(b_, h_, world, r).size == 0 for r in range(world)):
+            continue  # fewer heads than ranks: skipped on every rank alike
+        sh = shard.shard_heads(b_, h_, world, rank)
+        set_bytes = 10 * sh.size * s_ * d_
+        sets = []
+        for _ in range(copies(set_bytes)):
+            q, k, v = (torch.randn(1, sh.size, s_, d_, device=dev, generator=g).half() for _ in range(3))
+            t = None
+            if tab:  # the table rows of this shard's heads (head index = flattened index mod H)
+                full = torch.randn(h_, 2 * s_ - 1, device=dev, generator=g) * 0.02
+                t = full[torch.arange(sh.start, sh.stop, device=dev) % h_].contiguous()
+            sets.append((q, k, v, t, torch.empty(1, sh.size, s_, d_, device=dev)))
+        sc = 1 / math.sqrt(d_)
+        ms = time_rotating(ctx, sets, lambda st: ops.flash_attention(st[0], st[1], st[2], sc, causal=causal,
+                                                                      table=st[3], out=st[4]))
+        fl_rank = fa2_flops(1, sh.size, s_, d_, causal)
+        r = roofline(fl_rank, set_bytes + (4 * (2 * s_ - 1) * sh.size if tab else 0), ms * 1e-3, peaks)
+        out[name] = {"tflops": fa2_flops(b_, h_, s_, d_, causal) / (ms * 1e-3) / 1e12, "ms": ms,
+                     "heads_per_rank": sh.size, **r}
+        del sets
+
+    # config 5: quantized matmul K = 4096, N = 11008, output columns sharded
+    sh = shard.shard_columns(QN, world, rank, 16)
+    nc = sh.size
+    for kind in ("w8a16", "w4a16"):
+        if kind == "w8a16":
+            wbytes = QK * nc + 2 * nc
+            ws = [(torch.randint(-127, 128, (QK, nc), device=dev, dtype=torch.int8, generator=g),
+                   (torch.rand(nc, device=dev, generator=g) * 0.019 + 0.001).half()) for _ in range(copies(wbytes))]
+        else:
+            wbytes = QK * nc // 2 + 2 * (QK // 128) * nc
+            ws = [(torch.randint(0, 256, (QK // 2, nc), device=dev, dtype=torch.uint8, generator=g),
+                   (torch.rand(QK // 128, nc, device=dev, generator=g) * 0.019 + 0.001).half())
+                  for _ in range(copies(wbytes))]
+        for m in (1, 16, 128, 2048):
+            xq = torch.randn(m, QK, device=dev, generator=g).half()
+            yq = torch.empty(m, nc, device=dev)
+            if kind == "w8a16":
+                fn = lambda st: ops.w8a16_matmul(xq, st[0], st[1], out=yq)  # noqa: E731
+            else:
+                fn = lambda st: ops.w4a16_g128_matmul(xq, st[0], st[1], out=yq)  # noqa: E731
+            ms = time_rotating(ctx, ws, fn, 30)
+            fl = 2.0 * m * nc * QK
+            nbytes = wbytes + 2 * m * QK + 4 * m * nc
+            r = roofline(fl, nbytes, ms * 1e-3, peaks)
+            out[f"{kind}_m{m}"] = {"tflops": 2.0 * m * QN * QK / (ms * 1e-3) / 1e12, "us": ms * 1e3,
+                                   "weight_gbs_per_gpu": (QK * nc if kind == "w8a16" else QK * nc // 2) /
+                                   (ms * 1e-3) / 1e9, "cols_per_rank": nc, "weight_copies": len(ws), **r}
+            del xq, yq
+        del ws
+    torch.cuda.synchronize()
+    return out
 
 
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="neso", choices=["neso", "reference"])
     ap.add_argument("--cpu-budget", type=float, default=12.0, help="seconds of CPU-baseline work (rank 0, N=1)")
-    ap.add_argument("--no-extras", action="store_true", help="skip the quant-GEMM and e2e side measurements")
+    ap.add_argument("--no-extras", action="store_true", help="skip the BASELINE-config and e2e side measurements")
+    ap.add_argument("--min-timed-s", type=float, default=0.3,
+                    help="repeat the timed region until this much device time has been sampled")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -249,25 +419,30 @@ def main() -> None:
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
-        run_reference(args, rank)
+        run_reference(args, rank, world)
         return
 
     import torch
     import torch.distributed as dist
     from datetime import timedelta
 
-    from neso_b200 import _lib, ops
+    from neso_b200 import ops, shard
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
-    dist_on = world > 1
-    if dist_on:
+    if world > 1:
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
-    stream = torch.cuda.current_stream(dev)
+    ctx = Ctx(world, rank, dev, torch.cuda.current_stream(dev))
+    peaks, peak_src = load_peaks()
 
-    gen = torch.Generator(device=dev).manual_seed(SEED + rank)
-    q, k, v = (torch.randn(B, H, S, D, device=dev, generator=gen).half() for _ in range(3))
-    o = torch.empty(B, H, S, D, device=dev, dtype=torch.float32)
+    # This rank's heads of the fixed [16, 16, 2048, 64] batch: every rank draws
+    # the whole batch from the same seed and keeps its contiguous heads.
+    sh = shard.shard_heads(B, H, world, rank)
+    gen = torch.Generator(device=dev).manual_seed(SEED)
+    full = [torch.randn(B * H, S, D, device=dev, generator=gen).half() for _ in range(3)]
+    q, k, v = (t[sh.slice()].unsqueeze(0).contiguous() for t in full)
+    del full
+    o = torch.empty(1, sh.size, S, D, device=dev, dtype=torch.float32)
     scale = 1.0 / math.sqrt(D)
 
     def step():
@@ -276,114 +451,57 @@ def main() -> None:
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
+    regions = []
     with ClockSampler(local_rank) as clk:
-        ms = time_steps(step, args.steps, stream, dist_on)
+        regions.append(time_region(ctx, step, args.steps))
+        # the same repeat count on every rank (collectives inside time_region)
+        reps = int(min(50, max(3, math.ceil(args.min_timed_s / max(1e-6, regions[0] * 1e-3 * args.steps)))))
+        for _ in range(reps - 1):
+            regions.append(time_region(ctx, step, args.steps))
     clocks = clk.summary()
-    flops_rank = fa2_flops()
-    value = world * flops_rank / (ms * 1e-3) / 1e12
+    ms = statistics.median(regions)
+    value = fa2_flops() / (ms * 1e-3) / 1e12
 
-    # Roofline of the dominant (only) kernel in the step: one launch per step.
-    peaks, peak_src = load_peaks()
+    # Roofline of the dominant (only) kernel in the step: one launch per rank and step.
+    flops_rank = fa2_flops(1, sh.size, S, D)
     achieved = flops_rank / (ms * 1e-3) / 1e12
     peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
-    traffic = load_traffic("fa2_fwd_d64_s2048")
-    roofline = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                "frac": achieved / peak, "traffic": traffic,
-                "peak_source": f"{peak_src} bf16_tflops (burst, kernel timed alone)",
-                "kernel": "fa2_tile_kernel<64,1,false,0>"}
+    traffic = load_traffic("fa2_fwd_d64_s2048_b16h16")
+    roof = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+            "traffic": None if traffic is None else traffic["dram_bytes_per_launch"] * sh.size / (B * H),
+            "algorithmic_bytes": 10.0 * sh.size * S * D,
+            "peak_source": f"{peak_src} bf16_tflops (burst, kernel timed alone)",
+            "traffic_source": None if traffic is None else traffic["source"],
+            "kernel": "fa2_tile_kernel<64,1,false,0>"}
 
-    # Verification after timing: NCCL all-gather of each rank's first head to rank 0.
-    verified = None
-    if dist_on:
-        head = o[0, 0].contiguous()
-        gathered = torch.empty((world,) + tuple(head.shape), device=dev, dtype=head.dtype)
-        dist.all_gather_into_tensor(gathered, head)
+    # Verification after timing: NCCL all-gather of every rank's heads, then
+    # rank 0 checks sampled heads (first and last of every shard) on the CPU.
+    if ctx.dist_on:
+        sizes = [shard.shard_heads(B, H, world, r).size for r in range(world)]
+        gathered = shard.gather(o[0], sizes)
     else:
-        gathered = o[0, 0].unsqueeze(0)
+        gathered = o[0]
+    verified = None
+    if rank == 0:
+        import oracle
+        gv = torch.Generator(device=dev).manual_seed(SEED)
+        fullv = [torch.randn(B * H, S, D, device=dev, generator=gv).half() for _ in range(3)]
+        picks = sorted({i for r in range(world) for i in (shard.shard_heads(B, H, world, r).start,
+                                                           shard.shard_heads(B, H, world, r).stop - 1)})
+        ok = True
+        for i in picks:
+            ref = oracle.attention(fullv[0][i].cpu(), fullv[1][i].cpu(), fullv[2][i].cpu(), scale)
+            ok = ok and torch.allclose(gathered[i].cpu(), ref, atol=2e-3, rtol=2e-3)
+        verified = bool(ok)
+        del fullv
+    del gathered
+    ctx.barrier()
 
     extras: dict = {}
     e2e = None
-    if rank == 0:
-        import oracle
-        ok = True
-        for r in range(world):
-            gr = torch.Generator(device=dev).manual_seed(SEED + r)
-            qr, kr, vr = (torch.randn(B, H, S, D, device=dev, generator=gr).half() for _ in range(3))
-            ref = oracle.attention(qr[0, 0].cpu(), kr[0, 0].cpu(), vr[0, 0].cpu(), scale)
-            ok = ok and torch.allclose(gathered[r].cpu(), ref, atol=2e-3, rtol=2e-3)
-            del qr, kr, vr
-        verified = bool(ok)
-
-    if not args.no_extras and rank == 0:
-        # e2e through the public API with host buffers: every step copies its
-        # Q/K/V in from pinned host memory, runs FA2 and reads O back. Steps
-        # are pipelined over two device buffer sets on three streams (H2D,
-        # compute, D2H), so the H2D and D2H copy engines and the SMs work at
-        # the same time, as a serving loop would run them.
-        hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
-        ho = torch.empty(o.shape, dtype=o.dtype).pin_memory()
-        dqkv = [tuple(torch.empty_like(q) for _ in range(3)) for _ in range(2)]
-        dout = [o, torch.empty_like(o)]
-        s_h2d, s_comp, s_d2h = (torch.cuda.Stream(dev) for _ in range(3))
-        nslot = 2
-        comp_done = [None] * nslot
-        d2h_done = [None] * nslot
-
-        def e2e_run(steps: int) -> float:
-            for i in range(nslot):
-                comp_done[i] = d2h_done[i] = None
-            start = torch.cuda.Event(enable_timing=True)
-            end = torch.cuda.Event(enable_timing=True)
-            torch.cuda.synchronize()
-            start.record(stream)
-            for st in (s_h2d, s_comp, s_d2h):
-                st.wait_event(start)
-            for i in range(steps):
-                b = i % nslot
-                dq, dk, dv = dqkv[b]
-                with torch.cuda.stream(s_h2d):
-                    if comp_done[b] is not None:
-                        s_h2d.wait_event(comp_done[b])  # FA2 of step i-2 has read this buffer set
-                    dq.copy_(hq, non_blocking=True)
-                    dk.copy_(hk, non_blocking=True)
-                    dv.copy_(hv, non_blocking=True)
-                    h2d_done = torch.cuda.Event()
-                    h2d_done.record(s_h2d)
-                with torch.cuda.stream(s_comp):
-                    s_comp.wait_event(h2d_done)
-                    if d2h_done[b] is not None:
-                        s_comp.wait_event(d2h_done[b])  # O of step i-2 has been read back
-                    ops.flash_attention(dq, dk, dv, scale, out=dout[b])
-                    comp_done[b] = torch.cuda.Event()
-                    comp_done[b].record(s_comp)
-                with torch.cuda.stream(s_d2h):
-                    s_d2h.wait_event(comp_done[b])
-                    ho.copy_(dout[b], non_blocking=True)
-                    d2h_done[b] = torch.cuda.Event()
-                    d2h_done[b].record(s_d2h)
-            for st in (s_h2d, s_comp, s_d2h):
-                ev = torch.cuda.Event()
-                ev.record(st)
-                stream.wait_event(ev)
-            end.record(stream)
-            torch.cuda.synchronize()
-            return start.elapsed_time(end) / steps
-
-        e2e_run(2)
-        e2e_steps = max(3, min(args.steps, 20))
-        ms_e2e = e2e_run(e2e_steps)
-        e2e = {"value": flops_rank / (ms_e2e * 1e-3) / 1e12, "unit": "TFLOP/s",
-               "h2d_bytes_per_step": 3 * q.numel() * q.element_size(),
-               "d2h_bytes_per_step": o.numel() * o.element_size(), "ms_per_step": ms_e2e,
-               "steps": e2e_steps, "gpu_launches": e2e_steps,
-               "pipelined": "two buffer sets; H2D, FA2 and D2H of different steps overlap"}
-        del hq, hk, hv, ho, dqkv, dout
-
-        # Quantized GEMM side measurements, not part of `value`.
-        try:
-            extras["quant_gemm"] = quant_side(dev, stream)
-        except Exception as e:  # pragma: no cover - reported, not fatal
-            extras["quant_gemm"] = {"error": str(e)}
+    if not args.no_extras:
+        e2e = e2e_run(ctx, q, k, v, o, scale, args.steps)
+        extras["baseline_configs"] = baseline_configs(ctx, peaks)
 
     cpu = None
     if rank == 0 and world == 1:
@@ -392,55 +510,94 @@ def main() -> None:
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
-            "config": {"workload": f"FA2 fwd B={B} H={H} S={S} D={D} non-causal, fp16 in, fp32 acc/out, per GPU",
-                       "global_batch": B * world, "heads": H, "seq_len": S, "head_dim": D,
-                       "parallelism": f"dp{world} (batch x heads shards, no collective in the step)",
-                       "l2": "inputs 320 MiB > 126 MB L2 (no flush needed)"},
-            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": args.steps,
+            "config": {"workload": f"FA2 fwd B={B} H={H} S={S} D={D} non-causal, fp16 in, fp32 acc/out, "
+                                   f"heads split over {world} GPU(s)",
+                       "global_batch": B, "heads": H, "seq_len": S, "head_dim": D,
+                       "heads_per_gpu": sh.size,
+                       "parallelism": f"batch x heads sharded over {world} GPU(s), no collective in the step",
+                       "l2": "inputs > 126 MB L2 at every N (no flush needed)",
+                       "timed_regions": len(regions), "region_ms_per_step": regions},
+            "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": args.steps,
             "clocks": clocks, "verified": verified,
         }
         line.update(extras)
         print(json.dumps(line), file=_JSON_OUT, flush=True)
-    if dist_on:
+    if ctx.dist_on:
         dist.barrier()
         dist.destroy_process_group()
 
 
-def quant_side(dev, stream) -> dict:
-    """W8A16 / W4A16 TFLOP/s at M = 2048 and weight-stream GB/s at M = 1
-    (K = 4096, N = 11008); three weight copies rotate so M = 1 reads HBM."""
+def e2e_run(ctx: Ctx, q, k, v, o, scale: float, steps: int) -> dict:
+    """The headline metric through the public API with host buffers: every
+    step copies its Q/K/V in from pinned host memory, runs FA2 and reads O
+    back. Steps are pipelined over two device buffer sets on three streams
+    (H2D, compute, D2H) as a serving loop would run them; the time is the max
+    over ranks, each rank moving its own heads."""
     import torch
     from neso_b200 import ops
 
-    K, N = 4096, 11008
-    out = {}
-    g = torch.Generator(device=dev).manual_seed(7)
-    ws = [torch.randint(-127, 128, (K, N), device=dev, dtype=torch.int8, generator=g) for _ in range(3)]
-    wq = [torch.randint(0, 256, (K // 2, N), device=dev, dtype=torch.uint8, generator=g) for _ in range(3)]
-    s8 = (torch.rand(N, device=dev, generator=g) * 0.019 + 0.001).half()
-    s4 = (torch.rand(K // 128, N, device=dev, generator=g) * 0.019 + 0.001).half()
-    for M in (1, 16, 128, 2048):
-        x = torch.randn(M, K, device=dev, generator=g).half()
-        y = torch.empty(M, N, device=dev)
-        for name, fn in (("w8a16", lambda i: ops.w8a16_matmul(x, ws[i % 3], s8, out=y)),
-                         ("w4a16", lambda i: ops.w4a16_g128_matmul(x, wq[i % 3], s4, out=y))):
-            for i in range(3):
-                fn(i)
-            torch.cuda.synchronize()
-            iters = 30
-            st, en = torch.cuda.Event(True), torch.cuda.Event(True)
-            st.record(stream)
-            for i in range(iters):
-                fn(i)
-            en.record(stream)
-            torch.cuda.synchronize()
-            t = st.elapsed_time(en) / iters * 1e-3
-            wbytes = K * N if name == "w8a16" else K * N // 2
-            out[f"{name}_m{M}"] = {"tflops": 2.0 * M * N * K / t / 1e12, "us": t * 1e6,
-                                   "weight_gbs": wbytes / t / 1e9}
-    return out
+    dev, stream = ctx.dev, ctx.stream
+    hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
+    ho = torch.empty(o.shape, dtype=o.dtype).pin_memory()
+    dqkv = [tuple(torch.empty_like(q) for _ in range(3)) for _ in range(2)]
+    dout = [torch.empty_like(o), torch.empty_like(o)]
+    s_h2d, s_comp, s_d2h = (torch.cuda.Stream(dev) for _ in range(3))
+    nslot = 2
+
+    def run(n: int) -> float:
+        comp_done = [None] * nslot
+        d2h_done = [None] * nslot
+        ctx.barrier()
+        torch.cuda.synchronize()
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for st in (s_h2d, s_comp, s_d2h):
+            st.wait_event(start)
+        for i in range(n):
+            b = i % nslot
+            dq, dk, dv = dqkv[b]
+            with torch.cuda.stream(s_h2d):
+                if comp_done[b] is not None:
+                    s_h2d.wait_event(comp_done[b])  # FA2 of step i-2 has read this buffer set
+                dq.copy_(hq, non_blocking=True)
+                dk.copy_(hk, non_blocking=True)
+                dv.copy_(hv, non_blocking=True)
+                h2d_done = torch.cuda.Event()
+                h2d_done.record(s_h2d)
+            with torch.cuda.stream(s_comp):
+                s_comp.wait_event(h2d_done)
+                if d2h_done[b] is not None:
+                    s_comp.wait_event(d2h_done[b])  # O of step i-2 has been read back
+                ops.flash_attention(dq, dk, dv, scale, out=dout[b])
+                comp_done[b] = torch.cuda.Event()
+                comp_done[b].record(s_comp)
+            with torch.cuda.stream(s_d2h):
+                s_d2h.wait_event(comp_done[b])
+                ho.copy_(dout[b], non_blocking=True)
+                d2h_done[b] = torch.cuda.Event()
+                d2h_done[b].record(s_d2h)
+        for st in (s_h2d, s_comp, s_d2h):
+            ev = torch.cuda.Event()
+            ev.record(st)
+            stream.wait_event(ev)
+        end.record(stream)
+        torch.cuda.synchronize()
+        ctx.barrier()
+        return ctx.max_over_ranks(start.elapsed_time(end) / n)
+
+    run(2)
+    n = max(3, min(steps, 20))
+    ms = run(n)
+    res = {"value": fa2_flops() / (ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+           "h2d_bytes_per_step": 3 * q.numel() * q.element_size() * ctx.world,
+           "d2h_bytes_per_step": o.numel() * o.element_size() * ctx.world, "ms_per_step": ms,
+           "steps": n, "gpu_launches": n,
+           "pipelined": "two buffer sets per GPU; H2D, FA2 and D2H of different steps overlap"}
+    del hq, hk, hv, ho, dqkv, dout
+    return res
 
 
 if __name__ == "__main__":

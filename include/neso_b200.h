@@ -154,6 +154,32 @@ NESO_API int neso_rel_pos_fa2_fwd(const void* Q, const void* K, const void* V, c
                          int32_t stride, float scale, int32_t stride_h, int32_t bias_stride_h, int32_t HEAD_DIM,
                          uint32_t grid_x, uint32_t grid_y, uint32_t grid_z, neso_stream_t stream);
 
+/* The hand-written MSL FA2 kernels of the reference's benchmarks:
+ *   bench/bench_flash_attention.py:142-149      flash_attention_fwd
+ *   bench/bench_flash_attention_opt.py:145-152  flash_attention_opt
+ *   bench/bench_fa2_d128.py:116-123             flash_attention_d128
+ * each (Q, K, V, O, N, d_head, scale) with Q, K, V, O single-head [N, d]
+ * contiguous in one io_type: fp16 when use_half = 1, fp32 when use_half = 0.
+ * Constexprs are the MSL generator's parameters (BM, BN, d, THREADS,
+ * use_half); d_head must equal d (64 or 128; 128 for flash_attention_d128).
+ * Reference grid: (N / BM, 1, 1) with N a multiple of BM; THREADS (1024 in
+ * the reference) is accepted and ignored. fp32 operands are rounded to fp16
+ * for the tensor cores (the stream's input workspace holds the copies); O is
+ * written in io_type. The MSL flash_attention_fwd is exported with an _msl
+ * suffix because the TTIR kernel of the same name is exported above. */
+NESO_API int neso_flash_attention_fwd_msl(const void* Q, const void* K, const void* V, void* O, int32_t N,
+                                          int32_t d_head, float scale, int32_t BM, int32_t BN, int32_t d,
+                                          int32_t THREADS, int32_t use_half, uint32_t grid_x, uint32_t grid_y,
+                                          uint32_t grid_z, neso_stream_t stream);
+NESO_API int neso_flash_attention_opt(const void* Q, const void* K, const void* V, void* O, int32_t N, int32_t d_head,
+                                      float scale, int32_t BM, int32_t BN, int32_t d, int32_t THREADS,
+                                      int32_t use_half, uint32_t grid_x, uint32_t grid_y, uint32_t grid_z,
+                                      neso_stream_t stream);
+NESO_API int neso_flash_attention_d128(const void* Q, const void* K, const void* V, void* O, int32_t N,
+                                       int32_t d_head, float scale, int32_t BM, int32_t BN, int32_t d,
+                                       int32_t THREADS, int32_t use_half, uint32_t grid_x, uint32_t grid_y,
+                                       uint32_t grid_z, neso_stream_t stream);
+
 /* Extension (no reference kernel): multi-head FA2 forward over contiguous
  * [B, H, S, D] fp16 Q/K/V with fp32 O [B, H, S, D]. D in {64, 128}, any S >= 1.
  * causal != 0 masks keys j > i. */
@@ -200,6 +226,30 @@ NESO_API int neso_w8a16_matmul(const void* A, const int8_t* B, float* C, int32_t
 NESO_API int neso_w8a16_scaled_matmul(const void* A, const int8_t* B, float* C, const void* scale, int32_t K,
                              int32_t stride_am, int32_t stride_bk, int32_t stride_cm, int32_t BM, int32_t BN,
                              int32_t BK, uint32_t grid_x, uint32_t grid_y, uint32_t grid_z, neso_stream_t stream);
+
+/* tests/test_advanced12.py:19-48
+ *   w8a16_matmul_kernel(a_ptr, b_int8_ptr, c_ptr, scale_ptr, M, N, K,
+ *                       stride_am, stride_ak, stride_bk, stride_bn,
+ *                       stride_cm, stride_cn, BLOCK_M, BLOCK_N, BLOCK_K)
+ * a fp16 [M, K], b int8 [K, N], c fp32 [M, N], scale_ptr one fp32 value:
+ * c = (a . f16(b)) * scale_ptr[0], fp32 accumulation. Unit inner strides,
+ * stride_am a multiple of 8, stride_bk a multiple of 16. Reference grid:
+ * (cdiv(M, BLOCK_M), cdiv(N, BLOCK_N), 1). */
+NESO_API int neso_w8a16_matmul_kernel(const void* a_ptr, const int8_t* b_int8_ptr, float* c_ptr,
+                                      const float* scale_ptr, int32_t M, int32_t N, int32_t K, int32_t stride_am,
+                                      int32_t stride_ak, int32_t stride_bk, int32_t stride_bn, int32_t stride_cm,
+                                      int32_t stride_cn, int32_t BLOCK_M, int32_t BLOCK_N, int32_t BLOCK_K,
+                                      uint32_t grid_x, uint32_t grid_y, uint32_t grid_z, neso_stream_t stream);
+/* The same kernel with b held in an int32 tensor, as the reference's test
+ * passes it (tests/test_advanced12.py:184-186): values in [-128, 127]
+ * (others saturate), stride_bk in int32 elements, N a multiple of 16. The
+ * weights are narrowed to int8 in the stream's input workspace first. */
+NESO_API int neso_w8a16_matmul_kernel_i32(const void* a_ptr, const int32_t* b_int8_ptr, float* c_ptr,
+                                          const float* scale_ptr, int32_t M, int32_t N, int32_t K, int32_t stride_am,
+                                          int32_t stride_ak, int32_t stride_bk, int32_t stride_bn,
+                                          int32_t stride_cm, int32_t stride_cn, int32_t BLOCK_M, int32_t BLOCK_N,
+                                          int32_t BLOCK_K, uint32_t grid_x, uint32_t grid_y, uint32_t grid_z,
+                                          neso_stream_t stream);
 
 /* Extension with explicit sizes (any M >= 1): Y fp32 [M, N] = X fp16 [M, K] .
  * (W int8 [K, N] * scale fp16 [N]); scale may be NULL (unscaled W8A16).

@@ -80,12 +80,17 @@ SIGNATURES: dict[str, tuple[object, list]] = {
     "neso_quantize_kernel": (_int, [_p, _p, _p, _i32, _i32, *_GRID, _p]),
     "neso_flash_attention_fwd": (_int, [_p, _p, _p, _p, _i32, _i32, _i32, _f32, _i32, *_GRID, _p]),
     "neso_rel_pos_fa2_fwd": (_int, [_p, _p, _p, _p, _p, _i32, _i32, _f32, _i32, _i32, _i32, *_GRID, _p]),
+    "neso_flash_attention_fwd_msl": (_int, [_p, _p, _p, _p, _i32, _i32, _f32] + [_i32] * 5 + [*_GRID, _p]),
+    "neso_flash_attention_opt": (_int, [_p, _p, _p, _p, _i32, _i32, _f32] + [_i32] * 5 + [*_GRID, _p]),
+    "neso_flash_attention_d128": (_int, [_p, _p, _p, _p, _i32, _i32, _f32] + [_i32] * 5 + [*_GRID, _p]),
     "neso_fa2_fwd": (_int, [_p, _p, _p, _p, _i32, _i32, _i32, _i32, _f32, _i32, _p]),
     "neso_fa2_fwd_relpos_table": (_int, [_p, _p, _p, _p, _p, _i32, _i32, _i32, _i32, _f32, _i32, _p]),
     "neso_matmul_kernel": (_int, [_p, _p, _p] + [_i32] * 12 + [*_GRID, _p]),
     "neso_matmul_tiled": (_int, [_p, _p, _p] + [_i32] * 6 + [*_GRID, _p]),
     "neso_w8a16_matmul": (_int, [_p, _p, _p] + [_i32] * 7 + [*_GRID, _p]),
     "neso_w8a16_scaled_matmul": (_int, [_p, _p, _p, _p] + [_i32] * 7 + [*_GRID, _p]),
+    "neso_w8a16_matmul_kernel": (_int, [_p, _p, _p, _p] + [_i32] * 12 + [*_GRID, _p]),
+    "neso_w8a16_matmul_kernel_i32": (_int, [_p, _p, _p, _p] + [_i32] * 12 + [*_GRID, _p]),
     "neso_w8a16_matmul_mnk": (_int, [_p, _p, _p, _p, _i32, _i32, _i32, _p]),
     "neso_w4a16_g128_matmul": (_int, [_p, _p, _p, _p, _i32, _i32, _i32, _p]),
     "neso_w8a16_matmul_mnk_noalloc": (_int, [_p, _p, _p, _p, _i32, _i32, _i32, _p]),

@@ -4,10 +4,11 @@ The reference's ``compile_kernel(fn, signature, num_warps, grid, ...)``
 (src/neso/aot_compile.py:125-236) compiles a ``@triton.jit`` kernel to Metal and
 returns an ``AOTResult`` whose ``to_metadata()`` (aot_compile.py:108-117) native
 consumers read. Here the kernels are already compiled for sm_100a inside
-``libneso_b200.so``; ``compile_kernel`` resolves the kernel by name, parses the
-signature with the reference's grammar (src/neso/backend/abi.py:41-90: bare
-literals and known names become constexprs, ``:16`` / ``:1`` are
-specialisation hints), checks it against the kernel's argument list, and
+``libneso_b200.so``; ``compile_kernel`` resolves the kernel by name, reads the
+signature in the reference's grammar (src/neso/backend/abi.py:41-90: numbers,
+None and names bound in the kernel's namespace are constexpr values, ``:16``
+and ``:1`` are specialisation hints), checks it against the kernel's argument
+list, and
 returns an ``AOTResult`` with the same metadata schema. ``save(prefix)`` writes
 ``{prefix}.json`` (the launch metadata; the code is the shared library).
 
@@ -35,6 +36,11 @@ _C_TYPES = {
 
 @dataclass(frozen=True)
 class ParsedSignature:
+    """A parsed signature in the shape the reference's compiler consumes
+    (src/neso/backend/abi.py:10-16): per-argument Triton types ("constexpr"
+    for specialised arguments), constexpr values, divisibility attributes keyed
+    by argument path, and the type each entry was written with."""
+
     triton_signature: dict[str, str]
     constants: dict[str, Any]
     attributes: dict[tuple[int, ...], list[list[Any]]]
@@ -56,68 +62,105 @@ class KernelParameter:
         return asdict(self)
 
 
-def _parse_literal(value: str) -> int | float | None:
-    try:
-        return int(value)
-    except ValueError:
-        pass
-    try:
-        return float(value)
-    except ValueError:
+# --- signature grammar -------------------------------------------------------
+# One comma-separated entry per kernel argument. An entry is a body with an
+# optional ":hint" suffix:
+#   body  = <number> | None | <name bound in the kernel's namespace>  -> constexpr value
+#         | <Triton type> ("*fp16", "i32", ...)                        -> runtime argument
+#   hint  = 16 (pointer / integer divisible by 16: a tt.divisibility attribute)
+#         | 1  (the argument is the constant 1)
+# Behaviour and error texts follow src/neso/backend/abi.py:41-90.
+_HINTS = (1, 16)
+_NO_VALUE = object()
+
+
+def _number(text: str) -> int | float | None:
+    """An int if the text is one, else a float if it is one, else None."""
+    for conv in (int, float):
+        try:
+            return conv(text)
+        except ValueError:
+            continue
+    return None
+
+
+def _value_of(body: str, namespace: Mapping[str, Any]) -> Any:
+    """The constexpr value a body denotes, or _NO_VALUE for a type."""
+    num = _number(body)
+    if num is not None:
+        return num
+    if body == "None":
         return None
+    return namespace[body] if body in namespace else _NO_VALUE
+
+
+@dataclass(frozen=True)
+class SignatureEntry:
+    index: int
+    name: str
+    body: str
+    hint: int | None
+    value: Any  # _NO_VALUE when the body is a type
+
+    @property
+    def written_as_value(self) -> bool:
+        return self.value is not _NO_VALUE
+
+    @property
+    def constant(self) -> tuple[bool, Any]:
+        """(is a constexpr, its value): a value body wins over a hint of 1."""
+        if self.written_as_value:
+            return True, self.value
+        if self.hint == 1:
+            return True, 1
+        return False, None
+
+    @property
+    def source_type(self) -> str:
+        return "constexpr" if self.written_as_value else self.body
+
+
+def _read_entry(index: int, name: str, text: str, namespace: Mapping[str, Any]) -> SignatureEntry:
+    body, sep, hint_text = text.partition(":")
+    hint = None
+    if sep:
+        val = _number(hint_text)
+        if val not in _HINTS:
+            raise ValueError(f"only specialization hints 1 and 16 are supported, got {hint_text!r}")
+        hint = int(val)
+    body = body.strip()
+    return SignatureEntry(index, name, body, hint, _value_of(body, namespace))
+
+
+def read_signature(arg_names: Sequence[str], signature: str,
+                   namespace: Mapping[str, Any] | None = None) -> list[SignatureEntry]:
+    """One entry per argument, or ValueError when the counts differ."""
+    texts = [t.strip() for t in signature.split(",")]
+    if len(texts) != len(arg_names):
+        raise ValueError(f"signature has {len(texts)} entries but kernel has {len(arg_names)} "
+                         f"arguments: {list(arg_names)}")
+    ns = namespace or {}
+    return [_read_entry(i, n, t, ns) for i, (n, t) in enumerate(zip(arg_names, texts))]
 
 
 def parse_signature(arg_names: Sequence[str], signature: str,
                     namespace: Mapping[str, Any] | None = None) -> ParsedSignature:
-    """The reference's signature grammar (src/neso/backend/abi.py:41-90), with
-    the same error messages."""
-    parts = [part.strip() for part in signature.split(",")]
-    if len(parts) != len(arg_names):
-        raise ValueError(
-            f"signature has {len(parts)} entries but kernel has {len(arg_names)} "
-            f"arguments: {list(arg_names)}")
-    constants: dict[str, Any] = {}
-    hints: dict[tuple[int, ...], int] = {}
-    triton_signature: dict[str, str] = {}
-    source_types: dict[str, str] = {}
-    namespace = namespace or {}
-    for index, (name, entry) in enumerate(zip(arg_names, parts)):
-        if ":" in entry:
-            entry, hint_text = entry.split(":", 1)
-            hint = _parse_literal(hint_text)
-            if hint not in (1, 16):
-                raise ValueError(f"only specialization hints 1 and 16 are supported, got {hint_text!r}")
-            hints[(index,)] = int(hint)
-            if hint == 1:
-                constants[name] = 1
-        literal = _parse_literal(entry)
-        if literal is not None:
-            constants[name] = literal
-            source_types[name] = "constexpr"
-        elif entry == "None":
-            constants[name] = None
-            source_types[name] = "constexpr"
-        elif entry in namespace:
-            constants[name] = namespace[entry]
-            source_types[name] = "constexpr"
-        else:
-            source_types[name] = entry
-        triton_signature[name] = "constexpr" if name in constants else entry
-    attributes = {path: [["tt.divisibility", 16]] for path, hint in hints.items() if hint == 16}
-    return ParsedSignature(triton_signature, constants, attributes, source_types)
+    """Parse a signature into the structures the reference's compiler takes."""
+    entries = read_signature(arg_names, signature, namespace)
+    constants = {e.name: e.constant[1] for e in entries if e.constant[0]}
+    return ParsedSignature(
+        triton_signature={e.name: "constexpr" if e.constant[0] else e.body for e in entries},
+        constants=constants,
+        attributes={(e.index,): [["tt.divisibility", 16]] for e in entries if e.hint == 16},
+        source_types={e.name: e.source_type for e in entries},
+    )
 
 
 def build_parameters(parameter_names: Sequence[str], source_types: Mapping[str, str]) -> list[KernelParameter]:
-    """Runtime (non-constexpr) parameters in order, as the reference builds them
-    (src/neso/backend/abi.py:93-112)."""
-    params = []
-    for index, name in enumerate(parameter_names):
-        ttype = source_types.get(name, "i32")
-        if ttype == "constexpr":
-            continue
-        params.append(KernelParameter(index=index, name=name, type=ttype,
-                                      metal_type=_C_TYPES.get(ttype, ttype), is_pointer=ttype.startswith("*")))
-    return params
+    """The runtime (non-constexpr) parameters, each at its position among
+    `parameter_names`; a name without a written type is an i32 scalar."""
+    typed = ((i, n, source_types.get(n, "i32")) for i, n in enumerate(parameter_names))
+    return [KernelParameter(i, n, t, _C_TYPES.get(t, t), t.startswith("*")) for i, n, t in typed if t != "constexpr"]
 
 
 @dataclass

@@ -11,8 +11,9 @@ CUDA events on the current stream, and prints one JSON line with the mean
 time and the achieved TFLOP/s or GB/s (algorithmic work, as in bench.py).
 With ``--graph`` the timed calls are replayed from one CUDA graph instead, so
 small problems show their device time rather than the host's per-call cost.
-Weights rotate over three copies for the quantized cases so small-M runs
-read HBM rather than L2.
+Inputs smaller than twice the 126 MB L2 (quantized-matmul weights, small
+attention and GEMM problems) rotate over enough copies to exceed 256 MB, so
+every call reads HBM rather than L2.
 """
 from __future__ import annotations
 
@@ -26,6 +27,11 @@ from . import ops
 
 
 GRAPH = False
+L2_FLOOR = 256 << 20
+
+
+def _copies(nbytes: int) -> int:
+    return max(1, -(-L2_FLOOR // max(1, nbytes)))
 
 
 def _time(fn, warmup: int, iters: int) -> float:
@@ -91,32 +97,37 @@ def main() -> None:
     g = torch.Generator(device=dev).manual_seed(0)
     res: dict = {"case": a.case}
     if a.case == "fa2":
-        q, k, v = (torch.randn(a.B, a.H, a.S, a.D, device=dev, generator=g).half() for _ in range(3))
+        sets = [tuple(torch.randn(a.B, a.H, a.S, a.D, device=dev, generator=g).half() for _ in range(3))
+                for _ in range(_copies(10 * a.B * a.H * a.S * a.D))]
         o = torch.empty(a.B, a.H, a.S, a.D, device=dev)
         table = torch.randn(a.H, 2 * a.S - 1, device=dev, generator=g) * 0.02 if a.table else None
-        t = _time(lambda i: ops.flash_attention(q, k, v, 1 / math.sqrt(a.D), causal=a.causal, table=table, out=o),
-                  a.warmup, a.iters)
+        n = len(sets)
+        t = _time(lambda i: ops.flash_attention(*sets[i % n], 1 / math.sqrt(a.D), causal=a.causal, table=table,
+                                                out=o), a.warmup, a.iters)
         flops = 4.0 * a.B * a.H * a.S * a.S * a.D / (2 if a.causal else 1)
         res.update(shape=[a.B, a.H, a.S, a.D], causal=a.causal, table=a.table, us=t * 1e6, tflops=flops / t / 1e12)
     elif a.case == "gemm":
         x = (torch.randn(a.M, a.K, device=dev, generator=g) / math.sqrt(a.K)).half()
         w = (torch.randn(a.K, a.N, device=dev, generator=g) / math.sqrt(a.K)).half()
+        sets = [(x, w)] + [(x.clone(), w.clone()) for _ in range(_copies(2 * (a.M + a.N) * a.K + 4 * a.M * a.N) - 1)]
         c = torch.empty(a.M, a.N, device=dev)
-        t = _time(lambda i: ops.matmul(x, w, out=c), a.warmup, a.iters)
+        n = len(sets)
+        t = _time(lambda i: ops.matmul(*sets[i % n], out=c), a.warmup, a.iters)
         res.update(shape=[a.M, a.N, a.K], us=t * 1e6, tflops=2.0 * a.M * a.N * a.K / t / 1e12)
     elif a.case in ("w8a16", "w4a16"):
         x = torch.randn(a.M, a.K, device=dev, generator=g).half()
         y = torch.empty(a.M, a.N, device=dev)
         if a.case == "w8a16":
-            ws = [torch.randint(-127, 128, (a.K, a.N), device=dev, dtype=torch.int8, generator=g) for _ in range(3)]
+            ws = [torch.randint(-127, 128, (a.K, a.N), device=dev, dtype=torch.int8, generator=g)
+                  for _ in range(_copies(a.K * a.N))]
             s = (torch.rand(a.N, device=dev, generator=g) * 0.019 + 0.001).half()
-            t = _time(lambda i: ops.w8a16_matmul(x, ws[i % 3], s, out=y), a.warmup, a.iters)
+            t = _time(lambda i: ops.w8a16_matmul(x, ws[i % len(ws)], s, out=y), a.warmup, a.iters)
             wbytes = a.K * a.N
         else:
             ws = [torch.randint(0, 256, (a.K // 2, a.N), device=dev, dtype=torch.uint8, generator=g)
-                  for _ in range(3)]
+                  for _ in range(_copies(a.K * a.N // 2))]
             s = (torch.rand(a.K // 128, a.N, device=dev, generator=g) * 0.019 + 0.001).half()
-            t = _time(lambda i: ops.w4a16_g128_matmul(x, ws[i % 3], s, out=y), a.warmup, a.iters)
+            t = _time(lambda i: ops.w4a16_g128_matmul(x, ws[i % len(ws)], s, out=y), a.warmup, a.iters)
             wbytes = a.K * a.N // 2
         res.update(shape=[a.M, a.N, a.K], us=t * 1e6, tflops=2.0 * a.M * a.N * a.K / t / 1e12,
                    weight_gbs=wbytes / t / 1e9)

@@ -49,6 +49,7 @@
 // (measured S=2048, B=H=16 against 128 scattered global loads per row and
 // block: D=64 152 -> 506 TFLOP/s, D=128 614 -> 720-740; causal 113 -> 399 and
 // 422 -> 514-593).
+#include <algorithm>
 #include <cmath>
 
 #include "runtime.h"
@@ -1848,6 +1849,75 @@ int check_ref_grid_x(uint32_t gx, int N) {
   return NESO_OK;
 }
 
+// The hand-written MSL kernels (bench/bench_flash_attention.py:142-149,
+// bench/bench_flash_attention_opt.py:145-152, bench/bench_fa2_d128.py:116-123)
+// take Q, K, V and O in one `io_type` (half or float) with d_head and scale as
+// runtime constants. fp32 operands are rounded to fp16 for the tensor cores
+// (three [N, d] copies in the stream's input workspace); O stays in io_type.
+__global__ void f32_to_f16_kernel(const float* __restrict__ a, const float* __restrict__ b,
+                                  const float* __restrict__ c, __half* __restrict__ out, int64_t n) {
+  const bool vec = n % 4 == 0 && ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b) |
+                                   reinterpret_cast<uintptr_t>(c)) & 15u) == 0;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int t = 0; t < 3; ++t) {
+    const float* src = t == 0 ? a : (t == 1 ? b : c);
+    __half* dst = out + t * n;
+    if (vec) {
+      for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n / 4; i += stride) {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(src) + i);
+        __half2* d2 = reinterpret_cast<__half2*>(dst + 4 * i);
+        d2[0] = __floats2half2_rn(v.x, v.y);
+        d2[1] = __floats2half2_rn(v.z, v.w);
+      }
+    } else {
+      for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n; i += stride) {
+        dst[i] = __float2half_rn(__ldg(src + i));
+      }
+    }
+  }
+}
+
+int fa2_msl(const void* Q, const void* K, const void* V, void* O, int32_t N, int32_t d_head, float scale,
+            int32_t BM, int32_t BN, int32_t d, int32_t THREADS, int32_t use_half, uint32_t gx, uint32_t gy,
+            uint32_t gz, cudaStream_t stream, int only_d) {
+  if (BM <= 0 || BN <= 0 || THREADS <= 0) return fail(NESO_ERR_INVALID_ARG, "BM, BN and THREADS must be positive");
+  if (use_half != 0 && use_half != 1) return fail(NESO_ERR_INVALID_ARG, "use_half must be 0 or 1");
+  if (d != 64 && d != 128) return fail(NESO_ERR_UNSUPPORTED, "head dim d=%d not supported (64 or 128)", d);
+  if (only_d != 0 && d != only_d) return fail(NESO_ERR_UNSUPPORTED, "this kernel is compiled for d=%d", only_d);
+  if (d_head != d) return fail(NESO_ERR_INVALID_ARG, "d_head=%d differs from the kernel's d=%d", d_head, d);
+  if (N <= 0) return fail(NESO_ERR_INVALID_ARG, "N must be positive");
+  if (N % BM != 0 || gx != static_cast<uint32_t>(N / BM) || gy != 1 || gz != 1) {
+    return fail(NESO_ERR_GRID, "grid (%u,%u,%u) != (N/BM, 1, 1) with N=%d BM=%d (N a multiple of BM)", gx, gy, gz, N,
+                BM);
+  }
+  if (Q == nullptr || K == nullptr || V == nullptr || O == nullptr) {
+    return fail(NESO_ERR_INVALID_ARG, "null Q/K/V/O pointer");
+  }
+  FaProblem p{};
+  p.Q = Q; p.K = K; p.V = V; p.O = O;
+  p.q_row = p.k_row = p.v_row = p.o_row = d;
+  p.q_head = p.k_head = p.v_head = p.o_head = static_cast<int64_t>(N) * d;
+  p.out_f16 = use_half != 0;
+  p.BH = 1; p.H = 1; p.S = N; p.D = d;
+  p.scale = scale;
+  p.causal = false;
+  p.bias_mode = kBiasNone;
+  if (!use_half) {
+    const int64_t n = static_cast<int64_t>(N) * d;
+    void* ws = nullptr;
+    int rc = stream_workspace(stream, static_cast<size_t>(3 * n) * sizeof(__half), &ws, kWorkspaceInputs);
+    if (rc != NESO_OK) return rc;
+    __half* h = static_cast<__half*>(ws);
+    const int blocks = static_cast<int>(std::min<int64_t>((n / 4 + 255) / 256 + 1, 4 * sm_count()));
+    f32_to_f16_kernel<<<blocks, 256, 0, stream>>>(static_cast<const float*>(Q), static_cast<const float*>(K),
+                                                  static_cast<const float*>(V), h, n);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "fp32 -> fp16 operand launch");
+    p.Q = h; p.K = h + n; p.V = h + 2 * n;
+  }
+  return launch_fa2(p, stream);
+}
+
 }  // namespace
 }  // namespace neso
 
@@ -1933,6 +2003,27 @@ int neso_fa2_fwd_relpos_table(const void* Q, const void* K, const void* V, const
   p.bias_mode = kBiasTable;
   p.table = table;
   return launch_fa2(p, as_stream(stream));
+}
+
+int neso_flash_attention_fwd_msl(const void* Q, const void* K, const void* V, void* O, int32_t N, int32_t d_head,
+                                 float scale, int32_t BM, int32_t BN, int32_t d, int32_t THREADS, int32_t use_half,
+                                 uint32_t grid_x, uint32_t grid_y, uint32_t grid_z, neso_stream_t stream) {
+  return fa2_msl(Q, K, V, O, N, d_head, scale, BM, BN, d, THREADS, use_half, grid_x, grid_y, grid_z,
+                 as_stream(stream), 0);
+}
+
+int neso_flash_attention_opt(const void* Q, const void* K, const void* V, void* O, int32_t N, int32_t d_head,
+                             float scale, int32_t BM, int32_t BN, int32_t d, int32_t THREADS, int32_t use_half,
+                             uint32_t grid_x, uint32_t grid_y, uint32_t grid_z, neso_stream_t stream) {
+  return fa2_msl(Q, K, V, O, N, d_head, scale, BM, BN, d, THREADS, use_half, grid_x, grid_y, grid_z,
+                 as_stream(stream), 0);
+}
+
+int neso_flash_attention_d128(const void* Q, const void* K, const void* V, void* O, int32_t N, int32_t d_head,
+                              float scale, int32_t BM, int32_t BN, int32_t d, int32_t THREADS, int32_t use_half,
+                              uint32_t grid_x, uint32_t grid_y, uint32_t grid_z, neso_stream_t stream) {
+  return fa2_msl(Q, K, V, O, N, d_head, scale, BM, BN, d, THREADS, use_half, grid_x, grid_y, grid_z,
+                 as_stream(stream), 128);
 }
 
 }  // extern "C"

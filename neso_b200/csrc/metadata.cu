@@ -81,6 +81,20 @@ const std::unordered_map<std::string, std::string>& table() {
           {"B", "i32", "int32_t"}, {"H", "i32", "int32_t"}, {"S", "i32", "int32_t"}, {"D", "i32", "int32_t"},
           {"scale", "fp32", "float"}, {"causal", "i32", "int32_t"}},
          "{}", 384, {"cdiv(S, 256)", "B * H", "1"}},
+        // MSL FA2 kernels (fp16 io_type shown; use_half = 0 takes fp32 buffers).
+        {"flash_attention_fwd_msl",
+         {{"Q", "*fp16", F16P}, {"K", "*fp16", F16P}, {"V", "*fp16", F16P}, {"O", "*fp16", "__half*"},
+          {"N", "i32", "int32_t"}, {"d_head", "i32", "int32_t"}, {"scale", "fp32", "float"}},
+         "{\"BM\": 32, \"BN\": 32, \"d\": 64, \"THREADS\": 1024, \"use_half\": 1}", 384, {"N / BM", "1", "1"}},
+        {"flash_attention_opt",
+         {{"Q", "*fp16", F16P}, {"K", "*fp16", F16P}, {"V", "*fp16", F16P}, {"O", "*fp16", "__half*"},
+          {"N", "i32", "int32_t"}, {"d_head", "i32", "int32_t"}, {"scale", "fp32", "float"}},
+         "{\"BM\": 32, \"BN\": 32, \"d\": 64, \"THREADS\": 1024, \"use_half\": 1}", 384, {"N / BM", "1", "1"}},
+        {"flash_attention_d128",
+         {{"Q", "*fp16", F16P}, {"K", "*fp16", F16P}, {"V", "*fp16", F16P}, {"O", "*fp16", "__half*"},
+          {"N", "i32", "int32_t"}, {"d_head", "i32", "int32_t"}, {"scale", "fp32", "float"}},
+         "{\"BM\": 32, \"BN\": 32, \"d\": 128, \"THREADS\": 1024, \"use_half\": 1}", 384,
+         {"N / BM", "1", "1"}},
         {"fa2_fwd_relpos_table",
          {{"Q", "*fp16", F16P}, {"K", "*fp16", F16P}, {"V", "*fp16", F16P}, {"table", "*fp32", "const float*"},
           {"O", "*fp32", "float*"}, {"B", "i32", "int32_t"}, {"H", "i32", "int32_t"}, {"S", "i32", "int32_t"},
@@ -100,20 +114,28 @@ const std::unordered_map<std::string, std::string>& table() {
         {"w8a16_matmul",
          {{"A", "*fp16", F16P}, {"B", "*i8", "const int8_t*"}, {"C", "*fp32", "float*"}, {"K", "i32", "int32_t"},
           {"stride_am", "i32", "int32_t"}, {"stride_bk", "i32", "int32_t"}, {"stride_cm", "i32", "int32_t"}},
-         "{\"BM\": 128, \"BN\": 128, \"BK\": 64}", 256, {"cdiv(M, BM)", "cdiv(N, BN)", "1"}},
+         "{\"BM\": 128, \"BN\": 128, \"BK\": 64}", 512, {"cdiv(M, BM)", "cdiv(N, BN)", "1"}},
         {"w8a16_scaled_matmul",
          {{"A", "*fp16", F16P}, {"B", "*i8", "const int8_t*"}, {"C", "*fp32", "float*"},
           {"scale", "*fp16", F16P}, {"K", "i32", "int32_t"}, {"stride_am", "i32", "int32_t"},
           {"stride_bk", "i32", "int32_t"}, {"stride_cm", "i32", "int32_t"}},
-         "{\"BM\": 128, \"BN\": 128, \"BK\": 64}", 256, {"cdiv(M, BM)", "cdiv(N, BN)", "1"}},
+         "{\"BM\": 128, \"BN\": 128, \"BK\": 64}", 512, {"cdiv(M, BM)", "cdiv(N, BN)", "1"}},
+        {"w8a16_matmul_kernel",
+         {{"a_ptr", "*fp16", F16P}, {"b_int8_ptr", "*i8", "const int8_t*"}, {"c_ptr", "*fp32", "float*"},
+          {"scale_ptr", "*fp32", "const float*"}, {"M", "i32", "int32_t"}, {"N", "i32", "int32_t"},
+          {"K", "i32", "int32_t"}, {"stride_am", "i32", "int32_t"}, {"stride_ak", "i32", "int32_t"},
+          {"stride_bk", "i32", "int32_t"}, {"stride_bn", "i32", "int32_t"}, {"stride_cm", "i32", "int32_t"},
+          {"stride_cn", "i32", "int32_t"}},
+         "{\"BLOCK_M\": 32, \"BLOCK_N\": 32, \"BLOCK_K\": 32}", 512,
+         {"cdiv(M, BLOCK_M)", "cdiv(N, BLOCK_N)", "1"}},
         {"w8a16_matmul_mnk",
          {{"X", "*fp16", F16P}, {"W", "*i8", "const int8_t*"}, {"scale", "*fp16", F16P}, {"Y", "*fp32", "float*"},
           {"M", "i32", "int32_t"}, {"N", "i32", "int32_t"}, {"K", "i32", "int32_t"}},
-         "{}", 256, {"internal", "1", "1"}},
+         "{}", 512, {"internal", "1", "1"}},
         {"w4a16_g128_matmul",
          {{"X", "*fp16", F16P}, {"Wq", "*u8", "const uint8_t*"}, {"scales", "*fp16", F16P},
           {"Y", "*fp32", "float*"}, {"M", "i32", "int32_t"}, {"N", "i32", "int32_t"}, {"K", "i32", "int32_t"}},
-         "{\"GROUP\": 128}", 256, {"internal", "1", "1"}},
+         "{\"GROUP\": 128}", 512, {"internal", "1", "1"}},
         {"rmsnorm_kernel",
          {{"x_ptr", "*fp32", "const float*"}, {"weight_ptr", "*fp32", "const float*"}, {"out_ptr", "*fp32", "float*"},
           {"row_stride", "i32", "int32_t"}, {"n_cols", "i32", "int32_t"}, {"eps", "fp32", "float"}},

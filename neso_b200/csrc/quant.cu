@@ -99,6 +99,7 @@ struct QArgs {
   float* Y;
   int64_t ldy;
   const __half* chan_scale;  // int8: per-channel scale [N] (nullable)
+  const float* tensor_scale;  // int8: one fp32 scale for the whole output (nullable; exclusive with chan_scale)
   float* partial;            // split-K: [splits][M][N] fp32 partial sums, else null
   int M, N, K;
   int num_m, num_n, num_k;
@@ -424,6 +425,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       float* ydst = args.partial != nullptr ? args.partial + static_cast<int64_t>(u.ks) * args.M * args.N : args.Y;
       const int64_t ld = args.partial != nullptr ? args.N : args.ldy;
       const __half* csc = args.partial != nullptr ? nullptr : args.chan_scale;
+      const float* tsc = args.partial != nullptr ? nullptr : args.tensor_scale;
       const int buf = tc % Cfg::kAccBufs;
       const uint32_t use = tc / Cfg::kAccBufs;
       if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[buf], use & 1, abort_flag, args.st, 0x2400))) break;
@@ -433,7 +435,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll 1
         for (int g = 0; g < kNT; ++g) {
           const int n = nb * kUnitN + g * kTileN + lrow;
-          const float sc = (csc != nullptr && n < args.N) ? __half2float(csc[n]) : 1.f;
+          const float sc = (csc != nullptr && n < args.N) ? __half2float(csc[n])
+                                                          : (tsc != nullptr ? __ldg(tsc) : 1.f);
 #pragma unroll
           for (int c = 0; c < (kNX + 31) / 32; ++c) {
             uint32_t r[32];
@@ -474,6 +477,10 @@ __global__ void __launch_bounds__(kThreads, 1)
               const float sc = n0 + i < args.N ? __half2float(__ldg(csc + n0 + i)) : 0.f;
               r[i] = __float_as_uint(__uint_as_float(r[i]) * sc);
             }
+          } else if (tsc != nullptr) {
+            const float sc = __ldg(tsc);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * sc);
           }
 #pragma unroll
           for (int half = 0; half < 2; ++half) {
@@ -510,7 +517,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int i = 0; i < 32; ++i) {
               const int n = n0 + i;
               if (n < args.N) {
-                const float sc = csc != nullptr ? __half2float(__ldg(csc + n)) : 1.f;
+                const float sc = csc != nullptr ? __half2float(__ldg(csc + n)) : (tsc != nullptr ? __ldg(tsc) : 1.f);
                 yrow[n] = __uint_as_float(r[i]) * sc;
               }
             }
@@ -539,6 +546,7 @@ struct QProblem {
   int64_t ldw;  // bytes per stored row (int8: per k; int4: per pair of k)
   const void* scale;  // int8: [N] (nullable); int4: [K/128, N]
   int64_t lds;        // int4 scale row stride (elements)
+  const float* tscale = nullptr;  // int8 only: one fp32 scale for all of Y (when `scale` is null)
   float* Y;
   int64_t ldy;
   int M, N, K;
@@ -647,16 +655,22 @@ void plan_splits(QProblem& p, int sms, size_t max_partial = SIZE_MAX) {
   }
 }
 
-// Y[m, n] = scale[n] * sum_s partial[s][m][n], fixed summation order.
+// Y[m, n] = scale[n] * sum_s partial[s][m][n] (or tscale[0] * ...), fixed
+// summation order.
 __global__ void splitk_reduce_kernel(const float* __restrict__ partial, int splits, int M, int N,
-                                     const __half* __restrict__ scale, float* __restrict__ Y, int64_t ldy) {
+                                     const __half* __restrict__ scale, const float* __restrict__ tscale,
+                                     float* __restrict__ Y, int64_t ldy) {
   const int64_t total = static_cast<int64_t>(M) * N;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     float acc = 0.f;
     for (int sp = 0; sp < splits; ++sp) acc += partial[sp * total + i];
     const int n = static_cast<int>(i % N);
-    if (scale != nullptr) acc *= __half2float(scale[n]);
+    if (scale != nullptr) {
+      acc *= __half2float(scale[n]);
+    } else if (tscale != nullptr) {
+      acc *= __ldg(tscale);
+    }
     Y[(i / N) * ldy + n] = acc;
   }
 }
@@ -711,6 +725,7 @@ int launch_wq(const QProblem& p, cudaStream_t stream) {
   args.Y = p.Y;
   args.ldy = p.ldy;
   args.chan_scale = kQ == kInt8 ? static_cast<const __half*>(p.scale) : nullptr;
+  args.tensor_scale = kQ == kInt8 ? p.tscale : nullptr;
   args.partial = p.splits > 1 ? p.partial : nullptr;
   args.M = p.M;
   args.N = p.N;
@@ -734,7 +749,8 @@ int launch_wq(const QProblem& p, cudaStream_t stream) {
   if (args.partial != nullptr) {
     const int64_t total = static_cast<int64_t>(p.M) * p.N;
     const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, 4 * sm_count()));
-    splitk_reduce_kernel<<<blocks, 256, 0, stream>>>(args.partial, args.splits, p.M, p.N, args.chan_scale, p.Y, p.ldy);
+    splitk_reduce_kernel<<<blocks, 256, 0, stream>>>(args.partial, args.splits, p.M, p.N, args.chan_scale,
+                                                     args.tensor_scale, p.Y, p.ldy);
     e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "split-K reduce launch");
   }
@@ -776,6 +792,7 @@ struct GvArgs {
   int64_t ldw;          // bytes per stored row (int8: per k; int4: per pair of k)
   const __half* scale;  // int8: [N] per channel (nullable); int4: [K/128][lds]
   int64_t lds;
+  const float* tscale;  // int8: one fp32 scale for all of Y (nullable; exclusive with scale)
   float* Y;
   int64_t ldy;
   float* partial;  // [slices][M][N] when there is more than one slice
@@ -926,7 +943,11 @@ __global__ void __launch_bounds__(GvCfg<kQ, kM>::kThreads, 1) wq_gemv_kernel(GvA
 #pragma unroll 8
         for (int w = 0; w < NW; ++w) s += gsm[w * kGvWarpStride + off];
         if (single) {
-          if (kQ == kInt8 && a.scale != nullptr) s *= __half2float(a.scale[n]);
+          if (kQ == kInt8 && a.scale != nullptr) {
+            s *= __half2float(a.scale[n]);
+          } else if (kQ == kInt8 && a.tscale != nullptr) {
+            s *= __ldg(a.tscale);
+          }
           a.Y[static_cast<int64_t>(m) * a.ldy + n] = s;
         } else {
           a.partial[(static_cast<int64_t>(sl) * a.M + m) * a.N + n] = s;
@@ -959,7 +980,11 @@ __global__ void __launch_bounds__(GvCfg<kQ, kM>::kThreads, 1) wq_gemv_kernel(GvA
 #pragma unroll
       for (int i = 0; i < 8; ++i) s += v[i];
     }
-    if (kQ == kInt8 && a.scale != nullptr) s *= __half2float(a.scale[n]);
+    if (kQ == kInt8 && a.scale != nullptr) {
+      s *= __half2float(a.scale[n]);
+    } else if (kQ == kInt8 && a.tscale != nullptr) {
+      s *= __ldg(a.tscale);
+    }
     a.Y[static_cast<int64_t>(m) * a.ldy + n] = s;
   }
   if (threadIdx.x == 0) a.counters[cb] = 0;  // ready for the next launch on this stream
@@ -999,6 +1024,7 @@ int launch_gemv(const QProblem& p, cudaStream_t stream) {
   a.ldw = p.ldw;
   a.scale = static_cast<const __half*>(p.scale);
   a.lds = p.lds;
+  a.tscale = kQ == kInt8 ? p.tscale : nullptr;
   a.Y = p.Y;
   a.ldy = p.ldy;
   a.M = p.M;
@@ -1116,6 +1142,55 @@ int run_wq(const QProblem& p, cudaStream_t stream) {
     q.partial = static_cast<float*>(ws);
   }
   return q.kind == kInt8 ? dispatch_wq<kInt8>(q, stream) : dispatch_wq<kInt4G128>(q, stream);
+}
+
+// ------------------------------------ per-tensor scale, int32-held weights --
+// tests/test_advanced12.py:19-48 w8a16_matmul_kernel: C = (A . f16(B)) * scale[0]
+// with one fp32 scale; the reference's test holds the int8 values in an int32
+// tensor (:186). Those are narrowed to int8 rows of `ldo` bytes first (values
+// outside [-128, 127] saturate; the kernel's contract is int8 data).
+__global__ void narrow_i32_to_i8_kernel(const int32_t* __restrict__ b, int64_t ldb, int K, int N,
+                                        int8_t* __restrict__ out, int64_t ldo) {
+  const int64_t quads = static_cast<int64_t>(K) * (N / 4);
+  const bool vec = (ldb % 4 == 0) && ((reinterpret_cast<uintptr_t>(b) & 15u) == 0);
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < quads;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t k = i / (N / 4);
+    const int n = static_cast<int>(i % (N / 4)) * 4;
+    int v[4];
+    if (vec) {
+      const int4 q = __ldg(reinterpret_cast<const int4*>(b + k * ldb + n));
+      v[0] = q.x; v[1] = q.y; v[2] = q.z; v[3] = q.w;
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) v[j] = __ldg(b + k * ldb + n + j);
+    }
+    uint32_t packed = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) packed |= (static_cast<uint32_t>(max(-128, min(127, v[j]))) & 0xFFu) << (8 * j);
+    *reinterpret_cast<uint32_t*>(out + k * ldo + n) = packed;
+  }
+}
+
+// Reference-grid and stride checks shared by both storage forms of
+// w8a16_matmul_kernel (the grid is (cdiv(M, BLOCK_M), cdiv(N, BLOCK_N)), as
+// for matmul_kernel).
+int check_w8a16_tensor_scale(int M, int N, int K, int stride_ak, int stride_bn, int stride_cn, int BLOCK_M,
+                             int BLOCK_N, int BLOCK_K, uint32_t gx, uint32_t gy, uint32_t gz, const float* scale) {
+  if (BLOCK_M <= 0 || BLOCK_N <= 0 || BLOCK_K <= 0) return fail(NESO_ERR_INVALID_ARG, "BLOCK_* must be positive");
+  if (M < 0 || N < 0 || K < 0) return fail(NESO_ERR_INVALID_ARG, "negative size");
+  const uint32_t gm = static_cast<uint32_t>((static_cast<int64_t>(M) + BLOCK_M - 1) / BLOCK_M);
+  const uint32_t gn = static_cast<uint32_t>((static_cast<int64_t>(N) + BLOCK_N - 1) / BLOCK_N);
+  if (gx != gm || gy != gn || gz != 1) {
+    return fail(NESO_ERR_GRID, "grid (%u,%u,%u) != (cdiv(M,BLOCK_M)=%u, cdiv(N,BLOCK_N)=%u, 1)", gx, gy, gz, gm,
+                gn);
+  }
+  if (stride_ak != 1 || stride_bn != 1 || stride_cn != 1) {
+    return fail(NESO_ERR_UNSUPPORTED, "only unit inner strides are supported (stride_ak=%d stride_bn=%d "
+                                      "stride_cn=%d)", stride_ak, stride_bn, stride_cn);
+  }
+  if (scale == nullptr && M > 0 && N > 0) return fail(NESO_ERR_INVALID_ARG, "null scale_ptr");
+  return NESO_OK;
 }
 
 // ---------------------------------------------------- allocation-free entry --
@@ -1241,6 +1316,62 @@ int neso_w4a16_g128_matmul(const void* X, const uint8_t* Wq, const void* scales,
   return run_wq(p, as_stream(stream));
 }
 
+
+int neso_w8a16_matmul_kernel(const void* a_ptr, const int8_t* b_int8_ptr, float* c_ptr, const float* scale_ptr,
+                             int32_t M, int32_t N, int32_t K, int32_t stride_am, int32_t stride_ak, int32_t stride_bk,
+                             int32_t stride_bn, int32_t stride_cm, int32_t stride_cn, int32_t BLOCK_M, int32_t BLOCK_N,
+                             int32_t BLOCK_K, uint32_t grid_x, uint32_t grid_y, uint32_t grid_z,
+                             neso_stream_t stream) {
+  int rc = check_w8a16_tensor_scale(M, N, K, stride_ak, stride_bn, stride_cn, BLOCK_M, BLOCK_N, BLOCK_K, grid_x,
+                                    grid_y, grid_z, scale_ptr);
+  if (rc != NESO_OK) return rc;
+  QProblem p{};
+  p.X = a_ptr; p.ldx = stride_am;
+  p.W = b_int8_ptr; p.ldw = stride_bk;
+  p.scale = nullptr; p.lds = 0;
+  p.tscale = scale_ptr;
+  p.Y = c_ptr; p.ldy = stride_cm;
+  p.M = M; p.N = N; p.K = K;
+  p.kind = kInt8;
+  return run_wq(p, as_stream(stream));
+}
+
+int neso_w8a16_matmul_kernel_i32(const void* a_ptr, const int32_t* b_int8_ptr, float* c_ptr, const float* scale_ptr,
+                                 int32_t M, int32_t N, int32_t K, int32_t stride_am, int32_t stride_ak,
+                                 int32_t stride_bk, int32_t stride_bn, int32_t stride_cm, int32_t stride_cn,
+                                 int32_t BLOCK_M, int32_t BLOCK_N, int32_t BLOCK_K, uint32_t grid_x, uint32_t grid_y,
+                                 uint32_t grid_z, neso_stream_t stream) {
+  int rc = check_w8a16_tensor_scale(M, N, K, stride_ak, stride_bn, stride_cn, BLOCK_M, BLOCK_N, BLOCK_K, grid_x,
+                                    grid_y, grid_z, scale_ptr);
+  if (rc != NESO_OK) return rc;
+  if (M == 0 || N == 0) return ok();
+  if (stride_bk < N) return fail(NESO_ERR_INVALID_ARG, "stride_bk %d < N %d", stride_bk, N);
+  if (N % 16 != 0) return fail(NESO_ERR_UNSUPPORTED, "int32-held weights need N %% 16 == 0 (N=%d)", N);
+  cudaStream_t st = as_stream(stream);
+  const int64_t ldw = N;  // int8 rows on 16-byte boundaries for TMA
+  int8_t* w8 = nullptr;
+  if (K > 0) {
+    if (b_int8_ptr == nullptr) return fail(NESO_ERR_INVALID_ARG, "null input");
+    void* ws = nullptr;
+    rc = stream_workspace(st, static_cast<size_t>(K) * ldw, &ws, kWorkspaceInputs);
+    if (rc != NESO_OK) return rc;
+    w8 = static_cast<int8_t*>(ws);
+    const int64_t quads = static_cast<int64_t>(K) * (N / 4);
+    const int blocks = static_cast<int>(std::min<int64_t>((quads + 255) / 256, 8 * sm_count()));
+    narrow_i32_to_i8_kernel<<<blocks, 256, 0, st>>>(b_int8_ptr, stride_bk, K, N, w8, ldw);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "int32 -> int8 weight launch");
+  }
+  QProblem p{};
+  p.X = a_ptr; p.ldx = stride_am;
+  p.W = w8; p.ldw = ldw;
+  p.scale = nullptr; p.lds = 0;
+  p.tscale = scale_ptr;
+  p.Y = c_ptr; p.ldy = stride_cm;
+  p.M = M; p.N = N; p.K = K;
+  p.kind = kInt8;
+  return run_wq(p, st);
+}
 
 int neso_w8a16_matmul_mnk_noalloc(const void* X, const int8_t* W, const void* scale, float* Y, int32_t M, int32_t N,
                                   int32_t K, neso_stream_t stream) {

@@ -5,6 +5,7 @@
 #include <cstdio>
 #include <cstring>
 #include <map>
+#include <tuple>
 #include <mutex>
 #include <utility>
 
@@ -99,26 +100,29 @@ int device_status(DevStatus* out) {
   return NESO_OK;
 }
 
-int stream_workspace(cudaStream_t stream, size_t bytes, void** out) {
+int stream_workspace(cudaStream_t stream, size_t bytes, void** out, int which) {
   static std::mutex mu;
-  static std::map<std::pair<int, cudaStream_t>, std::pair<void*, size_t>> bufs;
+  static std::map<std::tuple<int, cudaStream_t, int>, std::pair<void*, size_t>> bufs;
   int dev = 0;
   int rc = current_device(&dev);
   if (rc != NESO_OK) return rc;
+  if (which != kWorkspacePartials && which != kWorkspaceInputs) {
+    return fail(NESO_ERR_INVALID_ARG, "unknown workspace %d", which);
+  }
   std::lock_guard<std::mutex> lock(mu);
-  auto& slot = bufs[{dev, stream}];
+  auto& slot = bufs[std::make_tuple(dev, stream, which)];
   if (slot.second < bytes) {
     cudaError_t e = cudaSuccess;
     if (slot.first != nullptr) {
       e = cudaStreamSynchronize(stream);  // earlier work on this stream may still read the old buffer
       if (e == cudaSuccess) e = cudaFree(slot.first);
       slot = {nullptr, 0};
-      if (e != cudaSuccess) return cuda_fail(e, "releasing the split-K workspace");
+      if (e != cudaSuccess) return cuda_fail(e, "releasing a stream workspace");
     }
     const size_t want = bytes + bytes / 4;
     void* p = nullptr;
     e = cudaMalloc(&p, want);
-    if (e != cudaSuccess) return cuda_fail(e, "allocating the split-K workspace");
+    if (e != cudaSuccess) return cuda_fail(e, "allocating a stream workspace");
     slot = {p, want};
   }
   *out = slot.first;

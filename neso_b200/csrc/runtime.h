@@ -30,9 +30,14 @@ int cuda_fail(cudaError_t e, const char* what);
 int device_status(DevStatus* out);
 
 // Scratch buffer of at least `bytes` for work queued on `stream` (one buffer
-// per device and stream, grown on demand; growing synchronises the stream
-// first). Stays allocated until the process exits.
-int stream_workspace(cudaStream_t stream, size_t bytes, void** out);
+// per device, stream and kind, grown on demand; growing synchronises the
+// stream first). Stays allocated until the process exits. Two kinds, so one
+// call can hold both: split-K partial sums, and inputs converted to the
+// layout a kernel reads (fp32 -> fp16 attention operands, int32-held int8
+// weights -> int8).
+constexpr int kWorkspacePartials = 0;
+constexpr int kWorkspaceInputs = 1;
+int stream_workspace(cudaStream_t stream, size_t bytes, void** out, int which = kWorkspacePartials);
 // kStreamCounters zero-initialised ints for kernels queued on `stream` that
 // hand out or count work through atomics (one block per device and stream,
 // allocated and zeroed on first use). A kernel that uses them leaves them

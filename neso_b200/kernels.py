@@ -67,6 +67,9 @@ class Kernel:
     args: list[tuple[str, str]]            # (name, kind): kind in {"ptr", "i32", "f32"}
     constexprs: dict[str, Any] = field(default_factory=dict)  # name -> default (None = required)
     infer: dict[str, Callable[[dict], Any]] = field(default_factory=dict)
+    # Picks the entry point from the bound arguments when the reference kernel
+    # is specialised on an argument's dtype (Triton compiles one per pointer type).
+    select: Callable[[dict], str] | None = None
 
     @property
     def arg_names(self) -> list[str]:
@@ -129,11 +132,22 @@ class Kernel:
         cargs.extend(int(bound[c]) for c in self.constexprs)
         cargs.extend(g)
         cargs.append(stream)
-        _lib.call(self.cfunc, *cargs)
+        _lib.call(self.select(bound) if self.select is not None else self.cfunc, *cargs)
 
 
 def _last_dim(key: str) -> Callable[[dict], int]:
     return lambda b: int(b[key].shape[-1])
+
+
+def _is_half(key: str) -> Callable[[dict], int]:
+    import torch
+    return lambda b: int(b[key].dtype == torch.float16)
+
+
+def _int32_weights(b: dict) -> str:
+    import torch
+    w = b["b_int8_ptr"]
+    return "neso_w8a16_matmul_kernel_i32" if getattr(w, "dtype", None) == torch.int32 else "neso_w8a16_matmul_kernel"
 
 
 P, I, F = "ptr", "i32", "f32"
@@ -148,6 +162,18 @@ flash_attention_fwd = Kernel(
     "flash_attention_fwd", "neso_flash_attention_fwd",
     [("Q", P), ("K", P), ("V", P), ("O", P), ("N", I), ("stride_qo", I), ("stride_kv", I), ("scale", F)],
     {"d": None}, infer={"d": _last_dim("Q")})
+# The hand-written MSL kernels of the reference's benchmarks (bench/bench_flash_attention.py:142-149,
+# bench_flash_attention_opt.py:145-152, bench_fa2_d128.py:116-123): one io_type for Q, K, V and O
+# (use_half follows Q's dtype unless given), d_head and scale at run time.
+_MSL_ARGS = [("Q", P), ("K", P), ("V", P), ("O", P), ("N", I), ("d_head", I), ("scale", F)]
+_MSL_CONST = {"BM": 32, "BN": 32, "d": None, "THREADS": 1024, "use_half": None}
+_MSL_INFER = {"d": lambda b: int(b["d_head"]), "use_half": _is_half("Q")}
+flash_attention_fwd_msl = Kernel("flash_attention_fwd_msl", "neso_flash_attention_fwd_msl", _MSL_ARGS,
+                                 dict(_MSL_CONST), dict(_MSL_INFER))
+flash_attention_opt = Kernel("flash_attention_opt", "neso_flash_attention_opt", _MSL_ARGS, dict(_MSL_CONST),
+                             dict(_MSL_INFER))
+flash_attention_d128 = Kernel("flash_attention_d128", "neso_flash_attention_d128", _MSL_ARGS,
+                              dict(_MSL_CONST, d=128), dict(_MSL_INFER))
 rel_pos_fa2_fwd = Kernel(
     "rel_pos_fa2_fwd", "neso_rel_pos_fa2_fwd",
     [("Q", P), ("K", P), ("V", P), ("bias", P), ("O", P), ("T", I), ("stride", I), ("scale", F),
@@ -171,6 +197,12 @@ w8a16_scaled_matmul = Kernel(
     [("A", P), ("B", P), ("C", P), ("scale", P), ("K", I), ("stride_am", I), ("stride_bk", I),
      ("stride_cm", I)],
     {"BM": 64, "BN": 64, "BK": 32})
+# tests/test_advanced12.py:19-48 (per-tensor fp32 scale; b as int8, or int32 as that test stores it)
+w8a16_matmul_kernel = Kernel(
+    "w8a16_matmul_kernel", "neso_w8a16_matmul_kernel",
+    [("a_ptr", P), ("b_int8_ptr", P), ("c_ptr", P), ("scale_ptr", P), ("M", I), ("N", I), ("K", I),
+     ("stride_am", I), ("stride_ak", I), ("stride_bk", I), ("stride_bn", I), ("stride_cm", I), ("stride_cn", I)],
+    {"BLOCK_M": None, "BLOCK_N": None, "BLOCK_K": None}, select=_int32_weights)
 
 # LLM building blocks (tests/test_advanced12.py:104-177)
 rmsnorm_kernel = Kernel(
@@ -205,7 +237,8 @@ quantize_kernel = Kernel(
     "quantize_kernel", "neso_quantize_kernel", [("x_ptr", P), ("scale_ptr", P), ("out_ptr", P), ("n", I)],
     {"BLOCK": None})
 
-KERNELS = {k.name: k for k in (vector_add, add_kernel, scale, flash_attention_fwd, rel_pos_fa2_fwd, matmul_kernel,
-                                matmul_tiled, w8a16_matmul, w8a16_scaled_matmul, rmsnorm_kernel,
+KERNELS = {k.name: k for k in (vector_add, add_kernel, scale, flash_attention_fwd, flash_attention_fwd_msl,
+                                flash_attention_opt, flash_attention_d128, rel_pos_fa2_fwd, matmul_kernel,
+                                matmul_tiled, w8a16_matmul, w8a16_scaled_matmul, w8a16_matmul_kernel, rmsnorm_kernel,
                                 residual_rmsnorm_kernel, rope_kernel, silu_kernel, softmax_kernel,
                                 per_channel_dequant_kernel, grouped_dequant_kernel, quantize_kernel)}

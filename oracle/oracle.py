@@ -148,6 +148,12 @@ def w8a16_matmul(x: torch.Tensor, w: torch.Tensor, scale: torch.Tensor | None = 
     return c
 
 
+def w8a16_matmul_tensor_scale(a: torch.Tensor, b: torch.Tensor, scale: float) -> torch.Tensor:
+    """tests/test_advanced12.py:193: C = A @ (B * scale) in fp32, one scale for
+    the whole weight matrix (the kernel, :19-48, multiplies the fp32 sum by it)."""
+    return torch.matmul(a.float(), b.float() * float(scale))
+
+
 def pack_int4(q: torch.Tensor) -> torch.Tensor:
     """Pack int4 values q [K, N] (in [-8, 7]) into uint8 [K/2, N]: byte (k/2, n)
     holds row 2i in bits 0-3 and row 2i+1 in bits 4-7, two's complement."""

@@ -27,7 +27,8 @@ def test_metadata_matches_reference_schema():
     keys = {"kernel_name", "params", "constants", "threadgroup_size", "num_warps", "grid"}
     for name in ["vector_add", "add_kernel", "scale", "flash_attention_fwd", "rel_pos_fa2_fwd", "matmul_kernel",
                  "matmul_tiled", "w8a16_matmul", "w8a16_scaled_matmul", "fa2_fwd", "fa2_fwd_relpos_table",
-                 "w8a16_matmul_mnk", "w4a16_g128_matmul"]:
+                 "w8a16_matmul_mnk", "w4a16_g128_matmul", "flash_attention_fwd_msl", "flash_attention_opt",
+                 "flash_attention_d128", "w8a16_matmul_kernel"]:
         meta = json.loads(lib.neso_kernel_metadata(name.encode()).decode())
         assert set(meta) == keys, name
         assert meta["kernel_name"] == name
@@ -85,6 +86,38 @@ def test_matmul_grid_and_strides_checked():
     assert rc == _lib.NESO_ERR_UNSUPPORTED
     rc = lib.neso_matmul_kernel(None, None, None, 256, 256, 64, 64, 1, 256, 1, 256, 1, 0, 128, 32, 2, 2, 1, None)
     assert rc == _lib.NESO_ERR_INVALID_ARG
+
+
+@pytest.mark.parametrize("fn", ["neso_flash_attention_fwd_msl", "neso_flash_attention_opt", "neso_flash_attention_d128"])
+def test_msl_fa2_entries_check_launch_before_the_device(fn):
+    # bench/bench_flash_attention.py:375: grid (N // BM, 1, 1); d_head equal to the compiled d.
+    f = getattr(_lib.lib(), fn)
+    d = 128
+    # (Q, K, V, O, N, d_head, scale, BM, BN, d, THREADS, use_half, grid, stream)
+    assert f(None, None, None, None, 256, d, 0.1, 32, 32, d, 1024, 1, 7, 1, 1, None) == _lib.NESO_ERR_GRID
+    assert f(None, None, None, None, 250, d, 0.1, 32, 32, d, 1024, 1, 7, 1, 1, None) == _lib.NESO_ERR_GRID
+    assert f(None, None, None, None, 256, 64, 0.1, 32, 32, d, 1024, 1, 8, 1, 1, None) == _lib.NESO_ERR_INVALID_ARG
+    assert f(None, None, None, None, 256, d, 0.1, 32, 32, d, 1024, 2, 8, 1, 1, None) == _lib.NESO_ERR_INVALID_ARG
+    assert f(None, None, None, None, 256, 96, 0.1, 32, 32, 96, 1024, 1, 8, 1, 1, None) == _lib.NESO_ERR_UNSUPPORTED
+    assert f(None, None, None, None, 256, d, 0.1, 32, 32, d, 1024, 1, 8, 1, 1, None) == _lib.NESO_ERR_INVALID_ARG  # null
+
+
+def test_flash_attention_d128_rejects_d64():
+    rc = _lib.lib().neso_flash_attention_d128(None, None, None, None, 256, 64, 0.1, 32, 32, 64, 1024, 1, 8, 1, 1, None)
+    assert rc == _lib.NESO_ERR_UNSUPPORTED
+
+
+@pytest.mark.parametrize("fn", ["neso_w8a16_matmul_kernel", "neso_w8a16_matmul_kernel_i32"])
+def test_w8a16_tensor_scale_checks_launch_before_the_device(fn):
+    # tests/test_advanced12.py:188-196: grid (cdiv(M, BLOCK_M), cdiv(N, BLOCK_N)).
+    f = getattr(_lib.lib(), fn)
+    ok_args = (32, 32, 32, 32, 1, 32, 1, 32, 1, 32, 32, 32)
+    assert f(None, None, None, None, *ok_args, 2, 1, 1, None) == _lib.NESO_ERR_GRID
+    bad_stride = (32, 32, 32, 32, 2, 32, 1, 32, 1, 32, 32, 32)
+    assert f(None, None, None, None, *bad_stride, 1, 1, 1, None) == _lib.NESO_ERR_UNSUPPORTED
+    assert f(None, None, None, None, *ok_args, 1, 1, 1, None) == _lib.NESO_ERR_INVALID_ARG  # null scale
+    zero_block = (32, 32, 32, 32, 1, 32, 1, 32, 1, 0, 32, 32)
+    assert f(None, None, None, None, *zero_block, 1, 1, 1, None) == _lib.NESO_ERR_INVALID_ARG
 
 
 def test_error_string_is_thread_local():

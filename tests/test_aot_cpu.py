@@ -68,3 +68,19 @@ def test_cli_writes_metadata(tmp_path):
     assert [(p["index"], p["name"]) for p in meta["params"]] == [(0, "x"), (1, "y"), (2, "output"),
                                                                  (3, "n_elements")]
     assert aot.main(["--kernel", "nope", "--signature", "i32"]) == 1
+
+
+def test_signature_value_forms_and_hints():
+    # src/neso/backend/abi.py:59-82: a value body wins over a hint of 1; None
+    # is a constexpr; a hint of 1 makes a typed argument the constant 1 while
+    # it keeps its written type; a hint of 16 is a divisibility attribute.
+    ps = aot.parse_signature(["a", "b", "c"], "64:1, None, *fp32:16")
+    assert ps.constants == {"a": 64, "b": None}
+    assert ps.source_types == {"a": "constexpr", "b": "constexpr", "c": "*fp32"}
+    assert ps.attributes == {(2,): [["tt.divisibility", 16]]}
+    ps = aot.parse_signature(["x"], "i32:1")
+    assert ps.constants == {"x": 1} and ps.source_types == {"x": "i32"}
+    assert ps.triton_signature == {"x": "constexpr"}
+    params = aot.build_parameters(["p", "n", "k"], {"p": "*fp16", "k": "constexpr"})
+    assert [(q.index, q.name, q.type, q.is_pointer) for q in params] == [(0, "p", "*fp16", True),
+                                                                         (1, "n", "i32", False)]

@@ -133,17 +133,83 @@ def test_relpos_table_many_units_sampled(dev, D):
             torch.testing.assert_close(o[b, h].cpu(), ref, **TOL)
 
 
+SWEEP_HEADS = [(0, 0), (7, 9), (15, 15)]  # first, a middle and the last (b, h) of B = H = 16
+
+
 @pytest.mark.parametrize("D", [64, 128])
-def test_baseline_sweep_s2048_sampled(dev, D):
-    # Full BASELINE shape B = H = 16, S = 2048; a sample of heads against the oracle.
-    B, H, S = 16, 16, 2048
-    gd = torch.Generator(device=dev).manual_seed(D)
+@pytest.mark.parametrize("S", [128, 256, 512, 1024, 2048])
+def test_baseline_sweep_sampled(dev, S, D):
+    # BASELINE config 3 at its full shape, B = H = 16: every S and D of the
+    # sweep, plain, causal, relative-position table N(0, 0.02) and causal with
+    # the table. The unit count (and so the persistent D = 128 scheduler's and
+    # the causal pair kernel's work split) changes with S; three heads per
+    # point against the oracle.
+    B, H = 16, 16
+    gd = torch.Generator(device=dev).manual_seed(1000 * D + S)
     q, k, v = (torch.randn(B, H, S, D, device=dev, generator=gd).half() for _ in range(3))
+    table = torch.randn(H, 2 * S - 1, device=dev, generator=gd) * 0.02
+    qc, kc, vc, tc = q.cpu(), k.cpu(), v.cpu(), table.cpu()
+    sc = 1 / math.sqrt(D)
     for causal in (False, True):
-        o = ops.flash_attention(q, k, v, 1 / math.sqrt(D), causal=causal)
-        for (b, h) in [(0, 0), (7, 9), (15, 15)]:
-            ref = oracle.attention(q[b, h].cpu(), k[b, h].cpu(), v[b, h].cpu(), 1 / math.sqrt(D), causal=causal)
-            torch.testing.assert_close(o[b, h].cpu(), ref, **TOL)
+        for tab in (None, table):
+            o = ops.flash_attention(q, k, v, sc, causal=causal, table=tab)
+            for (b, h) in SWEEP_HEADS:
+                ref = oracle.attention(qc[b, h], kc[b, h], vc[b, h], sc, causal=causal,
+                                       table=None if tab is None else tc[h:h + 1])
+                torch.testing.assert_close(o[b, h].cpu(), ref, **TOL)
+
+
+def _msl_inputs(N, d, seed=42):
+    # bench/bench_flash_attention.py:380-384: random.seed(42), then N*d
+    # gauss(0, 0.5) draws each for Q, K and V.
+    import random
+    rnd = random.Random(seed)
+    return tuple(torch.tensor([rnd.gauss(0, 0.5) for _ in range(N * d)], dtype=torch.float32).view(N, d)
+                 for _ in range(3))
+
+
+@pytest.mark.parametrize("name", ["flash_attention_fwd_msl", "flash_attention_opt", "flash_attention_d128"])
+@pytest.mark.parametrize("use_half", [1, 0])
+@pytest.mark.parametrize("N", [256, 2048])
+def test_msl_entries(dev, name, use_half, N):
+    # The reference's hand-written MSL kernels: one io_type for Q, K, V and O,
+    # d_head and scale at run time, grid (N / BM, 1, 1) with BM = 32.
+    d = 128 if name == "flash_attention_d128" else 64
+    q, k, v = _msl_inputs(N, d)
+    dt = torch.float16 if use_half else torch.float32
+    qd, kd, vd = (t.to(dt).to(dev) for t in (q, k, v))
+    o = torch.zeros(N, d, dtype=dt, device=dev)
+    sc = 1.0 / math.sqrt(d)
+    getattr(kernels, name)[(N // 32, 1, 1)](qd, kd, vd, o, N, d, sc, BM=32, BN=32)
+    out = o.float().cpu()
+    ref = oracle.attention(qd.cpu(), kd.cpu(), vd.cpu(), sc)
+    # the reference's own check: row 0 within 0.05 (fp16) / 0.01 (fp32)
+    assert (out[0] - ref[0]).abs().max().item() < (0.05 if use_half else 0.01)
+    torch.testing.assert_close(out, ref, **TOL)
+
+
+@pytest.mark.parametrize("name", ["fa2_N128_d64", "fa2_N256_d128"])
+def test_msl_entry_reference_golden(dev, golden_dir, name):
+    # The golden single-head cases through the MSL fp16 entry (O in fp16).
+    g = dict(np.load(golden_dir / f"{name}.npz"))
+    N, d = int(g["N"]), int(g["d"])
+    q, k, v = (torch.from_numpy(g[t]).half() for t in ("q", "k", "v"))
+    o = torch.empty(N, d, dtype=torch.float16, device=dev)
+    kernels.flash_attention_fwd_msl[(N // 16, 1, 1)](q.to(dev), k.to(dev), v.to(dev), o, N, d, float(g["scale"]),
+                                                     BM=16, BN=32)
+    out = o.float().cpu()
+    assert np.abs(out.numpy()[[0, N // 2]] - g["ref_out"][[0, N // 2]]).max() < 0.05
+    torch.testing.assert_close(out, oracle.attention(q, k, v, float(g["scale"])), **TOL)
+
+
+def test_msl_entry_rejects_mismatched_d_head(dev):
+    z = torch.zeros(128, 64, dtype=torch.float16, device=dev)
+    with pytest.raises(_lib.NesoError) as ei:
+        kernels.flash_attention_fwd_msl[(4, 1, 1)](z, z, z, z, 128, 64, 0.125, d=128)
+    assert ei.value.code == _lib.NESO_ERR_INVALID_ARG
+    with pytest.raises(_lib.NesoError) as ei:
+        kernels.flash_attention_d128[(4, 1, 1)](z, z, z, z, 128, 64, 0.125)
+    assert ei.value.code in (_lib.NESO_ERR_UNSUPPORTED, _lib.NESO_ERR_INVALID_ARG)
 
 
 def test_unsupported_head_dim(dev):

@@ -178,3 +178,48 @@ def test_int4_k_not_multiple_of_128_rejected(dev):
     with pytest.raises(_lib.NesoError) as ei:
         ops.w4a16_g128_matmul(x, wq, s)
     assert ei.value.code == _lib.NESO_ERR_UNSUPPORTED
+
+
+def test_w8a16_tensor_scale_reference_case_int32_weights(dev):
+    # tests/test_advanced12.py:182-197: M = N = K = 32, b drawn with
+    # randint(-128, 127) and held in int32, scale 0.01 (fp32), grid (1, 1),
+    # BLOCK_M = BLOCK_N = BLOCK_K = 32; the reference accepts max error < 0.5.
+    M = N = K = 32
+    g = torch.Generator().manual_seed(0)
+    a = torch.randn(M, K, generator=g).half()
+    b = torch.randint(-128, 127, (K, N), generator=g, dtype=torch.int32)
+    scale = torch.tensor([0.01], dtype=torch.float32)
+    c = torch.zeros(M, N, device=dev)
+    kernels.w8a16_matmul_kernel[(1, 1)](a.to(dev), b.to(dev), c, scale.to(dev), M, N, K, K, 1, N, 1, N, 1,
+                                        BLOCK_M=32, BLOCK_N=32, BLOCK_K=32)
+    ref = oracle.w8a16_matmul_tensor_scale(a, b, 0.01)
+    assert (c.cpu() - ref).abs().max().item() < 0.5
+    torch.testing.assert_close(c.cpu(), ref, **TOL)
+
+
+@pytest.mark.parametrize("M", [1, 4, 16, 64, 128, 2048])
+@pytest.mark.parametrize("wdtype", [torch.int8, torch.int32])
+def test_w8a16_tensor_scale_baseline_shapes(dev, M, wdtype):
+    # BASELINE weight shape (K = 4096, N = 11008): the GEMV (M <= 4), the
+    # swapped small-M layout with split-K, and the M >= 65 layouts, all with the
+    # one fp32 scale applied in the epilogue (or the split-K reduce).
+    N, K = 11008, 4096
+    x, w, _ = _w8(M, N, K, seed=300 + M)
+    s = 0.0137
+    c = torch.empty(M, N, device=dev)
+    grid = ((M + 63) // 64, (N + 127) // 128)
+    kernels.w8a16_matmul_kernel[grid](x.to(dev), w.to(wdtype).to(dev), c, torch.tensor([s], device=dev), M, N, K,
+                                      K, 1, N, 1, N, 1, BLOCK_M=64, BLOCK_N=128, BLOCK_K=64)
+    torch.testing.assert_close(c.cpu(), oracle.w8a16_matmul_tensor_scale(x, w, s), **TOL)
+
+
+def test_w8a16_tensor_scale_checks_grid_and_strides(dev):
+    z = torch.zeros(64, device=dev)
+    with pytest.raises(_lib.NesoError) as ei:
+        kernels.w8a16_matmul_kernel[(2, 1)](z, z, z, z, 32, 32, 32, 32, 1, 32, 1, 32, 1,
+                                            BLOCK_M=32, BLOCK_N=32, BLOCK_K=32)
+    assert ei.value.code == _lib.NESO_ERR_GRID
+    with pytest.raises(_lib.NesoError) as ei:
+        kernels.w8a16_matmul_kernel[(1, 1)](z, z, z, z, 32, 32, 32, 32, 2, 32, 1, 32, 1,
+                                            BLOCK_M=32, BLOCK_N=32, BLOCK_K=32)
+    assert ei.value.code == _lib.NESO_ERR_UNSUPPORTED
