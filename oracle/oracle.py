@@ -34,7 +34,8 @@ import numpy as np
 import torch
 
 __all__ = [
-    "vector_add", "scale", "attention", "attention_rows", "gemm", "w8a16_matmul", "pack_int4",
+    "vector_add", "scale", "attention", "attention_rows", "gemm", "w8a16_matmul", "w8a16_matmul_tensor_scale",
+    "pack_int4",
     "unpack_int4", "w4a16_g128_matmul", "harness_elementwise_inputs", "harness_fa2_values",
     "rmsnorm", "rope", "silu", "softmax_rows", "per_channel_dequant", "grouped_dequant", "quantize_int8",
 ]
