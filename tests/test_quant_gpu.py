@@ -223,3 +223,24 @@ def test_w8a16_tensor_scale_checks_grid_and_strides(dev):
         kernels.w8a16_matmul_kernel[(1, 1)](z, z, z, z, 32, 32, 32, 32, 2, 32, 1, 32, 1,
                                             BLOCK_M=32, BLOCK_N=32, BLOCK_K=32)
     assert ei.value.code == _lib.NESO_ERR_UNSUPPORTED
+
+
+@pytest.mark.parametrize("kind,M", [("w8", 5), ("w8", 16), ("w8", 40), ("w4", 16), ("w4", 64)])
+def test_swapped_split_k_sum_in_kernel_is_repeatable(dev, kind, M):
+    # Decode batches (M <= 64) at the BASELINE weight shape split K across
+    # CTAs; the last split of each channel group adds the partial sums in
+    # split order inside the kernel. Two launches give identical bits and the
+    # oracle's result.
+    N, K = 11008, 4096
+    if kind == "w8":
+        x, w, s = _w8(M, N, K, seed=500 + M)
+        run = lambda: ops.w8a16_matmul(x.to(dev), w.to(dev), s.to(dev))  # noqa: E731
+        expect = oracle.w8a16_matmul(x, w, s)
+    else:
+        x, q, s = _w4(M, N, K, seed=600 + M)
+        wq = oracle.pack_int4(q)
+        run = lambda: ops.w4a16_g128_matmul(x.to(dev), wq.to(dev), s.to(dev))  # noqa: E731
+        expect = oracle.w4a16_g128_matmul(x, wq, s)
+    y1, y2 = run().cpu(), run().cpu()
+    assert torch.equal(y1, y2)
+    torch.testing.assert_close(y1, expect, **TOL)
