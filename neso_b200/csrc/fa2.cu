@@ -16,12 +16,14 @@
 // softmax runs on the CUDA cores. Keys are consumed in 128-key blocks. Two
 // kernels share this design and the host picks the faster one per head dim
 // (measured on B200):
-//   D = 64   fa2_tile_kernel with one 128-row tile per CTA and two CTAs per
-//            SM (256 TMEM columns, 86 KB of shared memory each): the tiles
-//            of the two CTAs overlap as the ping-pong pair does, and one
-//            CTA's prologue and epilogue run under the other's main loop.
-//            Causal D = 64 runs fa2_pair_kernel: the same one-tile CTA
-//            processing tiles qb and nq-1-qb one after the other.
+//   D = 64   fa2_pair_kernel: one 128-row tile at a time per CTA and two
+//            CTAs per SM (256 TMEM columns, 100 KB of shared memory each):
+//            the tiles of the two CTAs overlap as the ping-pong pair does.
+//            Non-causal, each CTA walks the (head, query tile) units
+//            blockIdx.x, blockIdx.x + gridDim.x, ... (persistent: the next
+//            tile's Q load and first QK run under this tile's last blocks
+//            and epilogue); causal, it processes tiles qb and nq-1-qb.
+//            fa2_tile_kernel is the same CTA for one tile.
 //   D = 128  fa2_persistent_kernel: one two-tile CTA per SM walks units
 //            handed out from a per-launch counter.
 // The description below is of the two-tile form; the one-tile form drops
@@ -643,17 +645,18 @@ __global__ void __launch_bounds__(FaCfg<D, kT>::kThreads, FaCfg<D, kT>::min_bloc
   }
 }
 
-// Two query tiles of one head per CTA, one after the other (tiles bx and
-// nq-1-bx: under causal masking every CTA then has nq+1 key blocks), used
-// for causal attention (measured: S=2048 494 -> 515 TFLOP/s, S=512 214 ->
-// 231; without masking it gains nothing at S=2048 and loses at S=384). Same
-// roles and TMEM layout as the one-tile kernel; the CTA's prologue and
-// launch are paid once per two tiles, the second tile's first QK runs while
-// the first tile's epilogue drains O, and O leaves through a dedicated
-// staging area (the K/V ring is busy with the next tile by then). Every
-// mbarrier phase runs over the CTA's blocks of both tiles (running block
-// index g); q_empty hands the single Q buffer to the next tile's load after
-// the last QK, o_free the O columns to the next tile's first PV after the
+// Query tiles one after the other in one CTA (same roles and TMEM layout as
+// the one-tile kernel). Causal: tiles bx and nq-1-bx of one head, so every
+// CTA has nq+1 key blocks (S=2048 494 -> 515 TFLOP/s, S=512 214 -> 231
+// against one tile per CTA). Non-causal: a persistent walk over the (head,
+// query tile) units, two CTAs per SM (B=H=16 D=64: S=512 364 -> 431,
+// S=1024 535 -> 559, S=2048 639 -> 647 against one tile per CTA). The CTA's
+// prologue and launch are paid once, the next tile's first QK runs while
+// this tile's epilogue drains O, and O leaves through a dedicated staging
+// area (the K/V ring is busy with the next tile by then). Every mbarrier
+// phase runs over the CTA's blocks of all its tiles (running block index
+// g); q_empty hands the single Q buffer to the next tile's load after the
+// last QK, o_free the O columns to the next tile's first PV after the
 // epilogue has read them.
 template <int D, bool kCausal, int kBias>
 __global__ void __launch_bounds__(FaCfg<D, 1>::kThreads, 2)
@@ -693,10 +696,19 @@ __global__ void __launch_bounds__(FaCfg<D, 1>::kThreads, 2)
   const int S = a.S;
   const int nq = a.num_qblocks;
   const int bx = static_cast<int>(blockIdx.x);
-  const int bh = blockIdx.y;
   const int nkv = (S + 127) / 128;
-  const int ntiles = (nq - 1 - bx != bx) ? 2 : 1;
-  auto tile_qb = [&](int qt) { return qt == 0 ? nq - 1 - bx : bx; };  // heavier tile first under causal
+  // Work list. Causal: query tiles nq-1-bx (the heavier, first) and bx of head
+  // blockIdx.y, so every CTA has nq + 1 key blocks. Otherwise a persistent
+  // walk over the (head, query tile) units bx, bx + gridDim.x, ...: the CTA
+  // pays its prologue once, the next tile's Q load and first QK run under
+  // this tile's last blocks and epilogue, and the CTAs running at one time
+  // hold consecutive units, so they share K/V in L2.
+  const int total = kCausal ? 0 : a.BH * nq;
+  const int ntiles = kCausal ? ((nq - 1 - bx != bx) ? 2 : 1)
+                             : (bx < total ? (total - 1 - bx) / static_cast<int>(gridDim.x) + 1 : 0);
+  auto tile_unit = [&](int qt) { return bx + qt * static_cast<int>(gridDim.x); };
+  auto tile_qb = [&](int qt) { return kCausal ? (qt == 0 ? nq - 1 - bx : bx) : tile_unit(qt) % nq; };
+  auto tile_bh = [&](int qt) { return kCausal ? static_cast<int>(blockIdx.y) : tile_unit(qt) / nq; };
   auto tile_blocks = [&](int qt) { return kCausal ? min(nkv, tile_qb(qt) + 1) : nkv; };
 
   if (threadIdx.x == 0) {
@@ -745,7 +757,7 @@ __global__ void __launch_bounds__(FaCfg<D, 1>::kThreads, 2)
         mbar_arrive_expect_tx(q_full, Cfg::kTileBytes);
 #pragma unroll
         for (int c = 0; c < Cfg::kChunks; ++c) {
-          tma_load_3d(sQ + c * 16384, &tmQ, q_full, c * 64, tile_qb(qt) * 128, bh);
+          tma_load_3d(sQ + c * 16384, &tmQ, q_full, c * 64, tile_qb(qt) * 128, tile_bh(qt));
         }
         q_issued = qt + 1;
         const int n = tile_blocks(qt);
@@ -756,7 +768,7 @@ __global__ void __launch_bounds__(FaCfg<D, 1>::kThreads, 2)
           mbar_arrive_expect_tx(&k_full[s], Cfg::kTileBytes);
 #pragma unroll
           for (int c = 0; c < Cfg::kChunks; ++c) {
-            tma_load_3d(sK + s * Cfg::kTileBytes + c * 16384, &tmK, &k_full[s], c * 64, j * 128, bh);
+            tma_load_3d(sK + s * Cfg::kTileBytes + c * 16384, &tmK, &k_full[s], c * 64, j * 128, tile_bh(qt));
           }
           if (!mbar_wait(&v_empty[s], ph ^ 1, abort_flag, a.st, 0x1101)) {
             mbar_wait(&k_full[s], ph, never_flag, quiet, 0);  // K is in flight; V is not
@@ -766,7 +778,7 @@ __global__ void __launch_bounds__(FaCfg<D, 1>::kThreads, 2)
           mbar_arrive_expect_tx(&v_full[s], Cfg::kTileBytes);
 #pragma unroll
           for (int c = 0; c < Cfg::kChunks; ++c) {
-            tma_load_3d(sV + s * Cfg::kTileBytes + c * 16384, &tmV, &v_full[s], c * 64, j * 128, bh);
+            tma_load_3d(sV + s * Cfg::kTileBytes + c * 16384, &tmV, &v_full[s], c * 64, j * 128, tile_bh(qt));
           }
         }
       }
@@ -843,7 +855,6 @@ __global__ void __launch_bounds__(FaCfg<D, 1>::kThreads, 2)
     const uint32_t q = warp & 3;
     const int row = q * 32 + lane;
     const uint32_t lane_base = tmem + ((q * 32) << 16);
-    const int h = bh % a.H;
     const bool fast_path = a.qk_log2 > 0.f;
     const int ntile0 = 0, ntile1 = 0;  // turn handshake of the two-tile form: not used here
     (void)ntile0;
@@ -853,6 +864,8 @@ __global__ void __launch_bounds__(FaCfg<D, 1>::kThreads, 2)
     uint8_t* stage = sOut + (warp - 4) * 4096;
     for (int qt = 0; qt < ntiles && ok_run; ++qt) {
       const int q0 = tile_qb(qt) * 128;
+      const int bh = tile_bh(qt);
+      const int h = bh % a.H;
       const int qrow = q0 + row;
       const int n_t = tile_blocks(qt);
       const float* ttab = kBias == kBiasTable ? a.table + static_cast<int64_t>(h) * (2 * S - 1) : nullptr;
@@ -1731,8 +1744,8 @@ int run_fa2_kernel(Kernel kern, int threads, uint32_t regs_low, dim3 grid, int s
 }
 
 // Kernel per head dim, the faster one measured on B200: D = 128 runs the
-// persistent kernel, D = 64 one 128-row tile per CTA (two, one after the
-// other, under causal masking).
+// persistent two-tile kernel, D = 64 the one-tile CTA walking its tiles
+// (persistent when non-causal, tiles qb and nq-1-qb when causal).
 template <int D, bool kCausal, int kBias>
 int launch_fa2_t(const FaProblem& p, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                  const CUtensorMap& to, FaArgs& args, cudaStream_t stream) {
@@ -1754,8 +1767,11 @@ int launch_fa2_t(const FaProblem& p, const CUtensorMap& tq, const CUtensorMap& t
                             dim3((args.num_qblocks + 1) / 2, p.BH, 1), Cfg1::kSmemBytes + 4 * 4096, tq, tk, tv, to,
                             args, stream);
     } else {
-      return run_fa2_kernel(fa2_tile_kernel<D, 1, kCausal, kBias>, Cfg1::kThreads, Cfg1::regs_low(),
-                            dim3(args.num_qblocks, p.BH, 1), Cfg1::kSmemBytes, tq, tk, tv, to, args, stream);
+      // Persistent: two CTAs per SM walk the (head, query tile) units.
+      const int64_t total = static_cast<int64_t>(args.num_qblocks) * p.BH;
+      const int grid = static_cast<int>(std::min<int64_t>(total, 2 * static_cast<int64_t>(sm_count())));
+      return run_fa2_kernel(fa2_pair_kernel<D, kCausal, kBias>, Cfg1::kThreads, Cfg1::regs_low(), dim3(grid, 1, 1),
+                            Cfg1::kSmemBytes + 4 * 4096, tq, tk, tv, to, args, stream);
     }
   }
 }
