@@ -28,7 +28,11 @@ way as the headline (heads for attention, output columns for the matmuls,
 element ranges for the elementwise kernels) and timed as the max over ranks:
 every BASELINE config with its roofline fraction (``baseline_configs``), the
 e2e number through the public API with pinned host buffers, the roofline of
-the headline kernel and the CPU baseline.
+the headline kernel and the CPU baseline. A BASELINE config's time is the
+device time per launch with the launches replayed from one CUDA graph (its
+roofline fraction uses it); the same calls issued eagerly from Python are
+reported beside it (``ms_eager`` / ``us_eager``), which for problems of a
+few microseconds is the host's per-call cost.
 """
 from __future__ import annotations
 
@@ -251,16 +255,44 @@ def time_region(ctx: Ctx, fn, steps: int) -> float:
     return ctx.max_over_ranks(start.elapsed_time(end) / steps)
 
 
-def time_rotating(ctx: Ctx, sets: list, launch, iters: int = 20) -> float:
+def time_rotating(ctx: Ctx, sets: list, launch, iters: int = 20) -> tuple[float, float]:
     """ms per launch of `launch(set)` over rotating input sets (their total
     size exceeds L2, so every launch reads HBM), after one warm-up launch per
-    set; max over ranks."""
+    set; max over ranks. Returns (device ms, eager ms): the device time
+    replays the `iters` launches from one CUDA graph, so small problems show
+    the kernels' time rather than the host's per-call cost; the eager time
+    issues the same calls from Python back to back."""
     import torch
 
+    eager = None
+    side = torch.cuda.Stream(ctx.dev)
+    side.wait_stream(torch.cuda.current_stream(ctx.dev))
+    with torch.cuda.stream(side):  # the capture stream gets its per-stream state first
+        for st in sets:
+            launch(st)
+    torch.cuda.synchronize()
     for st in sets:
         launch(st)
     torch.cuda.synchronize()
-    return time_region(ctx, _Rotor(sets, launch), iters)
+    eager = time_region(ctx, _Rotor(sets, launch), iters)
+    graph = torch.cuda.CUDAGraph()
+    rot = _Rotor(sets, launch)
+    with torch.cuda.graph(graph, stream=side):
+        for _ in range(iters):
+            rot()
+    graph.replay()
+    torch.cuda.synchronize()
+    ctx.barrier()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record(side)
+    graph.replay()
+    end.record(side)
+    torch.cuda.synchronize()
+    ctx.barrier()
+    dev_ms = ctx.max_over_ranks(start.elapsed_time(end) / iters)
+    del graph
+    return dev_ms, eager
 
 
 class _Rotor:
@@ -309,9 +341,9 @@ def baseline_configs(ctx: Ctx, peaks: dict) -> dict:
     z = torch.empty_like(x)
     for name, fn, per_el in (("vector_add", lambda _: ops.vector_add(x, y, out=z), 12),
                              ("scale", lambda _: ops.scale(x, 0.5, out=z), 8)):
-        ms = time_rotating(ctx, [None], fn, 10)
+        ms, ms_e = time_rotating(ctx, [None], fn, 10)
         r = roofline(None, per_el * sh.size, ms * 1e-3, peaks)
-        out[name] = {"n": n, "gbs": per_el * n / (ms * 1e-3) / 1e9, "ms": ms, **r}
+        out[name] = {"n": n, "gbs": per_el * n / (ms * 1e-3) / 1e9, "ms": ms, "ms_eager": ms_e, **r}
     del x, y, z
 
     # config 4: dense GEMM M = N = K, output columns sharded (16-column groups)
@@ -325,10 +357,11 @@ def baseline_configs(ctx: Ctx, peaks: dict) -> dict:
         sets = [(a, b, torch.empty(m, sh.size, device=dev))]
         for _ in range(copies(set_bytes) - 1):
             sets.append((a.clone(), b.clone(), torch.empty(m, sh.size, device=dev)))
-        ms = time_rotating(ctx, sets, lambda s: ops.matmul(s[0], s[1], out=s[2]))
+        ms, ms_e = time_rotating(ctx, sets, lambda s: ops.matmul(s[0], s[1], out=s[2]))
         fl = 2.0 * m * sh.size * m
         r = roofline(fl, set_bytes, ms * 1e-3, peaks)
-        out[f"gemm_{m}"] = {"tflops": 2.0 * m ** 3 / (ms * 1e-3) / 1e12, "ms": ms, "cols_per_rank": sh.size, **r}
+        out[f"gemm_{m}"] = {"tflops": 2.0 * m ** 3 / (ms * 1e-3) / 1e12, "ms": ms, "ms_eager": ms_e,
+                            "cols_per_rank": sh.size, **r}
         del sets, a, b
 
     # configs 1 and 3: FA2, heads sharded
@@ -353,11 +386,11 @@ def baseline_configs(ctx: Ctx, peaks: dict) -> dict:
                 t = full[torch.arange(sh.start, sh.stop, device=dev) % h_].contiguous()
             sets.append((q, k, v, t, torch.empty(1, sh.size, s_, d_, device=dev)))
         sc = 1 / math.sqrt(d_)
-        ms = time_rotating(ctx, sets, lambda st: ops.flash_attention(st[0], st[1], st[2], sc, causal=causal,
+        ms, ms_e = time_rotating(ctx, sets, lambda st: ops.flash_attention(st[0], st[1], st[2], sc, causal=causal,
                                                                       table=st[3], out=st[4]))
         fl_rank = fa2_flops(1, sh.size, s_, d_, causal)
         r = roofline(fl_rank, set_bytes + (4 * (2 * s_ - 1) * sh.size if tab else 0), ms * 1e-3, peaks)
-        out[name] = {"tflops": fa2_flops(b_, h_, s_, d_, causal) / (ms * 1e-3) / 1e12, "ms": ms,
+        out[name] = {"tflops": fa2_flops(b_, h_, s_, d_, causal) / (ms * 1e-3) / 1e12, "ms": ms, "ms_eager": ms_e,
                      "heads_per_rank": sh.size, **r}
         del sets
 
@@ -381,11 +414,12 @@ def baseline_configs(ctx: Ctx, peaks: dict) -> dict:
                 fn = lambda st: ops.w8a16_matmul(xq, st[0], st[1], out=yq)  # noqa: E731
             else:
                 fn = lambda st: ops.w4a16_g128_matmul(xq, st[0], st[1], out=yq)  # noqa: E731
-            ms = time_rotating(ctx, ws, fn, 30)
+            ms, ms_e = time_rotating(ctx, ws, fn, 30)
             fl = 2.0 * m * nc * QK
             nbytes = wbytes + 2 * m * QK + 4 * m * nc
             r = roofline(fl, nbytes, ms * 1e-3, peaks)
             out[f"{kind}_m{m}"] = {"tflops": 2.0 * m * QN * QK / (ms * 1e-3) / 1e12, "us": ms * 1e3,
+                                   "us_eager": ms_e * 1e3,
                                    "weight_gbs_per_gpu": (QK * nc if kind == "w8a16" else QK * nc // 2) /
                                    (ms * 1e-3) / 1e9, "cols_per_rank": nc, "weight_copies": len(ws), **r}
             del xq, yq

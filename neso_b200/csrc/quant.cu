@@ -764,7 +764,7 @@ int launch_wq(const QProblem& p, cudaStream_t stream) {
 // straight from HBM with 16-byte streaming loads (lane = 16 channels of one
 // stored row: one k for int8, two k for packed int4), converts in registers
 // and accumulates M dot products per channel in fp32. A CTA covers 512
-// channels x one slice of K (one CTA per SM, one wave); its warps split the
+// channels x one slice of K (one wave of CTAs); its warps split the
 // slice and reduce through shared memory; the last CTA of a channel block to
 // finish adds the slices in a fixed order (deterministic) and writes Y.
 //   int8: fp32(b) = float_bits(0x4B000000 | (b ^ 0x80)) - (2^23 + 128), exact;
@@ -778,9 +778,12 @@ constexpr int kGvWarpStride = 32 * 17;            // reduction row per warp, pad
 
 template <int kQ, int kM>
 struct GvCfg {
-  // One CTA per SM: 32 warps for int8 M = 1 (64 registers per thread suffice),
-  // else 16 warps with up to 128 registers per thread.
-  static constexpr int kThreads = (kQ == kInt8 && kM == 1) ? 1024 : 512;
+  // 16 warps per CTA. int8 M = 1 needs 64 registers per thread, so two CTAs
+  // share an SM and one CTA's prologue and final sums overlap the other's
+  // weight stream (measured W8A16 M=1 17.3 -> 16.5 us against one CTA of 32
+  // warps); the other cases take up to 128 registers, one CTA per SM.
+  static constexpr int kThreads = 512;
+  static constexpr int kCtasPerSm = (kQ == kInt8 && kM == 1) ? 2 : 1;
   static constexpr int kWarps = kThreads / 32;
   static constexpr int kSmemBytes = kWarps * kGvWarpStride * 4;
 };
@@ -810,7 +813,7 @@ __device__ __forceinline__ void bytes_to_f32(uint32_t t, float bias, float* f) {
 }
 
 template <int kQ, int kM>
-__global__ void __launch_bounds__(GvCfg<kQ, kM>::kThreads, 1) wq_gemv_kernel(GvArgs a) {
+__global__ void __launch_bounds__(GvCfg<kQ, kM>::kThreads, GvCfg<kQ, kM>::kCtasPerSm) wq_gemv_kernel(GvArgs a) {
   using Cfg = GvCfg<kQ, kM>;
   constexpr int CPL = kGvChanPerLane;
   constexpr int NW = Cfg::kWarps;
@@ -1004,7 +1007,7 @@ GvPlan gemv_plan(const QProblem& p) {
   GvPlan g{};
   const int rows = kQ == kInt8 ? p.K : p.K / 2;
   g.nblk = (p.N + kGvChannels - 1) / kGvChannels;
-  const int want = std::max(1, sm_count() / g.nblk);
+  const int want = std::max(1, Cfg::kCtasPerSm * sm_count() / g.nblk);
   const int unit = 4 * Cfg::kWarps;  // rows per slice: a whole number of 4-row batches per warp
   int rps = (rows + want - 1) / want;
   rps = (rps + unit - 1) / unit * unit;
@@ -1051,403 +1054,6 @@ int launch_gemv(const QProblem& p, cudaStream_t stream) {
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "small-M GEMV launch");
   return ok();
-}
-
-// --------------------------------------------- small-M streaming path (TMA) --
-// Decode batches (M <= 4 int8, M <= 2 int4) read every weight byte once and
-// do a few multiply-adds per byte: the rate is set by how many weight bytes
-// each SM keeps in flight and by how evenly the bytes are spread over the
-// SMs. Here one CTA per SM streams an equal share of the weight matrix:
-//   * the stages are [32 stored rows x 256 channels] tiles (8 KB), ordered
-//     channel tile major, row block minor; CTA b takes stages
-//     [b T / G, (b + 1) T / G) of the T stages (G CTAs), so every SM moves
-//     the same number of bytes and a CTA's range spans one or two channel
-//     tiles;
-//   * warp 0 (one thread) keeps a 12-stage ring of TMA tile loads in flight
-//     (96 KB per SM), independent of the consumers' pace;
-//   * consumer warp w (8 warps) owns channels [32 w, 32 w + 32) of every
-//     stage: lane = (row group r8 = lane / 4, 8 channels cq = lane % 4), four
-//     rows per lane per stage, one 8-byte shared-memory load per row (two
-//     128-byte-swizzled 4 KB boxes per stage, so a warp's 32 loads cover
-//     every bank twice: two wavefronts, the minimum for 256 bytes);
-//   * conversion is exact (float_bits(0x4B000000 | byte) minus the bias, two
-//     lanes per packed add) and the M dot products accumulate in fp32 (two
-//     channels per packed FMA); int4 multiplies each stage's sums by its
-//     128-k group's scales;
-//   * when a CTA leaves a channel tile, each warp adds its eight row groups
-//     with a fixed butterfly of shuffles and writes the tile's partial sums;
-//     the last CTA to finish a channel tile (a per-stream counter) adds the
-//     contributing CTAs' partials in CTA order, applies the scale and writes
-//     Y. The summation order is fixed: results repeat bit for bit.
-// X (all of K, fp32) sits in shared memory; longer K takes the K-sliced GEMV.
-// 4 bytes (b ^ 0x80 for int8, q + 8 for int4 nibbles) -> 4 exact fp32 values
-// as two packed pairs (bytes 0-1, 2-3): float_bits(0x4B000000 | byte) = 2^23 +
-// byte, then one packed add of -(2^23 + 128) or -(2^23 + 8) per pair.
-constexpr uint64_t kNegBias8 = 0xCB000080CB000080ull;  // (-(2^23 + 128), -(2^23 + 128))
-constexpr uint64_t kNegBias4 = 0xCB000008CB000008ull;  // (-(2^23 + 8), -(2^23 + 8))
-__device__ __forceinline__ void bytes_to_f32x2(uint32_t t, uint64_t neg_bias2, uint64_t* w2) {
-#pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    const float lo = __int_as_float(__byte_perm(t, 0x4B000000u, 0x7440u + 2 * h));
-    const float hi = __int_as_float(__byte_perm(t, 0x4B000000u, 0x7441u + 2 * h));
-    w2[h] = fadd2(f2_pack(lo, hi), neg_bias2);
-  }
-}
-
-constexpr int kStC = 256;                    // channels per stage
-constexpr int kStR = 32;                     // stored rows per stage
-constexpr int kStBytes = kStC * kStR;        // 8 KB
-constexpr int kStRing = 12;                  // stages in flight per SM
-constexpr int kStWarps = 8;                  // consumer warps
-constexpr int kStThreads = 32 * (1 + kStWarps);
-constexpr int kStXBytes = 64 * 1024;         // X as fp32, at most
-constexpr int kStSmem = kStRing * kStBytes + kStXBytes + 1024 + 1024;
-
-struct StArgs {
-  const __half* X;
-  int64_t ldx;
-  const __half* scale;  // int8: [N] per channel (nullable); int4: [K/128][lds]
-  int64_t lds;
-  const float* tscale;  // int8: one fp32 scale for all of Y (nullable)
-  float* Y;
-  int64_t ldy;
-  float* partial;  // [G][nseg][kM][kStC]
-  int* counters;   // one per channel tile, zero between launches
-  int M, N, K;
-  int rows;        // stored rows (int8: K, int4: K / 2)
-  int nrb;         // row blocks (stages) per channel tile
-  int nct;         // channel tiles
-  int nseg;        // channel tiles a CTA's range can touch
-  int64_t total;   // stages
-  DevStatus st;
-};
-
-__device__ __forceinline__ int64_t st_start(int64_t b, int64_t total, int64_t G) { return b * total / G; }
-// The CTA whose range holds stage s.
-__device__ __forceinline__ int st_cta_of(int64_t s, int64_t total, int64_t G) {
-  int64_t b = s * G / total;
-  while (b + 1 < G && st_start(b + 1, total, G) <= s) ++b;
-  while (b > 0 && st_start(b, total, G) > s) --b;
-  return static_cast<int>(b);
-}
-
-template <int kQ, int kM>
-__global__ void __launch_bounds__(kStThreads, 1)
-    wq_stream_kernel(const __grid_constant__ CUtensorMap tmW, StArgs a) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* ring = smem;
-  float* xs = reinterpret_cast<float*>(smem + kStRing * kStBytes);  // [kM][K]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kStRing * kStBytes + kStXBytes);
-  uint64_t* full = bars;                  // [kStRing] stage landed (TMA)
-  uint64_t* empty = full + kStRing;       // [kStRing] consumed by the 8 consumer warps
-  uint64_t* x_ready = empty + kStRing;    // X staged (8 consumer warps)
-  uint64_t* seg_done = x_ready + 1;       // a channel tile's partials written (8 warps)
-  uint64_t* flag_ready = seg_done + 1;    // the last-CTA decision is in last_flag
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(flag_ready + 1);
-  volatile int* never_flag = abort_flag + 1;
-  volatile int* last_flag = never_flag + 1;
-
-  const int warp = static_cast<int>(warp_id());
-  const int lane = static_cast<int>(lane_id());
-  const int64_t G = gridDim.x;
-  const int64_t s0 = st_start(blockIdx.x, a.total, G);
-  const int64_t s1 = st_start(blockIdx.x + 1, a.total, G);
-  constexpr int KPR = kQ == kInt8 ? 1 : 2;  // k per stored row
-
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < kStRing; ++i) {
-      mbar_init(&full[i], 1);
-      mbar_init(&empty[i], kStWarps);
-    }
-    mbar_init(x_ready, kStWarps);
-    mbar_init(seg_done, kStWarps);
-    mbar_init(flag_ready, 1);
-    *abort_flag = 0;
-    *never_flag = 0;
-    *last_flag = 0;
-    fence_mbar_init();
-    tma_prefetch_desc(&tmW);
-  }
-  __syncthreads();
-  DevStatus quiet = a.st;
-  quiet.word = nullptr;
-
-  if (warp == 0) {
-    // ------------------------------------------------------------ producer --
-    if (lane == 0) {
-      int64_t issued = 0;
-      for (int64_t s = s0; s < s1; ++s, ++issued) {
-        const int slot = static_cast<int>(issued % kStRing);
-        const uint32_t ph = static_cast<uint32_t>((issued / kStRing) & 1);
-        if (!mbar_wait(&empty[slot], ph ^ 1, abort_flag, a.st, 0x2600)) break;
-        const int ct = static_cast<int>(s / a.nrb);
-        const int rb = static_cast<int>(s % a.nrb);
-        uint8_t* dst = ring + slot * kStBytes;
-        mbar_arrive_expect_tx(&full[slot], kStBytes);
-        tma_load_2d(dst, &tmW, &full[slot], ct * kStC, rb * kStR);
-        tma_load_2d(dst + kStBytes / 2, &tmW, &full[slot], ct * kStC + 128, rb * kStR);
-      }
-      if (*abort_flag) {  // drain this CTA's own copies before it exits
-        for (int64_t i = (issued > kStRing ? issued - kStRing : 0); i < issued; ++i) {
-          mbar_wait(&full[i % kStRing], static_cast<uint32_t>((i / kStRing) & 1), never_flag, quiet, 0);
-        }
-      }
-    }
-  } else {
-    // ------------------------------------------------------------ consumers --
-    const int cw = warp - 1;
-    const int r8 = lane >> 2, cq = lane & 3;
-    const int cbase = 32 * cw + 8 * cq;  // this lane's first channel within the tile
-    // X (all of K) as fp32, zero past K.
-    for (int i = cw * 32 + lane; i < kM * a.K; i += kStWarps * 32) {
-      const int m = i / a.K, k = i % a.K;
-      xs[i] = m < a.M ? __half2float(a.X[static_cast<int64_t>(m) * a.ldx + k]) : 0.f;
-    }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(x_ready);
-    bool ok_run = mbar_wait(x_ready, 0, abort_flag, a.st, 0x2610);
-
-    uint64_t acc[kM][4];  // 8 channels as packed pairs: int8 the sums, int4 this stage's group sums
-    float tot[kM][8];     // int4: scaled sums
-    auto zero_acc = [&]() {
-#pragma unroll
-      for (int m = 0; m < kM; ++m) {
-#pragma unroll
-        for (int i = 0; i < 4; ++i) acc[m][i] = 0ull;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) tot[m][i] = 0.f;
-      }
-    };
-    zero_acc();
-    int cur_ct = static_cast<int>(s0 / a.nrb);
-    const int ct0 = cur_ct;
-    int flushes = 0;
-    // Hand this CTA's sums for channel tile ct to the combine (see above).
-    auto flush = [&](int ct) -> bool {
-      float v[kM][8];
-#pragma unroll
-      for (int m = 0; m < kM; ++m)
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          float x = kQ == kInt8 ? ((i & 1) ? f2_hi(acc[m][i / 2]) : f2_lo(acc[m][i / 2])) : tot[m][i];
-          x += __shfl_xor_sync(0xffffffffu, x, 4);
-          x += __shfl_xor_sync(0xffffffffu, x, 8);
-          x += __shfl_xor_sync(0xffffffffu, x, 16);
-          v[m][i] = x;
-        }
-      const int seg = ct - ct0;
-      float* prow = a.partial + (static_cast<int64_t>(blockIdx.x) * a.nseg + seg) * kM * kStC;
-      if (r8 == 0) {
-#pragma unroll
-        for (int m = 0; m < kM; ++m) {
-          *reinterpret_cast<float4*>(prow + m * kStC + cbase) = make_float4(v[m][0], v[m][1], v[m][2], v[m][3]);
-          *reinterpret_cast<float4*>(prow + m * kStC + cbase + 4) = make_float4(v[m][4], v[m][5], v[m][6], v[m][7]);
-        }
-      }
-      __threadfence();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(seg_done);
-      const uint32_t ph = static_cast<uint32_t>(flushes & 1);
-      ++flushes;
-      if (cw == 0 && lane == 0) {
-        bool ok = mbar_wait(seg_done, ph, abort_flag, a.st, 0x2611);
-        // Contributors to this tile: the CTAs holding its first and last stage.
-        const int b0 = st_cta_of(static_cast<int64_t>(ct) * a.nrb, a.total, G);
-        const int b1 = st_cta_of(static_cast<int64_t>(ct + 1) * a.nrb - 1, a.total, G);
-        *last_flag = ok && (atomicAdd(&a.counters[ct], 1) == b1 - b0);
-        mbar_arrive(flag_ready);
-      }
-      if (!mbar_wait(flag_ready, ph, abort_flag, a.st, 0x2612)) return false;
-      if (*last_flag) {
-        __threadfence();
-        const int b0 = st_cta_of(static_cast<int64_t>(ct) * a.nrb, a.total, G);
-        const int b1 = st_cta_of(static_cast<int64_t>(ct + 1) * a.nrb - 1, a.total, G);
-        const int n = ct * kStC + 32 * cw + lane;  // one channel per lane
-        if (n < a.N) {
-          float sc = 1.f;
-          if (kQ == kInt8 && a.scale != nullptr) sc = __half2float(a.scale[n]);
-          if (kQ == kInt8 && a.scale == nullptr && a.tscale != nullptr) sc = __ldg(a.tscale);
-          const bool scaled = kQ == kInt8 && (a.scale != nullptr || a.tscale != nullptr);
-          for (int m = 0; m < a.M; ++m) {
-            float y = 0.f;
-            for (int b = b0; b <= b1; ++b) {
-              const int segb = ct - static_cast<int>(st_start(b, a.total, G) / a.nrb);
-              y += __ldcg(a.partial + ((static_cast<int64_t>(b) * a.nseg + segb) * kM + m) * kStC + 32 * cw + lane);
-            }
-            a.Y[static_cast<int64_t>(m) * a.ldy + n] = scaled ? y * sc : y;
-          }
-        }
-        __syncwarp();
-        if (cw == 0 && lane == 0) a.counters[ct] = 0;  // ready for the next launch on this stream
-      }
-      return true;
-    };
-
-    int64_t it = 0;
-    for (int64_t s = s0; s < s1 && ok_run; ++s, ++it) {
-      const int ct = static_cast<int>(s / a.nrb);
-      const int rb = static_cast<int>(s % a.nrb);
-      if (ct != cur_ct) {
-        if (!flush(cur_ct)) { ok_run = false; break; }
-        zero_acc();
-        cur_ct = ct;
-      }
-      const int slot = static_cast<int>(it % kStRing);
-      if (!mbar_wait(&full[slot], static_cast<uint32_t>((it / kStRing) & 1), abort_flag, a.st, 0x2613)) {
-        ok_run = false;
-        break;
-      }
-      // This lane's 8 channels sit in box cbase / 128, 16-byte chunk
-      // (cbase % 128) / 16, half cq & 1; chunk index XOR (row & 7) (128B swizzle).
-      const uint8_t* box = ring + slot * kStBytes + (cbase >> 7) * (kStBytes / 2);
-      const int chunk = (cbase & 127) >> 4;
-      const int kk0 = KPR * rb * kStR;  // first k of the stage
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int r = r8 + 8 * i;
-        const uint2 wv = *reinterpret_cast<const uint2*>(box + r * 128 + ((chunk ^ (r & 7)) << 4) + (cq & 1) * 8);
-        if (kQ == kInt8) {
-          uint64_t w2[4];
-          bytes_to_f32x2(wv.x ^ 0x80808080u, kNegBias8, w2);
-          bytes_to_f32x2(wv.y ^ 0x80808080u, kNegBias8, w2 + 2);
-#pragma unroll
-          for (int m = 0; m < kM; ++m) {
-            const float xv = xs[m * a.K + min(kk0 + r, a.K - 1)];
-            const uint64_t xx = f2_pack(xv, xv);
-#pragma unroll
-            for (int h = 0; h < 4; ++h) acc[m][h] = ffma2(xx, w2[h], acc[m][h]);
-          }
-        } else {
-          uint64_t lo[4], hi[4];
-          bytes_to_f32x2((wv.x & 0x0F0F0F0Fu) ^ 0x08080808u, kNegBias4, lo);
-          bytes_to_f32x2((wv.y & 0x0F0F0F0Fu) ^ 0x08080808u, kNegBias4, lo + 2);
-          bytes_to_f32x2(((wv.x >> 4) & 0x0F0F0F0Fu) ^ 0x08080808u, kNegBias4, hi);
-          bytes_to_f32x2(((wv.y >> 4) & 0x0F0F0F0Fu) ^ 0x08080808u, kNegBias4, hi + 2);
-          const int k = kk0 + 2 * r;
-#pragma unroll
-          for (int m = 0; m < kM; ++m) {
-            const float x0 = xs[m * a.K + min(k, a.K - 1)];
-            const float x1 = xs[m * a.K + min(k + 1, a.K - 1)];
-            const uint64_t xx0 = f2_pack(x0, x0), xx1 = f2_pack(x1, x1);
-#pragma unroll
-            for (int h = 0; h < 4; ++h) acc[m][h] = ffma2(xx1, hi[h], ffma2(xx0, lo[h], acc[m][h]));
-          }
-        }
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[slot]);
-      if (kQ == kInt4G128) {
-        // The stage lies in one 128-k group: scale its sums by the group's scales.
-        const int n0 = cur_ct * kStC + cbase;
-        float sc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        if (n0 < a.N) {
-          const uint4 sv = __ldg(reinterpret_cast<const uint4*>(a.scale + static_cast<int64_t>(kk0 / 128) * a.lds + n0));
-          const __half* sh = reinterpret_cast<const __half*>(&sv);
-#pragma unroll
-          for (int i = 0; i < 8; ++i) sc[i] = __half2float(sh[i]);
-        }
-#pragma unroll
-        for (int m = 0; m < kM; ++m) {
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const float v = (i & 1) ? f2_hi(acc[m][i / 2]) : f2_lo(acc[m][i / 2]);
-            tot[m][i] = fmaf(v, sc[i], tot[m][i]);
-          }
-#pragma unroll
-          for (int i = 0; i < 4; ++i) acc[m][i] = 0ull;
-        }
-      }
-    }
-    if (ok_run && s1 > s0) flush(cur_ct);
-  }
-  __syncthreads();
-}
-
-struct StPlan {
-  int64_t total;
-  int grid, nrb, nct, nseg;
-  bool ok;
-};
-StPlan stream_plan(const QProblem& p) {
-  StPlan g{};
-  const int rows = p.kind == kInt8 ? p.K : p.K / 2;
-  g.nrb = (rows + kStR - 1) / kStR;
-  g.nct = (p.N + kStC - 1) / kStC;
-  g.total = static_cast<int64_t>(g.nrb) * g.nct;
-  g.grid = static_cast<int>(std::min<int64_t>(g.total, sm_count()));
-  const int64_t longest = g.grid > 0 ? (g.total + g.grid - 1) / g.grid : 0;
-  g.nseg = static_cast<int>((longest + g.nrb - 1) / g.nrb) + 1;
-  g.ok = g.grid > 0 && g.nct <= kGemvCounterEnd - kGemvCounterBase;
-  return g;
-}
-
-// Streaming path: small M, all of X fits in shared memory as fp32, 16-byte
-// aligned weight rows (TMA), N a multiple of 16 (a lane's 8 channels are all
-// inside N or all past it).
-bool stream_eligible(const QProblem& p) {
-  const int max_m = p.kind == kInt8 ? 4 : 2;
-  const int km = p.M == 1 ? 1 : (p.M == 2 ? 2 : 4);
-  const bool scales_ok = p.kind == kInt8 || ((reinterpret_cast<uintptr_t>(p.scale) & 15u) == 0 && p.lds % 8 == 0);
-  return p.M <= max_m && p.N % 16 == 0 && p.ldw % 16 == 0 && (reinterpret_cast<uintptr_t>(p.W) & 15u) == 0 &&
-         scales_ok && static_cast<int64_t>(km) * p.K * 4 <= kStXBytes && stream_plan(p).ok;
-}
-
-template <int kQ, int kM>
-int launch_stream(const QProblem& p, cudaStream_t stream) {
-  const StPlan g = stream_plan(p);
-  CUtensorMap tmW;
-  {
-    const int rows = kQ == kInt8 ? p.K : p.K / 2;
-    uint64_t dims[2] = {static_cast<uint64_t>(p.N), static_cast<uint64_t>(rows)};
-    uint64_t strides[1] = {static_cast<uint64_t>(p.ldw)};
-    uint32_t box[2] = {128, kStR};
-    int rc = encode_tmap(&tmW, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, p.W, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
-    if (rc != NESO_OK) return rc;
-  }
-  StArgs a{};
-  a.X = static_cast<const __half*>(p.X);
-  a.ldx = p.ldx;
-  a.scale = static_cast<const __half*>(p.scale);
-  a.lds = p.lds;
-  a.tscale = kQ == kInt8 ? p.tscale : nullptr;
-  a.Y = p.Y;
-  a.ldy = p.ldy;
-  a.M = p.M;
-  a.N = p.N;
-  a.K = p.K;
-  a.rows = kQ == kInt8 ? p.K : p.K / 2;
-  a.nrb = g.nrb;
-  a.nct = g.nct;
-  a.nseg = g.nseg;
-  a.total = g.total;
-  int rc = device_status(&a.st);
-  if (rc != NESO_OK) return rc;
-  void* ws = nullptr;
-  rc = stream_workspace(stream, static_cast<size_t>(g.grid) * g.nseg * kM * kStC * sizeof(float), &ws);
-  if (rc != NESO_OK) return rc;
-  a.partial = static_cast<float*>(ws);
-  int* ctr = nullptr;
-  rc = stream_counters(stream, &ctr);
-  if (rc != NESO_OK) return rc;
-  a.counters = ctr + kGemvCounterBase;
-  auto kern = wq_stream_kernel<kQ, kM>;
-  rc = kernel_setup(reinterpret_cast<const void*>(kern), kStSmem, nullptr);
-  if (rc != NESO_OK) return rc;
-  kern<<<g.grid, kStThreads, kStSmem, stream>>>(tmW, a);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e, "small-M streaming launch");
-  return ok();
-}
-
-int run_stream(const QProblem& p, cudaStream_t stream) {
-  if (p.kind == kInt8) {
-    if (p.M == 1) return launch_stream<kInt8, 1>(p, stream);
-    if (p.M == 2) return launch_stream<kInt8, 2>(p, stream);
-    return launch_stream<kInt8, 4>(p, stream);
-  }
-  if (p.M == 1) return launch_stream<kInt4G128, 1>(p, stream);
-  return launch_stream<kInt4G128, 2>(p, stream);
 }
 
 // The small-M path applies when M is small, rows are 16-byte aligned and the
@@ -1527,7 +1133,6 @@ int run_wq(const QProblem& p, cudaStream_t stream) {
       return fail(NESO_ERR_MISALIGNED, "scale row stride must be >= N, multiple of 8");
     }
   }
-  if (stream_eligible(p)) return run_stream(p, stream);
   if (gemv_eligible(p)) return run_gemv(p, stream);
   QProblem q = p;
   int rc = device_status(&q.st);

@@ -34,7 +34,8 @@ import numpy as np
 import torch
 
 __all__ = [
-    "vector_add", "scale", "attention", "attention_rows", "gemm", "w8a16_matmul", "w8a16_matmul_tensor_scale",
+    "vector_add", "scale", "attention", "attention_rows", "gemm", "w8a16_matmul", "w8a16_matmul_f64",
+    "w8a16_matmul_tensor_scale",
     "pack_int4",
     "unpack_int4", "w4a16_g128_matmul", "harness_elementwise_inputs", "harness_fa2_values",
     "rmsnorm", "rope", "silu", "softmax_rows", "per_channel_dequant", "grouped_dequant", "quantize_int8",
@@ -146,6 +147,15 @@ def w8a16_matmul(x: torch.Tensor, w: torch.Tensor, scale: torch.Tensor | None = 
     c = torch.matmul(x.float(), w.float())
     if scale is not None:
         c = c * scale.float().view(1, -1)
+    return c
+
+
+def w8a16_matmul_f64(x: torch.Tensor, w: torch.Tensor, scale: torch.Tensor | None = None) -> torch.Tensor:
+    """The same product as w8a16_matmul summed in float64 (the exact value for
+    checking fp32 sums whose magnitude makes their rounding order visible)."""
+    c = torch.matmul(x.double(), w.double())
+    if scale is not None:
+        c = c * scale.double().view(1, -1)
     return c
 
 

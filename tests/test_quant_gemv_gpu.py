@@ -1,7 +1,9 @@
-"""Small-M (decode) path of the quantized matmul: the CUDA-core GEMV that
-W8A16 with M <= 4 and W4A16 with M <= 2 take, checked against the oracle
-(atol = rtol = 2e-3), its fixed-order (bit-reproducible) slice sum, and the
-shapes and alignments that send a call back to the tensor-core kernel."""
+"""Small-M (decode) paths of the quantized matmul that W8A16 with M <= 4 and
+W4A16 with M <= 2 take: the TMA-fed streaming kernel (all of X in shared
+memory as fp32, so M x K <= 16384) and, for longer K, the K-sliced CUDA-core
+GEMV. Checked against the oracle (atol = rtol = 2e-3), their fixed-order
+(bit-reproducible) cross-CTA sums, and the shapes and alignments that send a
+call to another kernel."""
 import pytest
 import torch
 
@@ -10,6 +12,15 @@ from neso_b200 import _lib, ops
 
 pytestmark = pytest.mark.gpu
 TOL = dict(atol=2e-3, rtol=2e-3)
+
+
+def _assert_unscaled(y, x, w):
+    # Without a scale the int8 products reach |y| ~ 1e3-1e4, where fp32 sums
+    # of K terms in different orders differ in absolute terms in proportion to
+    # the partial sums' size; the check is against a float64 sum with
+    # atol = 2e-3 + 4e-6 max|y| (the scaled results use plain 2e-3).
+    exact = oracle.w8a16_matmul_f64(x, w)
+    torch.testing.assert_close(y.cpu().double(), exact, atol=2e-3 + 4e-6 * exact.abs().max().item(), rtol=2e-3)
 
 
 def _w8(M, N, K, seed):
@@ -36,7 +47,7 @@ def test_w8a16_small_m(dev, M, N, K):
     y = ops.w8a16_matmul(x.to(dev), w.to(dev), s.to(dev))
     torch.testing.assert_close(y.cpu(), oracle.w8a16_matmul(x, w, s), **TOL)
     y0 = ops.w8a16_matmul(x.to(dev), w.to(dev))  # unscaled entry
-    torch.testing.assert_close(y0.cpu(), oracle.w8a16_matmul(x, w), **TOL)
+    _assert_unscaled(y0, x, w)
 
 
 @pytest.mark.parametrize("M", [1, 2])

@@ -12,6 +12,15 @@ pytestmark = pytest.mark.gpu
 TOL = dict(atol=2e-3, rtol=2e-3)
 
 
+def _assert_unscaled(y, x, w):
+    # Without a scale the int8 products reach |y| ~ 1e3-1e4, where fp32 sums
+    # of K terms in different orders differ in absolute terms in proportion to
+    # the partial sums' size; the check is against a float64 sum with
+    # atol = 2e-3 + 4e-6 max|y| (the scaled results use plain 2e-3).
+    exact = oracle.w8a16_matmul_f64(x, w)
+    torch.testing.assert_close(y.cpu().double(), exact, atol=2e-3 + 4e-6 * exact.abs().max().item(), rtol=2e-3)
+
+
 def _w8(M, N, K, seed=0):
     # BASELINE: X ~ N(0,1) fp16, W int8 uniform [-127, 127], scale U[0.001, 0.02] fp16
     g = torch.Generator().manual_seed(seed)
@@ -58,7 +67,7 @@ def test_w8a16_scaled_sizes(dev, M):
     y = ops.w8a16_matmul(x.to(dev), w.to(dev), s.to(dev))
     torch.testing.assert_close(y.cpu(), oracle.w8a16_matmul(x, w, s), **TOL)
     y2 = ops.w8a16_matmul(x.to(dev), w.to(dev))
-    torch.testing.assert_close(y2.cpu(), oracle.w8a16_matmul(x, w), **TOL)
+    _assert_unscaled(y2, x, w)
 
 
 @pytest.mark.parametrize("M", [1, 16, 128, 2048])
