@@ -285,9 +285,10 @@ def time_rotating(ctx: Ctx, sets: list, launch, iters: int = 20) -> tuple[float,
     ctx.barrier()
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
-    start.record(side)
-    graph.replay()
-    end.record(side)
+    with torch.cuda.stream(side):  # replay() runs on the current stream: time it there
+        start.record(side)
+        graph.replay()
+        end.record(side)
     torch.cuda.synchronize()
     ctx.barrier()
     dev_ms = ctx.max_over_ranks(start.elapsed_time(end) / iters)

@@ -223,3 +223,4 @@ def test_device_status_clean_after_runs(dev):
     code = torch.zeros(1, dtype=torch.int32)
     rc = _lib.lib().neso_device_status(0, None, None, None, None)
     assert rc == _lib.NESO_OK, _lib.last_error()
+
