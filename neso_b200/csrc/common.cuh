@@ -314,6 +314,15 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
+// Programmatic dependent launch. pdl_launch_dependents: the next kernel on the
+// stream (launched with the programmatic-serialization attribute) may now be
+// scheduled. pdl_wait: block until every prerequisite grid has completed and
+// its memory operations are visible; a no-op without such a prerequisite.
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // Blackwell packed fp32 pair arithmetic (two lanes per instruction).
 __device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
   return (static_cast<uint64_t>(__float_as_uint(hi)) << 32) | __float_as_uint(lo);

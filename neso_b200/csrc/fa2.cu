@@ -224,6 +224,10 @@ __global__ void __launch_bounds__(FaCfg<D, kT>::kThreads, FaCfg<D, kT>::min_bloc
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // Programmatic dependent launch: nothing global is read or written before
+  // the previous kernel on the stream has completed.
+  pdl_launch_dependents();
+  pdl_wait();
   if (warp < 4) {
     // Warpgroup 0: TMA producer, MMA issuer, TMEM allocator.
     setmaxnreg_dec<Cfg::regs_low()>();
@@ -743,6 +747,10 @@ __global__ void __launch_bounds__(FaCfg<D, 1>::kThreads, 2)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // Programmatic dependent launch: nothing global is read or written before
+  // the previous kernel on the stream has completed.
+  pdl_launch_dependents();
+  pdl_wait();
   DevStatus quiet = a.st;
   quiet.word = nullptr;
   if (warp < 4) {
@@ -1228,6 +1236,10 @@ __global__ void __launch_bounds__(FaCfg<D>::kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // Programmatic dependent launch: nothing global is read or written before
+  // the previous kernel on the stream has completed.
+  pdl_launch_dependents();
+  pdl_wait();
   DevStatus quiet = a.st;
   quiet.word = nullptr;
   // Unit k of this CTA for a single-thread consumer (see fetch_unit).
@@ -1737,8 +1749,7 @@ int run_fa2_kernel(Kernel kern, int threads, uint32_t regs_low, dim3 grid, int s
     return fail(NESO_ERR_LAUNCH, "fa2: %d registers/thread cannot fund the %u/%u warpgroup split", fa.numRegs,
                 regs_low, kRegsHigh);
   }
-  kern<<<grid, threads, smem_bytes, stream>>>(tq, tk, tv, to, args);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_pdl(kern, grid, dim3(threads), smem_bytes, stream, tq, tk, tv, to, args);
   if (e != cudaSuccess) return cuda_fail(e, "fa2 launch");
   return ok();
 }

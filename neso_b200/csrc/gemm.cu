@@ -119,6 +119,10 @@ __global__ void __launch_bounds__(GemmCfg<BN, MH>::kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Programmatic dependent launch: nothing global is read or written before
+  // the previous kernel on the stream has completed.
+  pdl_launch_dependents();
+  pdl_wait();
 
   if (warp == 0 && lane == 0) {
     // ---------------------------------------------------------- producer --
@@ -359,8 +363,7 @@ int launch_gemm_bn(const void* A, int64_t lda, const void* B, int64_t ldb, float
     int src = kernel_setup(reinterpret_cast<const void*>(kern), Cfg::kSmemBytes, nullptr);
     if (src != NESO_OK) return src;
   }
-  kern<<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(tmA, tmB, tmB3, tmC, args);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_pdl(kern, dim3(grid), dim3(Cfg::kThreads), Cfg::kSmemBytes, stream, tmA, tmB, tmB3, tmC, args);
   if (e != cudaSuccess) return cuda_fail(e, "gemm launch");
   return ok();
 }

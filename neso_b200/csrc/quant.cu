@@ -210,6 +210,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // Programmatic dependent launch: nothing global is read or written before
+  // the previous kernel on the stream has completed.
+  pdl_launch_dependents();
+  pdl_wait();
   DevStatus quiet = args.st;
   quiet.word = nullptr;
 
@@ -660,6 +664,8 @@ void plan_splits(QProblem& p, int sms, size_t max_partial = SIZE_MAX) {
 __global__ void splitk_reduce_kernel(const float* __restrict__ partial, int splits, int M, int N,
                                      const __half* __restrict__ scale, const float* __restrict__ tscale,
                                      float* __restrict__ Y, int64_t ldy) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int64_t total = static_cast<int64_t>(M) * N;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -743,15 +749,15 @@ int launch_wq(const QProblem& p, cudaStream_t stream) {
     int src = kernel_setup(reinterpret_cast<const void*>(kern), Cfg::kSmemBytes, nullptr);
     if (src != NESO_OK) return src;
   }
-  kern<<<grid, kThreads, Cfg::kSmemBytes, stream>>>(tmX, tmW, tmS, tmY, args);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_pdl(kern, dim3(grid), dim3(kThreads), Cfg::kSmemBytes, stream, tmX, tmW, tmS, tmY, args);
   if (e != cudaSuccess) return cuda_fail(e, "wq_gemm launch");
   if (args.partial != nullptr) {
     const int64_t total = static_cast<int64_t>(p.M) * p.N;
     const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, 4 * sm_count()));
-    splitk_reduce_kernel<<<blocks, 256, 0, stream>>>(args.partial, args.splits, p.M, p.N, args.chan_scale,
-                                                     args.tensor_scale, p.Y, p.ldy);
-    e = cudaGetLastError();
+    // Launched with programmatic serialization: its CTAs are scheduled as the
+    // matmul's CTAs exit and wait there for the partial sums.
+    e = launch_pdl(splitk_reduce_kernel, dim3(blocks), dim3(256), 0, stream, args.partial, args.splits, p.M, p.N,
+                   args.chan_scale, args.tensor_scale, p.Y, p.ldy);
     if (e != cudaSuccess) return cuda_fail(e, "split-K reduce launch");
   }
   return ok();
@@ -767,11 +773,18 @@ int launch_wq(const QProblem& p, cudaStream_t stream) {
 // channels x one slice of K (one wave of CTAs); its warps split the
 // slice and reduce through shared memory; the last CTA of a channel block to
 // finish adds the slices in a fixed order (deterministic) and writes Y.
-//   int8: fp32(b) = float_bits(0x4B000000 | (b ^ 0x80)) - (2^23 + 128), exact;
+// Weights become exact fp16 values two at a time and are multiplied by the
+// fp16 activations with Blackwell's mixed-precision fma.rn.f32.f16 (fp16 x
+// fp16 product, exact in fp32, added to the fp32 sum with one rounding: the
+// same result as converting both to fp32 first).
+//   int8: half2 bits 0x64xx | (b ^ 0x80) hold 1024 + b + 128 exactly (one
+//         byte permute per two weights), minus 1152 (one f16x2 subtract);
 //         the per-channel scale multiplies the final sum (as the reference's
 //         scaled kernel applies it in the epilogue, tests/test_quantized_matmul.py:250-260).
-//   int4: the same on nibbles (q + 8, minus 2^23 + 8); each warp multiplies
-//         a 128-wide group's sums by the group's scale when the group ends.
+//   int4: nibbles q ^ 8 = q + 8 masked into 0x6400 | n (1024 + q + 8, minus
+//         1032) or 0x6400 | 16 n (times 1/16, minus 72: both exact); each warp
+//         multiplies a 128-wide group's sums by the group's scale when the
+//         group ends.
 constexpr int kGvChanPerLane = 16;
 constexpr int kGvChannels = 32 * kGvChanPerLane;  // 512 per CTA
 constexpr int kGvWarpStride = 32 * 17;            // reduction row per warp, padded (bank-conflict free)
@@ -805,11 +818,28 @@ struct GvArgs {
   int rows_per_slice;  // stored rows per CTA (a multiple of 4 x warps)
 };
 
-// 4 bytes (b ^ 0x80 for int8, q + 8 for int4 nibbles) -> 4 exact fp32 values
-// offset by `bias` (2^23 + 128 or 2^23 + 8).
-__device__ __forceinline__ void bytes_to_f32(uint32_t t, float bias, float* f) {
-#pragma unroll
-  for (int j = 0; j < 4; ++j) f[j] = __int_as_float(__byte_perm(t, 0x4B000000u, 0x7440u + j)) - bias;
+__device__ __forceinline__ uint32_t hsub2_bits(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ uint32_t hfma2_bits(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+// acc + x * (low or high fp16 half of w2), product exact, one fp32 rounding.
+__device__ __forceinline__ float fma_h_lo(uint16_t x, uint32_t w2, float acc) {
+  float d;
+  asm("{\n\t.reg .b16 l, h;\n\tmov.b32 {l, h}, %2;\n\tfma.rn.f32.f16 %0, %1, l, %3;\n\t}"
+      : "=f"(d) : "h"(x), "r"(w2), "f"(acc));
+  return d;
+}
+__device__ __forceinline__ float fma_h_hi(uint16_t x, uint32_t w2, float acc) {
+  float d;
+  asm("{\n\t.reg .b16 l, h;\n\tmov.b32 {l, h}, %2;\n\tfma.rn.f32.f16 %0, %1, h, %3;\n\t}"
+      : "=f"(d) : "h"(x), "r"(w2), "f"(acc));
+  return d;
 }
 
 template <int kQ, int kM>
@@ -819,7 +849,7 @@ __global__ void __launch_bounds__(GvCfg<kQ, kM>::kThreads, GvCfg<kQ, kM>::kCtasP
   constexpr int NW = Cfg::kWarps;
   constexpr int U = 4;                      // stored rows per batch; two batches in flight per lane
   constexpr int KPR = kQ == kInt8 ? 1 : 2;  // k per stored row
-  extern __shared__ float gsm[];  // the slice of X as fp32, later [NW][kGvWarpStride] partial sums
+  extern __shared__ float gsm[];  // the slice of X as fp16, later [NW][kGvWarpStride] partial sums
   __shared__ int is_last;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -834,12 +864,19 @@ __global__ void __launch_bounds__(GvCfg<kQ, kM>::kThreads, GvCfg<kQ, kM>::kCtasP
   const int wr0 = r0 + warp * per_warp;
   const int wr1 = min(wr0 + per_warp, r1);
 
-  // The slice of X (k in [KPR r0, KPR r1)) as fp32 in shared memory.
-  float* xs = gsm;  // [kM][KPR * rows_per_slice]
+  // Launched with programmatic serialization: the next kernel's CTAs may take
+  // SM slots as this grid's CTAs exit; nothing global is touched before the
+  // previous kernel on the stream has completed.
+  pdl_launch_dependents();
+  pdl_wait();
+
+  // The slice of X (k in [KPR r0, KPR r1)) as fp16 bits in shared memory.
+  uint16_t* xs = reinterpret_cast<uint16_t*>(gsm);  // [kM][KPR * rows_per_slice]
   const int kspan = KPR * a.rows_per_slice;
+  const uint16_t* xg = reinterpret_cast<const uint16_t*>(a.X);
   for (int i = threadIdx.x; i < kM * kspan; i += Cfg::kThreads) {
     const int m = i / kspan, k = KPR * r0 + (i % kspan);
-    xs[i] = (m < a.M && k < KPR * r1) ? __half2float(a.X[static_cast<int64_t>(m) * a.ldx + k]) : 0.f;
+    xs[i] = (m < a.M && k < KPR * r1) ? xg[static_cast<int64_t>(m) * a.ldx + k] : uint16_t(0);
   }
   __syncthreads();
 
@@ -869,36 +906,47 @@ __global__ void __launch_bounds__(GvCfg<kQ, kM>::kThreads, GvCfg<kQ, kM>::kCtasP
         const int kl = KPR * (r + u - r0);  // k index within the slice
         const uint32_t words[4] = {cur[u].x, cur[u].y, cur[u].z, cur[u].w};
         if (kQ == kInt8) {
-          float xv[kM];
+          uint16_t xv[kM];
 #pragma unroll
-          for (int m = 0; m < kM; ++m) xv[m] = row_ok ? xs[m * kspan + kl] : 0.f;
+          for (int m = 0; m < kM; ++m) xv[m] = row_ok ? xs[m * kspan + kl] : uint16_t(0);
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
-            float f[4];
-            bytes_to_f32(words[q] ^ 0x80808080u, 8388736.f, f);
+            const uint32_t t = words[q] ^ 0x80808080u;
+            const uint32_t w01 = hsub2_bits(__byte_perm(t, 0x64646464u, 0x4140u), 0x64806480u);  // channels 4q, 4q+1
+            const uint32_t w23 = hsub2_bits(__byte_perm(t, 0x64646464u, 0x4342u), 0x64806480u);  // 4q+2, 4q+3
 #pragma unroll
-            for (int j = 0; j < 4; ++j)
-#pragma unroll
-              for (int m = 0; m < kM; ++m) acc[m][4 * q + j] = fmaf(xv[m], f[j], acc[m][4 * q + j]);
+            for (int m = 0; m < kM; ++m) {
+              acc[m][4 * q + 0] = fma_h_lo(xv[m], w01, acc[m][4 * q + 0]);
+              acc[m][4 * q + 1] = fma_h_hi(xv[m], w01, acc[m][4 * q + 1]);
+              acc[m][4 * q + 2] = fma_h_lo(xv[m], w23, acc[m][4 * q + 2]);
+              acc[m][4 * q + 3] = fma_h_hi(xv[m], w23, acc[m][4 * q + 3]);
+            }
           }
         } else {
           // stored row r holds k = 2r (low nibbles) and k = 2r + 1 (high nibbles)
-          float x0[kM], x1[kM];
+          uint16_t x0[kM], x1[kM];
 #pragma unroll
           for (int m = 0; m < kM; ++m) {
-            x0[m] = row_ok ? xs[m * kspan + kl] : 0.f;
-            x1[m] = row_ok ? xs[m * kspan + kl + 1] : 0.f;
+            x0[m] = row_ok ? xs[m * kspan + kl] : uint16_t(0);
+            x1[m] = row_ok ? xs[m * kspan + kl + 1] : uint16_t(0);
           }
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
-            float lo[4], hi[4];
-            bytes_to_f32((words[q] & 0x0F0F0F0Fu) ^ 0x08080808u, 8388616.f, lo);
-            bytes_to_f32(((words[q] >> 4) & 0x0F0F0F0Fu) ^ 0x08080808u, 8388616.f, hi);
+            // byte j = channel 4q + j; masks pick channels (4q, 4q+2), then
+            // (4q+1, 4q+3) after an 8-bit shift.
+            const uint32_t t = words[q] ^ 0x88888888u;  // every nibble q -> q + 8
+            const uint32_t u = t >> 8;
+            const uint32_t lo02 = hsub2_bits((t & 0x000F000Fu) | 0x64006400u, 0x64086408u);
+            const uint32_t lo13 = hsub2_bits((u & 0x000F000Fu) | 0x64006400u, 0x64086408u);
+            const uint32_t hi02 = hfma2_bits((t & 0x00F000F0u) | 0x64006400u, 0x2C002C00u, 0xD480D480u);
+            const uint32_t hi13 = hfma2_bits((u & 0x00F000F0u) | 0x64006400u, 0x2C002C00u, 0xD480D480u);
 #pragma unroll
-            for (int j = 0; j < 4; ++j)
-#pragma unroll
-              for (int m = 0; m < kM; ++m)
-                acc[m][4 * q + j] = fmaf(x1[m], hi[j], fmaf(x0[m], lo[j], acc[m][4 * q + j]));
+            for (int m = 0; m < kM; ++m) {
+              acc[m][4 * q + 0] = fma_h_lo(x1[m], hi02, fma_h_lo(x0[m], lo02, acc[m][4 * q + 0]));
+              acc[m][4 * q + 1] = fma_h_lo(x1[m], hi13, fma_h_lo(x0[m], lo13, acc[m][4 * q + 1]));
+              acc[m][4 * q + 2] = fma_h_hi(x1[m], hi02, fma_h_hi(x0[m], lo02, acc[m][4 * q + 2]));
+              acc[m][4 * q + 3] = fma_h_hi(x1[m], hi13, fma_h_hi(x0[m], lo13, acc[m][4 * q + 3]));
+            }
           }
         }
       }
@@ -961,27 +1009,32 @@ __global__ void __launch_bounds__(GvCfg<kQ, kM>::kThreads, GvCfg<kQ, kM>::kCtasP
   }
   if (single) return;
 
-  // The last CTA of this channel block adds the slices in order.
-  __threadfence();
+  // The last CTA of this channel block adds the slices in order. The CTA's
+  // partial stores are ordered before the ticket by the barrier and the
+  // ticket's release; its acquire orders the last CTA's loads after every
+  // other CTA's release.
   __syncthreads();
-  if (threadIdx.x == 0) is_last = atomicAdd(&a.counters[cb], 1) == slices - 1;
+  if (threadIdx.x == 0) {
+    int prev;
+    asm volatile("atom.add.acq_rel.gpu.global.s32 %0, [%1], 1;" : "=r"(prev) : "l"(a.counters + cb) : "memory");
+    is_last = prev == slices - 1;
+  }
   __syncthreads();
   if (!is_last) return;
-  __threadfence();
   for (int o = threadIdx.x; o < a.M * kGvChannels; o += Cfg::kThreads) {
     const int m = o / kGvChannels;
     const int n = cb * kGvChannels + (o % kGvChannels);
     if (n >= a.N) continue;
-    // Eight slices' loads in flight at a time, summed in slice order.
+    // Sixteen slices' loads in flight at a time, summed in slice order.
     const float* src = a.partial + static_cast<int64_t>(m) * a.N + n;
     const int64_t step = static_cast<int64_t>(a.M) * a.N;
     float s = 0.f;
-    for (int k = 0; k < slices; k += 8) {
-      float v[8];
+    for (int k = 0; k < slices; k += 16) {
+      float v[16];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) v[i] = (k + i < slices) ? __ldcg(src + (k + i) * step) : 0.f;
+      for (int i = 0; i < 16; ++i) v[i] = (k + i < slices) ? __ldcg(src + (k + i) * step) : 0.f;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) s += v[i];
+      for (int i = 0; i < 16; ++i) s += v[i];
     }
     if (kQ == kInt8 && a.scale != nullptr) {
       s *= __half2float(a.scale[n]);
@@ -1050,8 +1103,7 @@ int launch_gemv(const QProblem& p, cudaStream_t stream) {
     if (rc != NESO_OK) return rc;
     a.counters = ctr + kGemvCounterBase;
   }
-  kern<<<dim3(nblk, slices, 1), Cfg::kThreads, Cfg::kSmemBytes, stream>>>(a);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_pdl(kern, dim3(nblk, slices, 1), dim3(Cfg::kThreads), Cfg::kSmemBytes, stream, a);
   if (e != cudaSuccess) return cuda_fail(e, "small-M GEMV launch");
   return ok();
 }

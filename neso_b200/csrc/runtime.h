@@ -68,4 +68,27 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 
 inline cudaStream_t as_stream(neso_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
 
+// Launch with programmatic stream serialization (programmatic dependent
+// launch): the kernel's CTAs may be scheduled, into SM slots the previous
+// kernel on the stream no longer uses, before that kernel has finished, so
+// its launch and prologue overlap the previous kernel's tail. The kernel must
+// call pdl_wait() before it reads or writes global memory that an earlier
+// kernel on the stream may touch; launched without the attribute, pdl_wait()
+// returns at once.
+template <class... KArgs, class... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
 }  // namespace neso
