@@ -10,21 +10,29 @@
 //
 // One persistent CTA per SM; per 64-deep K block ("stage"):
 //   warp 0      TMA: raw weight tile(s) (int8 [64 k][128 n] or packed int4
-//               [32 byte-rows][128 n], 128-byte swizzled) and (int4) the
-//               group's fp16 scale row; warp 3: TMA of the fp16 activation tile.
+//               [32 byte-rows][128 n], 128-byte swizzled) and (int4, M >= 65)
+//               the group's fp16 scale row; warp 3: TMA of the activation tile.
 //   warps 4-7,  dequantise raw -> fp16 directly into the MN-major 128-byte
 //   12-15       swizzled layout tcgen05 reads; fence.proxy.async; arrive. The
 //               two groups take alternate K blocks (or, with two channel
 //               tiles per unit, one tile each of every K block).
 //                 int8: exact, (b ^ 0x80) | 0x6400 as fp16 is 1024 + b + 128.
-//                 int4: q exact the same way, then w = q * s is split into
-//                 w_hi = fp16(q * s) and w_lo = fma(q, s, -w_hi) (the exact
-//                 rounding error), so the MMA sums q * s without rounding it.
+//                 int4, M >= 65 layout: q exact the same way, then w = q * s
+//                 is split into w_hi = fp16(q * s) and w_lo = fma(q, s, -w_hi)
+//                 (the exact rounding error), so the MMA sums q * s without
+//                 rounding it.
+//                 int4, M <= 64 layout: q only (exact in fp16); the group
+//                 scale is applied to fp32 partial sums instead (below).
 //   warp 1      tcgen05.mma issuer (kind::f16, fp32 accumulators in TMEM);
-//               int4 issues hi and lo MMAs per K step.
+//               int4 M >= 65 issues hi and lo MMAs per K step; int4 M <= 64
+//               accumulates each run of K blocks inside one 128-wide scale
+//               group into its own buffer (double-buffered), so the epilogue
+//               applies that group's scales while the next run accumulates.
+//   warp 2      (int4, M <= 64) TMA producer of each run's scale row.
 //   warps 8-11  epilogue: TMEM -> registers -> (int8: * f32(scale[n])) ->
 //               swizzled staging -> TMA stores of Y (M >= 65 layout), or
-//               direct coalesced stores (M <= 64 layout).
+//               direct coalesced stores (M <= 64 layout). int4 M <= 64: the
+//               running sums stay in registers, += partial * scale[g][n].
 // Orientation: M >= 65 computes Y units of 128 or 256 rows x 128 or 256
 // channels (a host cost model picks the shape and any K split) with X as the
 // A operand; M <= 64 swaps operands (A = dequantised W^T with M' = 128 output
@@ -54,15 +62,21 @@ struct QCfg {
   // accumulator buffer).
   // Three decoupled rings so weight bytes stay in flight independently of
   // the dequant and MMA rate:
-  //   R  raw weight tiles (int8 [64 k][128 n] or packed int4 [32][128] plus
-  //      the group's 128 fp16 scales), deep: TMA -> convert warps;
+  //   R  raw weight tiles (int8 [64 k][128 n] or packed int4 [32][128] plus,
+  //      M >= 65, the group's 128 fp16 scales), deep: TMA -> convert warps;
   //   X  activation tiles [kNX rows][64 k] fp16: TMA -> MMA;
-  //   F  dequantised fp16 weight tiles (int4: hi and lo copies): convert -> MMA.
-  static constexpr int kRawTileBytes = (kQ == kInt8) ? 64 * 128 : 32 * 128 + 1024;
+  //   F  dequantised fp16 weight tiles (int4 M >= 65: hi and lo copies):
+  //      convert -> MMA.
+  // int4 M <= 64 (kGS, group-scaled partial sums) adds a ring of scale rows
+  // (one 128-channel row per tile and group run): TMA -> epilogue.
+  static constexpr bool kGS = kQ == kInt4G128 && kSwap;
+  static constexpr int kRawTileBytes = (kQ == kInt8) ? 64 * 128 : kGS ? 32 * 128 : 32 * 128 + 1024;
   static constexpr int kRawBytes = kNT * kRawTileBytes;
   static constexpr int kXBytes = kNX * kBK * 2;
   static constexpr int kW16Bytes = kBK * kTileN * 2;            // 16 KB per fp16 copy
-  static constexpr int kNumW16 = (kQ == kInt8) ? 1 : 2;
+  static constexpr int kNumW16 = (kQ == kInt4G128 && !kGS) ? 2 : 1;
+  static constexpr int kScSlots = kGS ? 16 : 0;
+  static constexpr int kScBytes = kNT * 256;
   static constexpr int kFTileBytes = kNumW16 * kW16Bytes;
   static constexpr int kFBytes = kNT * kFTileBytes;
   // kNX = 256 in the M >= 65 layout: 256-row units, two 128-row accumulators
@@ -78,16 +92,19 @@ struct QCfg {
   static constexpr int kBudget = 220 * 1024;
   // Y staging for TMA stores (M >= 65 layout): 16 rows x 32 fp32 per epilogue warp.
   static constexpr int kOutBytes = kSwap ? 0 : 4 * 2048;
-  static constexpr int kRStagesFit = (kBudget - kOutBytes - kFStages * kFBytes - kXStages * kXBytes) / kRawBytes;
+  static constexpr int kRStagesFit =
+      (kBudget - kOutBytes - kScSlots * kScBytes - kFStages * kFBytes - kXStages * kXBytes) / kRawBytes;
   static constexpr int kRStages = kRStagesFit > 16 ? 16 : kRStagesFit;
   static constexpr int kOffR = 0;
   static constexpr int kOffX = kRStages * kRawBytes;
   static constexpr int kOffF = kOffX + kXStages * kXBytes;
   static constexpr int kOffOut = kOffF + kFStages * kFBytes;
-  static constexpr int kOffBars = kOffOut + kOutBytes;
-  static constexpr int kRawTx = kNT * ((kQ == kInt8) ? 64 * 128 : 32 * 128 + 256);
+  static constexpr int kOffSc = kOffOut + kOutBytes;
+  static constexpr int kOffBars = kOffSc + kScSlots * kScBytes;
+  static constexpr int kRawTx = kNT * ((kQ == kInt8) ? 64 * 128 : kGS ? 32 * 128 : 32 * 128 + 256);
   static constexpr int kAccCols = kSwap ? kNT * kNX : kRowHalves * kNT * kTileN;  // accumulator columns per buffer
   static constexpr int kAccBufs = 2 * kAccCols <= 512 ? 2 : 1;
+  static_assert(!kGS || kAccBufs == 2, "group runs need two accumulator buffers");
   static constexpr int kTmemCols = (kAccBufs * kAccCols <= 32) ? 32 : (kAccBufs * kAccCols <= 64) ? 64
                                    : (kAccBufs * kAccCols <= 128) ? 128 : (kAccBufs * kAccCols <= 256) ? 256 : 512;
   static constexpr int kSmemBytes = kOffBars + 1024 + 1024;
@@ -123,6 +140,12 @@ __device__ __forceinline__ QUnit unit_of(int t, const QArgs& a) {
   u.kb1 = min(a.num_k, u.kb0 + a.kb_per_split);
   return u;
 }
+
+// int4: the K blocks of a unit are accumulated in runs that stay inside one
+// 128-wide scale group (two 64-deep K blocks); a unit's K range may start or
+// end inside a group (K splits), which only shortens a run.
+__device__ __forceinline__ bool run_starts(int kb, int kb0) { return kb == kb0 || (kb & 1) == 0; }
+__device__ __forceinline__ bool run_ends(int kb, int kb1) { return kb + 1 == kb1 || (kb & 1) == 1; }
 
 // fp16 pair (lo = byte b0, hi = byte b1 of x) -> 0x6400 | byte, i.e. 1024 + byte.
 __device__ __forceinline__ uint32_t bytes_to_h2(uint32_t x, uint32_t sel) {
@@ -166,9 +189,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* f_full = x_empty + XS;      // [FS] fp16 weights written (4 convert warps)
   uint64_t* f_empty = f_full + FS;      // [FS] MMAs done with them
   uint64_t* acc_full = f_empty + FS;    // [2]
-  uint64_t* acc_empty = acc_full + 2;   // [2] (4 epilogue warps)
+  uint64_t* acc_empty = acc_full + 2;   // [2] (the epilogue warps)
   uint64_t* mma_done = acc_empty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  uint64_t* sc_full = mma_done + 1;           // [kScSlots] int4 scale rows landed
+  uint64_t* sc_empty = sc_full + Cfg::kScSlots;  // [kScSlots] epilogue done with them
+  uint8_t* sSc = smem + Cfg::kOffSc;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sc_empty + Cfg::kScSlots);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* never_flag = abort_flag + 1;  // stays 0: drain waits ignore the abort
 
@@ -194,6 +220,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&acc_empty[b], 4);
     }
     mbar_init(mma_done, 1);
+    for (int i = 0; i < Cfg::kScSlots; ++i) {
+      mbar_init(&sc_full[i], 1);
+      mbar_init(&sc_empty[i], 4);
+    }
     *abort_flag = 0;
     *never_flag = 0;
     fence_mbar_init();
@@ -244,7 +274,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               tma_load_2d(sg, &tmW, &full[s], n0, kb * kBK);
             } else {
               tma_load_2d(sg, &tmW, &full[s], n0, kb * (kBK / 2));
-              tma_load_2d(sg + 4096, &tmS, &full[s], n0, (kb * kBK) / 128);
+              if (!Cfg::kGS) tma_load_2d(sg + 4096, &tmS, &full[s], n0, (kb * kBK) / 128);
             }
           }
         } else {
@@ -263,55 +293,148 @@ __global__ void __launch_bounds__(kThreads, 1)
     // normal: A = X [128 m x 64 k] K-major, B = W16 [64 k x 128 n] MN-major
     // swap:   A = W16 as [128 n x 64 k] MN-major, B = X [kNX m x 64 k] K-major
     constexpr uint32_t idesc = kSwap ? idesc_f16_f32(128, kNX, 1, 0) : idesc_f16_f32(128, kUnitN, 0, 1);
-    int it = 0, tc = 0;
-    bool aborted = false;
-    for (int t = blockIdx.x; t < num_units && !aborted; t += gridDim.x, ++tc) {
-      const QUnit u = unit_of(t, args);
-      const int buf = tc % Cfg::kAccBufs;
-      const uint32_t use = tc / Cfg::kAccBufs;
-      if (!mbar_wait(&acc_empty[buf], (use & 1) ^ 1, abort_flag, args.st, 0x2200)) break;
-      tc_fence_after();
-      const uint32_t d_tmem = tmem + buf * Cfg::kAccCols;
-      for (int kb = u.kb0; kb < u.kb1; ++kb, ++it) {
-        const int fs = it % FS, xs = it % XS;
-        if (!mbar_wait(&f_full[fs], (it / FS) & 1, abort_flag, args.st, 0x2201) ||
-            !mbar_wait(&x_full[xs], (it / XS) & 1, abort_flag, args.st, 0x2202)) {
-          aborted = true;
-          break;
-        }
-        tc_fence_after();
-        const uint64_t xd0 = sdesc_sw128(smem_u32(sX + xs * Cfg::kXBytes), 16, 1024);
-        // F stage = [fp16 copy p][channel tile g][64 k][128 n]: with kNT = 2
-        // one N = 256 instruction covers both tiles (64-channel chunks 8 KB
-        // apart throughout).
-        const uint64_t wd0 = sdesc_sw128(smem_u32(sF + fs * Cfg::kFBytes), 8192, 1024);
+    // The issuer's per-stage work bounds the small-M rate: the whole-unit
+    // form below keeps its loop minimal; group runs (kGS) add a buffer
+    // switch per run.
+    if constexpr (Cfg::kGS) {
+      int it = 0;
+      int tc = 0;  // accumulator runs: one per group run
+      bool aborted = false;
+      for (int t = blockIdx.x; t < num_units && !aborted; t += gridDim.x) {
+        const QUnit u = unit_of(t, args);
+        int buf = 0;
+        uint32_t d_tmem = tmem;
+        for (int kb = u.kb0; kb < u.kb1; ++kb, ++it) {
+          const bool first = run_starts(kb, u.kb0);
+          if (first) {
+            buf = tc % Cfg::kAccBufs;
+            const uint32_t use = tc / Cfg::kAccBufs;
+            if (!mbar_wait(&acc_empty[buf], (use & 1) ^ 1, abort_flag, args.st, 0x2200)) {
+              aborted = true;
+              break;
+            }
+            tc_fence_after();
+            d_tmem = tmem + buf * Cfg::kAccCols;
+          }
+          const int fs = it % FS, xs = it % XS;
+          if (!mbar_wait(&f_full[fs], (it / FS) & 1, abort_flag, args.st, 0x2201) ||
+              !mbar_wait(&x_full[xs], (it / XS) & 1, abort_flag, args.st, 0x2202)) {
+            aborted = true;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t xd0 = sdesc_sw128(smem_u32(sX + xs * Cfg::kXBytes), 16, 1024);
+          // F stage = [fp16 copy p][channel tile g][64 k][128 n]: with kNT = 2
+          // one N = 256 instruction covers both tiles (64-channel chunks 8 KB
+          // apart throughout).
+          const uint64_t wd0 = sdesc_sw128(smem_u32(sF + fs * Cfg::kFBytes), 8192, 1024);
 #pragma unroll
-        for (int k = 0; k < kBK / 16; ++k) {
-          const uint64_t xd = xd0 + static_cast<uint64_t>((k * 32) >> 4);
+          for (int k = 0; k < kBK / 16; ++k) {
+            const uint64_t xd = xd0 + static_cast<uint64_t>((k * 32) >> 4);
 #pragma unroll
-          for (int p = 0; p < Cfg::kNumW16; ++p) {
-            const uint64_t wd = wd0 + static_cast<uint64_t>((p * kNT * Cfg::kW16Bytes + k * 2048) >> 4);
-            const uint32_t acc = (kb != u.kb0 || k != 0 || p != 0) ? 1u : 0u;
-            if (kSwap) {
+            for (int p = 0; p < Cfg::kNumW16; ++p) {
+              const uint64_t wd = wd0 + static_cast<uint64_t>((p * kNT * Cfg::kW16Bytes + k * 2048) >> 4);
+              const uint32_t acc = (!first || k != 0 || p != 0) ? 1u : 0u;
+              if (kSwap) {
 #pragma unroll
-              for (int g = 0; g < kNT; ++g) {
-                umma_f16_ss(d_tmem + g * kNX, wd + static_cast<uint64_t>((g * Cfg::kW16Bytes) >> 4), xd, idesc, acc);
-              }
-            } else {
+                for (int g = 0; g < kNT; ++g) {
+                  umma_f16_ss(d_tmem + g * kNX, wd + static_cast<uint64_t>((g * Cfg::kW16Bytes) >> 4), xd, idesc, acc);
+                }
+              } else {
 #pragma unroll
-              for (int h = 0; h < Cfg::kRowHalves; ++h) {
-                umma_f16_ss(d_tmem + h * kUnitN, xd + static_cast<uint64_t>((h * 16384) >> 4), wd, idesc, acc);
+                for (int h = 0; h < Cfg::kRowHalves; ++h) {
+                  umma_f16_ss(d_tmem + h * kUnitN, xd + static_cast<uint64_t>((h * 16384) >> 4), wd, idesc, acc);
+                }
               }
             }
           }
+          umma_commit(&f_empty[fs]);
+          if (!kSwap) umma_commit(&x_empty[xs]);
+          if (run_ends(kb, u.kb1)) {
+            umma_commit(&acc_full[buf]);
+            ++tc;
+          }
         }
-        umma_commit(&f_empty[fs]);
-        if (!kSwap) umma_commit(&x_empty[xs]);
       }
-      if (!aborted) umma_commit(&acc_full[buf]);
+    } else {
+      int it = 0, tc = 0;
+      bool aborted = false;
+      for (int t = blockIdx.x; t < num_units && !aborted; t += gridDim.x, ++tc) {
+        const QUnit u = unit_of(t, args);
+        const int buf = tc % Cfg::kAccBufs;
+        const uint32_t use = tc / Cfg::kAccBufs;
+        if (!mbar_wait(&acc_empty[buf], (use & 1) ^ 1, abort_flag, args.st, 0x2200)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem + buf * Cfg::kAccCols;
+        for (int kb = u.kb0; kb < u.kb1; ++kb, ++it) {
+          const int fs = it % FS, xs = it % XS;
+          if (!mbar_wait(&f_full[fs], (it / FS) & 1, abort_flag, args.st, 0x2201) ||
+              !mbar_wait(&x_full[xs], (it / XS) & 1, abort_flag, args.st, 0x2202)) {
+            aborted = true;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t xd0 = sdesc_sw128(smem_u32(sX + xs * Cfg::kXBytes), 16, 1024);
+          // F stage = [fp16 copy p][channel tile g][64 k][128 n]: with kNT = 2
+          // one N = 256 instruction covers both tiles (64-channel chunks 8 KB
+          // apart throughout).
+          const uint64_t wd0 = sdesc_sw128(smem_u32(sF + fs * Cfg::kFBytes), 8192, 1024);
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k) {
+            const uint64_t xd = xd0 + static_cast<uint64_t>((k * 32) >> 4);
+#pragma unroll
+            for (int p = 0; p < Cfg::kNumW16; ++p) {
+              const uint64_t wd = wd0 + static_cast<uint64_t>((p * kNT * Cfg::kW16Bytes + k * 2048) >> 4);
+              const uint32_t acc = (kb != u.kb0 || k != 0 || p != 0) ? 1u : 0u;
+              if (kSwap) {
+#pragma unroll
+                for (int g = 0; g < kNT; ++g) {
+                  umma_f16_ss(d_tmem + g * kNX, wd + static_cast<uint64_t>((g * Cfg::kW16Bytes) >> 4), xd, idesc, acc);
+                }
+              } else {
+#pragma unroll
+                for (int h = 0; h < Cfg::kRowHalves; ++h) {
+                  umma_f16_ss(d_tmem + h * kUnitN, xd + static_cast<uint64_t>((h * 16384) >> 4), wd, idesc, acc);
+                }
+              }
+            }
+          }
+          umma_commit(&f_empty[fs]);
+          if (!kSwap) umma_commit(&x_empty[xs]);
+        }
+        if (!aborted) umma_commit(&acc_full[buf]);
+      }
     }
     umma_commit(mma_done);
     mbar_wait(mma_done, 0, never_flag, quiet, 0);
+  } else if (Cfg::kGS && warp == 2 && lane == 0) {
+    // ------------------------------------------------ scale rows (int4 TMA) --
+    // One row of 128 fp16 scales per weight tile and group run, into a ring
+    // the epilogue warps release.
+    constexpr int SS = Cfg::kScSlots;
+    int si = 0;
+    bool aborted = false;
+    for (int t = blockIdx.x; t < num_units && !aborted; t += gridDim.x) {
+      const QUnit u = unit_of(t, args);
+      for (int kb = u.kb0; kb < u.kb1; ++kb) {
+        if (!run_starts(kb, u.kb0)) continue;
+        const int slot = si % SS;
+        if (!mbar_wait(&sc_empty[slot], ((si / SS) & 1) ^ 1, abort_flag, args.st, 0x2102)) {
+          aborted = true;
+          break;
+        }
+        mbar_arrive_expect_tx(&sc_full[slot], Cfg::kScBytes);
+#pragma unroll
+        for (int g = 0; g < kNT; ++g) {
+          tma_load_2d(sSc + slot * Cfg::kScBytes + g * 256, &tmS, &sc_full[slot], u.nb * kUnitN + g * kTileN,
+                      (kb * kBK) / 128);
+        }
+        ++si;
+      }
+    }
+    if (aborted) {
+      for (int i = (si > SS ? si - SS : 0); i < si; ++i) mbar_wait(&sc_full[i % SS], (i / SS) & 1, never_flag, quiet, 0);
+    }
   } else if ((warp >= 4 && warp < 8) || warp >= 12) {
     // ------------------------------------------------------------- convert --
     // Two convert groups (warps 4-7 and 12-15) take alternate K blocks, so
@@ -354,57 +477,102 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int i = 0; i < 8; ++i) *reinterpret_cast<uint4*>(dst + ((i ^ sw) << 4)) = o[i];
         } else {
-          // thread -> (byte row kk: k rows 2kk and 2kk+1, n quarter qn: 32 channels)
-          const int kk = ct >> 2;
-          const int qn = ct & 3;
-          const int swr = kk & 7;
-          const __half* sc = reinterpret_cast<const __half*>(raw + 4096) + qn * 32;
-          const __half2 b8 = __float2half2_rn(1032.f);  // 1024 + 8
-          uint32_t hv[2][2][8], lv[2][2][8];  // [raw unit i][row r0/r1][16 channels as 8 half2]
+          if constexpr (Cfg::kGS) {
+            // thread -> (byte row kk: k rows 2kk and 2kk+1, n quarter qn: 32 channels)
+            const int kk = ct >> 2;
+            const int qn = ct & 3;
+            const int swr = kk & 7;
+            const __half2 b8 = __float2half2_rn(1032.f);  // 1024 + 8
+            uint32_t hv[2][2][8];  // [raw unit i][row r0/r1][16 channels as 8 half2]
 #pragma unroll
-          for (int i = 0; i < 2; ++i) {
-            const uint4 rv = *reinterpret_cast<const uint4*>(raw + kk * 128 + (((2 * qn + i) ^ swr) << 4));
-            const uint32_t words[4] = {rv.x, rv.y, rv.z, rv.w};
+            for (int i = 0; i < 2; ++i) {
+              const uint4 rv = *reinterpret_cast<const uint4*>(raw + kk * 128 + (((2 * qn + i) ^ swr) << 4));
+              const uint32_t words[4] = {rv.x, rv.y, rv.z, rv.w};
 #pragma unroll
-            for (int wdx = 0; wdx < 4; ++wdx) {
-              const uint32_t lo_n = (words[wdx] & 0x0F0F0F0Fu) ^ 0x08080808u;         // k even
-              const uint32_t hi_n = ((words[wdx] >> 4) & 0x0F0F0F0Fu) ^ 0x08080808u;  // k odd
+              for (int wdx = 0; wdx < 4; ++wdx) {
+                const uint32_t lo_n = (words[wdx] & 0x0F0F0F0Fu) ^ 0x08080808u;         // k even
+                const uint32_t hi_n = ((words[wdx] >> 4) & 0x0F0F0F0Fu) ^ 0x08080808u;  // k odd
 #pragma unroll
-              for (int half_sel = 0; half_sel < 2; ++half_sel) {
-                const uint32_t sel = half_sel ? 0x7362u : 0x5140u;
-                const __half2 s2 = *reinterpret_cast<const __half2*>(sc + 16 * i + 4 * wdx + 2 * half_sel);
-                const __half2 q0 = __hsub2(u32_as_h2(bytes_to_h2(lo_n, sel)), b8);
-                const __half2 q1 = __hsub2(u32_as_h2(bytes_to_h2(hi_n, sel)), b8);
-                const __half2 w0h = __hmul2(q0, s2);
-                const __half2 w1h = __hmul2(q1, s2);
-                hv[i][0][wdx * 2 + half_sel] = h2_as_u32(w0h);
-                lv[i][0][wdx * 2 + half_sel] = h2_as_u32(__hfma2(q0, s2, __hneg2(w0h)));
-                hv[i][1][wdx * 2 + half_sel] = h2_as_u32(w1h);
-                lv[i][1][wdx * 2 + half_sel] = h2_as_u32(__hfma2(q1, s2, __hneg2(w1h)));
+                for (int half_sel = 0; half_sel < 2; ++half_sel) {
+                  const uint32_t sel = half_sel ? 0x7362u : 0x5140u;
+                  hv[i][0][wdx * 2 + half_sel] = h2_as_u32(__hsub2(u32_as_h2(bytes_to_h2(lo_n, sel)), b8));
+                  hv[i][1][wdx * 2 + half_sel] = h2_as_u32(__hsub2(u32_as_h2(bytes_to_h2(hi_n, sel)), b8));
+                }
               }
             }
-          }
-          // Release the raw slot only after its bytes are consumed (see int8).
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&r_empty[rs]);
-          if (!mbar_wait(&f_empty[fs], ((it / FS) & 1) ^ 1, abort_flag, args.st, 0x2301)) { ok_run = false; break; }
-          uint8_t* hi = w16;
-          uint8_t* lo = w16 + kNT * Cfg::kW16Bytes;
-          const int chunk = qn >> 1;
+            // Release the raw slot only after its bytes are consumed (see int8).
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&r_empty[rs]);
+            if (!mbar_wait(&f_empty[fs], ((it / FS) & 1) ^ 1, abort_flag, args.st, 0x2301)) { ok_run = false; break; }
+            const int chunk = qn >> 1;
 #pragma unroll
-          for (int i = 0; i < 2; ++i) {
-            // 16 channels = two fp16 units; column within the chunk = 32 (qn & 1) + 16 i
-            const int v0 = 4 * (qn & 1) + 2 * i;
+            for (int i = 0; i < 2; ++i) {
+              // 16 channels = two fp16 units; column within the chunk = 32 (qn & 1) + 16 i
+              const int v0 = 4 * (qn & 1) + 2 * i;
 #pragma unroll
-            for (int rr = 0; rr < 2; ++rr) {
-              const int row = 2 * kk + rr;
+              for (int rr = 0; rr < 2; ++rr) {
+                const int row = 2 * kk + rr;
 #pragma unroll
-              for (int e = 0; e < 2; ++e) {
-                const int off = chunk * 8192 + row * 128 + (((v0 + e) ^ (row & 7)) << 4);
-                *reinterpret_cast<uint4*>(hi + off) = make_uint4(hv[i][rr][4 * e], hv[i][rr][4 * e + 1],
-                                                                 hv[i][rr][4 * e + 2], hv[i][rr][4 * e + 3]);
-                *reinterpret_cast<uint4*>(lo + off) = make_uint4(lv[i][rr][4 * e], lv[i][rr][4 * e + 1],
-                                                                 lv[i][rr][4 * e + 2], lv[i][rr][4 * e + 3]);
+                for (int e = 0; e < 2; ++e) {
+                  const int off = chunk * 8192 + row * 128 + (((v0 + e) ^ (row & 7)) << 4);
+                  *reinterpret_cast<uint4*>(w16 + off) = make_uint4(hv[i][rr][4 * e], hv[i][rr][4 * e + 1],
+                                                                    hv[i][rr][4 * e + 2], hv[i][rr][4 * e + 3]);
+                }
+              }
+            }
+          } else {
+            // thread -> (byte row kk: k rows 2kk and 2kk+1, n quarter qn: 32 channels)
+            const int kk = ct >> 2;
+            const int qn = ct & 3;
+            const int swr = kk & 7;
+            const __half* sc = reinterpret_cast<const __half*>(raw + 4096) + qn * 32;
+            const __half2 b8 = __float2half2_rn(1032.f);  // 1024 + 8
+            uint32_t hv[2][2][8], lv[2][2][8];  // [raw unit i][row r0/r1][16 channels as 8 half2]
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+              const uint4 rv = *reinterpret_cast<const uint4*>(raw + kk * 128 + (((2 * qn + i) ^ swr) << 4));
+              const uint32_t words[4] = {rv.x, rv.y, rv.z, rv.w};
+#pragma unroll
+              for (int wdx = 0; wdx < 4; ++wdx) {
+                const uint32_t lo_n = (words[wdx] & 0x0F0F0F0Fu) ^ 0x08080808u;         // k even
+                const uint32_t hi_n = ((words[wdx] >> 4) & 0x0F0F0F0Fu) ^ 0x08080808u;  // k odd
+#pragma unroll
+                for (int half_sel = 0; half_sel < 2; ++half_sel) {
+                  const uint32_t sel = half_sel ? 0x7362u : 0x5140u;
+                  const __half2 s2 = *reinterpret_cast<const __half2*>(sc + 16 * i + 4 * wdx + 2 * half_sel);
+                  const __half2 q0 = __hsub2(u32_as_h2(bytes_to_h2(lo_n, sel)), b8);
+                  const __half2 q1 = __hsub2(u32_as_h2(bytes_to_h2(hi_n, sel)), b8);
+                  const __half2 w0h = __hmul2(q0, s2);
+                  const __half2 w1h = __hmul2(q1, s2);
+                  hv[i][0][wdx * 2 + half_sel] = h2_as_u32(w0h);
+                  lv[i][0][wdx * 2 + half_sel] = h2_as_u32(__hfma2(q0, s2, __hneg2(w0h)));
+                  hv[i][1][wdx * 2 + half_sel] = h2_as_u32(w1h);
+                  lv[i][1][wdx * 2 + half_sel] = h2_as_u32(__hfma2(q1, s2, __hneg2(w1h)));
+                }
+              }
+            }
+            // Release the raw slot only after its bytes are consumed (see int8).
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&r_empty[rs]);
+            if (!mbar_wait(&f_empty[fs], ((it / FS) & 1) ^ 1, abort_flag, args.st, 0x2301)) { ok_run = false; break; }
+            uint8_t* hi = w16;
+            uint8_t* lo = w16 + kNT * Cfg::kW16Bytes;
+            const int chunk = qn >> 1;
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+              // 16 channels = two fp16 units; column within the chunk = 32 (qn & 1) + 16 i
+              const int v0 = 4 * (qn & 1) + 2 * i;
+#pragma unroll
+              for (int rr = 0; rr < 2; ++rr) {
+                const int row = 2 * kk + rr;
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                  const int off = chunk * 8192 + row * 128 + (((v0 + e) ^ (row & 7)) << 4);
+                  *reinterpret_cast<uint4*>(hi + off) = make_uint4(hv[i][rr][4 * e], hv[i][rr][4 * e + 1],
+                                                                   hv[i][rr][4 * e + 2], hv[i][rr][4 * e + 3]);
+                  *reinterpret_cast<uint4*>(lo + off) = make_uint4(lv[i][rr][4 * e], lv[i][rr][4 * e + 1],
+                                                                   lv[i][rr][4 * e + 2], lv[i][rr][4 * e + 3]);
+                }
               }
             }
           }
@@ -419,6 +587,77 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t q = warp & 3;
     const int lrow = q * 32 + lane;  // TMEM lane: m (normal) or n (swap)
     const uint32_t lane_base = tmem + ((q * 32) << 16);
+    if constexpr (Cfg::kGS) {
+      // Running sums in registers: += group-run partial * fp32(scale[g][n]);
+      // lane = channel, kNT tiles x kNX rows of X.
+      constexpr int SS = Cfg::kScSlots;
+      constexpr int NC = kNT * kNX;
+      int tc = 0, si = 0;
+      bool ok_run = true;
+      for (int t = blockIdx.x; t < num_units && ok_run; t += gridDim.x) {
+        const QUnit u = unit_of(t, args);
+        float accv[NC];
+#pragma unroll
+        for (int i = 0; i < NC; ++i) accv[i] = 0.f;
+        for (int kb = u.kb0; kb < u.kb1; ++kb) {
+          if (!run_ends(kb, u.kb1)) continue;
+          const int buf = tc & 1;
+          const int slot = si % SS;
+          const bool got = mbar_wait(&acc_full[buf], (tc >> 1) & 1, abort_flag, args.st, 0x2400) &&
+                           mbar_wait(&sc_full[slot], (si / SS) & 1, abort_flag, args.st, 0x2401);
+          if (!__all_sync(0xffffffffu, got)) {
+            ok_run = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t acc = lane_base + buf * Cfg::kAccCols;
+          const __half* scr = reinterpret_cast<const __half*>(sSc + slot * Cfg::kScBytes);
+#pragma unroll
+          for (int g = 0; g < kNT; ++g) {
+            const float sc = __half2float(scr[g * kTileN + lrow]);
+#pragma unroll
+            for (int c = 0; c < (kNX + 31) / 32; ++c) {
+              uint32_t r[32];
+              if constexpr (kNX >= 32) {
+                tmem_ld32(acc + g * kNX + c * 32, r);
+              } else {
+                uint32_t r16[16];
+                tmem_ld16(acc + g * kNX, r16);
+#pragma unroll
+                for (int i = 0; i < 16; ++i) r[i] = r16[i];
+              }
+              tmem_wait_ld();
+#pragma unroll
+              for (int i = 0; i < (kNX >= 32 ? 32 : kNX); ++i) {
+                accv[g * kNX + c * 32 + i] = fmaf(__uint_as_float(r[i]), sc, accv[g * kNX + c * 32 + i]);
+              }
+            }
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) {
+            mbar_arrive(&acc_empty[buf]);
+            mbar_arrive(&sc_empty[slot]);
+          }
+          ++tc;
+          ++si;
+        }
+        if (!ok_run) break;
+        // The unit's sums -> Y, or this K split's partial sums.
+        float* ydst = args.partial != nullptr ? args.partial + static_cast<int64_t>(u.ks) * args.M * args.N : args.Y;
+        const int64_t ld = args.partial != nullptr ? args.N : args.ldy;
+#pragma unroll
+        for (int g = 0; g < kNT; ++g) {
+          const int n = u.nb * kUnitN + g * kTileN + lrow;
+          if (n < args.N) {
+#pragma unroll
+            for (int m = 0; m < kNX; ++m) {
+              if (m < args.M) ydst[static_cast<int64_t>(m) * ld + n] = accv[g * kNX + m];
+            }
+          }
+        }
+      }
+    } else {
     int tc = 0;
     for (int t = blockIdx.x; t < num_units; t += gridDim.x, ++tc) {
       const QUnit u = unit_of(t, args);
@@ -531,6 +770,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[buf]);
+    }
     }
     if (lane == 0) bulk_wait_all();  // this warp's Y stores are complete before the CTA exits
   }
