@@ -314,6 +314,17 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
+// One lane of the (fully active) warp: the same lane on every call.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "elect.sync _|p, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
+}
+
 // Programmatic dependent launch. pdl_launch_dependents: the next kernel on the
 // stream (launched with the programmatic-serialization attribute) may now be
 // scheduled. pdl_wait: block until every prerequisite grid has completed and

@@ -288,8 +288,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_wait(&full[i % depth], (i / depth) & 1, never_flag, quiet, 0);
       }
     }
-  } else if (warp == 1 && lane == 0) {
+  } else if (warp == 1 && (kSwap || lane == 0)) {
     // ---------------------------------------------------------- MMA issuer --
+    // Swapped layout: the whole warp runs the loop (warp-uniform state stays
+    // in uniform registers, which tcgen05.mma takes its operands from) and one
+    // elected lane issues the MMAs and commits; its small N = 16..64 MMAs
+    // were issue-bound from a single lane (~90 cycles per MMA, measured; ~30
+    // this way). The M >= 65 layout keeps the single-lane loop (measured
+    // faster there: its N = 128..256 MMAs are bound by the tensor pipe).
+    const bool leader = kSwap ? elect_one() : true;
+    auto all_lanes = [](bool v) { return kSwap ? __all_sync(0xffffffffu, v) : v; };
     // normal: A = X [128 m x 64 k] K-major, B = W16 [64 k x 128 n] MN-major
     // swap:   A = W16 as [128 n x 64 k] MN-major, B = X [kNX m x 64 k] K-major
     constexpr uint32_t idesc = kSwap ? idesc_f16_f32(128, kNX, 1, 0) : idesc_f16_f32(128, kUnitN, 0, 1);
@@ -309,7 +317,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (first) {
             buf = tc % Cfg::kAccBufs;
             const uint32_t use = tc / Cfg::kAccBufs;
-            if (!mbar_wait(&acc_empty[buf], (use & 1) ^ 1, abort_flag, args.st, 0x2200)) {
+            if (!all_lanes(mbar_wait(&acc_empty[buf], (use & 1) ^ 1, abort_flag, args.st, 0x2200))) {
               aborted = true;
               break;
             }
@@ -317,8 +325,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             d_tmem = tmem + buf * Cfg::kAccCols;
           }
           const int fs = it % FS, xs = it % XS;
-          if (!mbar_wait(&f_full[fs], (it / FS) & 1, abort_flag, args.st, 0x2201) ||
-              !mbar_wait(&x_full[xs], (it / XS) & 1, abort_flag, args.st, 0x2202)) {
+          if (!all_lanes(mbar_wait(&f_full[fs], (it / FS) & 1, abort_flag, args.st, 0x2201) &&
+                                   mbar_wait(&x_full[xs], (it / XS) & 1, abort_flag, args.st, 0x2202))) {
             aborted = true;
             break;
           }
@@ -328,32 +336,33 @@ __global__ void __launch_bounds__(kThreads, 1)
           // one N = 256 instruction covers both tiles (64-channel chunks 8 KB
           // apart throughout).
           const uint64_t wd0 = sdesc_sw128(smem_u32(sF + fs * Cfg::kFBytes), 8192, 1024);
+          if (leader) {
 #pragma unroll
-          for (int k = 0; k < kBK / 16; ++k) {
-            const uint64_t xd = xd0 + static_cast<uint64_t>((k * 32) >> 4);
+            for (int k = 0; k < kBK / 16; ++k) {
+              const uint64_t xd = xd0 + static_cast<uint64_t>((k * 32) >> 4);
 #pragma unroll
-            for (int p = 0; p < Cfg::kNumW16; ++p) {
-              const uint64_t wd = wd0 + static_cast<uint64_t>((p * kNT * Cfg::kW16Bytes + k * 2048) >> 4);
-              const uint32_t acc = (!first || k != 0 || p != 0) ? 1u : 0u;
-              if (kSwap) {
+              for (int p = 0; p < Cfg::kNumW16; ++p) {
+                const uint64_t wd = wd0 + static_cast<uint64_t>((p * kNT * Cfg::kW16Bytes + k * 2048) >> 4);
+                const uint32_t acc = (!first || k != 0 || p != 0) ? 1u : 0u;
+                if (kSwap) {
 #pragma unroll
-                for (int g = 0; g < kNT; ++g) {
-                  umma_f16_ss(d_tmem + g * kNX, wd + static_cast<uint64_t>((g * Cfg::kW16Bytes) >> 4), xd, idesc, acc);
-                }
-              } else {
+                  for (int g = 0; g < kNT; ++g) {
+                    umma_f16_ss(d_tmem + g * kNX, wd + static_cast<uint64_t>((g * Cfg::kW16Bytes) >> 4), xd, idesc, acc);
+                  }
+                } else {
 #pragma unroll
-                for (int h = 0; h < Cfg::kRowHalves; ++h) {
-                  umma_f16_ss(d_tmem + h * kUnitN, xd + static_cast<uint64_t>((h * 16384) >> 4), wd, idesc, acc);
+                  for (int h = 0; h < Cfg::kRowHalves; ++h) {
+                    umma_f16_ss(d_tmem + h * kUnitN, xd + static_cast<uint64_t>((h * 16384) >> 4), wd, idesc, acc);
+                  }
                 }
               }
             }
+            umma_commit(&f_empty[fs]);
+            if (!kSwap) umma_commit(&x_empty[xs]);
+            if (run_ends(kb, u.kb1)) umma_commit(&acc_full[buf]);
           }
-          umma_commit(&f_empty[fs]);
-          if (!kSwap) umma_commit(&x_empty[xs]);
-          if (run_ends(kb, u.kb1)) {
-            umma_commit(&acc_full[buf]);
-            ++tc;
-          }
+          if (kSwap) __syncwarp();
+          if (run_ends(kb, u.kb1)) ++tc;
         }
       }
     } else {
@@ -363,13 +372,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         const QUnit u = unit_of(t, args);
         const int buf = tc % Cfg::kAccBufs;
         const uint32_t use = tc / Cfg::kAccBufs;
-        if (!mbar_wait(&acc_empty[buf], (use & 1) ^ 1, abort_flag, args.st, 0x2200)) break;
+        if (!all_lanes(mbar_wait(&acc_empty[buf], (use & 1) ^ 1, abort_flag, args.st, 0x2200))) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem + buf * Cfg::kAccCols;
         for (int kb = u.kb0; kb < u.kb1; ++kb, ++it) {
           const int fs = it % FS, xs = it % XS;
-          if (!mbar_wait(&f_full[fs], (it / FS) & 1, abort_flag, args.st, 0x2201) ||
-              !mbar_wait(&x_full[xs], (it / XS) & 1, abort_flag, args.st, 0x2202)) {
+          if (!all_lanes(mbar_wait(&f_full[fs], (it / FS) & 1, abort_flag, args.st, 0x2201) &&
+                                   mbar_wait(&x_full[xs], (it / XS) & 1, abort_flag, args.st, 0x2202))) {
             aborted = true;
             break;
           }
@@ -379,33 +388,37 @@ __global__ void __launch_bounds__(kThreads, 1)
           // one N = 256 instruction covers both tiles (64-channel chunks 8 KB
           // apart throughout).
           const uint64_t wd0 = sdesc_sw128(smem_u32(sF + fs * Cfg::kFBytes), 8192, 1024);
+          if (leader) {
 #pragma unroll
-          for (int k = 0; k < kBK / 16; ++k) {
-            const uint64_t xd = xd0 + static_cast<uint64_t>((k * 32) >> 4);
+            for (int k = 0; k < kBK / 16; ++k) {
+              const uint64_t xd = xd0 + static_cast<uint64_t>((k * 32) >> 4);
 #pragma unroll
-            for (int p = 0; p < Cfg::kNumW16; ++p) {
-              const uint64_t wd = wd0 + static_cast<uint64_t>((p * kNT * Cfg::kW16Bytes + k * 2048) >> 4);
-              const uint32_t acc = (kb != u.kb0 || k != 0 || p != 0) ? 1u : 0u;
-              if (kSwap) {
+              for (int p = 0; p < Cfg::kNumW16; ++p) {
+                const uint64_t wd = wd0 + static_cast<uint64_t>((p * kNT * Cfg::kW16Bytes + k * 2048) >> 4);
+                const uint32_t acc = (kb != u.kb0 || k != 0 || p != 0) ? 1u : 0u;
+                if (kSwap) {
 #pragma unroll
-                for (int g = 0; g < kNT; ++g) {
-                  umma_f16_ss(d_tmem + g * kNX, wd + static_cast<uint64_t>((g * Cfg::kW16Bytes) >> 4), xd, idesc, acc);
-                }
-              } else {
+                  for (int g = 0; g < kNT; ++g) {
+                    umma_f16_ss(d_tmem + g * kNX, wd + static_cast<uint64_t>((g * Cfg::kW16Bytes) >> 4), xd, idesc, acc);
+                  }
+                } else {
 #pragma unroll
-                for (int h = 0; h < Cfg::kRowHalves; ++h) {
-                  umma_f16_ss(d_tmem + h * kUnitN, xd + static_cast<uint64_t>((h * 16384) >> 4), wd, idesc, acc);
+                  for (int h = 0; h < Cfg::kRowHalves; ++h) {
+                    umma_f16_ss(d_tmem + h * kUnitN, xd + static_cast<uint64_t>((h * 16384) >> 4), wd, idesc, acc);
+                  }
                 }
               }
             }
+            umma_commit(&f_empty[fs]);
+            if (!kSwap) umma_commit(&x_empty[xs]);
           }
-          umma_commit(&f_empty[fs]);
-          if (!kSwap) umma_commit(&x_empty[xs]);
+          if (kSwap) __syncwarp();
         }
-        if (!aborted) umma_commit(&acc_full[buf]);
+        if (!aborted && leader) umma_commit(&acc_full[buf]);
       }
     }
-    umma_commit(mma_done);
+    if (leader) umma_commit(mma_done);
+    if (kSwap) __syncwarp();
     mbar_wait(mma_done, 0, never_flag, quiet, 0);
   } else if (Cfg::kGS && warp == 2 && lane == 0) {
     // ------------------------------------------------ scale rows (int4 TMA) --
