@@ -914,21 +914,68 @@ void plan_splits(QProblem& p, int sms, size_t max_partial = SIZE_MAX) {
 
 // Y[m, n] = scale[n] * sum_s partial[s][m][n] (or tscale[0] * ...), fixed
 // summation order.
+// Y = scale * sum over the K splits of the partial sums, added in split order.
+// Every split's value is requested before any is added (one round trip to
+// L2 instead of one per split); four consecutive outputs per thread when N
+// and the output rows allow 16-byte accesses.
+constexpr int kReduceMaxSplits = 16;
 __global__ void splitk_reduce_kernel(const float* __restrict__ partial, int splits, int M, int N,
                                      const __half* __restrict__ scale, const float* __restrict__ tscale,
-                                     float* __restrict__ Y, int64_t ldy) {
+                                     float* __restrict__ Y, int64_t ldy, int vec4) {
   pdl_launch_dependents();
   pdl_wait();
   const int64_t total = static_cast<int64_t>(M) * N;
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  const float ts = tscale != nullptr ? __ldg(tscale) : 1.f;
+  if (vec4) {
+    for (int64_t q = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; q < total / 4; q += stride) {
+      float4 v[kReduceMaxSplits];
+#pragma unroll
+      for (int sp = 0; sp < kReduceMaxSplits; ++sp) {
+        v[sp] = sp < splits ? __ldcg(reinterpret_cast<const float4*>(partial + sp * total) + q)
+                            : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int sp = 0; sp < kReduceMaxSplits; ++sp) {
+        if (sp < splits) {
+          acc.x += v[sp].x;
+          acc.y += v[sp].y;
+          acc.z += v[sp].z;
+          acc.w += v[sp].w;
+        }
+      }
+      const int64_t i = 4 * q;
+      const int n = static_cast<int>(i % N);
+      if (scale != nullptr) {
+        acc.x *= __half2float(scale[n]);
+        acc.y *= __half2float(scale[n + 1]);
+        acc.z *= __half2float(scale[n + 2]);
+        acc.w *= __half2float(scale[n + 3]);
+      } else if (tscale != nullptr) {
+        acc.x *= ts;
+        acc.y *= ts;
+        acc.z *= ts;
+        acc.w *= ts;
+      }
+      *reinterpret_cast<float4*>(Y + (i / N) * ldy + n) = acc;
+    }
+    return;
+  }
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total; i += stride) {
+    float v[kReduceMaxSplits];
+#pragma unroll
+    for (int sp = 0; sp < kReduceMaxSplits; ++sp) v[sp] = sp < splits ? __ldcg(partial + sp * total + i) : 0.f;
     float acc = 0.f;
-    for (int sp = 0; sp < splits; ++sp) acc += partial[sp * total + i];
+#pragma unroll
+    for (int sp = 0; sp < kReduceMaxSplits; ++sp) {
+      if (sp < splits) acc += v[sp];
+    }
     const int n = static_cast<int>(i % N);
     if (scale != nullptr) {
       acc *= __half2float(scale[n]);
     } else if (tscale != nullptr) {
-      acc *= __ldg(tscale);
+      acc *= ts;
     }
     Y[(i / N) * ldy + n] = acc;
   }
@@ -1005,12 +1052,15 @@ int launch_wq(const QProblem& p, cudaStream_t stream) {
   cudaError_t e = launch_pdl(kern, dim3(grid), dim3(kThreads), Cfg::kSmemBytes, stream, tmX, tmW, tmS, tmY, args);
   if (e != cudaSuccess) return cuda_fail(e, "wq_gemm launch");
   if (args.partial != nullptr) {
+    if (args.splits > kReduceMaxSplits) return fail(NESO_ERR_UNSUPPORTED, "split-K plan of %d splits", args.splits);
     const int64_t total = static_cast<int64_t>(p.M) * p.N;
-    const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, 4 * sm_count()));
+    const int vec4 = (p.N % 4 == 0 && p.ldy % 4 == 0 && (reinterpret_cast<uintptr_t>(p.Y) & 15u) == 0) ? 1 : 0;
+    const int64_t items = vec4 ? total / 4 : total;
+    const int blocks = static_cast<int>(std::min<int64_t>((items + 255) / 256, 4 * sm_count()));
     // Launched with programmatic serialization: its CTAs are scheduled as the
     // matmul's CTAs exit and wait there for the partial sums.
     e = launch_pdl(splitk_reduce_kernel, dim3(blocks), dim3(256), 0, stream, args.partial, args.splits, p.M, p.N,
-                   args.chan_scale, args.tensor_scale, p.Y, p.ldy);
+                   args.chan_scale, args.tensor_scale, p.Y, p.ldy, vec4);
     if (e != cudaSuccess) return cuda_fail(e, "split-K reduce launch");
   }
   return ok();
