@@ -75,6 +75,14 @@ struct QCfg {
   static constexpr int kXBytes = kNX * kBK * 2;
   static constexpr int kW16Bytes = kBK * kTileN * 2;            // 16 KB per fp16 copy
   static constexpr int kNumW16 = (kQ == kInt4G128 && !kGS) ? 2 : 1;
+  // Convert groups (warps 4-7, 12-15). A group's per-stage cost is mostly
+  // fixed (barrier waits, the proxy fence, loop control: ~1300 cycles per
+  // stage measured at M = 16), so the swapped layout lets each group take
+  // alternate stages and convert every tile of its stage; the M >= 65 paired
+  // layout keeps one tile per group on every stage.
+  static constexpr bool kAltStages = kSwap || kNT == 1;
+  static constexpr int kGroupTiles = kSwap ? kNT : 1;
+  static constexpr int kConvGroupsPerStage = kAltStages ? 1 : kNT;
   static constexpr int kScSlots = kGS ? 16 : 0;
   static constexpr int kScBytes = kNT * 256;
   static constexpr int kFTileBytes = kNumW16 * kW16Bytes;
@@ -205,14 +213,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int i = 0; i < RS; ++i) {
       mbar_init(&r_full[i], 1);
-      mbar_init(&r_empty[i], 4 * kNT);
+      mbar_init(&r_empty[i], 4 * Cfg::kConvGroupsPerStage);
     }
     for (int i = 0; i < XS; ++i) {
       mbar_init(&x_full[i], 1);
       mbar_init(&x_empty[i], 1);
     }
     for (int i = 0; i < FS; ++i) {
-      mbar_init(&f_full[i], 4 * kNT);
+      mbar_init(&f_full[i], 4 * Cfg::kConvGroupsPerStage);
       mbar_init(&f_empty[i], 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -451,9 +459,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if ((warp >= 4 && warp < 8) || warp >= 12) {
     // ------------------------------------------------------------- convert --
     // Two convert groups (warps 4-7 and 12-15) take alternate K blocks, so
-    // one block is dequantised while the other group's is being stored.
-    // With two weight tiles per unit each group instead converts its own
-    // tile (grp) of every K block.
+    // one block is dequantised while the other group's is being stored, and
+    // convert all tiles of their block (kGroupTiles). The M >= 65 layout with
+    // two weight tiles per unit instead gives each group its own tile (grp)
+    // of every K block.
     const int grp = warp >= 12 ? 1 : 0;
     const int ct = threadIdx.x - (grp ? 384 : 128);  // 0..127
     int it = 0;
@@ -461,11 +470,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int t = blockIdx.x; t < num_units && ok_run; t += gridDim.x) {
       const QUnit u = unit_of(t, args);
       for (int kb = u.kb0; kb < u.kb1; ++kb, ++it) {
-        if (kNT == 1 && (it & 1) != grp) continue;
+        if (Cfg::kAltStages && (it & 1) != grp) continue;
         const int rs = it % RS, fs = it % FS;
         if (!mbar_wait(&r_full[rs], (it / RS) & 1, abort_flag, args.st, 0x2300)) { ok_run = false; break; }
-        const uint8_t* raw = sR + rs * Cfg::kRawBytes + (kNT == 2 ? grp * Cfg::kRawTileBytes : 0);
-        uint8_t* w16 = sF + fs * Cfg::kFBytes + (kNT == 2 ? grp * Cfg::kW16Bytes : 0);
+        constexpr int GT = Cfg::kGroupTiles;
+        const uint8_t* raw = sR + rs * Cfg::kRawBytes + (Cfg::kAltStages ? 0 : grp * Cfg::kRawTileBytes);
+        uint8_t* w16 = sF + fs * Cfg::kFBytes + (Cfg::kAltStages ? 0 : grp * Cfg::kW16Bytes);
         if (kQ == kInt8) {
           // thread -> (k row r, n half h); raw unit u of row r sits at unit u ^ (r & 7).
           // Each group of 8 consecutive threads takes 8 consecutive rows of one
@@ -473,11 +483,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int r = (ct & 7) + 8 * (ct >> 4);
           const int h = (ct >> 3) & 1;
           const int sw = r & 7;
-          uint4 o[8];
+          uint4 o[GT][8];
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const uint4 rv = *reinterpret_cast<const uint4*>(raw + r * 128 + (((4 * h + i) ^ sw) << 4));
-            dequant_i8x16(rv, o[2 * i], o[2 * i + 1]);
+          for (int g = 0; g < GT; ++g) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const uint4 rv = *reinterpret_cast<const uint4*>(raw + g * Cfg::kRawTileBytes + r * 128 +
+                                                               (((4 * h + i) ^ sw) << 4));
+              dequant_i8x16(rv, o[g][2 * i], o[g][2 * i + 1]);
+            }
           }
           // The raw slot is released only once its bytes have been consumed
           // into registers (the dequantised values depend on them): a release
@@ -486,9 +500,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive(&r_empty[rs]);
           if (!mbar_wait(&f_empty[fs], ((it / FS) & 1) ^ 1, abort_flag, args.st, 0x2301)) { ok_run = false; break; }
-          uint8_t* dst = w16 + h * 8192 + r * 128;
 #pragma unroll
-          for (int i = 0; i < 8; ++i) *reinterpret_cast<uint4*>(dst + ((i ^ sw) << 4)) = o[i];
+          for (int g = 0; g < GT; ++g) {
+            uint8_t* dst = w16 + g * Cfg::kW16Bytes + h * 8192 + r * 128;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) *reinterpret_cast<uint4*>(dst + ((i ^ sw) << 4)) = o[g][i];
+          }
         } else {
           if constexpr (Cfg::kGS) {
             // thread -> (byte row kk: k rows 2kk and 2kk+1, n quarter qn: 32 channels)
@@ -496,20 +513,24 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int qn = ct & 3;
             const int swr = kk & 7;
             const __half2 b8 = __float2half2_rn(1032.f);  // 1024 + 8
-            uint32_t hv[2][2][8];  // [raw unit i][row r0/r1][16 channels as 8 half2]
+            uint32_t hv[GT][2][2][8];  // [tile][raw unit i][row r0/r1][16 channels as 8 half2]
 #pragma unroll
-            for (int i = 0; i < 2; ++i) {
-              const uint4 rv = *reinterpret_cast<const uint4*>(raw + kk * 128 + (((2 * qn + i) ^ swr) << 4));
-              const uint32_t words[4] = {rv.x, rv.y, rv.z, rv.w};
+            for (int g = 0; g < GT; ++g) {
 #pragma unroll
-              for (int wdx = 0; wdx < 4; ++wdx) {
-                const uint32_t lo_n = (words[wdx] & 0x0F0F0F0Fu) ^ 0x08080808u;         // k even
-                const uint32_t hi_n = ((words[wdx] >> 4) & 0x0F0F0F0Fu) ^ 0x08080808u;  // k odd
+              for (int i = 0; i < 2; ++i) {
+                const uint4 rv = *reinterpret_cast<const uint4*>(raw + g * Cfg::kRawTileBytes + kk * 128 +
+                                                                 (((2 * qn + i) ^ swr) << 4));
+                const uint32_t words[4] = {rv.x, rv.y, rv.z, rv.w};
 #pragma unroll
-                for (int half_sel = 0; half_sel < 2; ++half_sel) {
-                  const uint32_t sel = half_sel ? 0x7362u : 0x5140u;
-                  hv[i][0][wdx * 2 + half_sel] = h2_as_u32(__hsub2(u32_as_h2(bytes_to_h2(lo_n, sel)), b8));
-                  hv[i][1][wdx * 2 + half_sel] = h2_as_u32(__hsub2(u32_as_h2(bytes_to_h2(hi_n, sel)), b8));
+                for (int wdx = 0; wdx < 4; ++wdx) {
+                  const uint32_t lo_n = (words[wdx] & 0x0F0F0F0Fu) ^ 0x08080808u;         // k even
+                  const uint32_t hi_n = ((words[wdx] >> 4) & 0x0F0F0F0Fu) ^ 0x08080808u;  // k odd
+#pragma unroll
+                  for (int half_sel = 0; half_sel < 2; ++half_sel) {
+                    const uint32_t sel = half_sel ? 0x7362u : 0x5140u;
+                    hv[g][i][0][wdx * 2 + half_sel] = h2_as_u32(__hsub2(u32_as_h2(bytes_to_h2(lo_n, sel)), b8));
+                    hv[g][i][1][wdx * 2 + half_sel] = h2_as_u32(__hsub2(u32_as_h2(bytes_to_h2(hi_n, sel)), b8));
+                  }
                 }
               }
             }
@@ -519,17 +540,21 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!mbar_wait(&f_empty[fs], ((it / FS) & 1) ^ 1, abort_flag, args.st, 0x2301)) { ok_run = false; break; }
             const int chunk = qn >> 1;
 #pragma unroll
-            for (int i = 0; i < 2; ++i) {
-              // 16 channels = two fp16 units; column within the chunk = 32 (qn & 1) + 16 i
-              const int v0 = 4 * (qn & 1) + 2 * i;
+            for (int g = 0; g < GT; ++g) {
 #pragma unroll
-              for (int rr = 0; rr < 2; ++rr) {
-                const int row = 2 * kk + rr;
+              for (int i = 0; i < 2; ++i) {
+                // 16 channels = two fp16 units; column within the chunk = 32 (qn & 1) + 16 i
+                const int v0 = 4 * (qn & 1) + 2 * i;
 #pragma unroll
-                for (int e = 0; e < 2; ++e) {
-                  const int off = chunk * 8192 + row * 128 + (((v0 + e) ^ (row & 7)) << 4);
-                  *reinterpret_cast<uint4*>(w16 + off) = make_uint4(hv[i][rr][4 * e], hv[i][rr][4 * e + 1],
-                                                                    hv[i][rr][4 * e + 2], hv[i][rr][4 * e + 3]);
+                for (int rr = 0; rr < 2; ++rr) {
+                  const int row = 2 * kk + rr;
+#pragma unroll
+                  for (int e = 0; e < 2; ++e) {
+                    const int off = g * Cfg::kW16Bytes + chunk * 8192 + row * 128 + (((v0 + e) ^ (row & 7)) << 4);
+                    *reinterpret_cast<uint4*>(w16 + off) =
+                        make_uint4(hv[g][i][rr][4 * e], hv[g][i][rr][4 * e + 1], hv[g][i][rr][4 * e + 2],
+                                   hv[g][i][rr][4 * e + 3]);
+                  }
                 }
               }
             }
