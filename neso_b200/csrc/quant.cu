@@ -72,8 +72,17 @@ struct QCfg {
   static constexpr bool kGS = kQ == kInt4G128 && kSwap;
   static constexpr int kRawTileBytes = (kQ == kInt8) ? 64 * 128 : kGS ? 32 * 128 : 32 * 128 + 1024;
   static constexpr int kRawBytes = kNT * kRawTileBytes;
-  static constexpr int kXBytes = kNX * kBK * 2;
-  static constexpr int kW16Bytes = kBK * kTileN * 2;            // 16 KB per fp16 copy
+  // 64-deep K blocks per fp16 weight (F) and activation (X) stage: two in the
+  // swapped layout with paired tiles or int4, whose per-stage hand-offs
+  // (barrier waits, the proxy fence, commits) otherwise cost as much as its
+  // small MMAs (measured: W8A16 M=16 19.3 -> 17.8 us, W4A16 M=16/32/64
+  // 21.1 / 25.5 / 30.6 -> 19.9 / 23.2 / 28.8 us; single-tile W8A16 M=32/64
+  // measured slower, 20.9 / 22.9 -> 21.8 / 23.4); raw tiles stay one K block.
+  static constexpr int kFKB = (kSwap && (kNT == 2 || kQ == kInt4G128)) ? 2 : 1;
+  static constexpr int kXBlockBytes = kNX * kBK * 2;
+  static constexpr int kXBytes = kFKB * kXBlockBytes;
+  static constexpr int kW16BlockBytes = kBK * kTileN * 2;      // 16 KB: one K block of one tile
+  static constexpr int kW16Bytes = kFKB * kW16BlockBytes;      // one fp16 copy of one tile
   static constexpr int kNumW16 = (kQ == kInt4G128 && !kGS) ? 2 : 1;
   // Convert groups (warps 4-7, 12-15). A group's per-stage cost is mostly
   // fixed (barrier waits, the proxy fence, loop control: ~1300 cycles per
@@ -90,7 +99,8 @@ struct QCfg {
   // kNX = 256 in the M >= 65 layout: 256-row units, two 128-row accumulators
   // (every fp16 weight stage feeds two MMAs per K step).
   static constexpr int kRowHalves = kSwap ? 1 : kNX / 128;
-  static constexpr int kFStages = kRowHalves == 2 ? 2 : kNT == 2 ? (kQ == kInt8 ? 3 : 2) : (kQ == kInt4G128 && !kSwap) ? 3 : 4;
+  static constexpr int kFStages = kSwap ? (kFKB == 1 ? 4 : kNT == 2 ? 2 : 3)
+                                  : kRowHalves == 2 ? 2 : kNT == 2 ? (kQ == kInt8 ? 3 : 2) : (kQ == kInt4G128) ? 3 : 4;
   // X tiles come from L2 with about 2500 cycles of copy latency: a deep
   // ring keeps the MMAs fed when every K block needs a new 16 KB X tile.
   // Swapped layout: X tiles are 2-8 KB and the X ring moves in step with the
@@ -263,11 +273,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Swapped layout: an X slot is free when the F slot of the same K block is
     // (same ring depth and order, one commit per stage).
     uint64_t* empty = raw ? r_empty : (kSwap ? f_empty : x_empty);
-    int it = 0;
+    int it = 0;  // raw: K blocks; X: X stages of kFKB K blocks
     bool aborted = false;
     for (int t = blockIdx.x; t < num_units && !aborted; t += gridDim.x) {
       const QUnit u = unit_of(t, args);
-      for (int kb = u.kb0; kb < u.kb1; ++kb, ++it) {
+      for (int kb = u.kb0; kb < u.kb1; kb += raw ? 1 : Cfg::kFKB, ++it) {
         const int s = it % depth;
         const uint32_t ph = (it / depth) & 1;
         if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, args.st, raw ? 0x2100 : 0x2101)) { aborted = true; break; }
@@ -286,8 +296,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
         } else {
+          // Both K blocks of a stage (the second may lie past the unit's K
+          // range, or past K where the copy fills zeros; the MMAs skip it).
           mbar_arrive_expect_tx(&full[s], Cfg::kXBytes);
-          tma_load_2d(sX + s * Cfg::kXBytes, &tmX, &full[s], kb * kBK, kSwap ? 0 : u.mb * kNX);
+#pragma unroll
+          for (int b = 0; b < Cfg::kFKB; ++b) {
+            tma_load_2d(sX + s * Cfg::kXBytes + b * Cfg::kXBlockBytes, &tmX, &full[s], (kb + b) * kBK,
+                        kSwap ? 0 : u.mb * kNX);
+          }
         }
       }
     }
@@ -320,7 +336,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const QUnit u = unit_of(t, args);
         int buf = 0;
         uint32_t d_tmem = tmem;
-        for (int kb = u.kb0; kb < u.kb1; ++kb, ++it) {
+        for (int kb = u.kb0; kb < u.kb1; kb += Cfg::kFKB, ++it) {
+          const int nkb = Cfg::kFKB == 1 ? 1 : min(Cfg::kFKB, u.kb1 - kb);
           const bool first = run_starts(kb, u.kb0);
           if (first) {
             buf = tc % Cfg::kAccBufs;
@@ -346,12 +363,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint64_t wd0 = sdesc_sw128(smem_u32(sF + fs * Cfg::kFBytes), 8192, 1024);
           if (leader) {
 #pragma unroll
-            for (int k = 0; k < kBK / 16; ++k) {
-              const uint64_t xd = xd0 + static_cast<uint64_t>((k * 32) >> 4);
+            for (int kk = 0; kk < Cfg::kFKB * (kBK / 16); ++kk) {
+              const int b = kk / (kBK / 16), k = kk % (kBK / 16);
+              if (b >= nkb) break;
+              const uint64_t xd = xd0 + static_cast<uint64_t>((b * Cfg::kXBlockBytes + k * 32) >> 4);
 #pragma unroll
               for (int p = 0; p < Cfg::kNumW16; ++p) {
-                const uint64_t wd = wd0 + static_cast<uint64_t>((p * kNT * Cfg::kW16Bytes + k * 2048) >> 4);
-                const uint32_t acc = (!first || k != 0 || p != 0) ? 1u : 0u;
+                const uint64_t wd =
+                    wd0 + static_cast<uint64_t>((p * kNT * Cfg::kW16Bytes + b * Cfg::kW16BlockBytes + k * 2048) >> 4);
+                const uint32_t acc = (!first || kk != 0 || p != 0) ? 1u : 0u;
                 if (kSwap) {
 #pragma unroll
                   for (int g = 0; g < kNT; ++g) {
@@ -367,10 +387,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             umma_commit(&f_empty[fs]);
             if (!kSwap) umma_commit(&x_empty[xs]);
-            if (run_ends(kb, u.kb1)) umma_commit(&acc_full[buf]);
+            if (run_ends(kb + nkb - 1, u.kb1)) umma_commit(&acc_full[buf]);
           }
           if (kSwap) __syncwarp();
-          if (run_ends(kb, u.kb1)) ++tc;
+          if (run_ends(kb + nkb - 1, u.kb1)) ++tc;
         }
       }
     } else {
@@ -383,7 +403,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!all_lanes(mbar_wait(&acc_empty[buf], (use & 1) ^ 1, abort_flag, args.st, 0x2200))) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem + buf * Cfg::kAccCols;
-        for (int kb = u.kb0; kb < u.kb1; ++kb, ++it) {
+        for (int kb = u.kb0; kb < u.kb1; kb += Cfg::kFKB, ++it) {
+          const int nkb = Cfg::kFKB == 1 ? 1 : min(Cfg::kFKB, u.kb1 - kb);
           const int fs = it % FS, xs = it % XS;
           if (!all_lanes(mbar_wait(&f_full[fs], (it / FS) & 1, abort_flag, args.st, 0x2201) &&
                                    mbar_wait(&x_full[xs], (it / XS) & 1, abort_flag, args.st, 0x2202))) {
@@ -398,12 +419,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint64_t wd0 = sdesc_sw128(smem_u32(sF + fs * Cfg::kFBytes), 8192, 1024);
           if (leader) {
 #pragma unroll
-            for (int k = 0; k < kBK / 16; ++k) {
-              const uint64_t xd = xd0 + static_cast<uint64_t>((k * 32) >> 4);
+            for (int kk = 0; kk < Cfg::kFKB * (kBK / 16); ++kk) {
+              const int b = kk / (kBK / 16), k = kk % (kBK / 16);
+              if (b >= nkb) break;
+              const uint64_t xd = xd0 + static_cast<uint64_t>((b * Cfg::kXBlockBytes + k * 32) >> 4);
 #pragma unroll
               for (int p = 0; p < Cfg::kNumW16; ++p) {
-                const uint64_t wd = wd0 + static_cast<uint64_t>((p * kNT * Cfg::kW16Bytes + k * 2048) >> 4);
-                const uint32_t acc = (kb != u.kb0 || k != 0 || p != 0) ? 1u : 0u;
+                const uint64_t wd =
+                    wd0 + static_cast<uint64_t>((p * kNT * Cfg::kW16Bytes + b * Cfg::kW16BlockBytes + k * 2048) >> 4);
+                const uint32_t acc = (kb != u.kb0 || kk != 0 || p != 0) ? 1u : 0u;
                 if (kSwap) {
 #pragma unroll
                   for (int g = 0; g < kNT; ++g) {
@@ -432,7 +456,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------ scale rows (int4 TMA) --
     // One row of 128 fp16 scales per weight tile and group run, into a ring
     // the epilogue warps release.
-    constexpr int SS = Cfg::kScSlots;
+    constexpr int SS = Cfg::kScSlots > 0 ? Cfg::kScSlots : 1;
     int si = 0;
     bool aborted = false;
     for (int t = blockIdx.x; t < num_units && !aborted; t += gridDim.x) {
@@ -465,17 +489,24 @@ __global__ void __launch_bounds__(kThreads, 1)
     // of every K block.
     const int grp = warp >= 12 ? 1 : 0;
     const int ct = threadIdx.x - (grp ? 384 : 128);  // 0..127
-    int it = 0;
+    int it = 0;  // F stages
+    int ri = 0;  // K blocks: position in the raw ring
     bool ok_run = true;
     for (int t = blockIdx.x; t < num_units && ok_run; t += gridDim.x) {
       const QUnit u = unit_of(t, args);
-      for (int kb = u.kb0; kb < u.kb1; ++kb, ++it) {
-        if (Cfg::kAltStages && (it & 1) != grp) continue;
-        const int rs = it % RS, fs = it % FS;
-        if (!mbar_wait(&r_full[rs], (it / RS) & 1, abort_flag, args.st, 0x2300)) { ok_run = false; break; }
+      for (int kb = u.kb0; kb < u.kb1 && ok_run; kb += Cfg::kFKB, ++it) {
+        const int nkb = Cfg::kFKB == 1 ? 1 : min(Cfg::kFKB, u.kb1 - kb);
+        if (Cfg::kAltStages && (it & 1) != grp) {
+          ri += nkb;
+          continue;
+        }
+        const int fs = it % FS;
+        for (int b = 0; b < nkb; ++b, ++ri) {
+        const int rs = ri % RS;
+        if (!mbar_wait(&r_full[rs], (ri / RS) & 1, abort_flag, args.st, 0x2300)) { ok_run = false; break; }
         constexpr int GT = Cfg::kGroupTiles;
         const uint8_t* raw = sR + rs * Cfg::kRawBytes + (Cfg::kAltStages ? 0 : grp * Cfg::kRawTileBytes);
-        uint8_t* w16 = sF + fs * Cfg::kFBytes + (Cfg::kAltStages ? 0 : grp * Cfg::kW16Bytes);
+        uint8_t* w16 = sF + fs * Cfg::kFBytes + b * Cfg::kW16BlockBytes + (Cfg::kAltStages ? 0 : grp * Cfg::kW16Bytes);
         if (kQ == kInt8) {
           // thread -> (k row r, n half h); raw unit u of row r sits at unit u ^ (r & 7).
           // Each group of 8 consecutive threads takes 8 consecutive rows of one
@@ -499,7 +530,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           // loads that have not been performed yet.
           __syncwarp();
           if (lane == 0) mbar_arrive(&r_empty[rs]);
-          if (!mbar_wait(&f_empty[fs], ((it / FS) & 1) ^ 1, abort_flag, args.st, 0x2301)) { ok_run = false; break; }
+          if (b == 0 && !mbar_wait(&f_empty[fs], ((it / FS) & 1) ^ 1, abort_flag, args.st, 0x2301)) {
+            ok_run = false;
+            break;
+          }
 #pragma unroll
           for (int g = 0; g < GT; ++g) {
             uint8_t* dst = w16 + g * Cfg::kW16Bytes + h * 8192 + r * 128;
@@ -537,7 +571,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             // Release the raw slot only after its bytes are consumed (see int8).
             __syncwarp();
             if (lane == 0) mbar_arrive(&r_empty[rs]);
-            if (!mbar_wait(&f_empty[fs], ((it / FS) & 1) ^ 1, abort_flag, args.st, 0x2301)) { ok_run = false; break; }
+            if (b == 0 && !mbar_wait(&f_empty[fs], ((it / FS) & 1) ^ 1, abort_flag, args.st, 0x2301)) {
+            ok_run = false;
+            break;
+          }
             const int chunk = qn >> 1;
 #pragma unroll
             for (int g = 0; g < GT; ++g) {
@@ -592,7 +629,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             // Release the raw slot only after its bytes are consumed (see int8).
             __syncwarp();
             if (lane == 0) mbar_arrive(&r_empty[rs]);
-            if (!mbar_wait(&f_empty[fs], ((it / FS) & 1) ^ 1, abort_flag, args.st, 0x2301)) { ok_run = false; break; }
+            if (b == 0 && !mbar_wait(&f_empty[fs], ((it / FS) & 1) ^ 1, abort_flag, args.st, 0x2301)) {
+            ok_run = false;
+            break;
+          }
             uint8_t* hi = w16;
             uint8_t* lo = w16 + kNT * Cfg::kW16Bytes;
             const int chunk = qn >> 1;
@@ -615,6 +655,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
         }
+        }
+        if (!ok_run) break;
         fence_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(&f_full[fs]);
@@ -896,9 +938,7 @@ void plan_normal(QProblem& p, int sms, size_t max_partial) {
 void plan_splits(QProblem& p, int sms, size_t max_partial = SIZE_MAX) {
   const bool swap = p.M <= 64;
   const int num_m = swap ? 1 : (p.M + 127) / 128;
-  const int num_n = (p.N + kTileN - 1) / kTileN;
   const int num_k = (p.K + kBK - 1) / kBK;
-  const int base = num_m * num_n;
   p.splits = 1;
   p.kb_per_split = num_k;
   p.pair = 0;
@@ -923,7 +963,8 @@ void plan_splits(QProblem& p, int sms, size_t max_partial = SIZE_MAX) {
   if (max_splits < 2) return;
   double best = static_cast<double>(sbase) / sms;
   for (int sp = 2; sp <= 16 && sp <= num_k && sp <= max_splits; ++sp) {
-    const int kbps = (num_k + sp - 1) / sp;
+    int kbps = (num_k + sp - 1) / sp;
+    if (p.kind == kInt4G128 || p.pair) kbps += kbps & 1;  // splits start on a two-block stage boundary
     const int real = (num_k + kbps - 1) / kbps;  // no empty split
     if (static_cast<size_t>(real) * p.M * p.N > max_partial) continue;  // partial sums must fit the scratch
     const int64_t units = static_cast<int64_t>(sbase) * real;
