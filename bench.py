@@ -507,7 +507,7 @@ def main() -> None:
             "algorithmic_bytes": 10.0 * sh.size * S * D,
             "peak_source": f"{peak_src} bf16_tflops (burst, kernel timed alone)",
             "traffic_source": None if traffic is None else traffic["source"],
-            "kernel": "fa2_tile_kernel<64,1,false,0>"}
+            "kernel": "fa2_pair_kernel<64,false,0>"}
 
     # Verification after timing: NCCL all-gather of every rank's heads, then
     # rank 0 checks sampled heads (first and last of every shard) on the CPU.

@@ -23,7 +23,6 @@
 //            blockIdx.x, blockIdx.x + gridDim.x, ... (persistent: the next
 //            tile's Q load and first QK run under this tile's last blocks
 //            and epilogue); causal, it processes tiles qb and nq-1-qb.
-//            fa2_tile_kernel is the same CTA for one tile.
 //   D = 128  fa2_persistent_kernel: one two-tile CTA per SM walks units
 //            handed out from a per-launch counter.
 // The description below is of the two-tile form; the one-tile form drops
@@ -151,506 +150,8 @@ struct FaArgs {
   DevStatus st;
 };
 
-template <int D, int kT, bool kCausal, int kBias>
-__global__ void __launch_bounds__(FaCfg<D, kT>::kThreads, FaCfg<D, kT>::min_blocks())
-    fa2_tile_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
-                    FaArgs a) {
-  using Cfg = FaCfg<D, kT>;
-  constexpr int KS = Cfg::kStages;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;                                // kT tiles
-  uint8_t* sK = smem + kT * Cfg::kTileBytes;         // KS tiles
-  uint8_t* sV = sK + KS * Cfg::kTileBytes;           // KS tiles
-  float* tb_base = reinterpret_cast<float*>(sV + KS * Cfg::kTileBytes);  // table windows (kT = 1)
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + KS * Cfg::kTileBytes + Cfg::kTableBytes);
-  uint64_t* q_full = bars;
-  uint64_t* k_full = bars + 1;
-  uint64_t* k_empty = k_full + KS;
-  uint64_t* v_full = k_empty + KS;
-  uint64_t* v_empty = v_full + KS;
-  uint64_t* s_full = v_empty + KS;   // [2]
-  uint64_t* p_full = s_full + 2;     // [2]
-  uint64_t* o_done = p_full + 2;     // [2]
-  uint64_t* s_free = o_done + 2;     // [2] softmax has read S_t (4 warps)
-  uint64_t* mma_done = s_free + 2;   // [2] one per MMA issuer
-  uint64_t* turn = mma_done + 2;     // [2][4] exp-loop turn of tile t, lane quarter q
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(turn + 8);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  volatile int* never_flag = abort_flag + 1;  // stays 0: drain waits ignore the abort
-
-  const uint32_t warp = warp_id();
-  const uint32_t lane = lane_id();
-  const int S = a.S;
-  const int qb = kCausal ? (a.num_qblocks - 1 - static_cast<int>(blockIdx.x)) : static_cast<int>(blockIdx.x);
-  const int bh = blockIdx.y;
-  const int q0 = qb * 128 * kT;
-  const int nkv = (S + 127) / 128;
-  // KV blocks each Q tile visits (0 for a tile that starts past S)
-  const int ntile0 = kCausal ? min(nkv, q0 / 128 + 1) : nkv;
-  const int ntile1 = (kT == 1 || q0 + 128 >= S) ? 0 : (kCausal ? min(nkv, q0 / 128 + 2) : nkv);
-  const int nmax = max(ntile0, ntile1);
-
-  if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
-    for (int s = 0; s < KS; ++s) {
-      mbar_init(&k_full[s], 1);
-      mbar_init(&k_empty[s], 1);
-      mbar_init(&v_full[s], 1);
-      mbar_init(&v_empty[s], 1);
-    }
-    for (int t = 0; t < 2; ++t) {
-      mbar_init(&s_full[t], 1);
-      mbar_init(&p_full[t], 4);
-      mbar_init(&o_done[t], 1);
-      mbar_init(&s_free[t], 4);
-    }
-    mbar_init(&mma_done[0], 1);
-    mbar_init(&mma_done[1], 1);
-    for (int i = 0; i < 8; ++i) mbar_init(&turn[i], 1);
-    *abort_flag = 0;
-    *never_flag = 0;
-    fence_mbar_init();
-    tma_prefetch_desc(&tmQ);
-    tma_prefetch_desc(&tmK);
-    tma_prefetch_desc(&tmV);
-  }
-  if (warp == 2) {
-    tmem_alloc(tmem_slot, Cfg::kTmemCols);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-  // Programmatic dependent launch: nothing global is read or written before
-  // the previous kernel on the stream has completed.
-  pdl_launch_dependents();
-  pdl_wait();
-  if (warp < 4) {
-    // Warpgroup 0: TMA producer, MMA issuer, TMEM allocator.
-    setmaxnreg_dec<Cfg::regs_low()>();
-    if (warp == 0 && lane == 0) {
-      // ------------------------------------------------------------ producer --
-      const uint32_t qbytes = (ntile1 > 0 ? 2 : 1) * Cfg::kTileBytes;
-      mbar_arrive_expect_tx(q_full, qbytes);
-      for (int t = 0; t < 2; ++t) {
-        if ((t ? ntile1 : ntile0) == 0) continue;
-#pragma unroll
-        for (int c = 0; c < Cfg::kChunks; ++c) {
-          tma_load_3d(sQ + t * Cfg::kTileBytes + c * 16384, &tmQ, q_full, c * 64, q0 + 128 * t, bh);
-        }
-      }
-      int issued = 0;
-      bool aborted = false;
-      for (int j = 0; j < nmax; ++j) {
-        const int s = j % KS;
-        const uint32_t ph = (j / KS) & 1;
-        if (!mbar_wait(&k_empty[s], ph ^ 1, abort_flag, a.st, 0x1100)) { aborted = true; break; }
-        mbar_arrive_expect_tx(&k_full[s], Cfg::kTileBytes);
-#pragma unroll
-        for (int c = 0; c < Cfg::kChunks; ++c) {
-          tma_load_3d(sK + s * Cfg::kTileBytes + c * 16384, &tmK, &k_full[s], c * 64, j * 128, bh);
-        }
-        if (!mbar_wait(&v_empty[s], ph ^ 1, abort_flag, a.st, 0x1101)) {
-          issued = j;  // K_j is in flight; V_j is not
-          DevStatus quiet = a.st;
-          quiet.word = nullptr;
-          mbar_wait(&k_full[s], ph, never_flag, quiet, 0);
-          aborted = true;
-          break;
-        }
-        mbar_arrive_expect_tx(&v_full[s], Cfg::kTileBytes);
-#pragma unroll
-        for (int c = 0; c < Cfg::kChunks; ++c) {
-          tma_load_3d(sV + s * Cfg::kTileBytes + c * 16384, &tmV, &v_full[s], c * 64, j * 128, bh);
-        }
-        issued = j + 1;
-      }
-      if (aborted) {
-        DevStatus quiet = a.st;
-        quiet.word = nullptr;
-        mbar_wait(q_full, 0, never_flag, quiet, 0);
-        for (int i = (issued > KS ? issued - KS : 0); i < issued; ++i) {
-          mbar_wait(&k_full[i % KS], (i / KS) & 1, never_flag, quiet, 0);
-          mbar_wait(&v_full[i % KS], (i / KS) & 1, never_flag, quiet, 0);
-        }
-      }
-    } else if ((warp == 1 || warp == 3) && lane == 0) {
-      // ------------------------------------------------------- MMA issuers --
-      // Two single-thread issuers on different SM sub-partitions: warp 1
-      // issues S = Q K^T, warp 3 issues O += P V. A tcgen05.mma issue blocks
-      // until the tensor pipe accepts it, so one thread serving both streams
-      // (and sharing its scheduler with busy softmax warps) leaves the pipe
-      // idle between MMAs. The streams only meet through mbarriers.
-      constexpr uint32_t idesc_qk = idesc_f16_f32(128, 128, 0, 0);
-      constexpr uint32_t idesc_pv = idesc_f16_f32(128, D, 0, 1);
-      // Descriptor bases, computed once; a K step only moves the start
-      // address field (low bits), so the per-MMA work is one 64-bit add.
-      const uint64_t q_desc0 = sdesc_sw128(smem_u32(sQ), 16, 1024);
-      const uint64_t k_desc0 = sdesc_sw128(smem_u32(sK), 16, 1024);
-      const uint64_t v_desc0 = sdesc_sw128(smem_u32(sV), 16384, 1024);
-      auto n_of = [=](int t) { return t ? ntile1 : ntile0; };
-      bool ok_run = true;
-      if (warp == 1) {
-        auto issue_qk = [=](int t, int j) {
-          const uint64_t qd = q_desc0 + static_cast<uint64_t>((t * Cfg::kTileBytes) >> 4);
-          const uint64_t kd = k_desc0 + static_cast<uint64_t>(((j % KS) * Cfg::kTileBytes) >> 4);
-          const uint32_t d_tmem = tmem + Cfg::s_col(t);
-#pragma unroll
-          for (int k = 0; k < D / 16; ++k) {
-            const uint64_t off = static_cast<uint64_t>(((k >> 2) * 16384 + (k & 3) * 32) >> 4);
-            umma_f16_ss(d_tmem, qd + off, kd + off, idesc_qk, k > 0 ? 1u : 0u);
-          }
-          umma_commit(&s_full[t]);
-        };
-        ok_run = mbar_wait(q_full, 0, abort_flag, a.st, 0x1200) &&
-                 (nmax == 0 || mbar_wait(&k_full[0], 0, abort_flag, a.st, 0x1201));
-        if (ok_run && nmax > 0) {
-          tc_fence_after();
-          for (int t = 0; t < 2; ++t)
-            if (n_of(t) > 0) issue_qk(t, 0);
-          umma_commit(&k_empty[0]);
-        }
-        for (int j = 0; ok_run && j + 1 < nmax; ++j) {
-          const int sn = (j + 1) % KS;
-          const uint32_t phn = ((j + 1) / KS) & 1;
-          if (!mbar_wait(&k_full[sn], phn, abort_flag, a.st, 0x1213)) { ok_run = false; break; }
-          for (int t = 0; t < 2 && ok_run; ++t) {
-            if (j + 1 < n_of(t)) {
-              if (Cfg::kAliasP) {
-                // P_t lives in S_t's columns: PV_t(j) must have read it.
-                if (!mbar_wait(&o_done[t], j & 1, abort_flag, a.st, 0x1214 + t)) { ok_run = false; break; }
-              } else {
-                // P has its own columns: S_t may be overwritten once the softmax
-                // warps hold S_t(j) in registers, so QK(j+1) runs under softmax(j).
-                if (!mbar_wait(&s_free[t], j & 1, abort_flag, a.st, 0x1218 + t)) { ok_run = false; break; }
-              }
-              tc_fence_after();
-              issue_qk(t, j + 1);
-            }
-          }
-          if (!ok_run) break;
-          umma_commit(&k_empty[sn]);
-        }
-      } else {
-        auto issue_pv = [=](int t, int j) {
-          const uint64_t vd = v_desc0 + static_cast<uint64_t>(((j % KS) * Cfg::kTileBytes) >> 4);
-          const uint32_t d_tmem = tmem + Cfg::o_col(t);
-          const uint32_t p_tmem = tmem + Cfg::p_col(t);
-#pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            umma_f16_ts(d_tmem, p_tmem + (k >> 2) * Cfg::kPHalfStride + (k & 3) * 8,
-                        vd + static_cast<uint64_t>((k * 2048) >> 4), idesc_pv, (j > 0 || k > 0) ? 1u : 0u);
-          }
-          umma_commit(&o_done[t]);
-        };
-        for (int j = 0; ok_run && j < nmax; ++j) {
-          const int s = j % KS;
-          const uint32_t ph = (j / KS) & 1;
-          if (!mbar_wait(&v_full[s], ph, abort_flag, a.st, 0x1212)) { ok_run = false; break; }
-          for (int t = 0; t < 2 && ok_run; ++t) {
-            if (j < n_of(t)) {
-              if (!mbar_wait(&p_full[t], j & 1, abort_flag, a.st, 0x1210 + t)) { ok_run = false; break; }
-              tc_fence_after();
-              issue_pv(t, j);
-            }
-          }
-          if (!ok_run) break;
-          umma_commit(&v_empty[s]);
-        }
-      }
-      // Every MMA this thread issued must be complete before TMEM is freed.
-      uint64_t* done = warp == 1 ? mma_done : mma_done + 1;
-      umma_commit(done);
-      DevStatus quiet = a.st;
-      quiet.word = nullptr;
-      mbar_wait(done, 0, never_flag, quiet, 0);
-    }
-  } else {
-    // ------------------------------------------------- softmax / epilogue --
-    setmaxnreg_inc<kRegsHigh>();
-    const int t = (warp - 4) >> 2;
-    const uint32_t q = warp & 3;
-    const int row = q * 32 + lane;
-    const int qrow = q0 + 128 * t + row;
-    const uint32_t lane_base = tmem + ((q * 32) << 16);
-    const int n_t = t ? ntile1 : ntile0;
-    const int h = bh % a.H;
-    const float* ttab = kBias == kBiasTable ? a.table + static_cast<int64_t>(h) * (2 * S - 1) : nullptr;
-    const int d0 = (qrow - lane) - 127 + S - 1;  // this warp's window start, block 0
-    float* tb_win = tb_base + q * 160;
-    float tpre[5];
-    if (kBias == kBiasTable && n_t > 0) table_window_load(tpre, ttab, d0, 2 * S - 1, static_cast<int>(lane));
-    const __half* brow = nullptr;
-    if (kBias == kBiasDense) brow = a.bias + bh * a.bias_head + static_cast<int64_t>(min(qrow, S - 1)) * a.bias_row;
-
-    const bool fast_path = a.qk_log2 > 0.f;
-    float m_used = -INFINITY;
-    float l = 0.f;
-    bool ok_run = true;
-    for (int j = 0; j < n_t; ++j) {
-      // Warp-uniform: every lane must agree before the .sync.aligned TMEM ops.
-      if (!__all_sync(0xffffffffu, mbar_wait(&s_full[t], j & 1, abort_flag, a.st, 0x1300 + t))) {
-        ok_run = false;
-        break;
-      }
-      tc_fence_after();
-      float z[128];
-      {
-        // Four TMEM loads in flight, one wait.
-        uint32_t r0[32], r1[32], r2[32], r3[32];
-        tmem_ld32(lane_base + Cfg::s_col(t) + 0, r0);
-        tmem_ld32(lane_base + Cfg::s_col(t) + 32, r1);
-        tmem_ld32(lane_base + Cfg::s_col(t) + 64, r2);
-        tmem_ld32(lane_base + Cfg::s_col(t) + 96, r3);
-        tmem_wait_ld();
-        if (!Cfg::kAliasP) {
-          // S_t(j) is in registers: the issuer may compute S_t(j+1) now.
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&s_free[t]);
-        }
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          z[i] = __uint_as_float(r0[i]);
-          z[32 + i] = __uint_as_float(r1[i]);
-          z[64 + i] = __uint_as_float(r2[i]);
-          z[96 + i] = __uint_as_float(r3[i]);
-        }
-      }
-      const int k0 = j * 128;
-      const bool edge = (k0 + 128 > S) || (kCausal && k0 + 127 > qrow);
-      // Without a bias and with a positive scale, max(s) * c = max(s * c): the
-      // row max is taken on the raw scores and each probability costs one FFMA
-      // + one ex2. Otherwise z holds the log2-domain logits.
-      const bool raw_scores = (kBias == kBiasNone) && fast_path;
-      if (kBias == kBiasDense) {
-        const uint64_t qk2 = f2_pack(a.qk_log2, a.qk_log2);
-#pragma unroll
-        for (int v = 0; v < 16; ++v) {
-          const int key = k0 + v * 8;
-          uint4 raw = make_uint4(0, 0, 0, 0);
-          if (key + 8 <= S) raw = __ldg(reinterpret_cast<const uint4*>(brow + key));
-          const __half2* hp = reinterpret_cast<const __half2*>(&raw);
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float2 f = __half22float2(hp[e]);
-            const uint64_t r2 = fmul2(fadd2(f2_pack(z[v * 8 + 2 * e], z[v * 8 + 2 * e + 1]), f2_pack(f.x, f.y)), qk2);
-            z[v * 8 + 2 * e] = f2_lo(r2);
-            z[v * 8 + 2 * e + 1] = f2_hi(r2);
-          }
-        }
-      } else if (kBias == kBiasTable) {
-        const float* trow = table_window_store(tb_win, tpre, static_cast<int>(lane));
-        if (j + 1 < n_t) table_window_load(tpre, ttab, d0 - 128 * (j + 1), 2 * S - 1, static_cast<int>(lane));
-        const uint64_t qk2 = f2_pack(a.qk_log2, a.qk_log2);
-#pragma unroll
-        for (int col = 0; col < 128; col += 2) {
-          const uint64_t r2 = ffma2(f2_pack(z[col], z[col + 1]), qk2, f2_pack(trow[-col], trow[-col - 1]));
-          z[col] = f2_lo(r2);
-          z[col + 1] = f2_hi(r2);
-        }
-      } else if (!raw_scores) {
-#pragma unroll
-        for (int col = 0; col < 128; ++col) z[col] *= a.qk_log2;
-      }
-      if (edge) {
-#pragma unroll
-        for (int col = 0; col < 128; ++col) {
-          const int key = k0 + col;
-          if (key >= S || (kCausal && key > qrow)) z[col] = -INFINITY;
-        }
-      }
-      // Row max, 8 independent chains of 3-input max.
-      float pm[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) pm[i] = fmaxf(z[i], z[8 + i]);
-#pragma unroll
-      for (int c = 16; c < 128; c += 16) {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) pm[i] = fmax3(pm[i], z[c + i], z[c + 8 + i]);
-      }
-      float rmax = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])),
-                         fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7])));
-      if (raw_scores) rmax *= a.qk_log2;
-      const float m_new = fmaxf(m_used, rmax);
-      const bool need = m_new > m_used + kRescaleThreshold;
-      float alpha = 1.f;
-      if (need) {
-        alpha = ex2_approx(m_used - m_new);
-        m_used = m_new;
-      }
-      const float neg_m = (m_used == -INFINITY) ? 0.f : -m_used;
-      const float zc = raw_scores ? a.qk_log2 : 1.f;
-      // Ping-pong on the exp unit: the two warps that share this SM
-      // sub-partition (same lane quarter q, tiles 0 and 1) take strict turns
-      // for their exp loops, tile 0 first. Everything else a tile does (TMEM
-      // traffic, row max, P store, its MMAs) then hides under the other
-      // tile's exps instead of both tiles stalling at the same time.
-      // Tile 0 block j waits for tile 1's block j-1 (when tile 1 exists);
-      // tile 1 block j waits for tile 0's block j (an existing tile 1 never
-      // has fewer blocks than tile 0).
-      const bool wait_turn = kT == 2 && ((t == 0) ? (j > 0 && ntile1 > 0) : (j < ntile0));
-      if (wait_turn) {
-        const uint32_t par = (t == 0) ? ((j - 1) & 1) : (j & 1);
-        if (!__all_sync(0xffffffffu, mbar_wait(&turn[t * 4 + q], par, abort_flag, a.st, 0x1340 + t))) {
-          ok_run = false;
-          break;
-        }
-      }
-      // p = 2^(z * zc - m), one ex2 per element, fp32 row sums in 8
-      // partials; the exponent arguments and the sums are formed two
-      // lanes per instruction (packed fp32 FMA / add).
-      float ps[8];
-      uint32_t pk[64];
-      const uint64_t zc2 = f2_pack(zc, zc);
-      const uint64_t nm2 = f2_pack(neg_m, neg_m);
-      uint64_t acc2[4] = {0ull, 0ull, 0ull, 0ull};
-#pragma unroll
-      for (int i = 0; i < 64; ++i) {
-        const uint64_t x2 = ffma2(f2_pack(z[2 * i], z[2 * i + 1]), zc2, nm2);
-        const float p0 = ex2_approx(f2_lo(x2));
-        const float p1 = ex2_approx(f2_hi(x2));
-        acc2[i & 3] = fadd2(acc2[i & 3], f2_pack(p0, p1));
-        pk[i] = pack_half2(p0, p1);
-      }
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        ps[2 * i] = f2_lo(acc2[i]);
-        ps[2 * i + 1] = f2_hi(acc2[i]);
-      }
-      const float sum = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
-      // Hand the exp unit to the partner warp of the other tile.
-      if (kT == 2) {
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&turn[(1 - t) * 4 + q]);
-      }
-      if (!Cfg::kAliasP && j > 0) {
-        // P_t and O_t are still in use by PV_t(j-1) until it completes.
-        if (!__all_sync(0xffffffffu, mbar_wait(&o_done[t], (j - 1) & 1, abort_flag, a.st, 0x1320 + t))) {
-          ok_run = false;
-          break;
-        }
-        tc_fence_after();
-      }
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t q16[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) q16[i] = pk[c * 16 + i];
-        tmem_st16(lane_base + Cfg::p_col(t) + c * 16, q16);
-      }
-      l = l * alpha + sum;
-      if (j > 0 && __any_sync(0xffffffffu, need)) {
-        // PV_t(j-1) is complete (waited on above, or implied by s_full when P
-        // aliases S).
-        uint32_t r[32];
-#pragma unroll 1
-        for (int c = 0; c < D / 32; ++c) {
-          tmem_ld32(lane_base + Cfg::o_col(t) + c * 32, r);
-          tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-          tmem_st32(lane_base + Cfg::o_col(t) + c * 32, r);
-        }
-      }
-      tmem_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[t]);
-    }
-    if (ok_run && n_t > 0 &&
-        __all_sync(0xffffffffu, mbar_wait(&o_done[t], (n_t - 1) & 1, abort_flag, a.st, 0x1310 + t))) {
-      tc_fence_after();
-      const float inv_l = 1.f / l;
-      if (kT == 1) {
-        // The K ring is idle once the last PV has completed: each warp stages
-        // its 32 rows (128 bytes of O per row and store, 128-byte swizzled)
-        // there and writes them with TMA stores; rows past S are clipped.
-        uint8_t* stage = sK + (warp - 4) * 4096;
-        const int row0 = q0 + static_cast<int>(q) * 32;
-        constexpr int kStores = D / 32;  // fp32: 32 columns per store; fp16: 64
-#pragma unroll 1
-        for (int c = 0; c < (a.out_f16 ? kStores / 2 : kStores); ++c) {
-          uint32_t w[32];
-          if (a.out_f16) {
-            uint32_t r0[32], r1[32];
-            tmem_ld32(lane_base + Cfg::o_col(t) + c * 64, r0);
-            tmem_ld32(lane_base + Cfg::o_col(t) + c * 64 + 32, r1);
-            tmem_wait_ld();
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              w[i] = pack_half2(__uint_as_float(r0[2 * i]) * inv_l, __uint_as_float(r0[2 * i + 1]) * inv_l);
-              w[16 + i] = pack_half2(__uint_as_float(r1[2 * i]) * inv_l, __uint_as_float(r1[2 * i + 1]) * inv_l);
-            }
-          } else {
-            uint32_t r[32];
-            tmem_ld32(lane_base + Cfg::o_col(t) + c * 32, r);
-            tmem_wait_ld();
-#pragma unroll
-            for (int i = 0; i < 32; ++i) w[i] = __float_as_uint(__uint_as_float(r[i]) * inv_l);
-          }
-          if (lane == 0) bulk_wait_read_all();  // the previous store has read the staging rows
-          __syncwarp();
-#pragma unroll
-          for (int v = 0; v < 8; ++v) {
-            *reinterpret_cast<uint4*>(stage + lane * 128 + ((v ^ (lane & 7)) << 4)) =
-                make_uint4(w[4 * v], w[4 * v + 1], w[4 * v + 2], w[4 * v + 3]);
-          }
-          fence_async_smem();
-          __syncwarp();
-          if (lane == 0 && row0 < S) {
-            tma_store_3d(&tmO, stage, c * (a.out_f16 ? 64 : 32), row0, bh);
-            bulk_commit();
-          }
-        }
-        if (lane == 0) bulk_wait_all();
-      } else {
-        const bool store = qrow < S;
-        uint32_t r[32];
-#pragma unroll 1
-        for (int c = 0; c < D / 32; ++c) {
-          tmem_ld32(lane_base + Cfg::o_col(t) + c * 32, r);
-          tmem_wait_ld();
-          if (store) {
-            if (a.out_f16) {
-              __half* orow = static_cast<__half*>(a.O) + bh * a.o_head + static_cast<int64_t>(qrow) * a.o_row + c * 32;
-#pragma unroll
-              for (int v = 0; v < 4; ++v) {
-                uint4 w;
-                w.x = pack_half2(__uint_as_float(r[8 * v + 0]) * inv_l, __uint_as_float(r[8 * v + 1]) * inv_l);
-                w.y = pack_half2(__uint_as_float(r[8 * v + 2]) * inv_l, __uint_as_float(r[8 * v + 3]) * inv_l);
-                w.z = pack_half2(__uint_as_float(r[8 * v + 4]) * inv_l, __uint_as_float(r[8 * v + 5]) * inv_l);
-                w.w = pack_half2(__uint_as_float(r[8 * v + 6]) * inv_l, __uint_as_float(r[8 * v + 7]) * inv_l);
-                *reinterpret_cast<uint4*>(orow + 8 * v) = w;
-              }
-            } else {
-              float* orow = static_cast<float*>(a.O) + bh * a.o_head + static_cast<int64_t>(qrow) * a.o_row + c * 32;
-#pragma unroll
-              for (int v = 0; v < 8; ++v) {
-                *reinterpret_cast<float4*>(orow + 4 * v) =
-                    make_float4(__uint_as_float(r[4 * v]) * inv_l, __uint_as_float(r[4 * v + 1]) * inv_l,
-                                __uint_as_float(r[4 * v + 2]) * inv_l, __uint_as_float(r[4 * v + 3]) * inv_l);
-              }
-            }
-          }
-        }
-      }
-    }
-  }
-
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 2) {
-    tc_fence_after();
-    tmem_dealloc(tmem, Cfg::kTmemCols);
-  }
-}
-
-// Query tiles one after the other in one CTA (same roles and TMEM layout as
-// the one-tile kernel). Causal: tiles bx and nq-1-bx of one head, so every
+// Query tiles one after the other in one CTA (the roles above, one tile's
+// TMEM layout). Causal: tiles bx and nq-1-bx of one head, so every
 // CTA has nq+1 key blocks (S=2048 494 -> 515 TFLOP/s, S=512 214 -> 231
 // against one tile per CTA). Non-causal: a persistent walk over the (head,
 // query tile) units, two CTAs per SM (B=H=16 D=64: S=512 364 -> 431,
