@@ -43,7 +43,11 @@ struct GemmCfg {
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kAccBufs = MH == 2 ? 1 : 2;
   static constexpr int kTmemCols = kAccBufs * MH * BN;
-  static constexpr int kOutBytes = 4 * MH * 4096;  // C staging: 32 rows x 32 fp32 per epilogue warp
+  // C staging: 32 rows x 32 fp32 per epilogue warp, double-buffered for
+  // 128-row tiles (a store of one block overlaps loading the next), single
+  // for 256 x 256 tiles, whose stages fill the rest of shared memory.
+  static constexpr int kOutBufs = MH == 1 ? 2 : 1;
+  static constexpr int kOutBytes = 4 * MH * 4096 * kOutBufs;
   static constexpr int kSmemBytes = kStages * kStageBytes + kOutBytes + 1024 /*align*/ + 256 /*barriers*/;
 };
 
@@ -78,7 +82,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, MH>::kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;                       // S x MH x 16 KB
   uint8_t* sB = smem + S * Cfg::kABytes;    // S x (BN/64) x 8 KB
-  uint8_t* sOut = smem + S * Cfg::kStageBytes;  // 4 KB per epilogue warp
+  uint8_t* sOut = smem + S * Cfg::kStageBytes;  // 4 KB per epilogue warp and staging buffer
   uint64_t* bars = reinterpret_cast<uint64_t*>(sOut + Cfg::kOutBytes);
   uint64_t* full = bars;                    // [S]
   uint64_t* empty = bars + S;               // [S]
@@ -219,10 +223,10 @@ __global__ void __launch_bounds__(GemmCfg<BN, MH>::kThreads, 1)
         // TMEM -> registers -> this warp's 128-byte-swizzled staging rows ->
         // one TMA store per 32 x 32 block: full-line writes, and the
         // accumulator is released as soon as its last columns are loaded.
-        uint8_t* stage = sOut + (warp - 4) * 4096;
         const int row0 = mb * Cfg::kTileM + h * kBM + q * 32;
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
+          uint8_t* stage = sOut + ((warp - 4) * Cfg::kOutBufs + (c % Cfg::kOutBufs)) * 4096;
           uint32_t r[32];
           tmem_ld32(tmem_base + ((q * 32) << 16) + (buf * MH + h) * BN + c * 32, r);
           tmem_wait_ld();
@@ -231,7 +235,15 @@ __global__ void __launch_bounds__(GemmCfg<BN, MH>::kThreads, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(&acc_empty[buf]);
           }
-          if (lane == 0) bulk_wait_read_all();  // the previous store has read the staging rows
+          // The store that last used this staging block has read it (with two
+          // blocks, the previous block's store may still be reading the other).
+          if (lane == 0) {
+            if (Cfg::kOutBufs == 2) {
+              bulk_wait_read_but1();
+            } else {
+              bulk_wait_read_all();
+            }
+          }
           __syncwarp();
 #pragma unroll
           for (int v = 0; v < 8; ++v) {
