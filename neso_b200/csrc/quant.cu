@@ -107,9 +107,16 @@ struct QCfg {
   // F ring (same depth, released by the same commit; deeper X rings measured
   // no faster at M = 16).
   static constexpr int kXStages = kSwap ? kFStages : kRowHalves == 2 ? 3 : kNT == 2 ? (kQ == kInt8 ? 4 : 3) : 6;
-  static constexpr int kBudget = 220 * 1024;
-  // Y staging for TMA stores (M >= 65 layout): 16 rows x 32 fp32 per epilogue warp.
-  static constexpr int kOutBytes = kSwap ? 0 : 4 * 2048;
+  static constexpr int kBudget = 224 * 1024;
+  // Y staging for TMA stores (M >= 65 layout): 16 rows x 32 fp32 per epilogue
+  // warp, two blocks (one store's read overlaps filling the next) where the
+  // raw ring keeps its minimum depth.
+  static constexpr int kMinRStages = kNT == 2 ? 3 : 4;
+  static constexpr int kOutBufs =
+      (kBudget - 4 * 2048 * 2 - kScSlots * kScBytes - kFStages * kFBytes - kXStages * kXBytes) / kRawBytes >= kMinRStages
+          ? 2
+          : 1;
+  static constexpr int kOutBytes = kSwap ? 0 : 4 * 2048 * kOutBufs;
   static constexpr int kRStagesFit =
       (kBudget - kOutBytes - kScSlots * kScBytes - kFStages * kFBytes - kXStages * kXBytes) / kRawBytes;
   static constexpr int kRStages = kRStagesFit > 16 ? 16 : kRStagesFit;
@@ -126,7 +133,7 @@ struct QCfg {
   static constexpr int kTmemCols = (kAccBufs * kAccCols <= 32) ? 32 : (kAccBufs * kAccCols <= 64) ? 64
                                    : (kAccBufs * kAccCols <= 128) ? 128 : (kAccBufs * kAccCols <= 256) ? 256 : 512;
   static constexpr int kSmemBytes = kOffBars + 1024 + 1024;
-  static_assert(kRStages >= (kNT == 2 ? 3 : 4), "raw ring too shallow");
+  static_assert(kRStages >= kMinRStages, "raw ring too shallow");
   static_assert(kXBytes % 1024 == 0 && kRawBytes % 1024 == 0 && kFBytes % 1024 == 0, "1024-aligned stages");
 };
 
@@ -739,6 +746,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     } else {
     int tc = 0;
+    int y_commits = 0;  // TMA stores this warp committed (staging block parity)
     for (int t = blockIdx.x; t < num_units; t += gridDim.x, ++tc) {
       const QUnit u = unit_of(t, args);
       const int mb = u.mb;
@@ -785,7 +793,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // Rows of 32 channels through 128-byte-swizzled staging (16 rows at a
         // time) and TMA stores: full-line writes instead of one 4-byte store
         // per row and channel, which left the L1 busy with the epilogue.
-        uint8_t* stage = smem + Cfg::kOffOut + (warp - 8) * 2048;
+        uint8_t* stage0 = smem + Cfg::kOffOut + (warp - 8) * 2048 * Cfg::kOutBufs;
 #pragma unroll 1
         for (int hc = 0; hc < Cfg::kRowHalves * (kUnitN / 32); ++hc) {
           const int h = hc / (kUnitN / 32), c = hc % (kUnitN / 32);
@@ -807,7 +815,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
 #pragma unroll
           for (int half = 0; half < 2; ++half) {
-            if (lane == 0) bulk_wait_read_all();  // the previous store has read the staging rows
+            // Two blocks: write the one the latest committed store did not
+            // use, once every older store has read its block.
+            uint8_t* stage = stage0 + (Cfg::kOutBufs == 2 ? (y_commits & 1) * 2048 : 0);
+            if (lane == 0) {
+              if (Cfg::kOutBufs == 2) {
+                bulk_wait_read_but1();
+              } else {
+                bulk_wait_read_all();
+              }
+            }
             __syncwarp();
             if ((lane >> 4) == static_cast<uint32_t>(half)) {
               const uint32_t row = lane & 15;
@@ -819,9 +836,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             fence_async_smem();
             __syncwarp();
-            if (lane == 0 && m0 + 16 * half < args.M && n0 < args.N) {
-              tma_store_3d(&tmY, stage, n0, m0 + 16 * half, args.partial != nullptr ? u.ks : 0);
-              bulk_commit();
+            if (m0 + 16 * half < args.M && n0 < args.N) {  // warp-uniform
+              if (lane == 0) {
+                tma_store_3d(&tmY, stage, n0, m0 + 16 * half, args.partial != nullptr ? u.ks : 0);
+                bulk_commit();
+              }
+              ++y_commits;
             }
           }
         }
