@@ -224,3 +224,24 @@ def test_device_status_clean_after_runs(dev):
     rc = _lib.lib().neso_device_status(0, None, None, None, None)
     assert rc == _lib.NESO_OK, _lib.last_error()
 
+
+
+def test_dependent_launches_read_the_previous_output(dev):
+    # The kernels are launched with programmatic dependent launch: the next
+    # kernel's CTAs may start while the previous kernel finishes, and must not
+    # read its output before it is complete. A chain of fp16 MSL-entry calls on
+    # one stream, each taking the previous output as Q, with no host sync in
+    # between; every step is checked against the oracle applied to the
+    # previous step's output as the GPU wrote it.
+    N, d, steps = 4096, 64, 4
+    q, k, v = _msl_inputs(N, d)
+    sc = 1.0 / math.sqrt(d)
+    kd, vd = k.half().to(dev), v.half().to(dev)
+    outs = [q.half().to(dev)] + [torch.empty(N, d, dtype=torch.float16, device=dev) for _ in range(steps)]
+    for i in range(steps):
+        kernels.flash_attention_fwd_msl[(N // 32, 1, 1)](outs[i], kd, vd, outs[i + 1], N, d, sc, BM=32, BN=32)
+    torch.cuda.synchronize(dev)
+    kc, vc = kd.cpu(), vd.cpu()
+    for i in range(steps):
+        ref = oracle.attention(outs[i].cpu(), kc, vc, sc)
+        torch.testing.assert_close(outs[i + 1].float().cpu(), ref, **TOL)
