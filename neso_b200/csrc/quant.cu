@@ -509,58 +509,110 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         const int fs = it % FS;
         for (int b = 0; b < nkb; ++b, ++ri) {
-        const int rs = ri % RS;
-        if (!mbar_wait(&r_full[rs], (ri / RS) & 1, abort_flag, args.st, 0x2300)) { ok_run = false; break; }
-        constexpr int GT = Cfg::kGroupTiles;
-        const uint8_t* raw = sR + rs * Cfg::kRawBytes + (Cfg::kAltStages ? 0 : grp * Cfg::kRawTileBytes);
-        uint8_t* w16 = sF + fs * Cfg::kFBytes + b * Cfg::kW16BlockBytes + (Cfg::kAltStages ? 0 : grp * Cfg::kW16Bytes);
-        if (kQ == kInt8) {
-          // thread -> (k row r, n half h); raw unit u of row r sits at unit u ^ (r & 7).
-          // Each group of 8 consecutive threads takes 8 consecutive rows of one
-          // half, so its 16-byte accesses fall in 8 different bank groups.
-          const int r = (ct & 7) + 8 * (ct >> 4);
-          const int h = (ct >> 3) & 1;
-          const int sw = r & 7;
-          uint4 o[GT][8];
-#pragma unroll
-          for (int g = 0; g < GT; ++g) {
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const uint4 rv = *reinterpret_cast<const uint4*>(raw + g * Cfg::kRawTileBytes + r * 128 +
-                                                               (((4 * h + i) ^ sw) << 4));
-              dequant_i8x16(rv, o[g][2 * i], o[g][2 * i + 1]);
-            }
-          }
-          // The raw slot is released only once its bytes have been consumed
-          // into registers (the dequantised values depend on them): a release
-          // right after issuing the loads lets the next TMA write overtake
-          // loads that have not been performed yet.
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&r_empty[rs]);
-          if (b == 0 && !mbar_wait(&f_empty[fs], ((it / FS) & 1) ^ 1, abort_flag, args.st, 0x2301)) {
-            ok_run = false;
-            break;
-          }
-#pragma unroll
-          for (int g = 0; g < GT; ++g) {
-            uint8_t* dst = w16 + g * Cfg::kW16Bytes + h * 8192 + r * 128;
-#pragma unroll
-            for (int i = 0; i < 8; ++i) *reinterpret_cast<uint4*>(dst + ((i ^ sw) << 4)) = o[g][i];
-          }
-        } else {
-          if constexpr (Cfg::kGS) {
-            // thread -> (byte row kk: k rows 2kk and 2kk+1, n quarter qn: 32 channels)
-            const int kk = ct >> 2;
-            const int qn = ct & 3;
-            const int swr = kk & 7;
-            const __half2 b8 = __float2half2_rn(1032.f);  // 1024 + 8
-            uint32_t hv[GT][2][2][8];  // [tile][raw unit i][row r0/r1][16 channels as 8 half2]
+          const int rs = ri % RS;
+          if (!mbar_wait(&r_full[rs], (ri / RS) & 1, abort_flag, args.st, 0x2300)) { ok_run = false; break; }
+          constexpr int GT = Cfg::kGroupTiles;
+          const uint8_t* raw = sR + rs * Cfg::kRawBytes + (Cfg::kAltStages ? 0 : grp * Cfg::kRawTileBytes);
+          uint8_t* w16 = sF + fs * Cfg::kFBytes + b * Cfg::kW16BlockBytes + (Cfg::kAltStages ? 0 : grp * Cfg::kW16Bytes);
+          if (kQ == kInt8) {
+            // thread -> (k row r, n half h); raw unit u of row r sits at unit u ^ (r & 7).
+            // Each group of 8 consecutive threads takes 8 consecutive rows of one
+            // half, so its 16-byte accesses fall in 8 different bank groups.
+            const int r = (ct & 7) + 8 * (ct >> 4);
+            const int h = (ct >> 3) & 1;
+            const int sw = r & 7;
+            uint4 o[GT][8];
 #pragma unroll
             for (int g = 0; g < GT; ++g) {
 #pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const uint4 rv = *reinterpret_cast<const uint4*>(raw + g * Cfg::kRawTileBytes + r * 128 +
+                                                                 (((4 * h + i) ^ sw) << 4));
+                dequant_i8x16(rv, o[g][2 * i], o[g][2 * i + 1]);
+              }
+            }
+            // The raw slot is released only once its bytes have been consumed
+            // into registers (the dequantised values depend on them): a release
+            // right after issuing the loads lets the next TMA write overtake
+            // loads that have not been performed yet.
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&r_empty[rs]);
+            if (b == 0 && !mbar_wait(&f_empty[fs], ((it / FS) & 1) ^ 1, abort_flag, args.st, 0x2301)) {
+              ok_run = false;
+              break;
+            }
+#pragma unroll
+            for (int g = 0; g < GT; ++g) {
+              uint8_t* dst = w16 + g * Cfg::kW16Bytes + h * 8192 + r * 128;
+#pragma unroll
+              for (int i = 0; i < 8; ++i) *reinterpret_cast<uint4*>(dst + ((i ^ sw) << 4)) = o[g][i];
+            }
+          } else {
+            if constexpr (Cfg::kGS) {
+              // thread -> (byte row kk: k rows 2kk and 2kk+1, n quarter qn: 32 channels)
+              const int kk = ct >> 2;
+              const int qn = ct & 3;
+              const int swr = kk & 7;
+              const __half2 b8 = __float2half2_rn(1032.f);  // 1024 + 8
+              uint32_t hv[GT][2][2][8];  // [tile][raw unit i][row r0/r1][16 channels as 8 half2]
+#pragma unroll
+              for (int g = 0; g < GT; ++g) {
+#pragma unroll
+                for (int i = 0; i < 2; ++i) {
+                  const uint4 rv = *reinterpret_cast<const uint4*>(raw + g * Cfg::kRawTileBytes + kk * 128 +
+                                                                   (((2 * qn + i) ^ swr) << 4));
+                  const uint32_t words[4] = {rv.x, rv.y, rv.z, rv.w};
+#pragma unroll
+                  for (int wdx = 0; wdx < 4; ++wdx) {
+                    const uint32_t lo_n = (words[wdx] & 0x0F0F0F0Fu) ^ 0x08080808u;         // k even
+                    const uint32_t hi_n = ((words[wdx] >> 4) & 0x0F0F0F0Fu) ^ 0x08080808u;  // k odd
+#pragma unroll
+                    for (int half_sel = 0; half_sel < 2; ++half_sel) {
+                      const uint32_t sel = half_sel ? 0x7362u : 0x5140u;
+                      hv[g][i][0][wdx * 2 + half_sel] = h2_as_u32(__hsub2(u32_as_h2(bytes_to_h2(lo_n, sel)), b8));
+                      hv[g][i][1][wdx * 2 + half_sel] = h2_as_u32(__hsub2(u32_as_h2(bytes_to_h2(hi_n, sel)), b8));
+                    }
+                  }
+                }
+              }
+              // Release the raw slot only after its bytes are consumed (see int8).
+              __syncwarp();
+              if (lane == 0) mbar_arrive(&r_empty[rs]);
+              if (b == 0 && !mbar_wait(&f_empty[fs], ((it / FS) & 1) ^ 1, abort_flag, args.st, 0x2301)) {
+              ok_run = false;
+              break;
+            }
+              const int chunk = qn >> 1;
+#pragma unroll
+              for (int g = 0; g < GT; ++g) {
+#pragma unroll
+                for (int i = 0; i < 2; ++i) {
+                  // 16 channels = two fp16 units; column within the chunk = 32 (qn & 1) + 16 i
+                  const int v0 = 4 * (qn & 1) + 2 * i;
+#pragma unroll
+                  for (int rr = 0; rr < 2; ++rr) {
+                    const int row = 2 * kk + rr;
+#pragma unroll
+                    for (int e = 0; e < 2; ++e) {
+                      const int off = g * Cfg::kW16Bytes + chunk * 8192 + row * 128 + (((v0 + e) ^ (row & 7)) << 4);
+                      *reinterpret_cast<uint4*>(w16 + off) =
+                          make_uint4(hv[g][i][rr][4 * e], hv[g][i][rr][4 * e + 1], hv[g][i][rr][4 * e + 2],
+                                     hv[g][i][rr][4 * e + 3]);
+                    }
+                  }
+                }
+              }
+            } else {
+              // thread -> (byte row kk: k rows 2kk and 2kk+1, n quarter qn: 32 channels)
+              const int kk = ct >> 2;
+              const int qn = ct & 3;
+              const int swr = kk & 7;
+              const __half* sc = reinterpret_cast<const __half*>(raw + 4096) + qn * 32;
+              const __half2 b8 = __float2half2_rn(1032.f);  // 1024 + 8
+              uint32_t hv[2][2][8], lv[2][2][8];  // [raw unit i][row r0/r1][16 channels as 8 half2]
+#pragma unroll
               for (int i = 0; i < 2; ++i) {
-                const uint4 rv = *reinterpret_cast<const uint4*>(raw + g * Cfg::kRawTileBytes + kk * 128 +
-                                                                 (((2 * qn + i) ^ swr) << 4));
+                const uint4 rv = *reinterpret_cast<const uint4*>(raw + kk * 128 + (((2 * qn + i) ^ swr) << 4));
                 const uint32_t words[4] = {rv.x, rv.y, rv.z, rv.w};
 #pragma unroll
                 for (int wdx = 0; wdx < 4; ++wdx) {
@@ -569,22 +621,28 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                   for (int half_sel = 0; half_sel < 2; ++half_sel) {
                     const uint32_t sel = half_sel ? 0x7362u : 0x5140u;
-                    hv[g][i][0][wdx * 2 + half_sel] = h2_as_u32(__hsub2(u32_as_h2(bytes_to_h2(lo_n, sel)), b8));
-                    hv[g][i][1][wdx * 2 + half_sel] = h2_as_u32(__hsub2(u32_as_h2(bytes_to_h2(hi_n, sel)), b8));
+                    const __half2 s2 = *reinterpret_cast<const __half2*>(sc + 16 * i + 4 * wdx + 2 * half_sel);
+                    const __half2 q0 = __hsub2(u32_as_h2(bytes_to_h2(lo_n, sel)), b8);
+                    const __half2 q1 = __hsub2(u32_as_h2(bytes_to_h2(hi_n, sel)), b8);
+                    const __half2 w0h = __hmul2(q0, s2);
+                    const __half2 w1h = __hmul2(q1, s2);
+                    hv[i][0][wdx * 2 + half_sel] = h2_as_u32(w0h);
+                    lv[i][0][wdx * 2 + half_sel] = h2_as_u32(__hfma2(q0, s2, __hneg2(w0h)));
+                    hv[i][1][wdx * 2 + half_sel] = h2_as_u32(w1h);
+                    lv[i][1][wdx * 2 + half_sel] = h2_as_u32(__hfma2(q1, s2, __hneg2(w1h)));
                   }
                 }
               }
+              // Release the raw slot only after its bytes are consumed (see int8).
+              __syncwarp();
+              if (lane == 0) mbar_arrive(&r_empty[rs]);
+              if (b == 0 && !mbar_wait(&f_empty[fs], ((it / FS) & 1) ^ 1, abort_flag, args.st, 0x2301)) {
+              ok_run = false;
+              break;
             }
-            // Release the raw slot only after its bytes are consumed (see int8).
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&r_empty[rs]);
-            if (b == 0 && !mbar_wait(&f_empty[fs], ((it / FS) & 1) ^ 1, abort_flag, args.st, 0x2301)) {
-            ok_run = false;
-            break;
-          }
-            const int chunk = qn >> 1;
-#pragma unroll
-            for (int g = 0; g < GT; ++g) {
+              uint8_t* hi = w16;
+              uint8_t* lo = w16 + kNT * Cfg::kW16Bytes;
+              const int chunk = qn >> 1;
 #pragma unroll
               for (int i = 0; i < 2; ++i) {
                 // 16 channels = two fp16 units; column within the chunk = 32 (qn & 1) + 16 i
@@ -594,74 +652,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                   const int row = 2 * kk + rr;
 #pragma unroll
                   for (int e = 0; e < 2; ++e) {
-                    const int off = g * Cfg::kW16Bytes + chunk * 8192 + row * 128 + (((v0 + e) ^ (row & 7)) << 4);
-                    *reinterpret_cast<uint4*>(w16 + off) =
-                        make_uint4(hv[g][i][rr][4 * e], hv[g][i][rr][4 * e + 1], hv[g][i][rr][4 * e + 2],
-                                   hv[g][i][rr][4 * e + 3]);
+                    const int off = chunk * 8192 + row * 128 + (((v0 + e) ^ (row & 7)) << 4);
+                    *reinterpret_cast<uint4*>(hi + off) = make_uint4(hv[i][rr][4 * e], hv[i][rr][4 * e + 1],
+                                                                     hv[i][rr][4 * e + 2], hv[i][rr][4 * e + 3]);
+                    *reinterpret_cast<uint4*>(lo + off) = make_uint4(lv[i][rr][4 * e], lv[i][rr][4 * e + 1],
+                                                                     lv[i][rr][4 * e + 2], lv[i][rr][4 * e + 3]);
                   }
                 }
               }
             }
-          } else {
-            // thread -> (byte row kk: k rows 2kk and 2kk+1, n quarter qn: 32 channels)
-            const int kk = ct >> 2;
-            const int qn = ct & 3;
-            const int swr = kk & 7;
-            const __half* sc = reinterpret_cast<const __half*>(raw + 4096) + qn * 32;
-            const __half2 b8 = __float2half2_rn(1032.f);  // 1024 + 8
-            uint32_t hv[2][2][8], lv[2][2][8];  // [raw unit i][row r0/r1][16 channels as 8 half2]
-#pragma unroll
-            for (int i = 0; i < 2; ++i) {
-              const uint4 rv = *reinterpret_cast<const uint4*>(raw + kk * 128 + (((2 * qn + i) ^ swr) << 4));
-              const uint32_t words[4] = {rv.x, rv.y, rv.z, rv.w};
-#pragma unroll
-              for (int wdx = 0; wdx < 4; ++wdx) {
-                const uint32_t lo_n = (words[wdx] & 0x0F0F0F0Fu) ^ 0x08080808u;         // k even
-                const uint32_t hi_n = ((words[wdx] >> 4) & 0x0F0F0F0Fu) ^ 0x08080808u;  // k odd
-#pragma unroll
-                for (int half_sel = 0; half_sel < 2; ++half_sel) {
-                  const uint32_t sel = half_sel ? 0x7362u : 0x5140u;
-                  const __half2 s2 = *reinterpret_cast<const __half2*>(sc + 16 * i + 4 * wdx + 2 * half_sel);
-                  const __half2 q0 = __hsub2(u32_as_h2(bytes_to_h2(lo_n, sel)), b8);
-                  const __half2 q1 = __hsub2(u32_as_h2(bytes_to_h2(hi_n, sel)), b8);
-                  const __half2 w0h = __hmul2(q0, s2);
-                  const __half2 w1h = __hmul2(q1, s2);
-                  hv[i][0][wdx * 2 + half_sel] = h2_as_u32(w0h);
-                  lv[i][0][wdx * 2 + half_sel] = h2_as_u32(__hfma2(q0, s2, __hneg2(w0h)));
-                  hv[i][1][wdx * 2 + half_sel] = h2_as_u32(w1h);
-                  lv[i][1][wdx * 2 + half_sel] = h2_as_u32(__hfma2(q1, s2, __hneg2(w1h)));
-                }
-              }
-            }
-            // Release the raw slot only after its bytes are consumed (see int8).
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&r_empty[rs]);
-            if (b == 0 && !mbar_wait(&f_empty[fs], ((it / FS) & 1) ^ 1, abort_flag, args.st, 0x2301)) {
-            ok_run = false;
-            break;
           }
-            uint8_t* hi = w16;
-            uint8_t* lo = w16 + kNT * Cfg::kW16Bytes;
-            const int chunk = qn >> 1;
-#pragma unroll
-            for (int i = 0; i < 2; ++i) {
-              // 16 channels = two fp16 units; column within the chunk = 32 (qn & 1) + 16 i
-              const int v0 = 4 * (qn & 1) + 2 * i;
-#pragma unroll
-              for (int rr = 0; rr < 2; ++rr) {
-                const int row = 2 * kk + rr;
-#pragma unroll
-                for (int e = 0; e < 2; ++e) {
-                  const int off = chunk * 8192 + row * 128 + (((v0 + e) ^ (row & 7)) << 4);
-                  *reinterpret_cast<uint4*>(hi + off) = make_uint4(hv[i][rr][4 * e], hv[i][rr][4 * e + 1],
-                                                                   hv[i][rr][4 * e + 2], hv[i][rr][4 * e + 3]);
-                  *reinterpret_cast<uint4*>(lo + off) = make_uint4(lv[i][rr][4 * e], lv[i][rr][4 * e + 1],
-                                                                   lv[i][rr][4 * e + 2], lv[i][rr][4 * e + 3]);
-                }
-              }
-            }
-          }
-        }
         }
         if (!ok_run) break;
         fence_async_smem();
