@@ -1,6 +1,7 @@
 """Run one kernel of the library on synthetic inputs, for profiling and timing.
 
     python -m neso_b200.cases fa2 --B 16 --H 16 --S 2048 --D 64 [--causal] [--iters 5]
+    python -m neso_b200.cases relpos --H 64 --S 2048 --D 64      (rel_pos_fa2_fwd, dense fp16 bias)
     python -m neso_b200.cases gemm --M 4096 --N 4096 --K 4096
     python -m neso_b200.cases w8a16 --M 1 --N 11008 --K 4096
     python -m neso_b200.cases w4a16 --M 2048 --N 11008 --K 4096
@@ -75,7 +76,7 @@ def _time_graph(fn, warmup: int, iters: int) -> float:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["fa2", "gemm", "w8a16", "w4a16", "vector_add", "scale"])
+    ap.add_argument("case", choices=["fa2", "relpos", "gemm", "w8a16", "w4a16", "vector_add", "scale"])
     ap.add_argument("--B", type=int, default=16)
     ap.add_argument("--H", type=int, default=16)
     ap.add_argument("--S", type=int, default=2048)
@@ -106,6 +107,20 @@ def main() -> None:
                                                 out=o), a.warmup, a.iters)
         flops = 4.0 * a.B * a.H * a.S * a.S * a.D / (2 if a.causal else 1)
         res.update(shape=[a.B, a.H, a.S, a.D], causal=a.causal, table=a.table, us=t * 1e6, tflops=flops / t / 1e12)
+    elif a.case == "relpos":
+        from . import kernels
+        nh, T, d = a.H, a.S, a.D
+        sets = [(tuple(torch.randn(nh, T, d, device=dev, generator=g).half() for _ in range(3)),
+                 (0.5 * torch.randn(nh, T, T, device=dev, generator=g)).half())
+                for _ in range(_copies(2 * nh * T * T + 8 * nh * T * d))]
+        o = torch.empty(nh, T, d, dtype=torch.float16, device=dev)
+        bm = next(b for b in (128, 64, 32, 16, 8) if T % b == 0)
+        launch = kernels.rel_pos_fa2_fwd[(T // bm, nh, 1)]
+        n = len(sets)
+        t = _time(lambda i: launch(*sets[i % n][0], sets[i % n][1], o, T, d, 1 / math.sqrt(d), T * d, T * T),
+                  a.warmup, a.iters)
+        res.update(shape=[nh, T, d], us=t * 1e6, tflops=4.0 * nh * T * T * d / t / 1e12,
+                   bias_gbs=2.0 * nh * T * T / t / 1e9)
     elif a.case == "gemm":
         x = (torch.randn(a.M, a.K, device=dev, generator=g) / math.sqrt(a.K)).half()
         w = (torch.randn(a.K, a.N, device=dev, generator=g) / math.sqrt(a.K)).half()

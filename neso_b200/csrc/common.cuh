@@ -25,6 +25,7 @@ namespace neso {
 enum DeviceError : int {
   kDevOk = 0,
   kDevWaitTimeout = 1,  // a bounded mbarrier wait ran out of budget
+  kDevSmemMisaligned = 2,  // dynamic shared memory base not 1024-byte aligned
 };
 
 // Wait budget for a single mbarrier wait. A healthy wait in these kernels is

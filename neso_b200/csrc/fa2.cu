@@ -130,6 +130,19 @@ struct FaCfg {
       (kT * kQBuffers + 2 * kStages) * kTileBytes + kOutBytes + kTableBytes + 1024 + 512;
 };
 
+// Dynamic shared memory of the one-tile kernel: Q, the K/V ring, one block
+// per softmax warp, the table windows and the barriers. The softmax warp's
+// block is its 4 KB O staging, or with a dense bias 8 KB that hold its 32 rows
+// of the next key block's bias (two 64-key TMA boxes) and, in its first 4 KB,
+// the O staging. Two such CTAs fill an SM's 228 KB only without the 1 KB of
+// alignment slack, so the dense-bias kernel checks its base instead.
+template <int D, int kBias>
+constexpr int pair_smem_bytes() {
+  using Cfg = FaCfg<D, 1>;
+  return kBias == kBiasDense ? (1 + 2 * Cfg::kStages) * Cfg::kTileBytes + 4 * 8192 + 512
+                             : Cfg::kSmemBytes + 4 * 4096;
+}
+
 struct FaArgs {
   void* O;
   int64_t o_row;   // elements
@@ -167,18 +180,29 @@ template <int D, bool kCausal, int kBias>
 __global__ void __launch_bounds__(FaCfg<D, 1>::kThreads, 2)
     fa2_pair_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
-                    FaArgs a) {
+                    const __grid_constant__ CUtensorMap tmB, FaArgs a) {
   using Cfg = FaCfg<D, 1>;
   constexpr int kT = 1;
   constexpr int KS = Cfg::kStages;
+  constexpr bool kBiasTma = kBias == kBiasDense;
+  constexpr int kWarpBytes = kBiasTma ? 8192 : 4096;  // per softmax warp, see pair_smem_bytes
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  if constexpr (kBiasTma) {
+    // No alignment slack in this layout (see pair_smem_bytes).
+    if ((smem_u32(smem_raw) & 1023u) != 0) {
+      if (threadIdx.x == 0) record_error(a.st, kDevSmemMisaligned, 0x13f0);
+      return;
+    }
+  }
+  uint8_t* smem = kBiasTma ? smem_raw
+                           : reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                                        ~uintptr_t(1023));
   uint8_t* sQ = smem;
   uint8_t* sK = sQ + Cfg::kTileBytes;                // KS tiles
   uint8_t* sV = sK + KS * Cfg::kTileBytes;           // KS tiles
-  uint8_t* sOut = sV + KS * Cfg::kTileBytes;         // 4 KB per softmax warp
-  float* tb_base = reinterpret_cast<float*>(sOut + 4 * 4096);  // table windows
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sOut + 4 * 4096 + Cfg::kTableBytes);
+  uint8_t* sOut = sV + KS * Cfg::kTileBytes;         // kWarpBytes per softmax warp
+  float* tb_base = reinterpret_cast<float*>(sOut + 4 * kWarpBytes);  // table windows
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sOut + 4 * kWarpBytes + (kBiasTma ? 0 : Cfg::kTableBytes));
   uint64_t* q_full = bars;
   uint64_t* q_empty = bars + 1;
   uint64_t* k_full = bars + 2;
@@ -191,7 +215,7 @@ __global__ void __launch_bounds__(FaCfg<D, 1>::kThreads, 2)
   uint64_t* s_free = o_done + 1;     // [1] softmax has read S (4 warps)
   uint64_t* o_free = s_free + 1;     // [1] epilogue has read O (4 warps)
   uint64_t* mma_done = o_free + 1;   // [2] one per MMA issuer
-  uint64_t* turn = mma_done + 2;     // unused (one tile at a time)
+  uint64_t* turn = mma_done + 2;     // [4] dense bias of softmax warp q arrived (no exp turns here)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(turn + 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* never_flag = abort_flag + 1;  // stays 0: drain waits ignore the abort
@@ -232,6 +256,9 @@ __global__ void __launch_bounds__(FaCfg<D, 1>::kThreads, 2)
     mbar_init(o_free, 4);
     mbar_init(&mma_done[0], 1);
     mbar_init(&mma_done[1], 1);
+    if (kBiasTma) {
+      for (int i = 0; i < 4; ++i) mbar_init(&turn[i], 1);
+    }
     *abort_flag = 0;
     *never_flag = 0;
     fence_mbar_init();
@@ -239,6 +266,7 @@ __global__ void __launch_bounds__(FaCfg<D, 1>::kThreads, 2)
     tma_prefetch_desc(&tmK);
     tma_prefetch_desc(&tmV);
     tma_prefetch_desc(&tmO);
+    if (kBiasTma) tma_prefetch_desc(&tmB);
   }
   if (warp == 2) {
     tmem_alloc(tmem_slot, Cfg::kTmemCols);
@@ -370,7 +398,20 @@ __global__ void __launch_bounds__(FaCfg<D, 1>::kThreads, 2)
     (void)ntile1;
     bool ok_run = true;
     int g = 0;
-    uint8_t* stage = sOut + (warp - 4) * 4096;
+    uint8_t* stage = sOut + (warp - 4) * kWarpBytes;
+    // Dense bias: lane 0 requests the warp's 32 rows x 128 keys of key block
+    // j of tile qt one block ahead, two 64-key boxes into `stage` (the
+    // previous block's values are in registers by then).
+    uint64_t* bias_full = &turn[q];
+    int b_issued = 0;
+    auto bias_issue = [&](int qt_, int j_) {
+      const int y = tile_qb(qt_) * 128 + static_cast<int>(q) * 32;
+      mbar_arrive_expect_tx(bias_full, 8192);
+      tma_load_3d(stage, &tmB, bias_full, j_ * 128, y, tile_bh(qt_));
+      tma_load_3d(stage + 4096, &tmB, bias_full, j_ * 128 + 64, y, tile_bh(qt_));
+      ++b_issued;
+    };
+    if (kBiasTma && lane == 0 && ntiles > 0) bias_issue(0, 0);
     for (int qt = 0; qt < ntiles && ok_run; ++qt) {
       const int q0 = tile_qb(qt) * 128;
       const int bh = tile_bh(qt);
@@ -382,8 +423,6 @@ __global__ void __launch_bounds__(FaCfg<D, 1>::kThreads, 2)
       float* tb_win = tb_base + q * 160;
       float tpre[5];
       if (kBias == kBiasTable) table_window_load(tpre, ttab, d0, 2 * S - 1, static_cast<int>(lane));
-      const __half* brow = nullptr;
-      if (kBias == kBiasDense) brow = a.bias + bh * a.bias_head + static_cast<int64_t>(min(qrow, S - 1)) * a.bias_row;
       float m_used = -INFINITY;
       float l = 0.f;
       for (int j = 0; j < n_t; ++j, ++g) {
@@ -423,12 +462,17 @@ __global__ void __launch_bounds__(FaCfg<D, 1>::kThreads, 2)
         // + one ex2. Otherwise z holds the log2-domain logits.
         const bool raw_scores = (kBias == kBiasNone) && fast_path;
         if (kBias == kBiasDense) {
+          if (!__all_sync(0xffffffffu, mbar_wait(bias_full, g & 1, abort_flag, a.st, 0x1330))) {
+            ok_run = false;
+            break;
+          }
           const uint64_t qk2 = f2_pack(a.qk_log2, a.qk_log2);
 #pragma unroll
           for (int v = 0; v < 16; ++v) {
-            const int key = k0 + v * 8;
-            uint4 raw = make_uint4(0, 0, 0, 0);
-            if (key + 8 <= S) raw = __ldg(reinterpret_cast<const uint4*>(brow + key));
+            // Key chunk v & 7 of row `lane` in box v >> 3, 128-byte swizzle:
+            // the 8 lanes of a shared-memory phase hit 8 different chunks.
+            const uint4 raw =
+                *reinterpret_cast<const uint4*>(stage + (v >> 3) * 4096 + lane * 128 + (((v & 7) ^ (lane & 7)) << 4));
             const __half2* hp = reinterpret_cast<const __half2*>(&raw);
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
@@ -437,6 +481,11 @@ __global__ void __launch_bounds__(FaCfg<D, 1>::kThreads, 2)
               z[v * 8 + 2 * e] = f2_lo(r2);
               z[v * 8 + 2 * e + 1] = f2_hi(r2);
             }
+          }
+          __syncwarp();
+          if (lane == 0 && j + 1 < n_t) {
+            fence_async_smem();  // the warp's reads of `stage` before the copy that overwrites it
+            bias_issue(qt, j + 1);
           }
         } else if (kBias == kBiasTable) {
           const float* trow = table_window_store(tb_win, tpre, static_cast<int>(lane));
@@ -608,6 +657,14 @@ __global__ void __launch_bounds__(FaCfg<D, 1>::kThreads, 2)
           bulk_commit();
         }
       }
+      if (kBiasTma && lane == 0 && qt + 1 < ntiles) {
+        bulk_wait_read_all();  // the O stores have read the staging rows
+        bias_issue(qt + 1, 0);
+      }
+    }
+    if (kBiasTma && lane == 0 && b_issued > g) {
+      // Left early with the next block's bias in flight: let it land first.
+      mbar_wait(bias_full, (b_issued - 1) & 1, never_flag, quiet, 0);
     }
     if (lane == 0) bulk_wait_all();
   }
@@ -656,7 +713,8 @@ template <int D, bool kCausal, int kBias>
 __global__ void __launch_bounds__(FaCfg<D>::kThreads, 1)
     fa2_persistent_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                           const __grid_constant__ CUtensorMap tmV,
-                          const __grid_constant__ CUtensorMap tmO, FaArgs a) {
+                          const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmB,
+                          FaArgs a) {
   using Cfg = FaCfg<D>;
   constexpr int KS = Cfg::kStages;
   constexpr int QB = Cfg::kQBuffers;
@@ -1241,7 +1299,7 @@ struct FaProblem {
 
 template <class Kernel>
 int run_fa2_kernel(Kernel kern, int threads, uint32_t regs_low, dim3 grid, int smem_bytes, const CUtensorMap& tq,
-                   const CUtensorMap& tk, const CUtensorMap& tv, const CUtensorMap& to, const FaArgs& args,
+                   const CUtensorMap& tk, const CUtensorMap& tv, const CUtensorMap& to, const CUtensorMap& tb, const FaArgs& args,
                    cudaStream_t stream) {
   cudaFuncAttributes fa{};
   int rc = kernel_setup(reinterpret_cast<const void*>(kern), smem_bytes, &fa);
@@ -1250,7 +1308,7 @@ int run_fa2_kernel(Kernel kern, int threads, uint32_t regs_low, dim3 grid, int s
     return fail(NESO_ERR_LAUNCH, "fa2: %d registers/thread cannot fund the %u/%u warpgroup split", fa.numRegs,
                 regs_low, kRegsHigh);
   }
-  cudaError_t e = launch_pdl(kern, grid, dim3(threads), smem_bytes, stream, tq, tk, tv, to, args);
+  cudaError_t e = launch_pdl(kern, grid, dim3(threads), smem_bytes, stream, tq, tk, tv, to, tb, args);
   if (e != cudaSuccess) return cuda_fail(e, "fa2 launch");
   return ok();
 }
@@ -1260,45 +1318,45 @@ int run_fa2_kernel(Kernel kern, int threads, uint32_t regs_low, dim3 grid, int s
 // (persistent when non-causal, tiles qb and nq-1-qb when causal).
 template <int D, bool kCausal, int kBias>
 int launch_fa2_t(const FaProblem& p, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
-                 const CUtensorMap& to, FaArgs& args, cudaStream_t stream) {
+                 const CUtensorMap& to, const CUtensorMap& tb, FaArgs& args, cudaStream_t stream) {
   using Cfg = FaCfg<D>;
   if constexpr (D == 128) {
     const int units = args.num_qblocks * p.BH;
     int rc = stream_counters(stream, &args.unit_counter);
     if (rc != NESO_OK) return rc;
     return run_fa2_kernel(fa2_persistent_kernel<D, kCausal, kBias>, Cfg::kThreads, kRegsLowPersistent,
-                          dim3(units < sm_count() ? units : sm_count(), 1, 1), Cfg::kSmemBytes, tq, tk, tv, to,
+                          dim3(units < sm_count() ? units : sm_count(), 1, 1), Cfg::kSmemBytes, tq, tk, tv, to, tb,
                           args, stream);
   } else {
     // 128-row units, two CTAs per SM.
     using Cfg1 = FaCfg<D, 1>;
+    constexpr int smem = pair_smem_bytes<D, kBias>();
     args.num_qblocks = (p.S + 127) / 128;
     if constexpr (kCausal) {
       // Causal: tiles qb and nq-1-qb share a CTA (nq + 1 key blocks each CTA).
       return run_fa2_kernel(fa2_pair_kernel<D, kCausal, kBias>, Cfg1::kThreads, Cfg1::regs_low(),
-                            dim3((args.num_qblocks + 1) / 2, p.BH, 1), Cfg1::kSmemBytes + 4 * 4096, tq, tk, tv, to,
-                            args, stream);
+                            dim3((args.num_qblocks + 1) / 2, p.BH, 1), smem, tq, tk, tv, to, tb, args, stream);
     } else {
       // Persistent: two CTAs per SM walk the (head, query tile) units.
       const int64_t total = static_cast<int64_t>(args.num_qblocks) * p.BH;
       const int grid = static_cast<int>(std::min<int64_t>(total, 2 * static_cast<int64_t>(sm_count())));
       return run_fa2_kernel(fa2_pair_kernel<D, kCausal, kBias>, Cfg1::kThreads, Cfg1::regs_low(), dim3(grid, 1, 1),
-                            Cfg1::kSmemBytes + 4 * 4096, tq, tk, tv, to, args, stream);
+                            smem, tq, tk, tv, to, tb, args, stream);
     }
   }
 }
 
 template <int D>
 int launch_fa2_d(const FaProblem& p, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
-                 const CUtensorMap& to, FaArgs& args, cudaStream_t stream) {
+                 const CUtensorMap& to, const CUtensorMap& tb, FaArgs& args, cudaStream_t stream) {
   if (p.causal) {
-    if (p.bias_mode == kBiasTable) return launch_fa2_t<D, true, kBiasTable>(p, tq, tk, tv, to, args, stream);
-    if (p.bias_mode == kBiasDense) return launch_fa2_t<D, true, kBiasDense>(p, tq, tk, tv, to, args, stream);
-    return launch_fa2_t<D, true, kBiasNone>(p, tq, tk, tv, to, args, stream);
+    if (p.bias_mode == kBiasTable) return launch_fa2_t<D, true, kBiasTable>(p, tq, tk, tv, to, tb, args, stream);
+    if (p.bias_mode == kBiasDense) return launch_fa2_t<D, true, kBiasDense>(p, tq, tk, tv, to, tb, args, stream);
+    return launch_fa2_t<D, true, kBiasNone>(p, tq, tk, tv, to, tb, args, stream);
   }
-  if (p.bias_mode == kBiasTable) return launch_fa2_t<D, false, kBiasTable>(p, tq, tk, tv, to, args, stream);
-  if (p.bias_mode == kBiasDense) return launch_fa2_t<D, false, kBiasDense>(p, tq, tk, tv, to, args, stream);
-  return launch_fa2_t<D, false, kBiasNone>(p, tq, tk, tv, to, args, stream);
+  if (p.bias_mode == kBiasTable) return launch_fa2_t<D, false, kBiasTable>(p, tq, tk, tv, to, tb, args, stream);
+  if (p.bias_mode == kBiasDense) return launch_fa2_t<D, false, kBiasDense>(p, tq, tk, tv, to, tb, args, stream);
+  return launch_fa2_t<D, false, kBiasNone>(p, tq, tk, tv, to, tb, args, stream);
 }
 
 int make_qkv_map(CUtensorMap* m, const void* base, int D, int S, int BH, int64_t row, int64_t head) {
@@ -1343,6 +1401,16 @@ int launch_fa2(const FaProblem& p, cudaStream_t stream) {
                      strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc != NESO_OK) return rc;
   }
+  // Dense bias as [BH][S rows][S keys] for the one-tile kernel's TMA loads:
+  // boxes of 32 rows x 64 keys (128 bytes); keys and rows past S read 0.
+  CUtensorMap tb = to;
+  if (p.bias_mode == kBiasDense && p.D == 64) {
+    uint64_t dims[3] = {static_cast<uint64_t>(p.S), static_cast<uint64_t>(p.S), static_cast<uint64_t>(p.BH)};
+    uint64_t strides[2] = {static_cast<uint64_t>(p.bias_row) * 2, static_cast<uint64_t>(p.bias_head) * 2};
+    uint32_t box[3] = {64, 32, 1};
+    rc = encode_tmap(&tb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, p.bias, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc != NESO_OK) return rc;
+  }
   FaArgs args{};
   args.O = p.O;
   args.o_row = p.o_row;
@@ -1360,8 +1428,8 @@ int launch_fa2(const FaProblem& p, cudaStream_t stream) {
   args.out_f16 = p.out_f16 ? 1 : 0;
   rc = device_status(&args.st);
   if (rc != NESO_OK) return rc;
-  if (p.D == 64) return launch_fa2_d<64>(p, tq, tk, tv, to, args, stream);
-  return launch_fa2_d<128>(p, tq, tk, tv, to, args, stream);
+  if (p.D == 64) return launch_fa2_d<64>(p, tq, tk, tv, to, tb, args, stream);
+  return launch_fa2_d<128>(p, tq, tk, tv, to, tb, args, stream);
 }
 
 // The reference's BM is a compile-time tile height (8..128, power of two);

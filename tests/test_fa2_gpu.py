@@ -75,6 +75,25 @@ def test_reference_golden_relpos_dense(dev, golden_dir, name):
     torch.testing.assert_close(out, ref, **TOL)
 
 
+@pytest.mark.parametrize("T,d,nh", [(2048, 64, 40), (1032, 64, 9), (136, 64, 3), (24, 64, 2),
+                                    (1024, 128, 8), (264, 128, 2)])
+def test_relpos_dense_sampled_heads(dev, T, d, nh):
+    # rel_pos_fa2_fwd at sizes where CTAs walk several query tiles and the
+    # last key block and query tile are ragged; heads sampled against the oracle
+    g = torch.Generator().manual_seed(T + d + nh)
+    q, k, v = (torch.randn(nh, T, d, generator=g).half() for _ in range(3))
+    bias = (0.5 * torch.randn(nh, T, T, generator=g)).half()
+    o = torch.empty(nh, T, d, dtype=torch.float16, device=dev)
+    bm = next(b for b in (128, 64, 32, 16, 8) if T % b == 0)
+    sc = 1.0 / math.sqrt(d)
+    kernels.rel_pos_fa2_fwd[(T // bm, nh, 1)](q.to(dev), k.to(dev), v.to(dev), bias.to(dev), o, T, d, sc,
+                                               T * d, T * T)
+    out = o.float().cpu()
+    for h in sorted({0, nh // 2, nh - 1}):
+        ref = oracle.attention(q[h:h + 1], k[h:h + 1], v[h:h + 1], sc, dense_bias=bias[h:h + 1])
+        torch.testing.assert_close(out[h:h + 1], ref, **TOL)
+
+
 def test_config1_b1_h8_s512_d64(dev):
     _check(dev, 1, 8, 512, 64)
 
