@@ -72,6 +72,19 @@ constexpr int kUnitReaders = 10;  // QK issuer, PV issuer and the 8 softmax warp
 
 enum BiasMode : int { kBiasNone = 0, kBiasTable = 1, kBiasDense = 2 };
 
+// z + (low or high fp16 half of b2), the half widened exactly: one mixed-
+// precision add instead of a conversion and an fp32 add.
+__device__ __forceinline__ float add_f16_lo(uint32_t b2, float z) {
+  float d;
+  asm("{\n\t.reg .b16 l, h;\n\tmov.b32 {l, h}, %1;\n\tadd.rn.f32.f16 %0, l, %2;\n\t}" : "=f"(d) : "r"(b2), "f"(z));
+  return d;
+}
+__device__ __forceinline__ float add_f16_hi(uint32_t b2, float z) {
+  float d;
+  asm("{\n\t.reg .b16 l, h;\n\tmov.b32 {l, h}, %1;\n\tadd.rn.f32.f16 %0, h, %2;\n\t}" : "=f"(d) : "r"(b2), "f"(z));
+  return d;
+}
+
 // Relative-position table of one 128-row x 128-key block: row i, key c use
 // table[h, d0 + i - c + 127] with d0 = (tile row 0) - (key 0) - 127 + S - 1.
 // The 32 rows of softmax warp q need the 159 consecutive entries from
@@ -460,26 +473,25 @@ __global__ void __launch_bounds__(FaCfg<D, 1>::kThreads, 2)
         // Without a bias and with a positive scale, max(s) * c = max(s * c): the
         // row max is taken on the raw scores and each probability costs one FFMA
         // + one ex2. Otherwise z holds the log2-domain logits.
-        const bool raw_scores = (kBias == kBiasNone) && fast_path;
+        // A dense bias is added to the raw scores (one mixed fp16 + fp32 add
+        // per key, exact like converting first) and takes the same path.
+        const bool raw_scores = (kBias != kBiasTable) && fast_path;
         if (kBias == kBiasDense) {
           if (!__all_sync(0xffffffffu, mbar_wait(bias_full, g & 1, abort_flag, a.st, 0x1330))) {
             ok_run = false;
             break;
           }
-          const uint64_t qk2 = f2_pack(a.qk_log2, a.qk_log2);
 #pragma unroll
           for (int v = 0; v < 16; ++v) {
             // Key chunk v & 7 of row `lane` in box v >> 3, 128-byte swizzle:
             // the 8 lanes of a shared-memory phase hit 8 different chunks.
             const uint4 raw =
                 *reinterpret_cast<const uint4*>(stage + (v >> 3) * 4096 + lane * 128 + (((v & 7) ^ (lane & 7)) << 4));
-            const __half2* hp = reinterpret_cast<const __half2*>(&raw);
+            const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-              const float2 f = __half22float2(hp[e]);
-              const uint64_t r2 = fmul2(fadd2(f2_pack(z[v * 8 + 2 * e], z[v * 8 + 2 * e + 1]), f2_pack(f.x, f.y)), qk2);
-              z[v * 8 + 2 * e] = f2_lo(r2);
-              z[v * 8 + 2 * e + 1] = f2_hi(r2);
+              z[v * 8 + 2 * e] = add_f16_lo(w[e], z[v * 8 + 2 * e]);
+              z[v * 8 + 2 * e + 1] = add_f16_hi(w[e], z[v * 8 + 2 * e + 1]);
             }
           }
           __syncwarp();
@@ -497,7 +509,8 @@ __global__ void __launch_bounds__(FaCfg<D, 1>::kThreads, 2)
             z[col] = f2_lo(r2);
             z[col + 1] = f2_hi(r2);
           }
-        } else if (!raw_scores) {
+        }
+        if (kBias != kBiasTable && !raw_scores) {
 #pragma unroll
           for (int col = 0; col < 128; ++col) z[col] *= a.qk_log2;
         }
