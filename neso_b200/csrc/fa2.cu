@@ -1042,6 +1042,16 @@ __global__ void __launch_bounds__(FaCfg<D>::kThreads, 1)
       float m_used = -INFINITY;
       float l = 0.f;
       for (int j = 0; j < n_t; ++j, ph ^= 1u) {
+        // Dense bias: this row's 128 values of block j are requested before
+        // the wait for S, so their latency hides under the QK MMA.
+        uint4 braw[kBias == kBiasDense ? 16 : 1];
+        if (kBias == kBiasDense) {
+#pragma unroll
+          for (int v = 0; v < 16; ++v) {
+            const int key = j * 128 + v * 8;
+            braw[v] = key + 8 <= S ? __ldg(reinterpret_cast<const uint4*>(brow + key)) : make_uint4(0, 0, 0, 0);
+          }
+        }
         // Warp-uniform: every lane must agree before the .sync.aligned TMEM ops.
         if (!__all_sync(0xffffffffu, mbar_wait(&s_full[t], ph & 1u, abort_flag, a.st, 0x1300 + t))) {
           ok_run = false;
@@ -1076,21 +1086,17 @@ __global__ void __launch_bounds__(FaCfg<D>::kThreads, 1)
         // Without a bias and with a positive scale, max(s) * c = max(s * c): the
         // row max is taken on the raw scores and each probability costs one FFMA
         // + one ex2. Otherwise z holds the log2-domain logits.
-        const bool raw_scores = (kBias == kBiasNone) && fast_path;
+        // A dense bias is added to the raw scores (one mixed fp16 + fp32 add
+        // per key, exact like converting first) and takes the same path.
+        const bool raw_scores = (kBias != kBiasTable) && fast_path;
         if (kBias == kBiasDense) {
-          const uint64_t qk2 = f2_pack(a.qk_log2, a.qk_log2);
 #pragma unroll
           for (int v = 0; v < 16; ++v) {
-            const int key = k0 + v * 8;
-            uint4 raw = make_uint4(0, 0, 0, 0);
-            if (key + 8 <= S) raw = __ldg(reinterpret_cast<const uint4*>(brow + key));
-            const __half2* hp = reinterpret_cast<const __half2*>(&raw);
+            const uint32_t w[4] = {braw[v].x, braw[v].y, braw[v].z, braw[v].w};
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-              const float2 f = __half22float2(hp[e]);
-              const uint64_t r2 = fmul2(fadd2(f2_pack(z[v * 8 + 2 * e], z[v * 8 + 2 * e + 1]), f2_pack(f.x, f.y)), qk2);
-              z[v * 8 + 2 * e] = f2_lo(r2);
-              z[v * 8 + 2 * e + 1] = f2_hi(r2);
+              z[v * 8 + 2 * e] = add_f16_lo(w[e], z[v * 8 + 2 * e]);
+              z[v * 8 + 2 * e + 1] = add_f16_hi(w[e], z[v * 8 + 2 * e + 1]);
             }
           }
         } else if (kBias == kBiasTable) {
@@ -1108,7 +1114,8 @@ __global__ void __launch_bounds__(FaCfg<D>::kThreads, 1)
             z[col] = f2_lo(r2);
             z[col + 1] = f2_hi(r2);
           }
-        } else if (!raw_scores) {
+        }
+        if (kBias != kBiasTable && !raw_scores) {
 #pragma unroll
           for (int col = 0; col < 128; ++col) z[col] *= a.qk_log2;
         }
