@@ -1253,9 +1253,15 @@ __global__ void __launch_bounds__(GvCfg<kQ, kM>::kThreads, GvCfg<kQ, kM>::kCtasP
   const int wr0 = r0 + warp * per_warp;
   const int wr1 = min(wr0 + per_warp, r1);
 
+  // This CTA's weight rows start towards L2 while the previous kernel on the
+  // stream finishes (a prefetch reads nothing into the CTA).
+  for (int r = r0 + static_cast<int>(threadIdx.x); r < r1; r += Cfg::kThreads) {
+    bulk_prefetch_l2(a.W + static_cast<int64_t>(r) * a.ldw + cb * kGvChannels,
+                     static_cast<uint32_t>(min(kGvChannels, a.N - cb * kGvChannels)));
+  }
   // Launched with programmatic serialization: the next kernel's CTAs may take
-  // SM slots as this grid's CTAs exit; nothing global is touched before the
-  // previous kernel on the stream has completed.
+  // SM slots as this grid's CTAs exit; nothing global is read or written
+  // before the previous kernel on the stream has completed.
   pdl_launch_dependents();
   pdl_wait();
 
