@@ -395,6 +395,24 @@ def baseline_configs(ctx: Ctx, peaks: dict) -> dict:
                      "heads_per_rank": sh.size, **r}
         del sets
 
+    # the reference's rel_pos_fa2_fwd (dense fp16 bias [nh, T, T], fp16 O), heads sharded
+    from neso_b200 import kernels
+    for nh, t_, d_ in ((64, 2048, 64), (64, 1024, 128)):
+        sh = shard.shard_heads(1, nh, world, rank)
+        if sh.size == 0:
+            continue
+        set_bytes = 8 * sh.size * t_ * d_ + 2 * sh.size * t_ * t_
+        sets = [(tuple(torch.randn(sh.size, t_, d_, device=dev, generator=g).half() for _ in range(3)),
+                 (0.5 * torch.randn(sh.size, t_, t_, device=dev, generator=g)).half(),
+                 torch.empty(sh.size, t_, d_, dtype=torch.float16, device=dev)) for _ in range(copies(set_bytes))]
+        launch = kernels.rel_pos_fa2_fwd[(t_ // 128, sh.size, 1)]
+        sc = 1 / math.sqrt(d_)
+        ms, ms_e = time_rotating(ctx, sets, lambda st: launch(*st[0], st[1], st[2], t_, d_, sc, t_ * d_, t_ * t_))
+        r = roofline(fa2_flops(1, sh.size, t_, d_, False), set_bytes, ms * 1e-3, peaks)
+        out[f"relpos_dense_t{t_}_d{d_}"] = {"tflops": fa2_flops(1, nh, t_, d_, False) / (ms * 1e-3) / 1e12, "ms": ms,
+                                           "ms_eager": ms_e, "heads": nh, "heads_per_rank": sh.size, **r}
+        del sets
+
     # config 5: quantized matmul K = 4096, N = 11008, output columns sharded
     sh = shard.shard_columns(QN, world, rank, 16)
     nc = sh.size
