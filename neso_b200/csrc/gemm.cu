@@ -211,6 +211,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, MH>::kThreads, 1)
     const int row_in_tile = h * kBM + q * 32 + lane;
     const bool vec_ok = (args.ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(args.C) & 15u) == 0);
     int tc = 0;
+    int nstore = 0;  // TMA stores issued by this warp
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++tc) {
       int mb, nb;
       tile_coords(t, args.num_m, args.num_n, mb, nb);
@@ -226,7 +227,6 @@ __global__ void __launch_bounds__(GemmCfg<BN, MH>::kThreads, 1)
         const int row0 = mb * Cfg::kTileM + h * kBM + q * 32;
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
-          uint8_t* stage = sOut + ((warp - 4) * Cfg::kOutBufs + (c % Cfg::kOutBufs)) * 4096;
           uint32_t r[32];
           tmem_ld32(tmem_base + ((q * 32) << 16) + (buf * MH + h) * BN + c * 32, r);
           tmem_wait_ld();
@@ -235,8 +235,14 @@ __global__ void __launch_bounds__(GemmCfg<BN, MH>::kThreads, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(&acc_empty[buf]);
           }
-          // The store that last used this staging block has read it (with two
-          // blocks, the previous block's store may still be reading the other).
+          const int col0 = nb * BN + c * 32;
+          if (row0 >= args.M || col0 >= args.N) continue;  // warp-uniform: block wholly past C
+          // Staging blocks alternate by stores issued, so the block written
+          // here is the one the store before last read: with two blocks, the
+          // last store may still be reading the other. (Alternating by block
+          // index instead let a block skipped past the edge of C hand the
+          // next write the block the last store was still reading.)
+          uint8_t* stage = sOut + ((warp - 4) * Cfg::kOutBufs + (nstore++ % Cfg::kOutBufs)) * 4096;
           if (lane == 0) {
             if (Cfg::kOutBufs == 2) {
               bulk_wait_read_but1();
@@ -252,8 +258,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, MH>::kThreads, 1)
           }
           fence_async_smem();
           __syncwarp();
-          const int col0 = nb * BN + c * 32;
-          if (lane == 0 && row0 < args.M && col0 < args.N) {
+          if (lane == 0) {
             tma_store_2d(&tmC, stage, col0, row0);
             bulk_commit();
           }

@@ -53,6 +53,28 @@ def test_matmul_256_row_tiles_ragged(dev, M, N, K):
     torch.testing.assert_close(c.cpu(), oracle.gemm(a, b), **TOL)
 
 
+@pytest.mark.parametrize("M,N,K", [
+    (1928, 2040, 1000),  # ragged M, N not a multiple of 64 (2-D B copies), ragged K; C blocks past N skipped
+    (2048, 2048, 64),    # one K block per tile
+    (2304, 4352, 520),   # several tiles per CTA, both accumulators in use
+    (2048, 2080, 128),   # 128 x 256 tiles: the last column tile stores one 32-column block and skips seven
+])
+def test_matmul_ragged_large(dev, M, N, K):
+    a, b = _inputs(M, N, K, seed=M + N)
+    c = ops.matmul(a.to(dev), b.to(dev))
+    torch.testing.assert_close(c.cpu(), oracle.gemm(a, b), **TOL)
+
+
+def test_matmul_unaligned_c_large(dev):
+    # C row stride of N + 3 floats: the epilogue writes rows with plain stores
+    M, N, K = 2048, 2048, 256
+    a, b = _inputs(M, N, K, seed=11)
+    c = torch.zeros(M, N + 3, device=dev)
+    kernels.matmul_kernel[(M // 128, N // 128, 1)](a.to(dev), b.to(dev), c, M, N, K, K, 1, N, 1, N + 3, 1,
+                                                   BLOCK_M=128, BLOCK_N=128, BLOCK_K=64)
+    torch.testing.assert_close(c[:, :N].cpu(), oracle.gemm(a, b), **TOL)
+
+
 def test_matmul_8192_sampled(dev):
     # Full BASELINE size; compare a sample of rows against the oracle.
     n = 8192
