@@ -62,13 +62,15 @@ namespace {
 // FaCfg::regs_low(), the softmax warpgroups grow to kRegsHigh; the host checks
 // that the split fits the block's launch pool.
 constexpr uint32_t kRegsHigh = 216;
-// The persistent kernel's producer and issuers keep per-unit state across
-// units and get more registers; 128 * 72 + 256 * 216 fills the launch pool.
-constexpr uint32_t kRegsLowPersistent = 72;
+// The persistent kernel's producer and MMA issuer keep per-unit state across
+// units and get more registers; 128 * 88 + 256 * 208 fills the launch pool
+// (168 registers x 384 threads).
+constexpr uint32_t kRegsLowPersistent = 88;
+constexpr uint32_t kRegsHighPersistent = 208;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale only when max grows by > 2^8
 constexpr int kUnitRing = 4;      // unit indices the persistent producer may publish ahead
-constexpr int kUnitReaders = 10;  // QK issuer, PV issuer and the 8 softmax warps
+constexpr int kUnitReaders = 9;  // the MMA issuer and the 8 softmax warps
 
 enum BiasMode : int { kBiasNone = 0, kBiasTable = 1, kBiasDense = 2 };
 
@@ -890,23 +892,44 @@ __global__ void __launch_bounds__(FaCfg<D>::kThreads, 1)
         }
       }
     } else if (warp == 1 && lane == 0) {
-      // -------------------------------------------------------- QK issuer --
-      // Two single-thread MMA issuers on different SM sub-partitions: warp 1
-      // issues S = Q K^T, warp 3 issues O += P V. A tcgen05.mma issue blocks
-      // until the tensor pipe accepts it, so one thread serving both streams
-      // (and sharing its scheduler with busy softmax warps) leaves the pipe
-      // idle between MMAs. The streams only meet through mbarriers.
+      // ------------------------------------------------------- MMA issuer --
+      // One thread issues both tiles' MMAs in the order S_t(0) = Q_t K(0)^T,
+      // then per key block j: O_t += P_t(j) V(j) followed at once by
+      // S_t(j+1) = Q_t K(j+1)^T. P_t lives in S_t's columns; tcgen05.mma
+      // operations from one thread execute in issue order, so the QK that
+      // overwrites S_t runs after the PV that reads P_t without waiting for
+      // that PV to complete (a wait on its commit, then a second thread's
+      // issue, sat in every tile's chain before). s_full_t(j+1) completing
+      // also means PV_t(j) has, which is what the softmax needs before it
+      // rescales O_t.
       constexpr uint32_t idesc_qk = idesc_f16_f32(128, 128, 0, 0);
+      constexpr uint32_t idesc_pv = idesc_f16_f32(128, D, 0, 1);
       // Descriptor bases, computed once; a K step only moves the start
       // address field (low bits), so the per-MMA work is one 64-bit add.
       const uint64_t q_desc0 = sdesc_sw128(smem_u32(sQ), 16, 1024);
       const uint64_t k_desc0 = sdesc_sw128(smem_u32(sK), 16, 1024);
-      // bits 0-1: parity of the blocks tile 0/1 has had; bits 2-3: tile 0/1
-      // has had a block (its S buffer has a reader to wait for).
-      uint32_t ph = 0;
-      int s = 0;           // K stage
-      uint32_t kph = 0;    // K stage phase
+      const uint64_t v_desc0 = sdesc_sw128(smem_u32(sV), 16384, 1024);
+      // pph bits 0-1: parity of the P blocks tile 0/1 has had; bits 2-3:
+      // parity of the units tile 0/1 has finished; bits 4-5: tile 0/1 has
+      // finished a unit (its O buffer has an epilogue to wait for).
+      uint32_t pph = 0;
+      int ks = 0, vs = 0;            // K and V stages
+      uint32_t kph = 0, vph = 0;     // their phases
       bool ok_run = true;
+      auto issue_qk = [&](int t, int qi) {
+        const uint64_t qd = q_desc0 + static_cast<uint64_t>(((qi * 2 + t) * Cfg::kTileBytes) >> 4);
+        const uint64_t kd = k_desc0 + static_cast<uint64_t>((ks * Cfg::kTileBytes) >> 4);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint64_t off = static_cast<uint64_t>(((kk >> 2) * 16384 + (kk & 3) * 32) >> 4);
+          umma_f16_ss(tmem + Cfg::s_col(t), qd + off, kd + off, idesc_qk, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&s_full[t]);
+      };
+      auto next_k = [&]() {
+        umma_commit(&k_empty[ks]);
+        if (++ks == KS) { ks = 0; kph ^= 1u; }
+      };
       for (int k = 0; ok_run; ++k) {
         const int w = take_unit(k);
         if (w < 0) break;
@@ -916,71 +939,30 @@ __global__ void __launch_bounds__(FaCfg<D>::kThreads, 1)
         const int n0 = ntile(q0, 0), n1 = ntile(q0, 1), nmax = max(n0, n1);
         const int qi = QB == 1 ? 0 : (k & 1);
         if (!mbar_wait(&q_full[qi], (k / QB) & 1, abort_flag, a.st, 0x1200)) break;
-        for (int j = 0; ok_run && j < nmax; ++j) {
-          if (!mbar_wait(&k_full[s], kph, abort_flag, a.st, 0x1213)) { ok_run = false; break; }
-#pragma unroll
-          for (int t = 0; t < 2; ++t) {
-            if (j >= (t ? n1 : n0)) continue;
-            if (ph & (4u << t)) {
-              // S_t is overwritten: the previous block's S must be in the softmax
-              // registers (P own columns) or, when P aliases S, read by its PV.
-              uint64_t* gate = Cfg::kAliasP ? &o_done[t] : &s_free[t];
-              if (!mbar_wait(gate, ((ph >> t) & 1u) ^ 1u, abort_flag, a.st, 0x1218 + t)) { ok_run = false; break; }
-            }
-            tc_fence_after();
-            const uint64_t qd = q_desc0 + static_cast<uint64_t>(((qi * 2 + t) * Cfg::kTileBytes) >> 4);
-            const uint64_t kd = k_desc0 + static_cast<uint64_t>((s * Cfg::kTileBytes) >> 4);
-#pragma unroll
-            for (int kk = 0; kk < D / 16; ++kk) {
-              const uint64_t off = static_cast<uint64_t>(((kk >> 2) * 16384 + (kk & 3) * 32) >> 4);
-              umma_f16_ss(tmem + Cfg::s_col(t), qd + off, kd + off, idesc_qk, kk > 0 ? 1u : 0u);
-            }
-            umma_commit(&s_full[t]);
-            ph = (ph ^ (1u << t)) | (4u << t);
-          }
-          if (!ok_run) break;
-          umma_commit(&k_empty[s]);
-          if (++s == KS) { s = 0; kph ^= 1u; }
+        if (nmax > 0) {
+          if (!mbar_wait(&k_full[ks], kph, abort_flag, a.st, 0x1213)) break;
+          tc_fence_after();
+          if (n0 > 0) issue_qk(0, qi);
+          if (n1 > 0) issue_qk(1, qi);
+          next_k();
         }
-        if (ok_run) umma_commit(&q_empty[qi]);  // Q buffer free once this unit's QKs finish
-      }
-      // Every MMA this thread issued must be complete before TMEM is freed.
-      umma_commit(&mma_done[0]);
-      mbar_wait(&mma_done[0], 0, never_flag, quiet, 0);
-    } else if (warp == 3 && lane == 0) {
-      // -------------------------------------------------------- PV issuer --
-      constexpr uint32_t idesc_pv = idesc_f16_f32(128, D, 0, 1);
-      const uint64_t v_desc0 = sdesc_sw128(smem_u32(sV), 16384, 1024);
-      // bits 0-1: parity of the blocks tile 0/1 has had; bits 2-3: parity of
-      // the units tile 0/1 has finished; bits 4-5: tile 0/1 has finished a
-      // unit (its O buffer has an epilogue to wait for).
-      uint32_t ph = 0;
-      int s = 0;
-      uint32_t vph = 0;
-      bool ok_run = true;
-      for (int k = 0; ok_run; ++k) {
-        const int w = take_unit(k);
-        if (w < 0) break;
-        int qb, bh;
-        unit_coords(w, a.num_qblocks, a.BH, kCausal, qb, bh);
-        const int q0 = qb * 256;
-        const int n0 = ntile(q0, 0), n1 = ntile(q0, 1), nmax = max(n0, n1);
         for (int j = 0; ok_run && j < nmax; ++j) {
-          if (!mbar_wait(&v_full[s], vph, abort_flag, a.st, 0x1212)) { ok_run = false; break; }
+          if (!mbar_wait(&v_full[vs], vph, abort_flag, a.st, 0x1212)) { ok_run = false; break; }
+          if (j + 1 < nmax && !mbar_wait(&k_full[ks], kph, abort_flag, a.st, 0x1213)) { ok_run = false; break; }
 #pragma unroll
           for (int t = 0; t < 2; ++t) {
             if (j >= (t ? n1 : n0)) continue;
-            if (j == 0 && (ph & (16u << t))) {
+            if (j == 0 && (pph & (16u << t))) {
               // The first PV of a unit overwrites O_t: the previous unit's
               // epilogue must have read it.
-              if (!mbar_wait(&o_free[t], ((ph >> (2 + t)) & 1u) ^ 1u, abort_flag, a.st, 0x1222 + t)) {
+              if (!mbar_wait(&o_free[t], ((pph >> (2 + t)) & 1u) ^ 1u, abort_flag, a.st, 0x1222 + t)) {
                 ok_run = false;
                 break;
               }
             }
-            if (!mbar_wait(&p_full[t], (ph >> t) & 1u, abort_flag, a.st, 0x1210 + t)) { ok_run = false; break; }
+            if (!mbar_wait(&p_full[t], (pph >> t) & 1u, abort_flag, a.st, 0x1210 + t)) { ok_run = false; break; }
             tc_fence_after();
-            const uint64_t vd = v_desc0 + static_cast<uint64_t>((s * Cfg::kTileBytes) >> 4);
+            const uint64_t vd = v_desc0 + static_cast<uint64_t>((vs * Cfg::kTileBytes) >> 4);
             const uint32_t p_tmem = tmem + Cfg::p_col(t);
 #pragma unroll
             for (int kk = 0; kk < 8; ++kk) {
@@ -988,21 +970,26 @@ __global__ void __launch_bounds__(FaCfg<D>::kThreads, 1)
                           vd + static_cast<uint64_t>((kk * 2048) >> 4), idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
             }
             umma_commit(&o_done[t]);
-            ph ^= 1u << t;
+            pph ^= 1u << t;
+            if (j + 1 < (t ? n1 : n0)) issue_qk(t, qi);
           }
           if (!ok_run) break;
-          umma_commit(&v_empty[s]);
-          if (++s == KS) { s = 0; vph ^= 1u; }
+          umma_commit(&v_empty[vs]);
+          if (++vs == KS) { vs = 0; vph ^= 1u; }
+          if (j + 1 < nmax) next_k();
         }
-        if (n0 > 0) ph = (ph ^ 4u) | 16u;
-        if (n1 > 0) ph = (ph ^ 8u) | 32u;
+        if (!ok_run) break;
+        umma_commit(&q_empty[qi]);  // Q buffer free once this unit's MMAs finish
+        if (n0 > 0) pph = (pph ^ 4u) | 16u;
+        if (n1 > 0) pph = (pph ^ 8u) | 32u;
       }
-      umma_commit(&mma_done[1]);
-      mbar_wait(&mma_done[1], 0, never_flag, quiet, 0);
+      // Every MMA this thread issued must be complete before TMEM is freed.
+      umma_commit(&mma_done[0]);
+      mbar_wait(&mma_done[0], 0, never_flag, quiet, 0);
     }
   } else {
     // ------------------------------------------------- softmax / epilogue --
-    setmaxnreg_inc<kRegsHigh>();
+    setmaxnreg_inc<kRegsHighPersistent>();
     const int t = (warp - 4) >> 2;
     const uint32_t q = warp & 3;
     const int row = q * 32 + lane;
@@ -1318,15 +1305,16 @@ struct FaProblem {
 };
 
 template <class Kernel>
-int run_fa2_kernel(Kernel kern, int threads, uint32_t regs_low, dim3 grid, int smem_bytes, const CUtensorMap& tq,
+int run_fa2_kernel(Kernel kern, int threads, uint32_t regs_low, uint32_t regs_high, dim3 grid, int smem_bytes,
+                   const CUtensorMap& tq,
                    const CUtensorMap& tk, const CUtensorMap& tv, const CUtensorMap& to, const CUtensorMap& tb, const FaArgs& args,
                    cudaStream_t stream) {
   cudaFuncAttributes fa{};
   int rc = kernel_setup(reinterpret_cast<const void*>(kern), smem_bytes, &fa);
   if (rc != NESO_OK) return rc;
-  if (static_cast<int64_t>(fa.numRegs) * threads < 128 * regs_low + (threads - 128) * kRegsHigh) {
+  if (static_cast<int64_t>(fa.numRegs) * threads < 128 * regs_low + (threads - 128) * regs_high) {
     return fail(NESO_ERR_LAUNCH, "fa2: %d registers/thread cannot fund the %u/%u warpgroup split", fa.numRegs,
-                regs_low, kRegsHigh);
+                regs_low, regs_high);
   }
   cudaError_t e = launch_pdl(kern, grid, dim3(threads), smem_bytes, stream, tq, tk, tv, to, tb, args);
   if (e != cudaSuccess) return cuda_fail(e, "fa2 launch");
@@ -1344,7 +1332,7 @@ int launch_fa2_t(const FaProblem& p, const CUtensorMap& tq, const CUtensorMap& t
     const int units = args.num_qblocks * p.BH;
     int rc = stream_counters(stream, &args.unit_counter);
     if (rc != NESO_OK) return rc;
-    return run_fa2_kernel(fa2_persistent_kernel<D, kCausal, kBias>, Cfg::kThreads, kRegsLowPersistent,
+    return run_fa2_kernel(fa2_persistent_kernel<D, kCausal, kBias>, Cfg::kThreads, kRegsLowPersistent, kRegsHighPersistent,
                           dim3(units < sm_count() ? units : sm_count(), 1, 1), Cfg::kSmemBytes, tq, tk, tv, to, tb,
                           args, stream);
   } else {
@@ -1354,13 +1342,13 @@ int launch_fa2_t(const FaProblem& p, const CUtensorMap& tq, const CUtensorMap& t
     args.num_qblocks = (p.S + 127) / 128;
     if constexpr (kCausal) {
       // Causal: tiles qb and nq-1-qb share a CTA (nq + 1 key blocks each CTA).
-      return run_fa2_kernel(fa2_pair_kernel<D, kCausal, kBias>, Cfg1::kThreads, Cfg1::regs_low(),
+      return run_fa2_kernel(fa2_pair_kernel<D, kCausal, kBias>, Cfg1::kThreads, Cfg1::regs_low(), kRegsHigh,
                             dim3((args.num_qblocks + 1) / 2, p.BH, 1), smem, tq, tk, tv, to, tb, args, stream);
     } else {
       // Persistent: two CTAs per SM walk the (head, query tile) units.
       const int64_t total = static_cast<int64_t>(args.num_qblocks) * p.BH;
       const int grid = static_cast<int>(std::min<int64_t>(total, 2 * static_cast<int64_t>(sm_count())));
-      return run_fa2_kernel(fa2_pair_kernel<D, kCausal, kBias>, Cfg1::kThreads, Cfg1::regs_low(), dim3(grid, 1, 1),
+      return run_fa2_kernel(fa2_pair_kernel<D, kCausal, kBias>, Cfg1::kThreads, Cfg1::regs_low(), kRegsHigh, dim3(grid, 1, 1),
                             smem, tq, tk, tv, to, tb, args, stream);
     }
   }
