@@ -29,9 +29,11 @@
 // warps 8-11 and the turn handshake.
 //   warp 0       TMA producer: Q tiles once, then K_j / V_j into KV rings.
 //   warp 1       single-thread tcgen05.mma issuer of S_t = Q_t . K_j^T (SS,
-//                M=128 N=128 K=16 steps, fp32 in TMEM)
-//   warp 3       single-thread tcgen05.mma issuer of O_t += P_t . V_j (TS: P
-//                from TMEM, V MN-major from smem)
+//                M=128 N=128 K=16 steps, fp32 in TMEM); in the D = 128 kernel
+//                also of O_t += P_t . V_j, each PV_t(j) followed at once by
+//                S_t(j+1)
+//   warp 3       one-tile kernel: single-thread tcgen05.mma issuer of
+//                O += P . V_j (TS: P from TMEM, V MN-major from smem)
 //   warp 2       TMEM allocator (512 columns).
 //   warps 4-7    softmax + epilogue for tile 0; warps 8-11 for tile 1. Thread
 //                r owns query row r: it reads its S row from TMEM, computes the
@@ -41,7 +43,8 @@
 //                arithmetic because O and l always share one reference max).
 // TMEM columns: S0 [0,128) S1 [128,256) O0 [256,256+D) O1 [256+D,256+2D);
 //   D = 64: P0/P1 in [384,448)/[448,512); D = 128: P_t aliases the first 64
-//   columns of S_t and the issuer waits for PV_t(j) before QK_t(j+1).
+//   columns of S_t, and QK_t(j+1) is issued after PV_t(j) by the same thread
+//   (tcgen05.mma operations of one thread run in issue order).
 //   One-tile form (D = 64): S [0,128) O [128,192) P [192,256).
 // Relative-position table: the 32 rows of a softmax warp need 159
 // consecutive table entries per 128-key block; the warp stages them in its
@@ -751,7 +754,7 @@ __global__ void __launch_bounds__(FaCfg<D>::kThreads, 1)
   uint64_t* o_done = p_full + 2;        // [2]
   uint64_t* s_free = o_done + 2;        // [2] softmax has read S_t (4 warps)
   uint64_t* o_free = s_free + 2;        // [2] epilogue has read O_t (4 warps)
-  uint64_t* mma_done = o_free + 2;      // [2] one per MMA issuer
+  uint64_t* mma_done = o_free + 2;      // [2] [0]: the MMA issuer's last MMAs done ([1] unused)
   uint64_t* turn = mma_done + 2;        // [2][4] exp-loop turn of tile t, lane quarter q
   uint64_t* unit_full = turn + 8;       // [kUnitRing] unit index published
   uint64_t* unit_empty = unit_full + kUnitRing;  // [kUnitRing] read by all consumers
@@ -825,7 +828,7 @@ __global__ void __launch_bounds__(FaCfg<D>::kThreads, 1)
   };
 
   if (warp < 4) {
-    // Warpgroup 0: TMA producer, MMA issuers, TMEM allocator.
+    // Warpgroup 0: TMA producer, MMA issuer, TMEM allocator.
     setmaxnreg_dec<kRegsLowPersistent>();
     if (warp == 0 && lane == 0) {
       // ------------------------------------------------------------ producer --
