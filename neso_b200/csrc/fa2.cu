@@ -949,6 +949,10 @@ __global__ void __launch_bounds__(FaCfg<D>::kThreads, 1)
           if (n1 > 0) issue_qk(1, qi);
           next_k();
         }
+        // The Q buffer is free once this unit's last QKs finish: release it
+        // as soon as they are issued, so the next unit's Q load starts under
+        // this unit's last softmax blocks.
+        if (nmax <= 1) umma_commit(&q_empty[qi]);
         for (int j = 0; ok_run && j < nmax; ++j) {
           if (!mbar_wait(&v_full[vs], vph, abort_flag, a.st, 0x1212)) { ok_run = false; break; }
           if (j + 1 < nmax && !mbar_wait(&k_full[ks], kph, abort_flag, a.st, 0x1213)) { ok_run = false; break; }
@@ -980,9 +984,9 @@ __global__ void __launch_bounds__(FaCfg<D>::kThreads, 1)
           umma_commit(&v_empty[vs]);
           if (++vs == KS) { vs = 0; vph ^= 1u; }
           if (j + 1 < nmax) next_k();
+          if (j + 2 == nmax) umma_commit(&q_empty[qi]);  // the unit's last QKs are issued
         }
         if (!ok_run) break;
-        umma_commit(&q_empty[qi]);  // Q buffer free once this unit's MMAs finish
         if (n0 > 0) pph = (pph ^ 4u) | 16u;
         if (n1 > 0) pph = (pph ^ 8u) | 32u;
       }
