@@ -176,6 +176,17 @@ __device__ __forceinline__ void umma_f16_ss(uint32_t d_tmem, uint64_t a_desc, ui
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
 }
 
+// D[tmem] (+)= A[smem desc] * B[smem desc], kind::f8f6f4 (8-bit float A/B as
+// the instruction descriptor names them, K = 32 per instruction, fp32 acc).
+__device__ __forceinline__ void umma_f8_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                           uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
+}
+
 // D[tmem] (+)= A[tmem] * B[smem desc]; A is M lanes x K fp16 packed two per
 // 32-bit column (low half = even k).
 __device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
@@ -310,6 +321,13 @@ __device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr, uint32_t lbo_byt
   return d;
 }
 
+// The same descriptor with 64-byte swizzle (layout type 4): K-major rows of
+// 64 B, 8-row groups 512 B apart (sbo = 512).
+__device__ __forceinline__ uint64_t sdesc_sw64(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+  return (sdesc_sw128(saddr, lbo_bytes, sbo_bytes) & ~(static_cast<uint64_t>(7) << 61)) |
+         (static_cast<uint64_t>(4) << 61);
+}
+
 // Instruction descriptor for kind::f16 with fp16 A/B and fp32 accumulate.
 //   bits [4,6)  D format (1 = f32)
 //   bits [7,10) A format (0 = f16), [10,13) B format (0 = f16)
@@ -319,6 +337,13 @@ __host__ __device__ constexpr uint32_t idesc_f16_f32(uint32_t M, uint32_t N, uin
                                                      uint32_t b_mn_major) {
   return (1u << 4) | (0u << 7) | (0u << 10) | (a_mn_major << 15) | (b_mn_major << 16) | ((N >> 3) << 17) |
          ((M >> 4) << 24);
+}
+
+// kind::f8f6f4 with E5M2 A and B (format code 1 in bits [7,10) and [10,13)),
+// fp32 accumulate; the other fields as for kind::f16.
+__host__ __device__ constexpr uint32_t idesc_e5m2_f32(uint32_t M, uint32_t N, uint32_t a_mn_major,
+                                                      uint32_t b_mn_major) {
+  return idesc_f16_f32(M, N, a_mn_major, b_mn_major) | (1u << 7) | (1u << 10);
 }
 
 __device__ __forceinline__ float ex2_approx(float x) {

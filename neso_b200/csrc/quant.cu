@@ -11,7 +11,8 @@
 // One persistent CTA per SM; per 64-deep K block ("stage"):
 //   warp 0      TMA: raw weight tile(s) (int8 [64 k][128 n] or packed int4
 //               [32 byte-rows][128 n], 128-byte swizzled) and (int4, M >= 65)
-//               the group's fp16 scale row; warp 3: TMA of the activation tile.
+//               the group's fp16 scale row; warp 3: TMA of the activation tile
+//               (and, int4 M >= 65, of its E5M2 copy, 64-byte swizzled).
 //   warps 4-7,  dequantise raw -> fp16 directly into the MN-major 128-byte
 //   12-15       swizzled layout tcgen05 reads; fence.proxy.async; arrive. The
 //               two groups take alternate K blocks (or, with two channel
@@ -19,12 +20,15 @@
 //                 int8: exact, (b ^ 0x80) | 0x6400 as fp16 is 1024 + b + 128.
 //                 int4, M >= 65 layout: q exact the same way, then w = q * s
 //                 is split into w_hi = fp16(q * s) and w_lo = fma(q, s, -w_hi)
-//                 (the exact rounding error), so the MMA sums q * s without
-//                 rounding it.
+//                 (the exact rounding error, at most 3 significant bits),
+//                 stored as E5M2 of 2^8 w_lo (exact), so the MMAs sum q * s
+//                 up to the E5M2 rounding of X in the w_lo term.
 //                 int4, M <= 64 layout: q only (exact in fp16); the group
 //                 scale is applied to fp32 partial sums instead (below).
 //   warp 1      tcgen05.mma issuer (kind::f16, fp32 accumulators in TMEM);
-//               int4 M >= 65 issues hi and lo MMAs per K step; int4 M <= 64
+//               int4 M >= 65 adds two kind::f8f6f4 MMAs (K = 32) per K
+//               block for w_lo against an E5M2 copy of 2^-8 X (written by
+//               a conversion kernel before the matmul); int4 M <= 64
 //               accumulates each run of K blocks inside one 128-wide scale
 //               group into its own buffer (double-buffered), so the epilogue
 //               applies that group's scales while the next run accumulates.
@@ -65,11 +69,17 @@ struct QCfg {
   //   R  raw weight tiles (int8 [64 k][128 n] or packed int4 [32][128] plus,
   //      M >= 65, the group's 128 fp16 scales), deep: TMA -> convert warps;
   //   X  activation tiles [kNX rows][64 k] fp16: TMA -> MMA;
-  //   F  dequantised fp16 weight tiles (int4 M >= 65: hi and lo copies):
-  //      convert -> MMA.
+  //   F  dequantised fp16 weight tiles (int4 M >= 65: the fp16 w_hi tiles
+  //      followed by the E5M2 w_lo tiles): convert -> MMA.
   // int4 M <= 64 (kGS, group-scaled partial sums) adds a ring of scale rows
   // (one 128-channel row per tile and group run): TMA -> epilogue.
   static constexpr bool kGS = kQ == kInt4G128 && kSwap;
+  // int4, M >= 65 layout: w = q * s is carried as w_hi = fp16(q * s) (kind::f16
+  // MMAs) plus its exact remainder w_lo, which has at most 3 significant bits
+  // and so is exact as E5M2 once scaled by 2^8; the w_lo MMAs run as
+  // kind::f8f6f4 (twice the fp16 rate) against an E5M2 copy of X scaled by
+  // 2^-8, appended to each X stage.
+  static constexpr bool kF8Lo = kQ == kInt4G128 && !kSwap;
   static constexpr int kRawTileBytes = (kQ == kInt8) ? 64 * 128 : kGS ? 32 * 128 : 32 * 128 + 1024;
   static constexpr int kRawBytes = kNT * kRawTileBytes;
   // 64-deep K blocks per fp16 weight (F) and activation (X) stage: two in the
@@ -80,10 +90,12 @@ struct QCfg {
   // measured slower, 20.9 / 22.9 -> 21.8 / 23.4); raw tiles stay one K block.
   static constexpr int kFKB = (kSwap && (kNT == 2 || kQ == kInt4G128)) ? 2 : 1;
   static constexpr int kXBlockBytes = kNX * kBK * 2;
-  static constexpr int kXBytes = kFKB * kXBlockBytes;
+  static constexpr int kX8Bytes = kF8Lo ? kNX * kBK : 0;  // E5M2 X block: kNX rows x 64 bytes, 64-byte swizzle
+  static constexpr int kXBytes = kFKB * kXBlockBytes + kX8Bytes;
   static constexpr int kW16BlockBytes = kBK * kTileN * 2;      // 16 KB: one K block of one tile
   static constexpr int kW16Bytes = kFKB * kW16BlockBytes;      // one fp16 copy of one tile
-  static constexpr int kNumW16 = (kQ == kInt4G128 && !kGS) ? 2 : 1;
+  static constexpr int kNumW16 = 1;
+  static constexpr int kLoBlockBytes = kBK * kTileN;  // 8 KB: one K block of one tile's E5M2 w_lo
   // Convert groups (warps 4-7, 12-15). A group's per-stage cost is mostly
   // fixed (barrier waits, the proxy fence, loop control: ~1300 cycles per
   // stage measured at M = 16), so the swapped layout lets each group take
@@ -94,7 +106,7 @@ struct QCfg {
   static constexpr int kConvGroupsPerStage = kAltStages ? 1 : kNT;
   static constexpr int kScSlots = kGS ? 16 : 0;
   static constexpr int kScBytes = kNT * 256;
-  static constexpr int kFTileBytes = kNumW16 * kW16Bytes;
+  static constexpr int kFTileBytes = kNumW16 * kW16Bytes + (kF8Lo ? kLoBlockBytes : 0);
   static constexpr int kFBytes = kNT * kFTileBytes;
   // kNX = 256 in the M >= 65 layout: 256-row units, two 128-row accumulators
   // (every fp16 weight stage feeds two MMAs per K step).
@@ -106,7 +118,8 @@ struct QCfg {
   // Swapped layout: X tiles are 2-8 KB and the X ring moves in step with the
   // F ring (same depth, released by the same commit; deeper X rings measured
   // no faster at M = 16).
-  static constexpr int kXStages = kSwap ? kFStages : kRowHalves == 2 ? 3 : kNT == 2 ? (kQ == kInt8 ? 4 : 3) : 6;
+  static constexpr int kXStages = kSwap ? kFStages : kRowHalves == 2 ? 3 : kNT == 2 ? (kQ == kInt8 ? 4 : 3)
+                                  : kF8Lo ? 4 : 6;
   static constexpr int kBudget = 224 * 1024;
   // Y staging for TMA stores (M >= 65 layout): 16 rows x 32 fp32 per epilogue
   // warp, two blocks (one store's read overlaps filling the next) where the
@@ -197,7 +210,8 @@ __device__ __forceinline__ void dequant_i8x16(uint4 raw, uint4& o0, uint4& o1) {
 template <int kQ, bool kSwap, int kNX, int kNT>
 __global__ void __launch_bounds__(kThreads, 1)
     wq_gemm_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
-                   const __grid_constant__ CUtensorMap tmS, const __grid_constant__ CUtensorMap tmY, QArgs args) {
+                   const __grid_constant__ CUtensorMap tmS, const __grid_constant__ CUtensorMap tmY,
+                   const __grid_constant__ CUtensorMap tmX8, QArgs args) {
   using Cfg = QCfg<kQ, kSwap, kNX, kNT>;
   constexpr int kUnitN = kNT * kTileN;  // output channels per unit
   constexpr int RS = Cfg::kRStages, XS = Cfg::kXStages, FS = Cfg::kFStages;
@@ -255,6 +269,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_prefetch_desc(&tmX);
     tma_prefetch_desc(&tmW);
     if (kQ == kInt4G128) tma_prefetch_desc(&tmS);
+    if (Cfg::kF8Lo) tma_prefetch_desc(&tmX8);
     if (args.y_tma) tma_prefetch_desc(&tmY);
   }
   if (warp == 2) {
@@ -310,6 +325,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int b = 0; b < Cfg::kFKB; ++b) {
             tma_load_2d(sX + s * Cfg::kXBytes + b * Cfg::kXBlockBytes, &tmX, &full[s], (kb + b) * kBK,
                         kSwap ? 0 : u.mb * kNX);
+          }
+          if (Cfg::kF8Lo) {
+            tma_load_2d(sX + s * Cfg::kXBytes + Cfg::kFKB * Cfg::kXBlockBytes, &tmX8, &full[s], kb * kBK, u.mb * kNX);
           }
         }
       }
@@ -445,6 +463,23 @@ __global__ void __launch_bounds__(kThreads, 1)
                   for (int h = 0; h < Cfg::kRowHalves; ++h) {
                     umma_f16_ss(d_tmem + h * kUnitN, xd + static_cast<uint64_t>((h * 16384) >> 4), wd, idesc, acc);
                   }
+                }
+              }
+            }
+            if constexpr (Cfg::kF8Lo) {
+              // w_lo: A = E5M2 X (2^-8 x) [rows][64 k] K-major, 64-byte swizzle;
+              // B = E5M2 2^8 w_lo [64 k][kUnitN n] MN-major (tiles 8 KB apart).
+              // Two K = 32 steps per K block into the same accumulators.
+              constexpr uint32_t idesc8 = idesc_e5m2_f32(128, kUnitN, 0, 1);
+              const uint64_t x8d = sdesc_sw64(smem_u32(sX + xs * Cfg::kXBytes + Cfg::kFKB * Cfg::kXBlockBytes), 16, 512);
+              const uint64_t lod = sdesc_sw128(smem_u32(sF + fs * Cfg::kFBytes + kNT * Cfg::kW16Bytes),
+                                               Cfg::kLoBlockBytes, 1024);
+#pragma unroll
+              for (int k2 = 0; k2 < kBK / 32; ++k2) {
+#pragma unroll
+                for (int h = 0; h < Cfg::kRowHalves; ++h) {
+                  umma_f8_ss(d_tmem + h * kUnitN, x8d + static_cast<uint64_t>((h * 128 * kBK + k2 * 32) >> 4),
+                             lod + static_cast<uint64_t>((k2 * 32 * 128) >> 4), idesc8, 1u);
                 }
               }
             }
@@ -609,6 +644,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               const int swr = kk & 7;
               const __half* sc = reinterpret_cast<const __half*>(raw + 4096) + qn * 32;
               const __half2 b8 = __float2half2_rn(1032.f);  // 1024 + 8
+              const __half2 h256 = __float2half2_rn(256.f);
               uint32_t hv[2][2][8], lv[2][2][8];  // [raw unit i][row r0/r1][16 channels as 8 half2]
 #pragma unroll
               for (int i = 0; i < 2; ++i) {
@@ -626,10 +662,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const __half2 q1 = __hsub2(u32_as_h2(bytes_to_h2(hi_n, sel)), b8);
                     const __half2 w0h = __hmul2(q0, s2);
                     const __half2 w1h = __hmul2(q1, s2);
+                    // w_lo = q * s - w_hi (exact in fp16), times 2^8 (exact)
                     hv[i][0][wdx * 2 + half_sel] = h2_as_u32(w0h);
-                    lv[i][0][wdx * 2 + half_sel] = h2_as_u32(__hfma2(q0, s2, __hneg2(w0h)));
+                    lv[i][0][wdx * 2 + half_sel] = h2_as_u32(__hmul2(__hfma2(q0, s2, __hneg2(w0h)), h256));
                     hv[i][1][wdx * 2 + half_sel] = h2_as_u32(w1h);
-                    lv[i][1][wdx * 2 + half_sel] = h2_as_u32(__hfma2(q1, s2, __hneg2(w1h)));
+                    lv[i][1][wdx * 2 + half_sel] = h2_as_u32(__hmul2(__hfma2(q1, s2, __hneg2(w1h)), h256));
                   }
                 }
               }
@@ -641,7 +678,9 @@ __global__ void __launch_bounds__(kThreads, 1)
               break;
             }
               uint8_t* hi = w16;
-              uint8_t* lo = w16 + kNT * Cfg::kW16Bytes;
+              // E5M2 w_lo of this tile: [64 k][128 n] bytes, 128-byte swizzle.
+              uint8_t* lo8 = sF + fs * Cfg::kFBytes + kNT * Cfg::kW16Bytes +
+                             (Cfg::kAltStages ? 0 : grp * Cfg::kLoBlockBytes);
               const int chunk = qn >> 1;
 #pragma unroll
               for (int i = 0; i < 2; ++i) {
@@ -655,9 +694,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const int off = chunk * 8192 + row * 128 + (((v0 + e) ^ (row & 7)) << 4);
                     *reinterpret_cast<uint4*>(hi + off) = make_uint4(hv[i][rr][4 * e], hv[i][rr][4 * e + 1],
                                                                      hv[i][rr][4 * e + 2], hv[i][rr][4 * e + 3]);
-                    *reinterpret_cast<uint4*>(lo + off) = make_uint4(lv[i][rr][4 * e], lv[i][rr][4 * e + 1],
-                                                                     lv[i][rr][4 * e + 2], lv[i][rr][4 * e + 3]);
                   }
+                  // 2^8 w_lo has at most 3 significant bits: as a normal fp16
+                  // its low byte is zero and its high byte is the E5M2 value.
+                  uint32_t w8[4];
+#pragma unroll
+                  for (int j = 0; j < 4; ++j) w8[j] = __byte_perm(lv[i][rr][2 * j], lv[i][rr][2 * j + 1], 0x7531);
+                  *reinterpret_cast<uint4*>(lo8 + row * 128 + (((2 * qn + i) ^ (row & 7)) << 4)) =
+                      make_uint4(w8[0], w8[1], w8[2], w8[3]);
                 }
               }
             }
@@ -1067,6 +1111,35 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ partial, int spli
   }
 }
 
+// X8[m][k] = E5M2(2^-8 * X[m][k]) for the int4 M >= 65 layout's w_lo MMAs,
+// round to nearest, saturating (rows of K bytes). Eight values per thread.
+__global__ void x_to_e5m2_kernel(const __half* __restrict__ X, int64_t ldx, int M, int K, uint8_t* __restrict__ X8) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int per_row = K / 8;
+  const int64_t total = static_cast<int64_t>(M) * per_row;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t m = i / per_row;
+    const int k = static_cast<int>(i % per_row) * 8;
+    const uint4 v = __ldg(reinterpret_cast<const uint4*>(X + m * ldx + k));
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    uint32_t o[2];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      uint16_t b[2];
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        const float2 f = __half22float2(u32_as_h2(w[2 * j + t]));
+        // cvt.rn.satfinite.e5m2x2.f32 d, a, b: a -> high byte, b -> low byte
+        asm("cvt.rn.satfinite.e5m2x2.f32 %0, %1, %2;" : "=h"(b[t]) : "f"(f.y * 0.00390625f), "f"(f.x * 0.00390625f));
+      }
+      o[j] = static_cast<uint32_t>(b[0]) | (static_cast<uint32_t>(b[1]) << 16);
+    }
+    *reinterpret_cast<uint2*>(X8 + m * K + k) = make_uint2(o[0], o[1]);
+  }
+}
+
 template <int kQ, bool kSwap, int kNX, int kNT = 1>
 int launch_wq(const QProblem& p, cudaStream_t stream) {
   using Cfg = QCfg<kQ, kSwap, kNX, kNT>;
@@ -1112,6 +1185,22 @@ int launch_wq(const QProblem& p, cudaStream_t stream) {
     if (rc != NESO_OK) return rc;
     y_tma = 1;
   }
+  // int4 M >= 65: the E5M2 copy of X for the w_lo MMAs, in the stream's
+  // input workspace, written by a conversion kernel launched just before.
+  CUtensorMap tmX8 = tmX;
+  uint8_t* x8 = nullptr;
+  if constexpr (Cfg::kF8Lo) {
+    void* ws = nullptr;
+    int rc = stream_workspace(stream, static_cast<size_t>(p.M) * p.K, &ws, kWorkspaceInputs);
+    if (rc != NESO_OK) return rc;
+    x8 = static_cast<uint8_t*>(ws);
+    uint64_t dims[2] = {static_cast<uint64_t>(p.K), static_cast<uint64_t>(p.M)};
+    uint64_t strides[1] = {static_cast<uint64_t>(p.K)};
+    uint32_t box[2] = {64, static_cast<uint32_t>(kNX)};
+    rc = encode_tmap(&tmX8, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, x8, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B);
+    if (rc != NESO_OK) return rc;
+    if ((reinterpret_cast<uintptr_t>(p.X) & 15u) != 0) return fail(NESO_ERR_MISALIGNED, "activations must be 16-byte aligned");
+  }
   QArgs args{};
   args.y_tma = y_tma;
   args.Y = p.Y;
@@ -1135,7 +1224,15 @@ int launch_wq(const QProblem& p, cudaStream_t stream) {
     int src = kernel_setup(reinterpret_cast<const void*>(kern), Cfg::kSmemBytes, nullptr);
     if (src != NESO_OK) return src;
   }
-  cudaError_t e = launch_pdl(kern, dim3(grid), dim3(kThreads), Cfg::kSmemBytes, stream, tmX, tmW, tmS, tmY, args);
+  cudaError_t e = cudaSuccess;
+  if constexpr (Cfg::kF8Lo) {
+    const int64_t items = static_cast<int64_t>(p.M) * (p.K / 8);
+    const int blocks = static_cast<int>(std::min<int64_t>((items + 255) / 256, 8 * sm_count()));
+    e = launch_pdl(x_to_e5m2_kernel, dim3(blocks), dim3(256), 0, stream, static_cast<const __half*>(p.X),
+                   static_cast<int64_t>(p.ldx), p.M, p.K, x8);
+    if (e != cudaSuccess) return cuda_fail(e, "X conversion launch");
+  }
+  e = launch_pdl(kern, dim3(grid), dim3(kThreads), Cfg::kSmemBytes, stream, tmX, tmW, tmS, tmY, tmX8, args);
   if (e != cudaSuccess) return cuda_fail(e, "wq_gemm launch");
   if (args.partial != nullptr) {
     if (args.splits > kReduceMaxSplits) return fail(NESO_ERR_UNSUPPORTED, "split-K plan of %d splits", args.splits);
@@ -1538,7 +1635,8 @@ int dispatch_wq(const QProblem& p, cudaStream_t stream) {
   if (p.M <= 64) return launch_wq<kQ, true, 64>(p, stream);
   if (p.rows2) {
     // 256-row units: W8A16 with paired channel tiles (256 x 256), W4A16 with
-    // one tile (256 x 128; its hi/lo fp16 copies leave no room for pairs).
+    // one tile (256 x 128; its fp16 w_hi and E5M2 w_lo tiles and E5M2 X
+    // blocks leave no room for pairs).
     if constexpr (kQ == kInt8) {
       return launch_wq<kQ, false, 256, 2>(p, stream);
     } else {

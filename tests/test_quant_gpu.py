@@ -163,6 +163,26 @@ def test_w4a16_256_row_units_ragged(dev):
     torch.testing.assert_close(y.cpu(), oracle.w4a16_g128_matmul(x, wq, s), **TOL)
 
 
+@pytest.mark.parametrize("M,N,K", [(100, 256, 1024), (300, 384, 4096), (2048, 1376, 4096)])
+def test_w4a16_large_m_carries_the_product_remainder(dev, M, N, K):
+    # M >= 65 layout: each weight q * s enters as fp16(q * s) plus the exact
+    # remainder (at most 3 significant bits, E5M2 once scaled by 2^8) times
+    # an E5M2 copy of X. Against the float64 sum of x * q * s the error must
+    # stay well below both the 2e-3 tolerance and the error of fp16(q * s)
+    # alone, which shows the remainder term is applied.
+    x, q, s = _w4(M, N, K, seed=M + N)
+    wq = oracle.pack_int4(q)
+    y = ops.w4a16_g128_matmul(x.to(dev), wq.to(dev), s.to(dev))
+    rows = torch.arange(M) if M <= 300 else torch.tensor([0, 1, 511, 1024, 1500, M - 1])
+    srep = s.repeat_interleave(128, dim=0)
+    exact = x[rows].double() @ (q.double() * srep.double())
+    hi_only = x[rows].double() @ (q.half() * srep).double()
+    err = (y[rows.to(dev)].cpu().double() - exact).abs().max().item()
+    err_hi = (hi_only - exact).abs().max().item()
+    assert err < 5e-4, err
+    assert err < err_hi / 4, (err, err_hi)
+
+
 def test_w8a16_c_row_stride_not_multiple_of_4(dev):
     # Reference launch with stride_cm = N + 1: Y rows are not 16-byte aligned,
     # so the M >= 65 epilogue writes rows directly instead of TMA stores.
