@@ -18,30 +18,33 @@
 //               two groups take alternate K blocks (or, with two channel
 //               tiles per unit, one tile each of every K block).
 //                 int8: exact, (b ^ 0x80) | 0x6400 as fp16 is 1024 + b + 128.
-//                 int4, M >= 65 layout: q exact the same way, then w = q * s
+//                 int4, M >= 129 layout: q exact the same way, then w = q * s
 //                 is split into w_hi = fp16(q * s) and w_lo = fma(q, s, -w_hi)
 //                 (the exact rounding error, at most 3 significant bits),
 //                 stored as E5M2 of 2^8 w_lo (exact), so the MMAs sum q * s
 //                 up to the E5M2 rounding of X in the w_lo term.
-//                 int4, M <= 64 layout: q only (exact in fp16); the group
+//                 int4, swapped layout (M <= 128): q only (exact in fp16); the group
 //                 scale is applied to fp32 partial sums instead (below).
 //   warp 1      tcgen05.mma issuer (kind::f16, fp32 accumulators in TMEM);
-//               int4 M >= 65 adds two kind::f8f6f4 MMAs (K = 32) per K
+//               int4 M >= 129 adds two kind::f8f6f4 MMAs (K = 32) per K
 //               block for w_lo against an E5M2 copy of 2^-8 X (written by
-//               a conversion kernel before the matmul); int4 M <= 64
+//               a conversion kernel before the matmul); int4 M <= 128
 //               accumulates each run of K blocks inside one 128-wide scale
 //               group into its own buffer (double-buffered), so the epilogue
 //               applies that group's scales while the next run accumulates.
-//   warp 2      (int4, M <= 64) TMA producer of each run's scale row.
+//   warp 2      (int4, M <= 128) TMA producer of each run's scale row.
 //   warps 8-11  epilogue: TMEM -> registers -> (int8: * f32(scale[n])) ->
 //               swizzled staging -> TMA stores of Y (M >= 65 layout), or
-//               direct coalesced stores (M <= 64 layout). int4 M <= 64: the
-//               running sums stay in registers, += partial * scale[g][n].
+//               direct coalesced stores (swapped layout). int4 swapped: the
+//               running sums stay in registers, += partial * scale[g][n]
+//               (M = 65..128: 128 sums a thread, the epilogue warpgroup
+//               takes registers from warpgroup 0 with setmaxnreg).
 // Orientation: M >= 65 computes Y units of 128 or 256 rows x 128 or 256
 // channels (a host cost model picks the shape and any K split) with X as the
-// A operand; M <= 64 swaps operands (A = dequantised W^T with M' = 128 output
-// channels, B = X with N' = M rounded up to 16/32/64) so decode-sized batches
-// still run on the tensor cores and the weight stream stays at HBM speed.
+// A operand; M <= 64 (int4: M <= 128) swaps operands (A = dequantised W^T
+// with M' = 128 output channels, B = X with N' = M rounded up to
+// 16/32/64/128) so decode-sized batches still run on the tensor cores and the
+// weight stream stays at HBM speed.
 #include <algorithm>
 #include <mutex>
 
@@ -80,6 +83,14 @@ struct QCfg {
   // kind::f8f6f4 (twice the fp16 rate) against an E5M2 copy of X scaled by
   // 2^-8, appended to each X stage.
   static constexpr bool kF8Lo = kQ == kInt4G128 && !kSwap;
+  // int4 swapped layout with 128 activation rows (M = 65..128): each
+  // epilogue thread keeps 128 running sums, so warpgroup 2 (the epilogue)
+  // grows to kRegsEpi registers and warpgroup 0 (TMA, MMA issuer) shrinks to
+  // kRegsLow; the two convert warpgroups keep the launch's 128.
+  static constexpr bool kWideEpi = kGS && kNX * kNT > 64;
+  static constexpr uint32_t kRegsLow = 80;
+  static constexpr uint32_t kRegsEpi = 176;
+  static_assert(!kWideEpi || kRegsLow + kRegsEpi == 2 * 128, "register split must fit the launch pool");
   static constexpr int kRawTileBytes = (kQ == kInt8) ? 64 * 128 : kGS ? 32 * 128 : 32 * 128 + 1024;
   static constexpr int kRawBytes = kNT * kRawTileBytes;
   // 64-deep K blocks per fp16 weight (F) and activation (X) stage: two in the
@@ -286,6 +297,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   pdl_wait();
   DevStatus quiet = args.st;
   quiet.word = nullptr;
+  // Warpgroup 0 gives registers up here, converged; the epilogue takes them
+  // at the top of its branch.
+  if constexpr (Cfg::kWideEpi) {
+    if (warp < 4) setmaxnreg_dec<Cfg::kRegsLow>();
+  }
 
   if ((warp == 0 || warp == 3) && lane == 0) {
     // ----------------------------------------------- TMA producers (R / X) --
@@ -715,6 +731,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp >= 8 && warp < 12) {
     // ------------------------------------------------------------ epilogue --
+    if constexpr (Cfg::kWideEpi) setmaxnreg_inc<Cfg::kRegsEpi>();
     const uint32_t q = warp & 3;
     const int lrow = q * 32 + lane;  // TMEM lane: m (normal) or n (swap)
     const uint32_t lane_base = tmem + ((q * 32) << 16);
@@ -999,8 +1016,13 @@ void plan_normal(QProblem& p, int sms, size_t max_partial) {
 // Split K when the output tiles alone cannot fill the SMs (small M): pick the
 // split count whose units fill the persistent grid best, preferring fewer
 // splits (each split adds an M x N fp32 partial write and read).
+// Operands swapped (W as the 128-row A operand, X as B with N' = M): M <= 64,
+// and int4 up to M = 128 (its group-scaled sums keep the weights exact in one
+// fp16 MMA per K step; the M >= 65 layout leaves SMs idle at M = 128).
+bool swapped_layout(const QProblem& p) { return p.M <= 64 || (p.kind == kInt4G128 && p.M <= 128); }
+
 void plan_splits(QProblem& p, int sms, size_t max_partial = SIZE_MAX) {
-  const bool swap = p.M <= 64;
+  const bool swap = swapped_layout(p);
   const int num_m = swap ? 1 : (p.M + 127) / 128;
   const int num_k = (p.K + kBK - 1) / kBK;
   p.splits = 1;
@@ -1221,8 +1243,14 @@ int launch_wq(const QProblem& p, cudaStream_t stream) {
   const int grid = units < sm_count() ? units : sm_count();
   auto kern = wq_gemm_kernel<kQ, kSwap, kNX, kNT>;
   {
-    int src = kernel_setup(reinterpret_cast<const void*>(kern), Cfg::kSmemBytes, nullptr);
+    cudaFuncAttributes fa{};
+    int src = kernel_setup(reinterpret_cast<const void*>(kern), Cfg::kSmemBytes, &fa);
     if (src != NESO_OK) return src;
+    // setmaxnreg.inc draws on the block's launch pool: refuse a split it cannot fund.
+    if (Cfg::kWideEpi && fa.numRegs < 128) {
+      return fail(NESO_ERR_LAUNCH, "wq_gemm: %d registers/thread cannot fund the %u/%u warpgroup split", fa.numRegs,
+                  Cfg::kRegsLow, Cfg::kRegsEpi);
+    }
   }
   cudaError_t e = cudaSuccess;
   if constexpr (Cfg::kF8Lo) {
@@ -1633,6 +1661,9 @@ int dispatch_wq(const QProblem& p, cudaStream_t stream) {
   if (p.M <= 16) return p.pair ? launch_wq<kQ, true, 16, 2>(p, stream) : launch_wq<kQ, true, 16>(p, stream);
   if (p.M <= 32) return launch_wq<kQ, true, 32>(p, stream);
   if (p.M <= 64) return launch_wq<kQ, true, 64>(p, stream);
+  if constexpr (kQ == kInt4G128) {
+    if (p.M <= 128) return launch_wq<kQ, true, 128>(p, stream);
+  }
   if (p.rows2) {
     // 256-row units: W8A16 with paired channel tiles (256 x 256), W4A16 with
     // one tile (256 x 128; its fp16 w_hi and E5M2 w_lo tiles and E5M2 X
