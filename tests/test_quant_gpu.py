@@ -83,7 +83,7 @@ def test_w8a16_baseline_shapes(dev, M):
         torch.testing.assert_close(y.cpu(), oracle.w8a16_matmul(x, w, s), **TOL)
 
 
-@pytest.mark.parametrize("M", [1, 3, 16, 40, 64, 100, 128])
+@pytest.mark.parametrize("M", [1, 3, 16, 40, 64, 65, 100, 128, 129])
 def test_w4a16_sizes(dev, M):
     N, K = 256, 384
     x, q, s = _w4(M, N, K, seed=M)
@@ -163,9 +163,9 @@ def test_w4a16_256_row_units_ragged(dev):
     torch.testing.assert_close(y.cpu(), oracle.w4a16_g128_matmul(x, wq, s), **TOL)
 
 
-@pytest.mark.parametrize("M,N,K", [(100, 256, 1024), (300, 384, 4096), (2048, 1376, 4096)])
+@pytest.mark.parametrize("M,N,K", [(200, 256, 1024), (300, 384, 4096), (2048, 1376, 4096)])
 def test_w4a16_large_m_carries_the_product_remainder(dev, M, N, K):
-    # M >= 65 layout: each weight q * s enters as fp16(q * s) plus the exact
+    # M >= 129 layout: each weight q * s enters as fp16(q * s) plus the exact
     # remainder (at most 3 significant bits, E5M2 once scaled by 2^8) times
     # an E5M2 copy of X. Against the float64 sum of x * q * s the error must
     # stay well below both the 2e-3 tolerance and the error of fp16(q * s)
