@@ -10,7 +10,16 @@ None and names bound in the kernel's namespace are constexpr values, ``:16``
 and ``:1`` are specialisation hints), checks it against the kernel's argument
 list, and
 returns an ``AOTResult`` with the same metadata schema. ``save(prefix)`` writes
-``{prefix}.json`` (the launch metadata; the code is the shared library).
+``{prefix}.json`` (the launch metadata). For the elementwise kernels
+(``vector_add``, ``add_kernel``, ``scale``) it also writes ``{prefix}.cu`` and
+``{prefix}.cubin``: a standalone sm_100a kernel with the reference's parameter
+list and Triton program semantics (program ``i`` covers elements
+``[i*BLOCK_SIZE, (i+1)*BLOCK_SIZE)``, masked by ``n_elements``), which a native
+consumer loads with ``cuModuleLoadData`` and launches from the metadata alone
+(grid from ``grid``, block = ``threadgroup_size``, parameters in order), as the
+reference's consumers load ``{prefix}.metallib``. The other kernels are TMA /
+tcgen05 kernels whose launch needs host-built tensor maps and plans: their
+code is ``libneso_b200.so`` and they are launched through its C ABI.
 
 CLI (mirrors ``neso``, aot_compile.py:270-364)::
 
@@ -21,7 +30,9 @@ from __future__ import annotations
 
 import argparse
 import json
+import subprocess
 import sys
+import tempfile
 from dataclasses import asdict, dataclass, field
 from pathlib import Path
 from typing import Any, Mapping, Sequence
@@ -163,10 +174,74 @@ def build_parameters(parameter_names: Sequence[str], source_types: Mapping[str, 
     return [KernelParameter(i, n, t, _C_TYPES.get(t, t), t.startswith("*")) for i, n, t in typed if t != "constexpr"]
 
 
+# --- standalone cubins for the elementwise kernels --------------------------
+# Each entry: the reference's runtime parameters with the Triton type each must
+# have, and the per-element statement. The generated kernel is one CTA per
+# program (grid = cdiv(n_elements, BLOCK_SIZE)), its threads striding over the
+# program's BLOCK_SIZE elements: the same fp32 operation per element as the
+# library kernel, so results are bit-identical to it and to torch.
+_STANDALONE = {
+    "vector_add": ([("x", "*fp32"), ("y", "*fp32"), ("output", "*fp32"), ("n_elements", "i32")],
+                   "output[o] = x[o] + y[o];"),
+    "add_kernel": ([("x_ptr", "*fp32"), ("y_ptr", "*fp32"), ("z_ptr", "*fp32"), ("n_elements", "i32")],
+                   "z_ptr[o] = x_ptr[o] + y_ptr[o];"),
+    "scale": ([("x", "*fp32"), ("output", "*fp32"), ("factor", "fp32"), ("n_elements", "i32")],
+              "output[o] = x[o] * factor;"),
+}
+_OUT_PARAMS = {"output", "z_ptr"}
+
+
+def standalone_source(name: str, source_types: Mapping[str, str], block: int, threads: int) -> str | None:
+    """CUDA source of the standalone kernel, or None when `name` has none or
+    the signature's types differ from the ones it is written for."""
+    spec = _STANDALONE.get(name)
+    if spec is None or block <= 0 or threads <= 0:
+        return None
+    params, stmt = spec
+    if any(source_types.get(p) != t for p, t in params):
+        return None
+    decl = []
+    for p, t in params:
+        if t == "*fp32":
+            decl.append(f"{'' if p in _OUT_PARAMS else 'const '}float* __restrict__ {p}")
+        elif t == "fp32":
+            decl.append(f"float {p}")
+        else:
+            decl.append(f"int {p}")
+    return (f"// {name}: generated by neso_b200.aot for sm_100a. Program blockIdx.x covers elements\n"
+            f"// [blockIdx.x * {block}, (blockIdx.x + 1) * {block}) below n_elements; {threads} threads.\n"
+            f"extern \"C\" __global__ void __launch_bounds__({threads}) {name}({', '.join(decl)}) {{\n"
+            f"  const long long base = static_cast<long long>(blockIdx.x) * {block};\n"
+            f"  for (int i = threadIdx.x; i < {block}; i += {threads}) {{\n"
+            f"    const long long o = base + i;\n"
+            f"    if (o < n_elements) {stmt}\n"
+            f"  }}\n"
+            f"}}\n")
+
+
+def build_cubin(source: str) -> bytes | None:
+    """nvcc -cubin for sm_100a; None when nvcc is not available."""
+    try:
+        from .build import ARCH, nvcc
+        compiler = nvcc()
+    except (ImportError, RuntimeError):
+        return None
+    with tempfile.TemporaryDirectory() as d:
+        src, out = Path(d) / "k.cu", Path(d) / "k.cubin"
+        src.write_text(source)
+        res = subprocess.run([compiler, "-cubin", *ARCH, "-O3", "-o", str(out), str(src)],
+                             capture_output=True, text=True)
+        if res.returncode != 0:
+            raise RuntimeError(f"nvcc -cubin failed:\n{res.stdout}\n{res.stderr}")
+        return out.read_bytes()
+
+
 @dataclass
 class AOTResult:
     """Result of ``compile_kernel``; ``to_metadata()`` has the keys of the
-    reference's AOTResult.to_metadata() (src/neso/aot_compile.py:108-117)."""
+    reference's AOTResult.to_metadata() (src/neso/aot_compile.py:108-117).
+    ``source`` / ``cubin_bytes`` hold the standalone kernel where there is one
+    (the reference's ``msl_source`` / ``metallib_bytes``), else "" / None."""
 
     kernel_name: str
     parameters: list[KernelParameter]
@@ -175,6 +250,8 @@ class AOTResult:
     num_warps: int
     grid: list[str]
     library: str = field(default="")
+    source: str = field(default="")
+    cubin_bytes: bytes | None = field(default=None)
 
     def to_metadata(self) -> dict[str, Any]:
         return {
@@ -192,9 +269,19 @@ class AOTResult:
 
     def save(self, output_prefix: str) -> dict[str, str]:
         prefix = Path(output_prefix)
+        paths = {}
+        if self.cubin_bytes is not None:
+            cubin_path = prefix.with_suffix(".cubin")
+            cubin_path.write_bytes(self.cubin_bytes)
+            paths["cubin"] = str(cubin_path)
+        if self.source:
+            src_path = prefix.with_suffix(".cu")
+            src_path.write_text(self.source)
+            paths["source"] = str(src_path)
         json_path = prefix.with_suffix(".json")
         json_path.write_text(json.dumps(self.to_metadata(), indent=2))
-        return {"json": str(json_path)}
+        paths["json"] = str(json_path)
+        return paths
 
 
 def _resolve(fn) -> _kernels.Kernel:
@@ -208,9 +295,10 @@ def _resolve(fn) -> _kernels.Kernel:
 
 def compile_kernel(fn, signature: str, num_warps: int = 4, grid: list[str] | None = None,
                    target: str | None = None, require_metallib: bool = False,
-                   emit_metallib: bool = True) -> AOTResult:
+                   emit_metallib: bool = True, emit_cubin: bool = True) -> AOTResult:
     """Resolve ``fn`` (a kernel name, or a function with that ``__name__``) and
-    return its launch metadata for ``signature``.
+    return its launch metadata for ``signature``; for the elementwise kernels,
+    with ``emit_cubin`` and nvcc present, also the standalone sm_100a cubin.
 
     ``target``, if given, must name this backend ("neso_b200:sm_100a:32");
     ``require_metallib`` cannot be satisfied (there is no Metal toolchain).
@@ -241,10 +329,20 @@ def compile_kernel(fn, signature: str, num_warps: int = 4, grid: list[str] | Non
         if parsed.source_types.get(c) != "constexpr":
             raise ValueError(f"{c!r} is a constexpr of {k.name}; give it a literal value in the signature")
     meta = k.metadata()
+    source = ""
+    cubin = None
+    if emit_cubin:
+        block = parsed.constants.get("BLOCK_SIZE")
+        src = standalone_source(k.name, parsed.source_types, block if isinstance(block, int) else 0,
+                                int(meta["threadgroup_size"]))
+        if src is not None:
+            cubin = build_cubin(src)
+            source = src if cubin is not None else ""
     return AOTResult(kernel_name=k.name, parameters=build_parameters(runtime, parsed.source_types),
                      constants=dict(parsed.constants), threadgroup_size=meta["threadgroup_size"],
                      num_warps=meta["num_warps"], grid=grid or ["1", "1", "1"],
-                     library=str(Path(__file__).resolve().parent / "libneso_b200.so"))
+                     library=str(Path(__file__).resolve().parent / "libneso_b200.so"),
+                     source=source, cubin_bytes=cubin)
 
 
 def compile_many(fn, configs: list[dict[str, Any]], target: str | None = None) -> list[AOTResult]:
@@ -290,7 +388,9 @@ def main(argv: list[str] | None = None) -> int:
         print(f"  [{p['index']}] {p['name']}: {p['metal_type']}  ({'buffer' if p['is_pointer'] else 'scalar'})")
     print(f"Grid: ({', '.join(res.grid)})")
     paths = res.save(a.output or a.kernel)
-    print(f"  {paths['json']}")
+    for key in ("cubin", "source", "json"):
+        if key in paths:
+            print(f"  {paths[key]}")
     return 0
 
 

@@ -84,3 +84,65 @@ def test_signature_value_forms_and_hints():
     params = aot.build_parameters(["p", "n", "k"], {"p": "*fp16", "k": "constexpr"})
     assert [(q.index, q.name, q.type, q.is_pointer) for q in params] == [(0, "p", "*fp16", True),
                                                                          (1, "n", "i32", False)]
+
+
+def _elf_symbols(blob: bytes) -> dict[str, int]:
+    """Name -> st_info of every symbol in an ELF64 little-endian image."""
+    import struct
+    shoff = struct.unpack_from("<Q", blob, 0x28)[0]
+    shentsize, shnum = struct.unpack_from("<HH", blob, 0x3A)
+    secs = [struct.unpack_from("<IIQQQQIIQQ", blob, shoff + i * shentsize) for i in range(shnum)]
+    out = {}
+    for sec in secs:
+        if sec[1] != 2:  # SHT_SYMTAB
+            continue
+        strtab = secs[sec[6]]
+        for off in range(sec[4], sec[4] + sec[5], 24):
+            name_off, info = struct.unpack_from("<IB", blob, off)
+            end = blob.index(b"\0", strtab[4] + name_off)
+            out[blob[strtab[4] + name_off:end].decode()] = info
+    return out
+
+
+needs_nvcc = pytest.mark.skipif(__import__("shutil").which("nvcc") is None
+                                and not __import__("os").path.exists("/usr/local/cuda/bin/nvcc"),
+                                reason="nvcc not available")
+
+
+@needs_nvcc
+@pytest.mark.parametrize("name,sig", [("vector_add", "*fp32, *fp32, *fp32, i32, 1024"),
+                                      ("add_kernel", "*fp32, *fp32, *fp32, i32, 1024"),
+                                      ("scale", "*fp32, *fp32, fp32, i32, 256")])
+def test_elementwise_kernels_get_a_standalone_cubin(name, sig):
+    # The reference writes a compiled library beside the metadata
+    # (src/neso/aot_compile.py:56-106); here an sm_100a cubin whose entry has
+    # the kernel's name and its runtime parameters in metadata order.
+    r = aot.compile_kernel(name, sig, grid=[f"cdiv(n_elements, {sig.split(', ')[-1]})", "1", "1"])
+    blob = r.cubin_bytes
+    assert blob is not None and blob[:4] == b"\x7fELF"
+    assert int.from_bytes(blob[0x12:0x14], "little") == 190  # EM_CUDA
+    syms = _elf_symbols(blob)
+    assert name in syms and (syms[name] >> 4) == 1 and (syms[name] & 0xF) == 2  # global function
+    assert f'extern "C" __global__ void __launch_bounds__({r.threadgroup_size}) {name}(' in r.source
+    assert f"* {sig.split(', ')[-1]};" in r.source
+
+
+@needs_nvcc
+def test_save_writes_cubin_source_and_metadata(tmp_path):
+    r = aot.compile_kernel("vector_add", "*fp32, *fp32, *fp32, i32, 1024", grid=["cdiv(n_elements, 1024)", "1", "1"])
+    paths = r.save(str(tmp_path / "vector_add"))
+    assert set(paths) == {"cubin", "source", "json"}
+    assert (tmp_path / "vector_add.cubin").read_bytes() == r.cubin_bytes
+    assert json.loads((tmp_path / "vector_add.json").read_text())["kernel_name"] == "vector_add"
+
+
+def test_no_cubin_where_there_is_no_standalone_kernel():
+    # TMA / tcgen05 kernels are launched through the library's C ABI, and an
+    # elementwise signature with other element types has no standalone form.
+    r = aot.compile_kernel("matmul_kernel",
+                           "*fp16:16, *fp16:16, *fp32:16, i32, i32, i32, i32, i32, i32, i32, i32, i32, 128, 128, 32")
+    assert r.cubin_bytes is None and r.source == ""
+    r = aot.compile_kernel("add_kernel", "*fp16, *fp16, *fp16, i32, 1024")
+    assert r.cubin_bytes is None and r.source == ""
+    r = aot.compile_kernel("vector_add", "*fp32, *fp32, *fp32, i32, 1024", emit_cubin=False)
+    assert r.cubin_bytes is None and r.save is not None
