@@ -105,7 +105,6 @@ struct QCfg {
   static constexpr int kXBytes = kFKB * kXBlockBytes + kX8Bytes;
   static constexpr int kW16BlockBytes = kBK * kTileN * 2;      // 16 KB: one K block of one tile
   static constexpr int kW16Bytes = kFKB * kW16BlockBytes;      // one fp16 copy of one tile
-  static constexpr int kNumW16 = 1;
   static constexpr int kLoBlockBytes = kBK * kTileN;  // 8 KB: one K block of one tile's E5M2 w_lo
   // Convert groups (warps 4-7, 12-15). A group's per-stage cost is mostly
   // fixed (barrier waits, the proxy fence, loop control: ~1300 cycles per
@@ -117,7 +116,7 @@ struct QCfg {
   static constexpr int kConvGroupsPerStage = kAltStages ? 1 : kNT;
   static constexpr int kScSlots = kGS ? 16 : 0;
   static constexpr int kScBytes = kNT * 256;
-  static constexpr int kFTileBytes = kNumW16 * kW16Bytes + (kF8Lo ? kLoBlockBytes : 0);
+  static constexpr int kFTileBytes = kW16Bytes + (kF8Lo ? kLoBlockBytes : 0);
   static constexpr int kFBytes = kNT * kFTileBytes;
   // kNX = 256 in the M >= 65 layout: 256-row units, two 128-row accumulators
   // (every fp16 weight stage feeds two MMAs per K step).
@@ -398,9 +397,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           tc_fence_after();
           const uint64_t xd0 = sdesc_sw128(smem_u32(sX + xs * Cfg::kXBytes), 16, 1024);
-          // F stage = [fp16 copy p][channel tile g][64 k][128 n]: with kNT = 2
-          // one N = 256 instruction covers both tiles (64-channel chunks 8 KB
-          // apart throughout).
+          // F stage = [channel tile g][64 k][128 n] fp16 (then, int4 M >= 129,
+          // the E5M2 w_lo tiles): with kNT = 2 one N = 256 instruction covers
+          // both tiles (64-channel chunks 8 KB apart throughout).
           const uint64_t wd0 = sdesc_sw128(smem_u32(sF + fs * Cfg::kFBytes), 8192, 1024);
           if (leader) {
 #pragma unroll
@@ -408,21 +407,17 @@ __global__ void __launch_bounds__(kThreads, 1)
               const int b = kk / (kBK / 16), k = kk % (kBK / 16);
               if (b >= nkb) break;
               const uint64_t xd = xd0 + static_cast<uint64_t>((b * Cfg::kXBlockBytes + k * 32) >> 4);
+              const uint64_t wd = wd0 + static_cast<uint64_t>((b * Cfg::kW16BlockBytes + k * 2048) >> 4);
+              const uint32_t acc = (!first || kk != 0) ? 1u : 0u;
+              if (kSwap) {
 #pragma unroll
-              for (int p = 0; p < Cfg::kNumW16; ++p) {
-                const uint64_t wd =
-                    wd0 + static_cast<uint64_t>((p * kNT * Cfg::kW16Bytes + b * Cfg::kW16BlockBytes + k * 2048) >> 4);
-                const uint32_t acc = (!first || kk != 0 || p != 0) ? 1u : 0u;
-                if (kSwap) {
+                for (int g = 0; g < kNT; ++g) {
+                  umma_f16_ss(d_tmem + g * kNX, wd + static_cast<uint64_t>((g * Cfg::kW16Bytes) >> 4), xd, idesc, acc);
+                }
+              } else {
 #pragma unroll
-                  for (int g = 0; g < kNT; ++g) {
-                    umma_f16_ss(d_tmem + g * kNX, wd + static_cast<uint64_t>((g * Cfg::kW16Bytes) >> 4), xd, idesc, acc);
-                  }
-                } else {
-#pragma unroll
-                  for (int h = 0; h < Cfg::kRowHalves; ++h) {
-                    umma_f16_ss(d_tmem + h * kUnitN, xd + static_cast<uint64_t>((h * 16384) >> 4), wd, idesc, acc);
-                  }
+                for (int h = 0; h < Cfg::kRowHalves; ++h) {
+                  umma_f16_ss(d_tmem + h * kUnitN, xd + static_cast<uint64_t>((h * 16384) >> 4), wd, idesc, acc);
                 }
               }
             }
@@ -454,9 +449,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           tc_fence_after();
           const uint64_t xd0 = sdesc_sw128(smem_u32(sX + xs * Cfg::kXBytes), 16, 1024);
-          // F stage = [fp16 copy p][channel tile g][64 k][128 n]: with kNT = 2
-          // one N = 256 instruction covers both tiles (64-channel chunks 8 KB
-          // apart throughout).
+          // F stage = [channel tile g][64 k][128 n] fp16 (then, int4 M >= 129,
+          // the E5M2 w_lo tiles): with kNT = 2 one N = 256 instruction covers
+          // both tiles (64-channel chunks 8 KB apart throughout).
           const uint64_t wd0 = sdesc_sw128(smem_u32(sF + fs * Cfg::kFBytes), 8192, 1024);
           if (leader) {
 #pragma unroll
@@ -464,21 +459,17 @@ __global__ void __launch_bounds__(kThreads, 1)
               const int b = kk / (kBK / 16), k = kk % (kBK / 16);
               if (b >= nkb) break;
               const uint64_t xd = xd0 + static_cast<uint64_t>((b * Cfg::kXBlockBytes + k * 32) >> 4);
+              const uint64_t wd = wd0 + static_cast<uint64_t>((b * Cfg::kW16BlockBytes + k * 2048) >> 4);
+              const uint32_t acc = (kb != u.kb0 || kk != 0) ? 1u : 0u;
+              if (kSwap) {
 #pragma unroll
-              for (int p = 0; p < Cfg::kNumW16; ++p) {
-                const uint64_t wd =
-                    wd0 + static_cast<uint64_t>((p * kNT * Cfg::kW16Bytes + b * Cfg::kW16BlockBytes + k * 2048) >> 4);
-                const uint32_t acc = (kb != u.kb0 || kk != 0 || p != 0) ? 1u : 0u;
-                if (kSwap) {
+                for (int g = 0; g < kNT; ++g) {
+                  umma_f16_ss(d_tmem + g * kNX, wd + static_cast<uint64_t>((g * Cfg::kW16Bytes) >> 4), xd, idesc, acc);
+                }
+              } else {
 #pragma unroll
-                  for (int g = 0; g < kNT; ++g) {
-                    umma_f16_ss(d_tmem + g * kNX, wd + static_cast<uint64_t>((g * Cfg::kW16Bytes) >> 4), xd, idesc, acc);
-                  }
-                } else {
-#pragma unroll
-                  for (int h = 0; h < Cfg::kRowHalves; ++h) {
-                    umma_f16_ss(d_tmem + h * kUnitN, xd + static_cast<uint64_t>((h * 16384) >> 4), wd, idesc, acc);
-                  }
+                for (int h = 0; h < Cfg::kRowHalves; ++h) {
+                  umma_f16_ss(d_tmem + h * kUnitN, xd + static_cast<uint64_t>((h * 16384) >> 4), wd, idesc, acc);
                 }
               }
             }
