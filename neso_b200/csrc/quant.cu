@@ -10,9 +10,9 @@
 //
 // One persistent CTA per SM; per 64-deep K block ("stage"):
 //   warp 0      TMA: raw weight tile(s) (int8 [64 k][128 n] or packed int4
-//               [32 byte-rows][128 n], 128-byte swizzled) and (int4, M >= 65)
+//               [32 byte-rows][128 n], 128-byte swizzled) and (int4, M >= 129)
 //               the group's fp16 scale row; warp 3: TMA of the activation tile
-//               (and, int4 M >= 65, of its E5M2 copy, 64-byte swizzled).
+//               (and, int4 M >= 129, of its E5M2 copy, 64-byte swizzled).
 //   warps 4-7,  dequantise raw -> fp16 directly into the MN-major 128-byte
 //   12-15       swizzled layout tcgen05 reads; fence.proxy.async; arrive. The
 //               two groups take alternate K blocks (or, with two channel
@@ -70,14 +70,14 @@ struct QCfg {
   // Three decoupled rings so weight bytes stay in flight independently of
   // the dequant and MMA rate:
   //   R  raw weight tiles (int8 [64 k][128 n] or packed int4 [32][128] plus,
-  //      M >= 65, the group's 128 fp16 scales), deep: TMA -> convert warps;
+  //      int4 M >= 129, the group's 128 fp16 scales), deep: TMA -> convert warps;
   //   X  activation tiles [kNX rows][64 k] fp16: TMA -> MMA;
-  //   F  dequantised fp16 weight tiles (int4 M >= 65: the fp16 w_hi tiles
+  //   F  dequantised fp16 weight tiles (int4 M >= 129: the fp16 w_hi tiles
   //      followed by the E5M2 w_lo tiles): convert -> MMA.
-  // int4 M <= 64 (kGS, group-scaled partial sums) adds a ring of scale rows
+  // int4 swapped layout (kGS, group-scaled partial sums) adds a ring of scale rows
   // (one 128-channel row per tile and group run): TMA -> epilogue.
   static constexpr bool kGS = kQ == kInt4G128 && kSwap;
-  // int4, M >= 65 layout: w = q * s is carried as w_hi = fp16(q * s) (kind::f16
+  // int4, M >= 65 layout (M >= 129): w = q * s is carried as w_hi = fp16(q * s) (kind::f16
   // MMAs) plus its exact remainder w_lo, which has at most 3 significant bits
   // and so is exact as E5M2 once scaled by 2^8; the w_lo MMAs run as
   // kind::f8f6f4 (twice the fp16 rate) against an E5M2 copy of X scaled by
@@ -1124,7 +1124,7 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ partial, int spli
   }
 }
 
-// X8[m][k] = E5M2(2^-8 * X[m][k]) for the int4 M >= 65 layout's w_lo MMAs,
+// X8[m][k] = E5M2(2^-8 * X[m][k]) for the w_lo MMAs of int4 in the M >= 65 layout (M >= 129),
 // round to nearest, saturating (rows of K bytes). Eight values per thread.
 __global__ void x_to_e5m2_kernel(const __half* __restrict__ X, int64_t ldx, int M, int K, uint8_t* __restrict__ X8) {
   pdl_launch_dependents();
@@ -1198,7 +1198,7 @@ int launch_wq(const QProblem& p, cudaStream_t stream) {
     if (rc != NESO_OK) return rc;
     y_tma = 1;
   }
-  // int4 M >= 65: the E5M2 copy of X for the w_lo MMAs, in the stream's
+  // int4 M >= 129: the E5M2 copy of X for the w_lo MMAs, in the stream's
   // input workspace, written by a conversion kernel launched just before.
   CUtensorMap tmX8 = tmX;
   uint8_t* x8 = nullptr;
